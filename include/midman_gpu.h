@@ -1,0 +1,69 @@
+/* Kernel-level C ABI of libmidman_gpu.so: the sm_100a kernels behind the
+ * training step, callable one at a time on caller-owned device buffers.
+ *
+ * The reference (MidManStudio/midman-ai) runs these computations as Rust
+ * functions over host slices; each entry point below names the reference
+ * function it replaces (path:line inside the reference project). A Rust FFI
+ * crate, or ctypes, binds these directly; INTEGRATION.md shows both.
+ *
+ * Conventions
+ *   - All pointers are device pointers unless a parameter says "host".
+ *   - f32 everywhere; token ids are int32.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = the legacy default
+ *     stream). Every call is asynchronous on that stream.
+ *   - Return value: 0 on success, a negative MM_GPU_ERR_* code otherwise, with a
+ *     message from mm_gpu_last_error(). Kernels that wait on hardware pipelines
+ *     record timeouts in a device flag read by mm_gpu_device_status().
+ *   - Row-major 2-D arrays with an explicit leading dimension in elements.
+ */
+#ifndef MIDMAN_GPU_H
+#define MIDMAN_GPU_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MM_GPU_EXPORT __attribute__((visibility("default")))
+#else
+#define MM_GPU_EXPORT
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MM_GPU_OK 0
+#define MM_GPU_ERR_ARGUMENT -1
+#define MM_GPU_ERR_SHAPE -3
+#define MM_GPU_ERR_DEVICE -6
+
+/* Arithmetic of the tensor-core products. */
+#define MM_GPU_TF32 0   /* one TF32 pass: ~1e-3 relative error per product */
+#define MM_GPU_3XTF32 1 /* hi*hi + hi*lo + lo*hi: close to f32 accuracy */
+
+/* Message of the last failing call on this thread (NUL-terminated, static until
+ * the next call). */
+MM_GPU_EXPORT const char *mm_gpu_last_error(void);
+
+/* Synchronizes `stream`, returns and clears the device error flag (0 = no
+ * kernel reported a timeout). */
+MM_GPU_EXPORT int32_t mm_gpu_device_status(void *stream);
+
+/* C[m, n] = sum_k A(m, k) * B(n, k)  (+ R[m, n] when R is not NULL; R may be C).
+ * A(m, k) = A[m * lda + k] when a_mn_major == 0 (K-major), A[k * lda + m] when 1.
+ * B(n, k) = B[n * ldb + k] when b_mn_major == 0, B[k * ldb + n] when 1.
+ * Leading dimensions must be multiples of 4 and pointers 16-byte aligned.
+ * Replaces crates/midman-tensor/src/kernels.rs:49-84 (gemm_nn, gemm_nt, gemm_tn)
+ * as called from ops_matmul.rs:55-125:
+ *   gemm_nn  C = A B     -> a K-major,  b MN-major
+ *   gemm_nt  C = A B^T   -> a K-major,  b K-major
+ *   gemm_tn  C = A^T B   -> a MN-major, b MN-major */
+MM_GPU_EXPORT int32_t mm_gpu_gemm(int32_t m, int32_t n, int32_t k, const float *a, int64_t lda, int32_t a_mn_major,
+                    const float *b, int64_t ldb, int32_t b_mn_major, float *c, int64_t ldc,
+                    const float *r, int64_t ldr, int32_t precision, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

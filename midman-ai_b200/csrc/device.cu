@@ -1,0 +1,72 @@
+#include "device.h"
+
+#include <mutex>
+#include <stdexcept>
+#include <vector>
+
+#include "ptx.cuh"
+
+namespace mm {
+
+namespace {
+std::mutex g_mu;
+std::vector<DeviceContext> g_ctx;
+}  // namespace
+
+void check_cuda(cudaError_t e, const char* what) {
+  if (e != cudaSuccess)
+    throw std::runtime_error(std::string(what) + ": " + cudaGetErrorName(e) + " (" + cudaGetErrorString(e) + ")");
+}
+
+DeviceContext& device_context() {
+  int dev = 0;
+  check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+  std::lock_guard<std::mutex> lock(g_mu);
+  if (g_ctx.size() <= static_cast<size_t>(dev)) g_ctx.resize(dev + 1);
+  DeviceContext& c = g_ctx[dev];
+  if (c.device < 0) {
+    c.device = dev;
+    check_cuda(cudaMalloc(&c.d_err, 64), "cudaMalloc(error flag)");
+    check_cuda(cudaMemset(c.d_err, 0, 64), "cudaMemset(error flag)");
+    check_cuda(cudaDeviceGetAttribute(&c.sm_count, cudaDevAttrMultiProcessorCount, dev), "sm count");
+  }
+  return c;
+}
+
+void* device_scratch(size_t bytes, cudaStream_t stream) {
+  DeviceContext& c = device_context();
+  if (bytes > c.scratch_bytes) {
+    if (c.scratch) {
+      check_cuda(cudaStreamSynchronize(stream), "scratch sync");
+      check_cuda(cudaFree(c.scratch), "cudaFree(scratch)");
+      c.scratch = nullptr;
+    }
+    size_t want = bytes + bytes / 4 + (1u << 20);
+    check_cuda(cudaMalloc(&c.scratch, want), "cudaMalloc(scratch)");
+    c.scratch_bytes = want;
+  }
+  return c.scratch;
+}
+
+int take_device_error(cudaStream_t stream) {
+  DeviceContext& c = device_context();
+  int code = 0;
+  check_cuda(cudaMemcpyAsync(&code, c.d_err, sizeof(int), cudaMemcpyDeviceToHost, stream), "read error flag");
+  check_cuda(cudaStreamSynchronize(stream), "sync error flag");
+  if (code) check_cuda(cudaMemsetAsync(c.d_err, 0, sizeof(int), stream), "clear error flag");
+  return code;
+}
+
+std::string device_error_message(int code) {
+  switch (code) {
+    case kErrNone: return "no device error";
+    case kErrWaitFull: return "GEMM: UMMA issuer timed out waiting for a TMA stage";
+    case kErrWaitEmpty: return "GEMM: TMA producer timed out waiting for a free stage";
+    case kErrWaitAccum: return "GEMM: epilogue timed out waiting for the accumulator";
+    case kErrWaitDrain: return "GEMM: teardown timed out draining TMA copies";
+    case kErrBadShape: return "kernel rejected its shape";
+    default: return "device error " + std::to_string(code);
+  }
+}
+
+}  // namespace mm

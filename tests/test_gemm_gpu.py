@@ -1,0 +1,87 @@
+"""The tcgen05 TF32 GEMM against a float64 PyTorch product of the same operands.
+
+The reference computes these products with the plain f32 loops of
+crates/midman-tensor/src/kernels.rs:87-109 (gemm_nn / gemm_tn, gemm_nt through a
+transposed copy, kernels.rs:66-75). TF32 keeps 10 mantissa bits per operand, so
+one TF32 pass is held to relative L2 error 5e-3; the 3xTF32 split to 1e-5 (the
+tolerances the training-step parity gates use for gradients).
+"""
+import pytest
+
+torch = pytest.importorskip("torch")
+
+pytestmark = pytest.mark.gpu
+
+TF32_TOL = 5e-3
+X3_TOL = 1e-5
+
+
+def round4(n):
+    return (n + 3) // 4 * 4
+
+
+def operand(rows, cols, mn_major, gen):
+    """Logical [rows x cols] (rows = M or N, cols = K) stored K- or MN-major, ld a multiple of 4."""
+    if not mn_major:
+        ld = round4(cols)
+        store = torch.randn(rows, ld, generator=gen, device="cuda")
+        return store, ld, store[:, :cols]
+    ld = round4(rows)
+    store = torch.randn(cols, ld, generator=gen, device="cuda")
+    return store, ld, store[:, :rows].t()
+
+
+def rel_l2(got, want):
+    return ((got.double() - want).norm() / want.norm().clamp_min(1e-300)).item()
+
+
+SHAPES = [(128, 256, 32), (256, 512, 512), (300, 344, 200), (64, 8, 12), (1000, 1032, 1000),
+          (4096, 1408, 512)]
+MAJORS = [(False, True), (False, False), (True, True), (True, False)]
+
+
+@pytest.mark.parametrize("shape", SHAPES)
+@pytest.mark.parametrize("majors", MAJORS)
+@pytest.mark.parametrize("precision", [0, 1])
+def test_gemm_matches_float64(mm, shape, majors, precision):
+    m, n, k = shape
+    a_mn, b_mn = majors
+    gen = torch.Generator(device="cuda").manual_seed(m * 7 + n * 3 + k + a_mn * 2 + b_mn)
+    a_store, lda, a = operand(m, k, a_mn, gen)
+    b_store, ldb, b = operand(n, k, b_mn, gen)
+    ldc = round4(n)
+    c = torch.full((m, ldc), float("nan"), device="cuda")
+    mm.gemm(a_store, b_store, c, m=m, n=n, k=k, lda=lda, ldb=ldb, ldc=ldc,
+            a_mn_major=a_mn, b_mn_major=b_mn, precision=precision)
+    mm.device_status()
+    want = a.double() @ b.double().t()
+    got = c[:, :n]
+    assert torch.isfinite(got).all()
+    err = rel_l2(got, want)
+    assert err < (TF32_TOL if precision == 0 else X3_TOL), err
+    if ldc > n:  # padding columns are not written
+        assert torch.isnan(c[:, n:]).all()
+
+
+@pytest.mark.parametrize("precision", [0, 1])
+def test_gemm_adds_the_residual_in_place(mm, precision):
+    m, n, k = 384, 512, 256
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    a = torch.randn(m, k, generator=gen, device="cuda")
+    w = torch.randn(k, n, generator=gen, device="cuda")
+    resid = torch.randn(m, n, generator=gen, device="cuda")
+    c = resid.clone()
+    mm.gemm(a, w, c, m=m, n=n, k=k, lda=k, ldb=n, ldc=n, a_mn_major=False, b_mn_major=True,
+            r=c, ldr=n, precision=precision)
+    mm.device_status()
+    want = resid.double() + a.double() @ w.double()
+    assert rel_l2(c, want) < (TF32_TOL if precision == 0 else X3_TOL)
+
+
+def test_gemm_rejects_misaligned_leading_dimensions(mm):
+    a = torch.randn(16, 10, device="cuda")
+    b = torch.randn(16, 12, device="cuda")
+    c = torch.empty(16, 16, device="cuda")
+    with pytest.raises(mm.MidmanGpuError):
+        mm.gemm(a, b, c, m=16, n=16, k=10, lda=10, ldb=12, ldc=16, a_mn_major=False,
+                b_mn_major=False)
