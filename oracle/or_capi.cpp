@@ -196,6 +196,28 @@ void or_adamw_moments(void* op, float* m, float* v) {
   std::memcpy(v, o->v.data(), o->v.size() * sizeof(float));
 }
 
+}  // extern "C"
+
+namespace orc {
+void adamw_update(float* x, const float* g, float* m, float* v, size_t n, bool decay_on, uint64_t step, float lr,
+                  float beta1, float beta2, float eps, float weight_decay) {
+  const double t = static_cast<double>(step);
+  const float bias1 = static_cast<float>(1.0 - std::pow(static_cast<double>(beta1), t));
+  const float bias2_sqrt = static_cast<float>(std::sqrt(1.0 - std::pow(static_cast<double>(beta2), t)));
+  const float step_size = lr / bias1;
+  const float decay = decay_on ? 1.0f - lr * weight_decay : 1.0f;
+#pragma omp parallel for schedule(static) if (n > (1u << 16))
+  for (long long i = 0; i < static_cast<long long>(n); ++i) {
+    x[i] *= decay;
+    m[i] = beta1 * m[i] + (1.0f - beta1) * g[i];
+    v[i] = beta2 * v[i] + (1.0f - beta2) * g[i] * g[i];
+    x[i] -= step_size * m[i] / (std::sqrt(v[i]) / bias2_sqrt + eps);
+  }
+}
+}  // namespace orc
+
+extern "C" {
+
 // adamw.rs:141-217 (validated first: a non-finite gradient or lr changes nothing)
 int or_adamw_step(void* op, void* mp, const float* g, float lr) {
   AdamW* o = static_cast<AdamW*>(op);
@@ -205,21 +227,30 @@ int or_adamw_step(void* op, void* mp, const float* g, float lr) {
   for (size_t i = 0; i < n; ++i)
     if (!std::isfinite(g[i])) return -1;
   o->steps += 1;
-  const double t = static_cast<double>(o->steps);
-  const float bias1 = static_cast<float>(1.0 - std::pow(static_cast<double>(o->beta1), t));
-  const float bias2_sqrt = static_cast<float>(std::sqrt(1.0 - std::pow(static_cast<double>(o->beta2), t)));
-  const float b1 = o->beta1, b2 = o->beta2, eps = o->eps;
-  const float step_size = lr / bias1;
-  const float decay_on = 1.0f - lr * o->wd;
-  float* x = m->params.data();
-#pragma omp parallel for schedule(static)
-  for (long long i = 0; i < static_cast<long long>(n); ++i) {
-    const float decay = o->decay[i] ? decay_on : 1.0f;
-    x[i] *= decay;
-    o->m[i] = b1 * o->m[i] + (1.0f - b1) * g[i];
-    o->v[i] = b2 * o->v[i] + (1.0f - b2) * g[i] * g[i];
-    x[i] -= step_size * o->m[i] / (std::sqrt(o->v[i]) / bias2_sqrt + eps);
-  }
+  for (const ParamTensor& t : m->tensors)
+    adamw_update(m->params.data() + t.offset, g + t.offset, o->m.data() + t.offset, o->v.data() + t.offset,
+                 t.numel, t.shape.size() >= 2, o->steps, lr, o->beta1, o->beta2, o->eps, o->wd);
+  return 0;
+}
+
+int or_adamw_update(float* x, const float* g, float* m, float* v, size_t n, int decay, uint64_t step, float lr,
+                    float beta1, float beta2, float eps, float weight_decay) {
+  adamw_update(x, g, m, v, n, decay != 0, step, lr, beta1, beta2, eps, weight_decay);
+  return 0;
+}
+
+void or_gemm_nn(const float* a, const float* b, float* c, size_t m, size_t k, size_t n) { gemm_nn(a, b, c, m, k, n); }
+void or_gemm_nt(const float* a, const float* b, float* c, size_t m, size_t k, size_t n) { gemm_nt(a, b, c, m, k, n); }
+void or_gemm_tn(const float* a, const float* b, float* c, size_t k, size_t m, size_t n) { gemm_tn(a, b, c, k, m, n); }
+void or_softmax_rows(const float* x, float* y, size_t rows, size_t cols) { softmax_rows(x, y, rows, cols); }
+float or_cross_entropy(const float* logits, const int32_t* targets, size_t n, size_t v, float* grad) {
+  return cross_entropy(logits, targets, n, v, grad);
+}
+int or_causal_attention(const double* cfg, const float* q, const float* k, const float* v, int batch, int seq,
+                        float* out, float* probs) {
+  const Config c = config_from(cfg);
+  if (!validate(c).empty()) return -2;
+  causal_attention(c, q, k, v, batch, seq, out, probs);
   return 0;
 }
 

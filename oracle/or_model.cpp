@@ -449,3 +449,59 @@ int model_loss(Model& m, const int32_t* inputs, const int32_t* targets, int batc
 }
 
 }  // namespace orc
+
+namespace orc {
+
+// Stand-alone entry points for the known-answer tests: the same code paths the
+// model uses, on caller-provided arrays.
+void causal_attention(const Config& c, const float* q, const float* k, const float* v, size_t B, size_t T,
+                      float* out, float* probs) {
+  LayerSaved L;
+  const size_t H = c.n_heads, Hkv = c.n_kv_heads, hd = c.head_dim();
+  L.q.assign(q, q + B * H * T * hd);
+  L.k.assign(k, k + B * Hkv * T * hd);
+  L.v.assign(v, v + B * Hkv * T * hd);
+  Vec ctx;
+  attention_fwd(c, B, T, L, ctx);
+  std::memcpy(out, ctx.data(), ctx.size() * sizeof(float));
+  if (probs) std::memcpy(probs, L.probs.data(), L.probs.size() * sizeof(float));
+}
+
+// ops_reduce.rs:97-126, contiguous-axis path.
+void softmax_rows(const float* x, float* y, size_t rows, size_t cols) {
+  for (size_t r = 0; r < rows; ++r) {
+    const float* row = x + r * cols;
+    float* dst = y + r * cols;
+    float mx = -std::numeric_limits<float>::infinity();
+    for (size_t j = 0; j < cols; ++j) mx = std::fmax(mx, row[j]);
+    float sum = 0.0f;
+    for (size_t j = 0; j < cols; ++j) {
+      const float e = std::exp(row[j] - mx);
+      dst[j] = e;
+      sum += e;
+    }
+    const float inv = 1.0f / sum;
+    for (size_t j = 0; j < cols; ++j) dst[j] *= inv;
+  }
+}
+
+// ops_reduce.rs:236-276: mean loss (f64 total) and, if grad != null, d loss / d logits.
+float cross_entropy(const float* logits, const int32_t* targets, size_t n, size_t v, float* grad) {
+  double total = 0.0;
+  const float scale = 1.0f / static_cast<float>(n);
+  for (size_t r = 0; r < n; ++r) {
+    const float* row = logits + r * v;
+    float mx = -std::numeric_limits<float>::infinity();
+    for (size_t j = 0; j < v; ++j) mx = std::fmax(mx, row[j]);
+    float sum = 0.0f;
+    for (size_t j = 0; j < v; ++j) sum += std::exp(row[j] - mx);
+    total += static_cast<double>(mx + std::log(sum) - row[targets[r]]);
+    if (grad) {
+      for (size_t j = 0; j < v; ++j) grad[r * v + j] = std::exp(row[j] - mx) / sum * scale;
+      grad[r * v + targets[r]] -= scale;
+    }
+  }
+  return static_cast<float>(total / static_cast<double>(n));
+}
+
+}  // namespace orc

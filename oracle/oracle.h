@@ -95,6 +95,23 @@ size_t or_batcher_num_sequences(void *b);
 /* inputs/targets: batch * seq ids each. Writes epoch and index of the batch. */
 void or_batcher_next(void *b, int32_t *inputs, int32_t *targets, uint64_t *epoch, uint64_t *index);
 
+/* ---- Single-op known-answer entry points ---- */
+/* kernels.rs:87-109 and :66-75. gemm_tn: C[m,n] += A[k,m]^T B[k,n]. */
+void or_gemm_nn(const float *a, const float *b, float *c, size_t m, size_t k, size_t n);
+void or_gemm_nt(const float *a, const float *b, float *c, size_t m, size_t k, size_t n);
+void or_gemm_tn(const float *a, const float *b, float *c, size_t k, size_t m, size_t n);
+/* ops_reduce.rs:97-126 (contiguous path). */
+void or_softmax_rows(const float *x, float *y, size_t rows, size_t cols);
+/* ops_reduce.rs:236-276: mean loss; grad (nullable) = d loss / d logits. */
+float or_cross_entropy(const float *logits, const int32_t *targets, size_t n, size_t v, float *grad);
+/* causal_attention (attention.rs:98-102): q [B,H,T,hd], k/v [B,Hkv,T,hd] -> out [B,H,T,hd],
+ * probs [B,H,T,T] (nullable). Head counts and head_dim from cfg. */
+int or_causal_attention(const double *cfg, const float *q, const float *k, const float *v, int batch, int seq,
+                        float *out, float *probs);
+/* One AdamW update of one parameter (adamw.rs:192-215). */
+int or_adamw_update(float *x, const float *g, float *m, float *v, size_t n, int decay, uint64_t step, float lr,
+                    float beta1, float beta2, float eps, float weight_decay);
+
 /* Threads the oracle uses for its parallel loops (0 = OpenMP default). */
 void or_set_threads(int n);
 

@@ -82,4 +82,14 @@ void gemm_tn(const float* a, const float* b, float* c, size_t k, size_t m, size_
 
 void set_threads(int n);
 
+// Known-answer entry points (or_model.cpp).
+void causal_attention(const Config& c, const float* q, const float* k, const float* v, size_t B, size_t T,
+                      float* out, float* probs);
+void softmax_rows(const float* x, float* y, size_t rows, size_t cols);
+float cross_entropy(const float* logits, const int32_t* targets, size_t n, size_t v, float* grad);
+
+// One AdamW update over a flat array (adamw.rs:192-215); decay: the parameter has rank >= 2.
+void adamw_update(float* x, const float* g, float* m, float* v, size_t n, bool decay, uint64_t step, float lr,
+                  float beta1, float beta2, float eps, float weight_decay);
+
 }  // namespace orc
