@@ -1,0 +1,33 @@
+// Causal grouped-query attention, forward and backward, on token-major
+// projections (no head split/merge copies): q [B*T, H, hd] with row stride ldq,
+// k and v [B*T, Hkv, hd] with row strides ldk/ldv, o [B*T, H, hd] (ldo).
+// Replaces crates/midman-nn/src/attention.rs:79-102 and :146-170 (scores,
+// -1e9 mask, softmax, P v, GQA head expansion) and their autograd backward.
+#pragma once
+#include <cuda_runtime.h>
+
+namespace mm {
+
+struct AttnShape {
+  int B, T, H, Hkv, hd;
+  long long ldq, ldk, ldv, ldo;
+  float scale;  // 1 / sqrt(hd)
+};
+
+// o = softmax(q k^T * scale + causal mask) v; lse [B, H, T] = log-sum-exp of each
+// scaled score row (natural log), saved for the backward pass.
+void attention_forward(const AttnShape& s, const float* q, const float* k, const float* v, float* o, float* lse,
+                       cudaStream_t stream);
+
+// Given do (same layout as o), writes dq, dk, dv (dk/dv summed over each key
+// head's group of query heads). `delta` is scratch of B*H*T floats.
+void attention_backward(const AttnShape& s, const float* q, const float* k, const float* v, const float* o,
+                        const float* lse, const float* dout, long long lddo, float* dq, float* dk, float* dv,
+                        float* delta, cudaStream_t stream);
+
+// Attention probabilities [B, H, T, T] (zeros above the diagonal), for the
+// traced forward (model.rs:116-125, attention.rs:79-85).
+void attention_probs(const AttnShape& s, const float* q, const float* k, const float* lse, float* probs,
+                     cudaStream_t stream);
+
+}  // namespace mm

@@ -1,0 +1,460 @@
+// Bandwidth-bound kernels of the training step: embedding, RMSNorm, RoPE,
+// SwiGLU, softmax cross-entropy and the elementwise helpers. Each cites the
+// reference function whose arithmetic it follows. Rows are processed by whole
+// blocks with 128-bit accesses where the widths allow; reductions are tree
+// reductions in a fixed order, so results are identical from run to run.
+#include <cuda_runtime.h>
+
+#include <cfloat>
+#include <cmath>
+#include <stdexcept>
+
+#include "kernels.h"
+
+namespace mm {
+
+namespace {
+
+constexpr int kThreads = 256;
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Sum over the block; every thread gets the result. `red` holds 32 floats.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  const int nw = (blockDim.x + 31) >> 5;
+  float t = lane < nw ? red[lane] : 0.0f;
+  return warp_sum(t);
+}
+
+__device__ __forceinline__ double block_sum_d(double v, double* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = warp_sum_d(v);
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  const int nw = (blockDim.x + 31) >> 5;
+  double t = lane < nw ? red[lane] : 0.0;
+  return warp_sum_d(t);
+}
+
+int grid_for(long long n, int per_thread = 4) {
+  long long b = (n + static_cast<long long>(kThreads) * per_thread - 1) / (static_cast<long long>(kThreads) * per_thread);
+  if (b < 1) b = 1;
+  if (b > 148 * 64) b = 148 * 64;
+  return static_cast<int>(b);
+}
+
+void check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+// ---------------------------------------------------------------- embedding
+__global__ void embedding_fwd_kernel(const int32_t* __restrict__ ids, const float* __restrict__ table, int dim,
+                                     float* __restrict__ out) {
+  const int r = blockIdx.x;
+  const float4* src = reinterpret_cast<const float4*>(table + static_cast<long long>(ids[r]) * dim);
+  float4* dst = reinterpret_cast<float4*>(out + static_cast<long long>(r) * dim);
+  for (int j = threadIdx.x; j < dim / 4; j += blockDim.x) dst[j] = src[j];
+}
+
+// One block per distinct id: the existing row plus the positions' rows in
+// ascending position order (ops_shape.rs:262-272 adds them in that order).
+__global__ void embedding_bwd_kernel(const int32_t* __restrict__ uniq, const int32_t* __restrict__ offsets,
+                                     const int32_t* __restrict__ positions, const float* __restrict__ dx, int dim,
+                                     float* __restrict__ dtable) {
+  const int u = blockIdx.x;
+  const int beg = offsets[u], end = offsets[u + 1];
+  float* row = dtable + static_cast<long long>(uniq[u]) * dim;
+  for (int j = threadIdx.x; j < dim; j += blockDim.x) {
+    float acc = row[j];
+    for (int p = beg; p < end; ++p) acc += dx[static_cast<long long>(positions[p]) * dim + j];
+    row[j] = acc;
+  }
+}
+
+// ---------------------------------------------------------------- RMSNorm
+__global__ void rmsnorm_fwd_kernel(const float* __restrict__ x, const float* __restrict__ w, int dim, float eps,
+                                   float* __restrict__ y, float* __restrict__ rstd) {
+  __shared__ float red[32];
+  const long long r = blockIdx.x;
+  const float4* xr = reinterpret_cast<const float4*>(x + r * dim);
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+  float4* yr = reinterpret_cast<float4*>(y + r * dim);
+  float ss = 0.0f;
+  for (int j = threadIdx.x; j < dim / 4; j += blockDim.x) {
+    const float4 v = xr[j];
+    ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+  }
+  ss = block_sum(ss, red);
+  // mean_axis = sum * (1/len) (ops_reduce.rs:87-90), + eps, ^(-1/2)
+  const float t = ss * (1.0f / static_cast<float>(dim)) + eps;
+  const float inv = 1.0f / sqrtf(t);
+  if (threadIdx.x == 0) rstd[r] = inv;
+  for (int j = threadIdx.x; j < dim / 4; j += blockDim.x) {
+    const float4 v = xr[j], g = w4[j];
+    yr[j] = make_float4((v.x * inv) * g.x, (v.y * inv) * g.y, (v.z * inv) * g.z, (v.w * inv) * g.w);
+  }
+}
+
+// Each block owns a contiguous range of rows; per row it writes dx and keeps the
+// row's contribution to dw in registers (G float4 column groups per thread).
+template <int G>
+__global__ void rmsnorm_bwd_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                                   const float* __restrict__ rstd, const float* __restrict__ dy, int rows, int dim,
+                                   int rows_per_block, float* dx, const float* dres, float* __restrict__ ws) {
+  __shared__ float red[32];
+  const int r0 = blockIdx.x * rows_per_block;
+  const int r1 = min(rows, r0 + rows_per_block);
+  const int nv = dim / 4;
+  const float4* w4 = reinterpret_cast<const float4*>(w);
+  float4 acc[G];
+  float4 wv[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    acc[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+    const int j = threadIdx.x + g * blockDim.x;
+    wv[g] = j < nv ? w4[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  const float inv_dim = 1.0f / static_cast<float>(dim);
+  for (int r = r0; r < r1; ++r) {
+    const float4* xr = reinterpret_cast<const float4*>(x + static_cast<long long>(r) * dim);
+    const float4* gr = reinterpret_cast<const float4*>(dy + static_cast<long long>(r) * dim);
+    float4 xv[G], gv[G];
+    float dot = 0.0f;
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const int j = threadIdx.x + g * blockDim.x;
+      if (j < nv) {
+        xv[g] = xr[j];
+        gv[g] = gr[j];
+        dot += (gv[g].x * wv[g].x) * xv[g].x + (gv[g].y * wv[g].y) * xv[g].y + (gv[g].z * wv[g].z) * xv[g].z +
+               (gv[g].w * wv[g].w) * xv[g].w;
+      }
+    }
+    dot = block_sum(dot, red);
+    const float inv = rstd[r];
+    // d/dx of x*inv*w through inv = (mean(x^2)+eps)^-1/2: the powf closure gives
+    // -0.5*t^-1.5 = -0.5*inv^3, the mean's 1/len, and x*x contributes twice.
+    const float dsum = (dot * (-0.5f * inv * inv * inv)) * inv_dim;
+    float4* dxr = reinterpret_cast<float4*>(dx + static_cast<long long>(r) * dim);
+    const float4* dr = dres ? reinterpret_cast<const float4*>(dres + static_cast<long long>(r) * dim) : nullptr;
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const int j = threadIdx.x + g * blockDim.x;
+      if (j < nv) {
+        const float4 b = make_float4(dsum * xv[g].x, dsum * xv[g].y, dsum * xv[g].z, dsum * xv[g].w);
+        float4 o = make_float4(((gv[g].x * wv[g].x) * inv + b.x) + b.x, ((gv[g].y * wv[g].y) * inv + b.y) + b.y,
+                               ((gv[g].z * wv[g].z) * inv + b.z) + b.z, ((gv[g].w * wv[g].w) * inv + b.w) + b.w);
+        if (dr) {
+          const float4 d = dr[j];
+          o.x += d.x; o.y += d.y; o.z += d.z; o.w += d.w;
+        }
+        dxr[j] = o;
+        acc[g].x += gv[g].x * (xv[g].x * inv);
+        acc[g].y += gv[g].y * (xv[g].y * inv);
+        acc[g].z += gv[g].z * (xv[g].z * inv);
+        acc[g].w += gv[g].w * (xv[g].w * inv);
+      }
+    }
+  }
+  float4* out = reinterpret_cast<float4*>(ws + static_cast<long long>(blockIdx.x) * dim);
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const int j = threadIdx.x + g * blockDim.x;
+    if (j < nv) out[j] = acc[g];
+  }
+}
+
+// dw[j] = sum over blocks of the partials, in block order.
+__global__ void column_sum_kernel(const float* __restrict__ ws, int nblk, int dim, float* __restrict__ dw) {
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= dim) return;
+  float s = 0.0f;
+  for (int b = 0; b < nblk; ++b) s += ws[static_cast<long long>(b) * dim + j];
+  dw[j] = s;
+}
+
+int rmsnorm_bwd_blocks(int rows) { return rows < 296 ? rows : 296; }
+
+// ---------------------------------------------------------------- RoPE
+__global__ void rope_kernel(float* x, int rows, int T, int heads, int half, long long ld,
+                            const float* __restrict__ cos_t, const float* __restrict__ sin_t, float sign) {
+  const long long total = static_cast<long long>(rows) * heads * half;
+  for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int i = static_cast<int>(idx % half);
+    const long long rh = idx / half;
+    const int h = static_cast<int>(rh % heads);
+    const long long r = rh / heads;
+    const int t = static_cast<int>(r % T);
+    float* v = x + r * ld + static_cast<long long>(h) * 2 * half;
+    const float c = cos_t[t * half + i], s = sign * sin_t[t * half + i];
+    const float x1 = v[i], x2 = v[i + half];
+    // forward (rope.rs:30-31): (x1 c - x2 s, x2 c + x1 s); gradient: s -> -s
+    v[i] = x1 * c - x2 * s;
+    v[i + half] = x2 * c + x1 * s;
+  }
+}
+
+// ---------------------------------------------------------------- SwiGLU
+__device__ __forceinline__ float sigmoidf_ref(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+__global__ void swiglu_fwd_kernel(const float* __restrict__ g, const float* __restrict__ u, float* __restrict__ act,
+                                  long long n) {
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const float x = g[i];
+    act[i] = (x * sigmoidf_ref(x)) * u[i];  // silu (ops_elementwise.rs:355-364) then mul
+  }
+}
+
+__global__ void swiglu_bwd_kernel(float* g, float* u, const float* __restrict__ dact, long long n) {
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const float x = g[i], up = u[i], d = dact[i];
+    const float s = sigmoidf_ref(x);
+    const float silu = x * s;
+    g[i] = (d * up) * (s * (1.0f + x * (1.0f - s)));
+    u[i] = d * silu;
+  }
+}
+
+// ---------------------------------------------------------------- cross-entropy
+struct MaxSum {
+  float m, s;
+};
+
+__device__ __forceinline__ MaxSum combine(MaxSum a, MaxSum b) {
+  if (a.m == -INFINITY) return b;
+  if (b.m == -INFINITY) return a;
+  const float m = fmaxf(a.m, b.m);
+  return {m, a.s * expf(a.m - m) + b.s * expf(b.m - m)};
+}
+
+__global__ void cross_entropy_kernel(float* logits, long long ld, const int32_t* __restrict__ targets, int vocab,
+                                     float grad_scale, float* __restrict__ row_loss) {
+  __shared__ float sm[32], ss[32];
+  __shared__ float row_max, row_sum;
+  const long long r = blockIdx.x;
+  float* z = logits + r * ld;
+  MaxSum acc{-INFINITY, 0.0f};
+  for (int j = threadIdx.x; j < vocab; j += blockDim.x) {
+    const float v = z[j];
+    if (v > acc.m) {
+      acc.s = (acc.m == -INFINITY ? 0.0f : acc.s * expf(acc.m - v)) + 1.0f;
+      acc.m = v;
+    } else {
+      acc.s += expf(v - acc.m);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    MaxSum other{__shfl_xor_sync(0xffffffffu, acc.m, o), __shfl_xor_sync(0xffffffffu, acc.s, o)};
+    acc = combine(acc, other);
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) {
+    sm[warp] = acc.m;
+    ss[warp] = acc.s;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = blockDim.x >> 5;
+    MaxSum a = lane < nw ? MaxSum{sm[lane], ss[lane]} : MaxSum{-INFINITY, 0.0f};
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      MaxSum other{__shfl_xor_sync(0xffffffffu, a.m, o), __shfl_xor_sync(0xffffffffu, a.s, o)};
+      a = combine(a, other);
+    }
+    if (lane == 0) {
+      row_max = a.m;
+      row_sum = a.s;
+      const int t = targets[r];
+      row_loss[r] = a.m + logf(a.s) - z[t];  // ops_reduce.rs:256-258
+    }
+  }
+  __syncthreads();
+  const float mx = row_max, sum = row_sum;
+  const int t = targets[r];
+  for (int j = threadIdx.x; j < vocab; j += blockDim.x) {
+    float d = expf(z[j] - mx) / sum * grad_scale;  // ops_reduce.rs:266-270
+    if (j == t) d -= grad_scale;
+    z[j] = d;
+  }
+}
+
+__global__ void mean_loss_kernel(const float* __restrict__ row_loss, int rows, double* out) {
+  __shared__ double red[32];
+  double s = 0.0;
+  for (int i = threadIdx.x; i < rows; i += blockDim.x) s += static_cast<double>(row_loss[i]);
+  s = block_sum_d(s, red);
+  if (threadIdx.x == 0) out[0] = s / static_cast<double>(rows);
+}
+
+__global__ void argmax_kernel(const float* __restrict__ logits, long long ld, int vocab, int32_t* out) {
+  __shared__ float bv[32];
+  __shared__ int bi[32];
+  const float* z = logits + blockIdx.x * ld;
+  float best = -INFINITY;
+  int idx = 0x7fffffff;
+  for (int j = threadIdx.x; j < vocab; j += blockDim.x) {
+    const float v = z[j];
+    if (v > best || (v == best && j < idx)) {
+      best = v;
+      idx = j;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+    if (ov > best || (ov == best && oi < idx)) {
+      best = ov;
+      idx = oi;
+    }
+  }
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) {
+    bv[warp] = best;
+    bi[warp] = idx;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float b = bv[0];
+    int i = bi[0];
+    for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w)
+      if (bv[w] > b || (bv[w] == b && bi[w] < i)) {
+        b = bv[w];
+        i = bi[w];
+      }
+    out[blockIdx.x] = i == 0x7fffffff ? 0 : i;
+  }
+}
+
+// ---------------------------------------------------------------- misc
+__global__ void add_kernel(const float* a, const float* b, float* out, long long n) {
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x)
+    out[i] = a[i] + b[i];
+}
+
+__global__ void scale_kernel(float* x, float f, long long n) {
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x)
+    x[i] *= f;
+}
+
+}  // namespace
+
+void embedding_forward(const int32_t* ids, int rows, const float* table, int dim, float* out, cudaStream_t s) {
+  if (rows <= 0) return;
+  embedding_fwd_kernel<<<rows, 128, 0, s>>>(ids, table, dim, out);
+  check_launch("embedding_forward");
+}
+
+void embedding_backward(const int32_t* uniq, const int32_t* offsets, const int32_t* positions, int n_uniq,
+                        const float* dx, int dim, float* dtable, cudaStream_t s) {
+  if (n_uniq <= 0) return;
+  embedding_bwd_kernel<<<n_uniq, 256, 0, s>>>(uniq, offsets, positions, dx, dim, dtable);
+  check_launch("embedding_backward");
+}
+
+void rmsnorm_forward(const float* x, const float* w, int rows, int dim, float eps, float* y, float* rstd,
+                     cudaStream_t s) {
+  if (rows <= 0) return;
+  rmsnorm_fwd_kernel<<<rows, kThreads, 0, s>>>(x, w, dim, eps, y, rstd);
+  check_launch("rmsnorm_forward");
+}
+
+long long rmsnorm_ws_floats(int rows, int dim) { return static_cast<long long>(rmsnorm_bwd_blocks(rows)) * dim; }
+
+void rmsnorm_backward(const float* x, const float* w, const float* rstd, const float* dy, int rows, int dim,
+                      float* dx, const float* dres, float* dw, float* ws, cudaStream_t s) {
+  if (rows <= 0) return;
+  const int nblk = rmsnorm_bwd_blocks(rows);
+  const int rpb = (rows + nblk - 1) / nblk;
+  const int groups = (dim / 4 + kThreads - 1) / kThreads;
+  if (groups <= 1)
+    rmsnorm_bwd_kernel<1><<<nblk, kThreads, 0, s>>>(x, w, rstd, dy, rows, dim, rpb, dx, dres, ws);
+  else if (groups <= 2)
+    rmsnorm_bwd_kernel<2><<<nblk, kThreads, 0, s>>>(x, w, rstd, dy, rows, dim, rpb, dx, dres, ws);
+  else if (groups <= 4)
+    rmsnorm_bwd_kernel<4><<<nblk, kThreads, 0, s>>>(x, w, rstd, dy, rows, dim, rpb, dx, dres, ws);
+  else if (groups <= 8)
+    rmsnorm_bwd_kernel<8><<<nblk, kThreads, 0, s>>>(x, w, rstd, dy, rows, dim, rpb, dx, dres, ws);
+  else
+    throw std::runtime_error("rmsnorm_backward: d_model above 8192 is not supported");
+  check_launch("rmsnorm_backward");
+  column_sum_kernel<<<(dim + 255) / 256, 256, 0, s>>>(ws, nblk, dim, dw);
+  check_launch("rmsnorm_backward(column sum)");
+}
+
+void rope(float* x, int rows, int T, int heads, int hd, long long ld, const float* cos_t, const float* sin_t,
+          bool backward, cudaStream_t s) {
+  const long long total = static_cast<long long>(rows) * heads * (hd / 2);
+  if (total <= 0) return;
+  rope_kernel<<<grid_for(total, 1), kThreads, 0, s>>>(x, rows, T, heads, hd / 2, ld, cos_t, sin_t,
+                                                       backward ? -1.0f : 1.0f);
+  check_launch("rope");
+}
+
+void swiglu_forward(const float* g, const float* u, float* act, long long n, cudaStream_t s) {
+  if (n <= 0) return;
+  swiglu_fwd_kernel<<<grid_for(n, 4), kThreads, 0, s>>>(g, u, act, n);
+  check_launch("swiglu_forward");
+}
+
+void swiglu_backward(float* g, float* u, const float* dact, long long n, cudaStream_t s) {
+  if (n <= 0) return;
+  swiglu_bwd_kernel<<<grid_for(n, 4), kThreads, 0, s>>>(g, u, dact, n);
+  check_launch("swiglu_backward");
+}
+
+void cross_entropy(float* logits, long long ld, const int32_t* targets, int rows, int vocab, float grad_scale,
+                   float* row_loss, cudaStream_t s) {
+  if (rows <= 0) return;
+  const int threads = vocab >= 8192 ? 1024 : 256;
+  cross_entropy_kernel<<<rows, threads, 0, s>>>(logits, ld, targets, vocab, grad_scale, row_loss);
+  check_launch("cross_entropy");
+}
+
+void mean_loss(const float* row_loss, int rows, double* loss_out, cudaStream_t s) {
+  mean_loss_kernel<<<1, 1024, 0, s>>>(row_loss, rows, loss_out);
+  check_launch("mean_loss");
+}
+
+void argmax_rows(const float* logits, long long ld, int rows, int vocab, int32_t* out, cudaStream_t s) {
+  if (rows <= 0) return;
+  argmax_kernel<<<rows, 256, 0, s>>>(logits, ld, vocab, out);
+  check_launch("argmax_rows");
+}
+
+void add(const float* a, const float* b, float* out, long long n, cudaStream_t s) {
+  if (n <= 0) return;
+  add_kernel<<<grid_for(n, 4), kThreads, 0, s>>>(a, b, out, n);
+  check_launch("add");
+}
+
+void scale(float* x, float factor, long long n, cudaStream_t s) {
+  if (n <= 0) return;
+  scale_kernel<<<grid_for(n, 4), kThreads, 0, s>>>(x, factor, n);
+  check_launch("scale");
+}
+
+}  // namespace mm

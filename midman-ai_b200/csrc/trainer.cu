@@ -1,0 +1,299 @@
+// Trainer: buffers, parameter I/O and batch upload. The step itself is in
+// trainer_step.cu.
+#include "trainer.h"
+
+#include <nccl.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <stdexcept>
+
+#include "attention.h"
+#include "device.h"
+#include "gemm.h"
+
+namespace mm {
+
+namespace {
+
+void nccl_check(ncclResult_t r, const char* what) {
+  if (r != ncclSuccess) throw std::runtime_error(std::string(what) + ": " + ncclGetErrorString(r));
+}
+
+}  // namespace
+
+Trainer::Trainer(const ModelConfig& cfg, int batch, int seq, int precision, int world, int rank,
+                 const void* nccl_unique_id)
+    : cfg_(cfg), batch_(batch), seq_(seq), precision_(precision), world_(world), rank_(rank) {
+  const std::string bad = validate_config(cfg);
+  if (!bad.empty()) throw std::invalid_argument(bad);
+  if (batch <= 0 || seq <= 0) throw std::invalid_argument("batch and seq must be at least 1");
+  if (static_cast<uint64_t>(seq) > cfg.max_seq_len)
+    throw std::invalid_argument("sequence length " + std::to_string(seq) + " exceeds max_seq_len " +
+                                std::to_string(cfg.max_seq_len));
+  if (precision != kPrecisionTF32 && precision != kPrecision3xTF32)
+    throw std::invalid_argument("precision must be 0 (TF32) or 1 (3xTF32)");
+  // The tensor-memory GEMMs load rows with TMA, which needs 16-byte row strides.
+  if (cfg.d_model % 4 || cfg.d_ff % 4 || cfg.vocab % 4 || cfg.kv_dim() % 4)
+    throw std::invalid_argument(
+        "the GPU path needs d_model, d_ff, vocab_size and n_kv_heads * head_dim to be multiples of 4");
+  if (cfg.head_dim() > 128) throw std::invalid_argument("the GPU path supports head_dim up to 128");
+  if (world < 1 || rank < 0 || rank >= world) throw std::invalid_argument("bad data-parallel rank/world");
+  layout_ = param_layout(cfg);
+
+  check_cuda(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "stream");
+  if (world_ > 1) {
+    if (!nccl_unique_id) throw std::invalid_argument("data parallelism needs an NCCL unique id");
+    ncclUniqueId id;
+    std::memcpy(&id, nccl_unique_id, sizeof(id));
+    ncclComm_t comm;
+    nccl_check(ncclCommInitRank(&comm, world_, id, rank_), "ncclCommInitRank");
+    comm_ = comm;
+    check_cuda(cudaStreamCreateWithFlags(&comm_stream_, cudaStreamNonBlocking), "comm stream");
+    layer_done_.resize(cfg.n_layers + 1);
+    for (auto& e : layer_done_) check_cuda(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "event");
+    check_cuda(cudaEventCreateWithFlags(&comm_done_, cudaEventDisableTiming), "event");
+  }
+
+  auto alloc = [&](size_t bytes) {
+    void* p = nullptr;
+    check_cuda(cudaMalloc(&p, std::max<size_t>(bytes, 256)), "cudaMalloc");
+    allocations_.push_back(p);
+    return p;
+  };
+  auto falloc = [&](uint64_t n) { return static_cast<float*>(alloc(n * sizeof(float))); };
+  const uint64_t total = layout_.total;
+  P_ = falloc(total);
+  G_ = falloc(total);
+  M_ = falloc(total);
+  V_ = falloc(total);
+  check_cuda(cudaMemset(G_, 0, total * 4), "memset");
+  check_cuda(cudaMemset(M_, 0, total * 4), "memset");
+  check_cuda(cudaMemset(V_, 0, total * 4), "memset");
+
+  // AdamW chunks: never across a parameter boundary; decay for rank >= 2 (adamw.rs:197).
+  std::vector<AdamChunk> chunks;
+  for (const TensorInfo& t : layout_.tensors)
+    for (uint64_t o = 0; o < t.numel; o += 16384)
+      chunks.push_back({static_cast<long long>(t.offset + o), static_cast<int>(std::min<uint64_t>(16384, t.numel - o)),
+                        t.shape.size() >= 2 ? 1 : 0});
+  n_chunks_ = static_cast<int>(chunks.size());
+  d_chunks_ = static_cast<AdamChunk*>(alloc(chunks.size() * sizeof(AdamChunk)));
+  check_cuda(cudaMemcpy(d_chunks_, chunks.data(), chunks.size() * sizeof(AdamChunk), cudaMemcpyHostToDevice), "chunks");
+
+  std::vector<float> cs, sn;
+  rope_tables(cfg.head_dim(), cfg.max_seq_len, cfg.rope_theta, cs, sn);
+  d_cos_ = falloc(cs.size());
+  d_sin_ = falloc(sn.size());
+  check_cuda(cudaMemcpy(d_cos_, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice), "rope");
+  check_cuda(cudaMemcpy(d_sin_, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice), "rope");
+
+  const uint64_t N = static_cast<uint64_t>(batch) * seq;
+  const uint64_t D = cfg.d_model, F = cfg.d_ff, KV = cfg.kv_dim(), V = cfg.vocab, H = cfg.n_heads;
+  d_ids_ = static_cast<int32_t*>(alloc(N * 4));
+  d_tgt_ = static_cast<int32_t*>(alloc(N * 4));
+  d_uniq_ = static_cast<int32_t*>(alloc(N * 4));
+  d_off_ = static_cast<int32_t*>(alloc((N + 1) * 4));
+  d_pos_ = static_cast<int32_t*>(alloc(N * 4));
+  d_pred_ = static_cast<int32_t*>(alloc(N * 4));
+  check_cuda(cudaMallocHost(&h_pinned_, (5 * N + 1) * sizeof(int32_t)), "pinned ids");
+  check_cuda(cudaMallocHost(&h_out_, 64), "pinned out");
+
+  acts_.resize(cfg.n_layers);
+  for (auto& a : acts_) {
+    a.x = falloc(N * D);
+    a.xn1 = falloc(N * D);
+    a.rstd1 = falloc(N);
+    a.q = falloc(N * D);
+    a.k = falloc(N * KV);
+    a.v = falloc(N * KV);
+    a.o = falloc(N * D);
+    a.lse = falloc(N * H);
+    a.h = falloc(N * D);
+    a.xn2 = falloc(N * D);
+    a.rstd2 = falloc(N);
+    a.g = falloc(N * F);
+    a.u = falloc(N * F);
+    a.act = falloc(N * F);
+  }
+  x_final_ = falloc(N * D);
+  xf_ = falloc(N * D);
+  rstdf_ = falloc(N);
+  logits_ = falloc(N * V);
+  row_loss_ = falloc(N);
+  dx_[0] = falloc(N * D);
+  dx_[1] = falloc(N * D);
+  dxn_ = falloc(N * D);
+  do_ = falloc(N * D);
+  dq_ = falloc(N * D);
+  dk_ = falloc(N * KV);
+  dv_ = falloc(N * KV);
+  dact_ = falloc(N * F);
+  tmp_ = falloc(N * std::max(D, F));
+  delta_ = falloc(N * H);
+  norm_ws_ = falloc(std::max<long long>(rmsnorm_ws_floats(static_cast<int>(N), static_cast<int>(D)), 1));
+  d_partials_ = static_cast<double*>(alloc(kNormBlocks * sizeof(double)));
+  d_loss_ = static_cast<double*>(alloc(sizeof(double)));
+  d_norm_ = falloc(4);
+  check_cuda(cudaDeviceSynchronize(), "trainer setup");
+}
+
+Trainer::~Trainer() {
+  if (stream_) cudaStreamSynchronize(stream_);
+  if (comm_stream_) cudaStreamSynchronize(comm_stream_);
+  for (void* p : allocations_) cudaFree(p);
+  if (h_pinned_) cudaFreeHost(h_pinned_);
+  if (h_out_) cudaFreeHost(h_out_);
+  for (auto e : layer_done_) cudaEventDestroy(e);
+  for (auto e : prof_events_) cudaEventDestroy(e);
+  if (comm_done_) cudaEventDestroy(comm_done_);
+  if (comm_) ncclCommDestroy(static_cast<ncclComm_t>(comm_));
+  if (comm_stream_) cudaStreamDestroy(comm_stream_);
+  if (stream_) cudaStreamDestroy(stream_);
+}
+
+void Trainer::init_params(HostRng& rng, float init_std, int threads) {
+  if (!(std::isfinite(init_std) && init_std > 0.0f)) throw std::invalid_argument("init std must be positive and finite");
+  std::vector<float> host(layout_.total);
+  mm::init_params(cfg_, layout_, rng, init_std, host.data(), threads);
+  load_params(host.data());
+}
+
+void Trainer::load_params(const float* host) {
+  check_cuda(cudaMemcpyAsync(P_, host, layout_.total * 4, cudaMemcpyHostToDevice, stream_), "load params");
+  check_cuda(cudaStreamSynchronize(stream_), "load params");
+}
+
+void Trainer::read_params(float* host) { read_tensor(0, layout_.total, host, 0); }
+void Trainer::read_grads(float* host) { read_tensor(0, layout_.total, host, 1); }
+
+void Trainer::read_tensor(uint64_t offset, uint64_t n, float* host, int which) {
+  if (offset + n > layout_.total) throw std::out_of_range("tensor range outside the parameter vector");
+  const float* src = (which == 0 ? P_ : which == 1 ? G_ : which == 2 ? M_ : V_) + offset;
+  check_cuda(cudaMemcpyAsync(host, src, n * 4, cudaMemcpyDeviceToHost, stream_), "read tensor");
+  check_cuda(cudaStreamSynchronize(stream_), "read tensor");
+}
+
+void Trainer::read_moments(float* m, float* v) {
+  read_tensor(0, layout_.total, m, 2);
+  read_tensor(0, layout_.total, v, 3);
+}
+
+// Groups token positions by id, positions ascending within each id, so the
+// embedding gradient adds rows in the reference's order (ops_shape.rs:262-272).
+void Trainer::build_embedding_csr(const int32_t* inputs, int N) {
+  std::vector<std::pair<int32_t, int32_t>> order(N);
+  for (int i = 0; i < N; ++i) order[i] = {inputs[i], i};
+  std::sort(order.begin(), order.end());
+  int32_t* uniq = h_pinned_ + 2 * N;
+  int32_t* offs = h_pinned_ + 3 * N;
+  int32_t* pos = h_pinned_ + 4 * N + 1;
+  int nu = 0;
+  for (int i = 0; i < N; ++i) {
+    if (i == 0 || order[i].first != order[i - 1].first) {
+      uniq[nu] = order[i].first;
+      offs[nu] = i;
+      ++nu;
+    }
+    pos[i] = order[i].second;
+  }
+  offs[nu] = N;
+  n_uniq_ = nu;
+}
+
+void Trainer::upload_batch(const int32_t* inputs, const int32_t* targets, int B, int T) {
+  const int N = B * T;
+  if (N > batch_ * seq_) throw std::invalid_argument("batch larger than the trainer's capacity");
+  if (static_cast<uint64_t>(T) > cfg_.max_seq_len) throw std::invalid_argument("sequence longer than max_seq_len");
+  for (int i = 0; i < N; ++i) {
+    if (inputs[i] < 0 || static_cast<uint64_t>(inputs[i]) >= cfg_.vocab)
+      throw std::out_of_range("token id " + std::to_string(inputs[i]) + " is out of range for vocab " +
+                              std::to_string(cfg_.vocab));
+    if (targets && (targets[i] < 0 || static_cast<uint64_t>(targets[i]) >= cfg_.vocab))
+      throw std::out_of_range("target class " + std::to_string(targets[i]) + " is out of range for vocab " +
+                              std::to_string(cfg_.vocab));
+  }
+  // The previous step's copies out of the staging buffer have finished (each
+  // step ends with a synchronizing read of its results).
+  std::memcpy(h_pinned_, inputs, N * 4);
+  if (targets) std::memcpy(h_pinned_ + N, targets, N * 4);
+  build_embedding_csr(inputs, N);
+  check_cuda(cudaMemcpyAsync(d_ids_, h_pinned_, N * 4, cudaMemcpyHostToDevice, stream_), "ids");
+  if (targets) check_cuda(cudaMemcpyAsync(d_tgt_, h_pinned_ + N, N * 4, cudaMemcpyHostToDevice, stream_), "targets");
+  check_cuda(cudaMemcpyAsync(d_uniq_, h_pinned_ + 2 * N, n_uniq_ * 4, cudaMemcpyHostToDevice, stream_), "uniq");
+  check_cuda(cudaMemcpyAsync(d_off_, h_pinned_ + 3 * N, (n_uniq_ + 1) * 4, cudaMemcpyHostToDevice, stream_), "offs");
+  check_cuda(cudaMemcpyAsync(d_pos_, h_pinned_ + 4 * N + 1, N * 4, cudaMemcpyHostToDevice, stream_), "pos");
+}
+
+void Trainer::set_profile(bool on) {
+  profiling_ = on;
+  profile_.clear();
+  pending_.clear();
+  prof_next_ = 0;
+}
+
+int Trainer::prof_begin() {
+  if (!profiling_) return -1;
+  const int slot = prof_next_;
+  prof_next_ += 2;
+  while (static_cast<int>(prof_events_.size()) < prof_next_) {
+    cudaEvent_t e;
+    check_cuda(cudaEventCreate(&e), "profile event");
+    prof_events_.push_back(e);
+  }
+  check_cuda(cudaEventRecord(prof_events_[slot], stream_), "profile event");
+  return slot;
+}
+
+void Trainer::prof_end(int slot, const char* cls, double flops) {
+  if (slot < 0) return;
+  check_cuda(cudaEventRecord(prof_events_[slot + 1], stream_), "profile event");
+  pending_.push_back({slot, cls, flops});
+}
+
+// Called after the stream has synchronized.
+void Trainer::prof_collect() {
+  for (const Pending& p : pending_) {
+    float ms = 0.0f;
+    check_cuda(cudaEventElapsedTime(&ms, prof_events_[p.slot], prof_events_[p.slot + 1]), "profile elapsed");
+    auto it = profile_.begin();
+    for (; it != profile_.end(); ++it)
+      if (it->first == p.cls) break;
+    if (it == profile_.end()) {
+      profile_.push_back({p.cls, ProfileEntry{}});
+      it = profile_.end() - 1;
+    }
+    it->second.launches += 1;
+    it->second.ms += ms;
+    it->second.flops += p.flops;
+  }
+  pending_.clear();
+  prof_next_ = 0;
+}
+
+void Trainer::gemm(int M, int N, int K, const float* A, long long lda, bool a_mn, const float* B, long long ldb,
+                   bool b_mn, float* C, long long ldc, const float* R, long long ldr) {
+  const int slot = prof_begin();
+  DeviceContext& ctx = device_context();
+  GemmOperand a{A, lda, a_mn}, b{B, ldb, b_mn};
+  const int rc = precision_ == kPrecisionTF32 ? gemm_tf32(M, N, K, a, b, C, ldc, R, ldr, ctx.d_err, stream_)
+                                              : gemm_3xtf32(M, N, K, a, b, C, ldc, R, ldr, ctx.d_err, stream_);
+  if (rc) throw std::runtime_error(std::string("GEMM: ") + gemm_status_string(rc));
+  launches_ += precision_ == kPrecisionTF32 ? 1 : 5;
+  prof_end(slot, precision_ == kPrecisionTF32 ? "gemm_tf32" : "gemm_3xtf32", 2.0 * M * N * K);
+}
+
+void Trainer::check_device(const char* where) {
+  const int code = take_device_error(stream_);
+  if (code) throw std::runtime_error(std::string(where) + ": " + device_error_message(code));
+}
+
+void Trainer::allreduce_grads_range(uint64_t offset, uint64_t n) {
+  if (world_ <= 1 || n == 0) return;
+  nccl_check(ncclAllReduce(G_ + offset, G_ + offset, n, ncclFloat, ncclAvg, static_cast<ncclComm_t>(comm_),
+                           comm_stream_),
+             "ncclAllReduce(grads)");
+}
+
+}  // namespace mm

@@ -17,7 +17,19 @@ LIB_PATH = HERE / "lib" / "libmidman_gpu.so"
 GPU_SYMBOLS = [
     "mm_gpu_last_error", "mm_gpu_device_status", "mm_gpu_gemm",
 ]
-API_SYMBOLS: list[str] = []
+API_SYMBOLS = [
+    "midman_abi_version", "midman_alloc", "midman_free", "midman_text_ptr", "midman_text_len",
+    "midman_floats_ptr", "midman_floats_len", "midman_error_ptr", "midman_error_len", "midman_describe",
+    "midman_preset_config", "midman_config_report", "midman_rope_table", "midman_lab_create",
+    "midman_lab_step", "midman_lab_eval", "midman_lab_stats", "midman_lab_attention", "midman_lab_embedding",
+    "midman_lab_destroy", "midman_nccl_unique_id", "midman_train_create", "midman_train_step",
+    "midman_train_stage", "midman_train_step_staged", "midman_train_loss_and_grads", "midman_train_read",
+    "midman_train_load", "midman_train_describe", "midman_train_eval", "midman_train_destroy",
+    "midman_train_stream", "midman_train_profile", "midman_batcher_create", "midman_batcher_synthetic",
+    "midman_batcher_next", "midman_batcher_destroy",
+]
+STATUS = {0: "OK", 1: "STOPPED", -1: "ARGUMENT", -2: "CONFIG", -3: "SHAPE", -4: "INDEX", -5: "OTHER",
+          -6: "DEVICE", -99: "PANIC"}
 
 _lib = None
 
@@ -41,6 +53,44 @@ def load(path: str | os.PathLike | None = None) -> C.CDLL:
     _sig(lib, "mm_gpu_last_error", C.c_char_p)
     _sig(lib, "mm_gpu_device_status", i32, vp)
     _sig(lib, "mm_gpu_gemm", i32, i32, i32, i32, vp, i64, i32, vp, i64, i32, vp, i64, vp, i64, i32, vp)
+    u32, u8p, dp, i32p = C.c_uint32, C.POINTER(C.c_uint8), C.POINTER(C.c_double), C.POINTER(C.c_int32)
+    _sig(lib, "midman_abi_version", u32)
+    _sig(lib, "midman_alloc", u8p, u32)
+    _sig(lib, "midman_free", None, u8p, u32)
+    _sig(lib, "midman_text_ptr", u8p)
+    _sig(lib, "midman_text_len", u32)
+    _sig(lib, "midman_floats_ptr", f32p)
+    _sig(lib, "midman_floats_len", u32)
+    _sig(lib, "midman_error_ptr", u8p)
+    _sig(lib, "midman_error_len", u32)
+    _sig(lib, "midman_describe", i32)
+    _sig(lib, "midman_preset_config", i32, u32, dp)
+    _sig(lib, "midman_config_report", i32, dp)
+    _sig(lib, "midman_rope_table", i32, u32, u32, C.c_double)
+    _sig(lib, "midman_lab_create", u32, dp, dp, u32, u32, u32, u32)
+    _sig(lib, "midman_lab_step", i32, u32, u32)
+    _sig(lib, "midman_lab_eval", i32, u32)
+    _sig(lib, "midman_lab_stats", i32, u32)
+    _sig(lib, "midman_lab_attention", i32, u32, u32)
+    _sig(lib, "midman_lab_embedding", i32, u32)
+    _sig(lib, "midman_lab_destroy", i32, u32)
+    _sig(lib, "midman_nccl_unique_id", i32, u8p)
+    _sig(lib, "midman_train_create", u32, dp, dp, u32, u32, u32, u32, u32, u32, u32, u8p)
+    _sig(lib, "midman_train_step", i32, u32, i32p, i32p)
+    _sig(lib, "midman_train_stage", i32, u32, i32p, i32p)
+    _sig(lib, "midman_train_step_staged", i32, u32, u32)
+    _sig(lib, "midman_train_loss_and_grads", i32, u32, i32p, i32p)
+    _sig(lib, "midman_train_read", i32, u32, u32, u32)
+    _sig(lib, "midman_train_load", i32, u32, f32p, C.c_uint64)
+    _sig(lib, "midman_train_describe", i32, u32)
+    _sig(lib, "midman_train_eval", i32, u32, i32p, i32p, u32, u32)
+    _sig(lib, "midman_train_destroy", i32, u32)
+    _sig(lib, "midman_train_stream", i32, u32, C.POINTER(C.c_uint64))
+    _sig(lib, "midman_train_profile", i32, u32, u32)
+    _sig(lib, "midman_batcher_create", i32, C.POINTER(C.c_uint32), C.c_uint64, u32, u32, u32, u32, u32)
+    _sig(lib, "midman_batcher_synthetic", i32, u32, u32, C.c_uint64, u32, u32, u32, u32)
+    _sig(lib, "midman_batcher_next", i32, u32, i32p, i32p)
+    _sig(lib, "midman_batcher_destroy", i32, u32)
     _lib = lib
     return lib
 
@@ -77,3 +127,235 @@ def gemm(a, b, c, *, m, n, k, lda, ldb, ldc, a_mn_major, b_mn_major, r=None, ldr
 
 def device_status(stream=None):
     return check(load().mm_gpu_device_status(_stream(stream)))
+
+
+# ---------------------------------------------------------------- midman_api.h
+
+import json as _json
+
+import numpy as _np
+
+
+class MidmanError(RuntimeError):
+    def __init__(self, status, message):
+        super().__init__(f"{STATUS.get(status, status)}: {message}")
+        self.status = status
+        self.message = message
+
+
+def text() -> str:
+    L = load()
+    n = L.midman_text_len()
+    return C.string_at(L.midman_text_ptr(), n).decode() if n else ""
+
+
+def floats() -> _np.ndarray:
+    L = load()
+    n = L.midman_floats_len()
+    if n == 0:
+        return _np.zeros(0, _np.float32)
+    return _np.ctypeslib.as_array(L.midman_floats_ptr(), shape=(n,)).copy()
+
+
+def error() -> str:
+    L = load()
+    n = L.midman_error_len()
+    return C.string_at(L.midman_error_ptr(), n).decode(errors="replace") if n else ""
+
+
+def api(status: int, ok=(0,)) -> int:
+    if status not in ok:
+        raise MidmanError(status, error())
+    return status
+
+
+def _dp(a):
+    return a.ctypes.data_as(C.POINTER(C.c_double))
+
+
+def _ip(a):
+    return a.ctypes.data_as(C.POINTER(C.c_int32))
+
+
+def config_array(vocab, d_model, n_layers, n_heads, n_kv_heads, d_ff, max_seq_len, rope_theta=10000.0,
+                 norm_eps=1e-5, tie=True):
+    return _np.array([vocab, d_model, n_layers, n_heads, n_kv_heads, d_ff, max_seq_len, rope_theta, norm_eps,
+                      1.0 if tie else 0.0], dtype=_np.float64)
+
+
+def hyper_array(max_lr=3e-4, min_lr=3e-4, warmup=0, total=1_000_000, weight_decay=0.1, clip_norm=1.0, beta1=0.9,
+                beta2=0.95):
+    return _np.array([max_lr, min_lr, warmup, total, weight_decay, clip_norm, beta1, beta2], dtype=_np.float64)
+
+
+def describe() -> dict:
+    api(load().midman_describe())
+    return _json.loads(text())
+
+
+def preset_config(index: int) -> _np.ndarray:
+    out = _np.zeros(10, _np.float64)
+    api(load().midman_preset_config(index, _dp(out)))
+    return out
+
+
+def config_report(cfg) -> dict:
+    c = _np.ascontiguousarray(cfg, _np.float64)
+    api(load().midman_config_report(_dp(c)))
+    return _json.loads(text())
+
+
+def rope_table(head_dim, max_seq_len, theta):
+    api(load().midman_rope_table(head_dim, max_seq_len, theta))
+    f = floats()
+    half = head_dim // 2
+    return f[: max_seq_len * half].reshape(max_seq_len, half), f[max_seq_len * half:].reshape(max_seq_len, half)
+
+
+class Lab:
+    """midman_lab_* (the reference's lab API) on the GPU."""
+
+    def __init__(self, cfg, hyper, seed: int, batch: int, seq: int):
+        c = _np.ascontiguousarray(cfg, _np.float64)
+        h = _np.ascontiguousarray(hyper, _np.float64)
+        self.h = load().midman_lab_create(_dp(c), _dp(h), seed & 0xFFFFFFFF, (seed >> 32) & 0xFFFFFFFF, batch, seq)
+        if self.h == 0:
+            raise MidmanError(-1, error())
+
+    def step(self, steps: int):
+        st = api(load().midman_lab_step(self.h, steps), ok=(0, 1))
+        return floats().reshape(-1, 3), st, error()
+
+    def eval(self):
+        api(load().midman_lab_eval(self.h))
+        return _json.loads(text())
+
+    def stats(self):
+        api(load().midman_lab_stats(self.h))
+        return _json.loads(text())
+
+    def attention(self, sequence: int):
+        api(load().midman_lab_attention(self.h, sequence))
+        meta = _json.loads(text())
+        return floats().reshape(meta["layers"], meta["heads"], meta["seq"], meta["seq"])
+
+    def embedding(self):
+        api(load().midman_lab_embedding(self.h))
+        meta = _json.loads(text())
+        return floats().reshape(meta["rows"], meta["cols"])
+
+    def close(self):
+        if self.h:
+            api(load().midman_lab_destroy(self.h))
+            self.h = 0
+
+
+def nccl_unique_id() -> bytes:
+    buf = (C.c_uint8 * 128)()
+    api(load().midman_nccl_unique_id(buf))
+    return bytes(buf)
+
+
+class Trainer:
+    """midman_train_* on the current CUDA device."""
+
+    def __init__(self, cfg, hyper, seed: int, batch: int, seq: int, precision: int = 0, world: int = 1,
+                 rank: int = 0, nccl_id: bytes | None = None):
+        c = _np.ascontiguousarray(cfg, _np.float64)
+        h = _np.ascontiguousarray(hyper, _np.float64)
+        idp = None
+        if nccl_id is not None:
+            self._id = (C.c_uint8 * 128).from_buffer_copy(nccl_id)
+            idp = C.cast(self._id, C.POINTER(C.c_uint8))
+        self.h = load().midman_train_create(_dp(c), _dp(h), seed & 0xFFFFFFFF, (seed >> 32) & 0xFFFFFFFF, batch, seq,
+                                            precision, world, rank, idp)
+        if self.h == 0:
+            raise MidmanError(-1, error())
+        self.batch, self.seq = batch, seq
+
+    def step(self, inputs, targets):
+        i = _np.ascontiguousarray(inputs, _np.int32)
+        t = _np.ascontiguousarray(targets, _np.int32)
+        st = api(load().midman_train_step(self.h, _ip(i), _ip(t)), ok=(0, 1))
+        return floats(), st
+
+    def stage(self, inputs, targets):
+        self._si = _np.ascontiguousarray(inputs, _np.int32)
+        self._st = _np.ascontiguousarray(targets, _np.int32)
+        api(load().midman_train_stage(self.h, _ip(self._si), _ip(self._st)))
+
+    def step_staged(self, steps: int = 1):
+        st = api(load().midman_train_step_staged(self.h, steps), ok=(0, 1))
+        return floats().reshape(-1, 3), st
+
+    def loss_and_grads(self, inputs, targets) -> float:
+        i = _np.ascontiguousarray(inputs, _np.int32)
+        t = _np.ascontiguousarray(targets, _np.int32)
+        api(load().midman_train_loss_and_grads(self.h, _ip(i), _ip(t)))
+        return float(floats()[0])
+
+    def read(self, which: int = 0, index: int = 0xFFFFFFFF) -> _np.ndarray:
+        api(load().midman_train_read(self.h, which, index))
+        return floats()
+
+    def params(self):
+        return self.read(0)
+
+    def grads(self):
+        return self.read(1)
+
+    def load_params(self, values):
+        v = _np.ascontiguousarray(values, _np.float32)
+        api(load().midman_train_load(self.h, v.ctypes.data_as(C.POINTER(C.c_float)), v.size))
+
+    def describe(self) -> dict:
+        api(load().midman_train_describe(self.h))
+        return _json.loads(text())
+
+    def eval(self, inputs, targets, batch, seq) -> float:
+        i = _np.ascontiguousarray(inputs, _np.int32)
+        t = _np.ascontiguousarray(targets, _np.int32)
+        api(load().midman_train_eval(self.h, _ip(i), _ip(t), batch, seq))
+        return float(floats()[0])
+
+    def stream(self) -> int:
+        out = C.c_uint64()
+        api(load().midman_train_stream(self.h, C.byref(out)))
+        return out.value
+
+    def profile(self, enable: bool):
+        api(load().midman_train_profile(self.h, int(enable)))
+
+    def close(self):
+        if self.h:
+            api(load().midman_train_destroy(self.h))
+            self.h = 0
+
+
+class Batcher:
+    """midman_batcher_*: the reference's Sequences + Batcher over one shard."""
+
+    def __init__(self, tokens=None, *, vocab, seq, batch, seed=0, synthetic_tokens=None, token_seed=0):
+        L = load()
+        s_lo, s_hi = seed & 0xFFFFFFFF, (seed >> 32) & 0xFFFFFFFF
+        if tokens is not None:
+            self._tok = _np.ascontiguousarray(tokens, _np.uint32)
+            st = L.midman_batcher_create(self._tok.ctypes.data_as(C.POINTER(C.c_uint32)), self._tok.size, vocab,
+                                         seq, batch, s_lo, s_hi)
+        else:
+            st = L.midman_batcher_synthetic(token_seed, vocab, synthetic_tokens, seq, batch, s_lo, s_hi)
+        if st <= 0:
+            raise MidmanError(st, error())
+        self.h, self.seq, self.batch = st, seq, batch
+
+    def next(self):
+        i = _np.zeros(self.batch * self.seq, _np.int32)
+        t = _np.zeros(self.batch * self.seq, _np.int32)
+        api(load().midman_batcher_next(self.h, _ip(i), _ip(t)))
+        meta = _json.loads(text())
+        return i, t, meta["epoch"], meta["index"]
+
+    def close(self):
+        if self.h:
+            api(load().midman_batcher_destroy(self.h))
+            self.h = 0

@@ -1,7 +1,10 @@
 // Oracle part 1: Rng, ModelConfig, parameter layout, seeded init, rotary tables.
+#include <algorithm>
 // Test infrastructure only (see oracle.h).
+#include <array>
 #include <cmath>
 #include <cstring>
+#include <tuple>
 
 #include "oracle_internal.h"
 
@@ -153,28 +156,74 @@ void build_layout(Model& m) {
 void init_weights(Model& m, Rng& rng, float std_) {
   const Config& c = m.cfg;
   const float out_std = std_ / std::sqrt(2.0f * static_cast<float>(c.n_layers));
-  auto randn = [&](uint64_t off, uint64_t n, float s) {
-    float* p = m.params.data() + off;
-    for (uint64_t i = 0; i < n; ++i) p[i] = s * rng.normal();
-  };
-  auto ones = [&](uint64_t off, uint64_t n) {
-    for (uint64_t i = 0; i < n; ++i) m.params[off + i] = 1.0f;
-  };
   const uint64_t d = c.d_model, kv = c.kv_dim(), ff = c.d_ff;
-  randn(m.embed, c.vocab * d, std_);
+  // Drawn tensors in draw order (offset, count, std); norms are ones and draw nothing.
+  std::vector<std::tuple<uint64_t, uint64_t, float>> runs;
+  runs.emplace_back(m.embed, c.vocab * d, std_);
   for (const BlockParams& b : m.blocks) {
-    ones(b.attn_norm, d);
-    randn(b.q, d * d, std_);
-    randn(b.k, d * kv, std_);
-    randn(b.v, d * kv, std_);
-    randn(b.o, d * d, out_std);
-    ones(b.mlp_norm, d);
-    randn(b.gate, d * ff, std_);
-    randn(b.up, d * ff, std_);
-    randn(b.down, ff * d, out_std);
+    for (uint64_t i = 0; i < d; ++i) m.params[b.attn_norm + i] = 1.0f;
+    runs.emplace_back(b.q, d * d, std_);
+    runs.emplace_back(b.k, d * kv, std_);
+    runs.emplace_back(b.v, d * kv, std_);
+    runs.emplace_back(b.o, d * d, out_std);
+    for (uint64_t i = 0; i < d; ++i) m.params[b.mlp_norm + i] = 1.0f;
+    runs.emplace_back(b.gate, d * ff, std_);
+    runs.emplace_back(b.up, d * ff, std_);
+    runs.emplace_back(b.down, ff * d, out_std);
   }
-  ones(m.final_norm, d);
-  if (!c.tie) randn(m.lm_head, d * c.vocab, std_);
+  for (uint64_t i = 0; i < d; ++i) m.params[m.final_norm + i] = 1.0f;
+  if (!c.tie) runs.emplace_back(m.lm_head, d * c.vocab, std_);
+  // Element e of the drawn stream is std * normal() for the e-th call. normal()
+  // consumes two 64-bit draws per pair of values (rng.rs:74-85), so pair p starts
+  // 2p draws after the stream start: walk the state once to find each chunk's
+  // start, then evaluate the chunks' Box-Muller pairs on several threads.
+  std::vector<uint64_t> where;  // flat element -> parameter offset, by run
+  uint64_t total = 0;
+  for (auto& r : runs) total += std::get<1>(r);
+  std::vector<float> stream(total);
+  uint64_t first = 0;
+  if (total && rng.has_spare) {
+    stream[0] = rng.spare;
+    rng.has_spare = false;
+    first = 1;
+  }
+  const uint64_t pairs = (total - first + 1) / 2;
+  const uint64_t chunk = 1ull << 16;
+  const uint64_t nchunks = (pairs + chunk - 1) / chunk;
+  std::vector<std::array<uint64_t, 4>> starts(nchunks);
+  for (uint64_t ch = 0; ch < nchunks; ++ch) {
+    for (int w = 0; w < 4; ++w) starts[ch][w] = rng.s[w];
+    const uint64_t np = std::min(chunk, pairs - ch * chunk);
+    for (uint64_t k = 0; k < 2 * np; ++k) rng.next_u64();
+  }
+  float last_sin = 0.0f;
+#pragma omp parallel for schedule(dynamic)
+  for (long long ch = 0; ch < static_cast<long long>(nchunks); ++ch) {
+    Rng local(0);
+    for (int w = 0; w < 4; ++w) local.s[w] = starts[ch][w];
+    const uint64_t p0 = ch * chunk, p1 = std::min(pairs, p0 + chunk);
+    for (uint64_t p = p0; p < p1; ++p) {
+      local.has_spare = false;
+      const float cs = local.normal();  // draws two values, caches the sine part
+      const uint64_t e = first + 2 * p;
+      stream[e] = cs;
+      if (e + 1 < total)
+        stream[e + 1] = local.spare;
+      else
+        last_sin = local.spare;
+    }
+  }
+  if ((total - first) & 1) {
+    rng.spare = last_sin;
+    rng.has_spare = true;
+  }
+  uint64_t pos = 0;
+  for (auto& r : runs) {
+    float* p = m.params.data() + std::get<0>(r);
+    const float s = std::get<2>(r);
+    for (uint64_t i = 0; i < std::get<1>(r); ++i) p[i] = s * stream[pos + i];
+    pos += std::get<1>(r);
+  }
   rope_tables(c.head_dim(), c.max_seq_len, c.rope_theta, m.rope_cos, m.rope_sin);
 }
 

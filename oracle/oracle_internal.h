@@ -11,7 +11,7 @@ namespace orc {
 // crates/midman-foundation/src/rng.rs:26-119 (xoshiro256** seeded by SplitMix64).
 struct Rng {
   uint64_t s[4];
-  bool has_spare = false;
+  bool has_spare = false;  // the cached second Box-Muller value (rng.rs:31)
   float spare = 0.0f;
   explicit Rng(uint64_t seed);
   uint64_t next_u64();

@@ -1,0 +1,189 @@
+"""The GPU training step against the CPU oracle on identical seeded weights and ids.
+
+Gates: the seeded init and token handling are bit-exact;
+per-tensor gradients within relative L2 1e-5 in 3xTF32 mode and 1e-2 in TF32
+mode; the loss after 20 AdamW steps within 1e-3 relative. Everything goes
+through the C ABI (include/midman_api.h) of libmidman_gpu.so.
+"""
+import math
+
+import numpy as np
+import pytest
+
+import oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+TOL = {0: 1e-2, 1: 1e-5}  # precision -> per-tensor gradient rel-L2
+
+
+def rel_l2(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def ids(vocab, n, seed):
+    r = orc.Rng(seed)
+    return np.array([r.below(vocab) for _ in range(n)], np.int32)
+
+
+CASES = {
+    # name: (config, batch, seq, init_std) -- GQA, odd sequence tails, all head sizes
+    "gqa_small": (orc.config_array(64, 32, 2, 4, 2, 48, 16), 2, 16, 0.3),
+    "untied": (orc.config_array(64, 32, 2, 4, 2, 48, 16, tie=False), 2, 16, 0.3),
+    "smoke_preset": (orc.preset("smoke"), 4, 32, 0.02),
+    "ragged_seq_hd16": (orc.config_array(128, 64, 1, 4, 1, 64, 128), 2, 100, 0.1),
+    "hd128": (orc.config_array(128, 256, 1, 2, 1, 64, 96), 2, 80, 0.05),
+    "hd64_gqa": (orc.config_array(96, 256, 2, 4, 2, 128, 130), 1, 130, 0.05),
+}
+
+
+@pytest.fixture(scope="module")
+def gpu(mm):
+    torch = pytest.importorskip("torch")
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    return mm
+
+
+def test_seeded_init_is_bit_identical_to_the_oracle(gpu):
+    cfg = orc.preset("tiny")
+    t = gpu.Trainer(cfg, gpu.hyper_array(), seed=0, batch=1, seq=8)
+    o = orc.Model(cfg, seed=0)
+    got, want = t.params(), o.params
+    assert got.size == want.size == 1315968
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32))
+    names = [x["name"] for x in t.describe()["tensors"]]
+    assert names == [x[0] for x in o.tensors()]
+    t.close()
+
+
+@pytest.mark.parametrize("precision", [1, 0])
+@pytest.mark.parametrize("case", list(CASES))
+def test_loss_and_gradients_match_the_oracle(gpu, case, precision):
+    cfg, B, T, std = CASES[case]
+    model = orc.Model(cfg, seed=11, init_std=std)
+    inputs = ids(int(cfg[0]), B * T, 12)
+    targets = ids(int(cfg[0]), B * T, 13)
+    want_loss, want_g = model.loss(inputs, targets, B, T, grads=True)
+    t = gpu.Trainer(cfg, gpu.hyper_array(), seed=11, batch=B, seq=T, precision=precision)
+    t.load_params(model.params)
+    loss = t.loss_and_grads(inputs, targets)
+    g = t.grads()
+    assert abs(loss - want_loss) <= 1e-6 * 10 ** (3 * (1 - precision)) * max(1.0, abs(want_loss)), (loss, want_loss)
+    worst = []
+    for name, _shape, off, n in model.tensors():
+        err = rel_l2(g[off:off + n], want_g[off:off + n])
+        worst.append((err, name))
+    worst.sort(reverse=True)
+    assert worst[0][0] <= TOL[precision], worst[:4]
+    t.close()
+
+
+def test_attention_probabilities_and_logits_match(gpu):
+    cfg, B, T, std = CASES["gqa_small"]
+    lab_cfg = cfg.copy()
+    lab = gpu.Lab(lab_cfg, gpu.hyper_array(max_lr=1e-3, min_lr=1e-4, warmup=2, total=20), seed=5, batch=B, seq=T)
+    model, inputs, _targets = orc.lab_task(lab_cfg, 5, B, T)
+    probs = lab.attention(1)
+    want = model.attention(inputs[T:2 * T], 1, T)[:, 0]
+    assert probs.shape == want.shape
+    np.testing.assert_allclose(probs, want, atol=2e-6)
+    assert np.all(np.triu(probs[0, 0], 1) == 0)
+    emb = lab.embedding()
+    assert np.array_equal(emb.ravel().view(np.uint32), model.params[:emb.size].view(np.uint32))
+    lab.close()
+
+
+def test_lab_trains_like_the_oracle(gpu):
+    # lab.rs:266-289 through the reference's own ABI: losses, norms and lr per step
+    cfg = orc.preset("smoke")
+    hyper = gpu.hyper_array(max_lr=0.02, min_lr=0.002, warmup=4, total=30, weight_decay=0.01, clip_norm=1.0,
+                            beta1=0.9, beta2=0.99)
+    B, T = 2, 16
+    lab = gpu.Lab(cfg, hyper, seed=2024, batch=B, seq=T)
+    rec, status, _ = lab.step(10)
+    assert status == 0 and rec.shape == (10, 3)
+    model, inputs, targets = orc.lab_task(cfg, 2024, B, T)
+    opt = orc.AdamW(model, 0.9, 0.99, 1e-8, 0.01)
+    for step in range(10):
+        lr = orc.schedule_lr(0.02, 0.002, 4, 30, step)
+        loss, norm, ok = orc.train_update(model, opt, inputs, targets, B, T, 1.0, lr)
+        assert ok
+        assert rec[step, 2] == np.float32(lr)
+        assert abs(rec[step, 0] - loss) <= 1e-4 * abs(loss), (step, rec[step], loss)
+        assert abs(rec[step, 1] - norm) <= 1e-3 * abs(norm), (step, rec[step], norm)
+    ev = lab.eval()
+    assert ev["step"] == 10 and len(ev["predictions"]) == B and len(ev["inputs"][0]) == T
+    assert ev["inputs"][0] == inputs[:T].tolist() and ev["targets"][1] == targets[T:].tolist()
+    st = lab.stats()
+    assert st["step"] == 10 and st["num_parameters"] == 117056
+    assert all(p["grad_norm"] is not None and p["grad_norm"] > 0 for p in st["params"])
+    lab.close()
+
+
+_TINY = {}
+
+
+def tiny_oracle_curve(steps=20):
+    """tiny preset, batch 8 x seq 256, ids uniform from seed 0 drawn after the
+    seeded init, lr 3e-4 constant, wd 0.1, clip 1.0, betas 0.9/0.95 (config.rs:49-64)."""
+    if "curve" not in _TINY:
+        cfg = orc.preset("tiny")
+        B, T = 8, 256
+        model, inputs, targets = orc.lab_task(cfg, 0, B, T)
+        opt = orc.AdamW(model, 0.9, 0.95, 1e-8, 0.1)
+        want = []
+        for _ in range(steps):
+            loss, _norm, ok = orc.train_update(model, opt, inputs, targets, B, T, 1.0, 3e-4)
+            assert ok
+            want.append(loss)
+        _TINY.update(curve=want, inputs=inputs, targets=targets)
+    return _TINY["curve"], _TINY["inputs"], _TINY["targets"]
+
+
+@pytest.mark.parametrize("precision", [1, 0])
+def test_twenty_steps_of_the_tiny_preset_match_the_oracle(gpu, precision):
+    cfg = orc.preset("tiny")
+    B, T, steps = 8, 256, 20
+    want, inputs, targets = tiny_oracle_curve(steps)
+    t = gpu.Trainer(cfg, gpu.hyper_array(max_lr=3e-4, min_lr=3e-4, warmup=0, total=10**6), seed=0, batch=B, seq=T,
+                    precision=precision)
+    t.stage(inputs, targets)
+    rec, status = t.step_staged(steps)
+    assert status == 0
+    got = rec[:, 0]
+    assert abs(got[0] - want[0]) <= 1e-5 * want[0]
+    rel = abs(got[-1] - want[-1]) / want[-1]
+    assert rel <= 1e-3, (precision, got[-1], want[-1], rel)
+    assert got[-1] < got[0]
+    t.close()
+
+
+def test_non_finite_loss_stops_and_changes_nothing(gpu):
+    cfg, B, T, std = CASES["gqa_small"]
+    model = orc.Model(cfg, seed=3, init_std=std)
+    bad = model.params
+    bad[5] = np.inf  # an embedding weight of token 0 -> the loss is not finite
+    t = gpu.Trainer(cfg, gpu.hyper_array(), seed=3, batch=B, seq=T, precision=1)
+    t.load_params(bad)
+    inputs = np.zeros(B * T, np.int32)
+    rec, status = t.step(inputs, inputs)
+    assert status == 1 and "not a finite" in gpu.error()
+    after = t.params()
+    assert np.array_equal(np.isinf(after), np.isinf(bad)) and np.array_equal(after[6:], bad[6:])
+    assert t.describe()["steps"] == 0
+    t.close()
+
+
+def test_bad_token_ids_are_index_errors(gpu):
+    cfg, B, T, _ = CASES["gqa_small"]
+    t = gpu.Trainer(cfg, gpu.hyper_array(), seed=1, batch=B, seq=T)
+    x = np.zeros(B * T, np.int32)
+    y = x.copy()
+    y[3] = 64
+    with pytest.raises(gpu.MidmanError) as e:
+        t.step(x, y)
+    assert e.value.status == -4
+    t.close()
