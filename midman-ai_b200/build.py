@@ -70,7 +70,7 @@ def build(force: bool = False, jobs: int | None = None, verbose: bool = False) -
     newest_obj = max(o.stat().st_mtime for o in objs)
     if force or not LIB.exists() or LIB.stat().st_mtime < newest_obj:
         cmd = [nvcc(), *ARCH, "-shared", "-Xcompiler", "-fPIC", "-o", str(LIB), *map(str, objs),
-               "-lnccl", "-lpthread", "-ldl"]
+               "-lpthread", "-ldl"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

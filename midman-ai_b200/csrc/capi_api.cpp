@@ -3,7 +3,7 @@
 // training entry points. State is thread-local; every call but the accessors
 // clears the text, floats and error buffers first (ffi.rs:119-145).
 #include <cuda_runtime.h>
-#include <nccl.h>
+#include "nccl_api.h"
 
 #include <cmath>
 #include <cstdlib>
@@ -541,8 +541,8 @@ int32_t midman_nccl_unique_id(uint8_t* out128) {
   return run([&] {
     if (!out128) throw ArgumentError("out is a null pointer");
     ncclUniqueId id;
-    const ncclResult_t r = ncclGetUniqueId(&id);
-    if (r != ncclSuccess) throw DeviceError(std::string("ncclGetUniqueId: ") + ncclGetErrorString(r));
+    const ncclResult_t r = nccl().GetUniqueId(&id);
+    if (r != ncclSuccess) throw DeviceError(std::string("ncclGetUniqueId: ") + nccl().GetErrorString(r));
     static_assert(sizeof(id) == 128, "NCCL unique id is 128 bytes");
     std::memcpy(out128, &id, sizeof(id));
     return MIDMAN_OK;

@@ -2,7 +2,7 @@
 // trainer_step.cu.
 #include "trainer.h"
 
-#include <nccl.h>
+#include "nccl_api.h"
 
 #include <algorithm>
 #include <cmath>
@@ -18,7 +18,7 @@ namespace mm {
 namespace {
 
 void nccl_check(ncclResult_t r, const char* what) {
-  if (r != ncclSuccess) throw std::runtime_error(std::string(what) + ": " + ncclGetErrorString(r));
+  if (r != ncclSuccess) throw std::runtime_error(std::string(what) + ": " + nccl().GetErrorString(r));
 }
 
 }  // namespace
@@ -48,7 +48,7 @@ Trainer::Trainer(const ModelConfig& cfg, int batch, int seq, int precision, int 
     ncclUniqueId id;
     std::memcpy(&id, nccl_unique_id, sizeof(id));
     ncclComm_t comm;
-    nccl_check(ncclCommInitRank(&comm, world_, id, rank_), "ncclCommInitRank");
+    nccl_check(nccl().CommInitRank(&comm, world_, id, rank_), "ncclCommInitRank");
     comm_ = comm;
     check_cuda(cudaStreamCreateWithFlags(&comm_stream_, cudaStreamNonBlocking), "comm stream");
     layer_done_.resize(cfg.n_layers + 1);
@@ -148,7 +148,7 @@ Trainer::~Trainer() {
   for (auto e : layer_done_) cudaEventDestroy(e);
   for (auto e : prof_events_) cudaEventDestroy(e);
   if (comm_done_) cudaEventDestroy(comm_done_);
-  if (comm_) ncclCommDestroy(static_cast<ncclComm_t>(comm_));
+  if (comm_) nccl().CommDestroy(static_cast<ncclComm_t>(comm_));
   if (comm_stream_) cudaStreamDestroy(comm_stream_);
   if (stream_) cudaStreamDestroy(stream_);
 }
@@ -291,7 +291,7 @@ void Trainer::check_device(const char* where) {
 
 void Trainer::allreduce_grads_range(uint64_t offset, uint64_t n) {
   if (world_ <= 1 || n == 0) return;
-  nccl_check(ncclAllReduce(G_ + offset, G_ + offset, n, ncclFloat, ncclAvg, static_cast<ncclComm_t>(comm_),
+  nccl_check(nccl().AllReduce(G_ + offset, G_ + offset, n, ncclFloat, ncclAvg, static_cast<ncclComm_t>(comm_),
                            comm_stream_),
              "ncclAllReduce(grads)");
 }

@@ -9,7 +9,7 @@
 //   dW = X^T dY   -> A = X MN-major, B = dY MN-major
 // and no transposed copies are made (the reference copies W for the tied head,
 // model.rs:163, and B for every gemm_nt, kernels.rs:66-75).
-#include <nccl.h>
+#include "nccl_api.h"
 
 #include <cmath>
 #include <cstring>
@@ -23,7 +23,7 @@ namespace mm {
 
 namespace {
 void nccl_ok(ncclResult_t r, const char* what) {
-  if (r != ncclSuccess) throw std::runtime_error(std::string(what) + ": " + ncclGetErrorString(r));
+  if (r != ncclSuccess) throw std::runtime_error(std::string(what) + ": " + nccl().GetErrorString(r));
 }
 }  // namespace
 
@@ -139,7 +139,7 @@ void Trainer::backward(int B, int T) {
     check_cuda(cudaStreamWaitEvent(comm_stream_, layer_done_[L], 0), "wait");
     allreduce_grads_range(layout_.embed, static_cast<uint64_t>(V) * D);
     allreduce_grads_range(layout_.final_norm, layout_.total - layout_.final_norm);
-    nccl_ok(ncclAllReduce(d_loss_, d_loss_, 1, ncclDouble, ncclAvg, static_cast<ncclComm_t>(comm_), comm_stream_),
+    nccl_ok(nccl().AllReduce(d_loss_, d_loss_, 1, ncclDouble, ncclAvg, static_cast<ncclComm_t>(comm_), comm_stream_),
             "ncclAllReduce(loss)");
     check_cuda(cudaEventRecord(comm_done_, comm_stream_), "event");
     check_cuda(cudaStreamWaitEvent(stream_, comm_done_, 0), "wait");
