@@ -62,6 +62,24 @@ MM_GPU_EXPORT int32_t mm_gpu_gemm(int32_t m, int32_t n, int32_t k, const float *
                     const float *b, int64_t ldb, int32_t b_mn_major, float *c, int64_t ldc,
                     const float *r, int64_t ldr, int32_t precision, void *stream);
 
+/* Causal grouped-query attention (crates/midman-nn/src/attention.rs:79-102 forward,
+ * and its autograd backward). Token-major operands: q, o, dout, dq are
+ * [batch * seq, n_heads * head_dim] with row stride ldq (= ldo = lddo = lddq);
+ * k, v, dk, dv are [batch * seq, n_kv_heads * head_dim] with row stride ldk.
+ * lse and delta are [batch, n_heads, seq]. precision MM_GPU_TF32 runs the score
+ * and value products on the tensor cores (head_dim 32, 64 or 128; other sizes
+ * fall back to the FP32 path), MM_GPU_3XTF32 the FP32 flash kernels. The
+ * library keeps the score scratch (2 * batch * n_heads * seq * seq floats). */
+MM_GPU_EXPORT int32_t mm_gpu_attention_forward(int32_t batch, int32_t seq, int32_t n_heads, int32_t n_kv_heads,
+                                               int32_t head_dim, const float *q, const float *k, const float *v,
+                                               int64_t ldq, int64_t ldk, float *o, float *lse, int32_t precision,
+                                               void *stream);
+MM_GPU_EXPORT int32_t mm_gpu_attention_backward(int32_t batch, int32_t seq, int32_t n_heads, int32_t n_kv_heads,
+                                                int32_t head_dim, const float *q, const float *k, const float *v,
+                                                const float *o, const float *lse, const float *dout, int64_t ldq,
+                                                int64_t ldk, float *dq, float *dk, float *dv, int32_t precision,
+                                                void *stream);
+
 #ifdef __cplusplus
 }
 #endif

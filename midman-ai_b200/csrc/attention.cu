@@ -451,13 +451,18 @@ void attention_backward(const AttnShape& s, const float* q, const float* k, cons
                         const float* lse, const float* dout, long long lddo, float* dq, float* dk, float* dv,
                         float* delta, cudaStream_t stream) {
   validate(s);
-  const long long rows = static_cast<long long>(s.B) * s.H * s.T;
-  attn_delta_kernel<<<static_cast<unsigned>((rows * 32 + 255) / 256), 256, 0, stream>>>(s, o, dout, lddo, delta);
-  check("attention_backward(delta)");
+  attention_delta(s, o, dout, lddo, delta, stream);
   if (s.hd <= 16) launch_bwd<16>(s, q, k, v, dout, lddo, lse, delta, dq, dk, dv, stream);
   else if (s.hd <= 32) launch_bwd<32>(s, q, k, v, dout, lddo, lse, delta, dq, dk, dv, stream);
   else if (s.hd <= 64) launch_bwd<64>(s, q, k, v, dout, lddo, lse, delta, dq, dk, dv, stream);
   else launch_bwd<128>(s, q, k, v, dout, lddo, lse, delta, dq, dk, dv, stream);
+}
+
+void attention_delta(const AttnShape& s, const float* o, const float* dout, long long lddo, float* delta,
+                     cudaStream_t stream) {
+  const long long rows = static_cast<long long>(s.B) * s.H * s.T;
+  attn_delta_kernel<<<static_cast<unsigned>((rows * 32 + 255) / 256), 256, 0, stream>>>(s, o, dout, lddo, delta);
+  check("attention delta");
 }
 
 void attention_probs(const AttnShape& s, const float* q, const float* k, const float* lse, float* probs,

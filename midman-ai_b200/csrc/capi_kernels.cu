@@ -1,10 +1,12 @@
 // Kernel-level C ABI (include/midman_gpu.h): argument checks, then the launchers.
 #include <cuda_runtime.h>
 
+#include <cmath>
 #include <exception>
 #include <string>
 
 #include "../../include/midman_gpu.h"
+#include "attention.h"
 #include "device.h"
 #include "gemm.h"
 
@@ -55,6 +57,62 @@ int32_t mm_gpu_gemm(int32_t m, int32_t n, int32_t k, const float* a, int64_t lda
                        ? mm::gemm_tf32(m, n, k, A, B, c, ldc, r, ldr, ctx.d_err, as_stream(stream))
                        : mm::gemm_3xtf32(m, n, k, A, B, c, ldc, r, ldr, ctx.d_err, as_stream(stream));
     if (rc) return fail(rc == mm::kGemmLaunch ? MM_GPU_ERR_DEVICE : MM_GPU_ERR_ARGUMENT, mm::gemm_status_string(rc));
+    return MM_GPU_OK;
+  });
+}
+
+namespace {
+int32_t attention_shape(int32_t B, int32_t T, int32_t H, int32_t Hkv, int32_t hd, int64_t ldq, int64_t ldk,
+                        mm::AttnShape* s) {
+  if (B <= 0 || T <= 0 || H <= 0 || Hkv <= 0 || hd <= 0 || H % Hkv != 0 || hd > 128 || (hd & 1))
+    return fail(MM_GPU_ERR_SHAPE, "attention: need positive sizes, n_heads a multiple of n_kv_heads, even head_dim <= 128");
+  if (ldq < static_cast<int64_t>(H) * hd || ldk < static_cast<int64_t>(Hkv) * hd)
+    return fail(MM_GPU_ERR_SHAPE, "attention: row strides smaller than the heads they hold");
+  *s = mm::AttnShape{B, T, H, Hkv, hd, ldq, ldk, ldk, ldq, 1.0f / std::sqrt(static_cast<float>(hd))};
+  return MM_GPU_OK;
+}
+}  // namespace
+
+int32_t mm_gpu_attention_forward(int32_t batch, int32_t seq, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
+                                 const float* q, const float* k, const float* v, int64_t ldq, int64_t ldk, float* o,
+                                 float* lse, int32_t precision, void* stream) {
+  return guarded([&]() -> int32_t {
+    mm::AttnShape s;
+    if (int32_t rc = attention_shape(batch, seq, n_heads, n_kv_heads, head_dim, ldq, ldk, &s)) return rc;
+    if (!q || !k || !v || !o || !lse) return fail(MM_GPU_ERR_ARGUMENT, "attention: null pointer");
+    cudaStream_t st = as_stream(stream);
+    if (precision == MM_GPU_TF32 && mm::attention_tc_supported(s)) {
+      const size_t n = static_cast<size_t>(batch) * n_heads * seq * mm::attention_scores_ld(seq);
+      float* S = static_cast<float*>(mm::device_scratch(n * sizeof(float), st));
+      mm::attention_forward_tc(s, q, k, v, o, lse, S, st);
+    } else {
+      mm::attention_forward(s, q, k, v, o, lse, st);
+    }
+    return MM_GPU_OK;
+  });
+}
+
+int32_t mm_gpu_attention_backward(int32_t batch, int32_t seq, int32_t n_heads, int32_t n_kv_heads, int32_t head_dim,
+                                  const float* q, const float* k, const float* v, const float* o, const float* lse,
+                                  const float* dout, int64_t ldq, int64_t ldk, float* dq, float* dk, float* dv,
+                                  int32_t precision, void* stream) {
+  return guarded([&]() -> int32_t {
+    mm::AttnShape s;
+    if (int32_t rc = attention_shape(batch, seq, n_heads, n_kv_heads, head_dim, ldq, ldk, &s)) return rc;
+    if (!q || !k || !v || !o || !lse || !dout || !dq || !dk || !dv)
+      return fail(MM_GPU_ERR_ARGUMENT, "attention: null pointer");
+    cudaStream_t st = as_stream(stream);
+    const size_t rows = static_cast<size_t>(batch) * n_heads * seq;
+    if (precision == MM_GPU_TF32 && mm::attention_tc_supported(s)) {
+      const size_t n = rows * mm::attention_scores_ld(seq);
+      const size_t tmp = static_cast<size_t>(batch) * seq * n_heads * head_dim;
+      float* ws = static_cast<float*>(mm::device_scratch((2 * n + tmp + rows) * sizeof(float), st));
+      mm::attention_backward_tc(s, q, k, v, o, lse, dout, ldq, dq, dk, dv, ws + 2 * n + tmp, ws, ws + n, ws + 2 * n,
+                                st);
+    } else {
+      float* delta = static_cast<float*>(mm::device_scratch(rows * sizeof(float), st));
+      mm::attention_backward(s, q, k, v, o, lse, dout, ldq, dq, dk, dv, delta, st);
+    }
     return MM_GPU_OK;
   });
 }

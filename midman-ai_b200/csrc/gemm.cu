@@ -11,7 +11,13 @@
 //   dX = dY W^T   : A = dY K-major,  B = W  K-major   (kernels.rs:66-75 gemm_nt)
 //   dW = X^T dY   : A = X  MN-major, B = dY MN-major  (kernels.rs:78-84 gemm_tn)
 //
-// Warp roles (192 threads, one CTA per 128 x 256 output tile):
+// The batched form (grid.z = batch) addresses every operand through a 4-D tensor
+// map (inner, head, row, batch), so per-head slices of token-major activations
+// and grouped-query key/value heads are read in place; it also restricts the
+// work to the causal part of an attention product (tiles above the diagonal
+// skipped, or the K loop cut at the diagonal).
+//
+// Warp roles (192 threads, one CTA per BM x BN output tile):
 //   warp 0      TMA producer (one lane), STAGES-deep ring of A/B stages
 //   warp 1      TMEM allocator + UMMA issuer (one lane)
 //   warps 2..5  epilogue: TMEM -> registers -> global (optionally + R)
@@ -31,25 +37,62 @@ namespace mm {
 namespace {
 
 constexpr int BM = 128;
-constexpr int BN = 256;
 constexpr int BK = 32;  // 32 fp32 = 128 bytes = one swizzle row
-constexpr int STAGES = 4;
 constexpr int A_STAGE_BYTES = BM * BK * 4;  // 16 KB
-constexpr int B_STAGE_BYTES = BN * BK * 4;  // 32 KB
-constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
-constexpr int TMEM_COLS = 256;
 constexpr int THREADS = 192;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers, TMEM slot, counters*/;
+constexpr int SMEM_BUDGET = 196608;  // operand ring; leaves room for barriers and alignment
+
+template <int BN>
+struct Tile {
+  static constexpr int B_STAGE_BYTES = BN * BK * 4;
+  static constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
+  static constexpr int STAGES = SMEM_BUDGET / STAGE_BYTES > 8 ? 8 : SMEM_BUDGET / STAGE_BYTES;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers, slot, counters*/;
+  static constexpr int TMEM_COLS = BN < 32 ? 32 : BN;
+};
 
 // Byte offset of the 4 KB block that holds MN columns [32j, 32j+32) of an
 // MN-major tile; its 32 K-rows sit 128 bytes apart.
 constexpr uint32_t MN_BLOCK_BYTES = BK * 128;
 
-template <bool A_MN, bool B_MN>
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int32_t x,
+                                            int32_t h, int32_t y, int32_t b) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(h), "r"(y), "r"(b)
+      : "memory");
+}
+
+template <bool BATCHED>
+__device__ __forceinline__ void load_box(uint32_t dst, const CUtensorMap* map, uint32_t bar, int32_t x, int32_t y,
+                                         int32_t zh, int32_t zb) {
+  if (BATCHED)
+    tma_load_4d(dst, map, bar, x, zh, y, zb);
+  else
+    tma_load_2d(dst, map, bar, x, y);
+}
+
+template <bool A_MN, bool B_MN, int BN, bool BATCHED>
 __global__ void __launch_bounds__(THREADS, 1)
-    gemm_tf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                     float* C, long long ldc, const float* R, long long ldr, int M,
-                     int N, int K, int* err) {
+    gemm_tf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, float* C,
+                     long long ldc, const float* R, long long ldr, int M, int N, int K, int* err, GemmBatch bt) {
+  using TL = Tile<BN>;
+  constexpr int STAGES = TL::STAGES;
+  constexpr int STAGE_BYTES = TL::STAGE_BYTES;
+  const int m0 = blockIdx.y * BM;
+  const int n0 = blockIdx.x * BN;
+  if (BATCHED && bt.causal == kCausalSkipUpper && n0 > m0 + BM - 1) return;  // whole tile above the diagonal
+  int kt_begin = 0, k_end = K;
+  if (BATCHED && bt.causal == kCausalKBelow) k_end = min(K, m0 + BM);
+  if (BATCHED && bt.causal == kCausalKAbove) kt_begin = m0 / BK;
+  const int kt_end = (k_end + BK - 1) / BK;
+  const int n_k = kt_end > kt_begin ? kt_end - kt_begin : 0;
+  const int z = blockIdx.z;
+  const int a_zb = BATCHED ? z / bt.a_zdiv : 0, a_zh = BATCHED ? (z % bt.a_zdiv) / bt.a_zgroup : 0;
+  const int b_zb = BATCHED ? z / bt.b_zdiv : 0, b_zh = BATCHED ? (z % bt.b_zdiv) / bt.b_zgroup : 0;
+  if (BATCHED) C += (z / bt.c_zdiv) * bt.c_sb + ((z % bt.c_zdiv) / bt.c_zgroup) * bt.c_sh;
+
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   const uint32_t base = (raw_addr + 1023u) & ~1023u;  // SW128 atoms want 1024-byte alignment
@@ -68,9 +111,6 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
-  const int m0 = blockIdx.y * BM;
-  const int n0 = blockIdx.x * BN;
-  const int k_tiles = (K + BK - 1) / BK;
 
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tmA);
@@ -86,7 +126,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     fence_proxy_async_smem();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_alloc(tmem_slot, TL::TMEM_COLS);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -97,54 +137,53 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- TMA producer
-      for (int kt = 0; kt < k_tiles; ++kt) {
-        const int s = kt % STAGES;
-        const int round = kt / STAGES;
+      for (int i = 0; i < n_k; ++i) {
+        const int s = i % STAGES;
+        const int round = i / STAGES;
         if (round > 0 && !mbar_wait(empty_bar(s), (round - 1) & 1, err, kErrWaitEmpty)) break;
         const uint32_t sa = base + s * STAGE_BYTES;
         const uint32_t sb = sa + A_STAGE_BYTES;
         mbar_arrive_expect_tx(full_bar(s), STAGE_BYTES);
-        const int k0 = kt * BK;
+        const int k0 = (kt_begin + i) * BK;
         if (!A_MN) {
-          tma_load_2d(sa, &tmA, full_bar(s), k0, m0);
+          load_box<BATCHED>(sa, &tmA, full_bar(s), k0, m0, a_zh, a_zb);
         } else {
 #pragma unroll
-          for (int j = 0; j < BM / 32; ++j) tma_load_2d(sa + j * MN_BLOCK_BYTES, &tmA, full_bar(s), m0 + 32 * j, k0);
+          for (int j = 0; j < BM / 32; ++j)
+            load_box<BATCHED>(sa + j * MN_BLOCK_BYTES, &tmA, full_bar(s), m0 + 32 * j, k0, a_zh, a_zb);
         }
         if (!B_MN) {
-          tma_load_2d(sb, &tmB, full_bar(s), k0, n0);
+          load_box<BATCHED>(sb, &tmB, full_bar(s), k0, n0, b_zh, b_zb);
         } else {
 #pragma unroll
-          for (int j = 0; j < BN / 32; ++j) tma_load_2d(sb + j * MN_BLOCK_BYTES, &tmB, full_bar(s), n0 + 32 * j, k0);
+          for (int j = 0; j < BN / 32; ++j)
+            load_box<BATCHED>(sb + j * MN_BLOCK_BYTES, &tmB, full_bar(s), n0 + 32 * j, k0, b_zh, b_zb);
         }
-        *loads_issued = kt + 1;
+        *loads_issued = i + 1;
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- UMMA issuer
       constexpr uint32_t idesc = idesc_tf32(BM, BN, A_MN, B_MN);
-      bool ok = true;
-      for (int kt = 0; kt < k_tiles && ok; ++kt) {
-        const int s = kt % STAGES;
-        const int round = kt / STAGES;
-        ok = mbar_wait(full_bar(s), round & 1, err, kErrWaitFull);
-        if (!ok) break;
+      for (int i = 0; i < n_k; ++i) {
+        const int s = i % STAGES;
+        const int round = i / STAGES;
+        if (!mbar_wait(full_bar(s), round & 1, err, kErrWaitFull)) break;
         tc_fence_after();
-        *loads_consumed = kt + 1;
+        *loads_consumed = i + 1;
         const uint32_t sa = base + s * STAGE_BYTES;
         const uint32_t sb = sa + A_STAGE_BYTES;
 #pragma unroll
         for (int k = 0; k < BK / 8; ++k) {
           // K-major: step 8 tf32 = 32 bytes along the swizzled row.
-          // MN-major: step 8 K-rows = 1024 bytes.
-          // MN-major (32-byte swizzle atoms of 4 K-rows): LBO = next 32-wide MN block,
-          // SBO = next group of 4 K-rows (512 bytes).
+          // MN-major (32-byte swizzle atoms of 4 K-rows): step 8 K-rows = 1024
+          // bytes; LBO = next 32-wide MN block, SBO = next group of 4 K-rows.
           const uint64_t adesc = A_MN ? smem_desc(sa + k * 1024, MN_BLOCK_BYTES, 512, kLayoutSw128Base32)
                                       : smem_desc(sa + k * 32, 16, 1024, kLayoutSw128);
           const uint64_t bdesc = B_MN ? smem_desc(sb + k * 1024, MN_BLOCK_BYTES, 512, kLayoutSw128Base32)
                                       : smem_desc(sb + k * 32, 16, 1024, kLayoutSw128);
-          umma_tf32(tmem_acc, adesc, bdesc, idesc, (kt | k) != 0 ? 1u : 0u);
+          umma_tf32(tmem_acc, adesc, bdesc, idesc, (i | k) != 0 ? 1u : 0u);
         }
         umma_commit(empty_bar(s));
       }
@@ -156,7 +195,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int row = m0 + quarter * 32 + lane;
     const bool ok = mbar_wait(accum_bar, 0, err, kErrWaitAccum);
     tc_fence_after();
-    if (ok && k_tiles > 0) {
+    if (ok && n_k > 0) {
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
@@ -184,8 +223,8 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
         }
       }
-    } else if (k_tiles == 0 && row < M) {
-      // K == 0: the product is empty, C = R (or 0).
+    } else if (ok && row < M) {
+      // Empty K range: the product is zero, C = R (or 0).
       for (int col = n0; col < n0 + BN && col < N; ++col)
         C[static_cast<long long>(row) * ldc + col] = R ? R[static_cast<long long>(row) * ldr + col] : 0.0f;
     }
@@ -196,15 +235,16 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (threadIdx.x == 0) {
     // Only after a timed-out wait can a TMA stage still be in flight here: let
     // each one land (bounded) before the CTA's shared memory is released.
-    for (int kt = *loads_consumed; kt < *loads_issued; ++kt)
-      if (!mbar_wait(full_bar(kt % STAGES), (kt / STAGES) & 1, err, kErrWaitDrain, 1000000000ull)) break;
+    for (int i = *loads_consumed; i < *loads_issued; ++i)
+      if (!mbar_wait(full_bar(i % STAGES), (i / STAGES) & 1, err, kErrWaitDrain, 1000000000ull)) break;
   }
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_acc, TMEM_COLS);
+    tmem_dealloc(tmem_acc, TL::TMEM_COLS);
   }
   __syncthreads();
 }
+
 
 // ------------------------------------------------------------------ host side
 
@@ -222,39 +262,66 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
   return fn;
 }
 
-// 2-D fp32 tensor map: `inner` contiguous elements per row, `outer` rows,
-// `ld` elements between rows; box of box_inner x box_outer, 128-byte swizzle
-// (of 32-byte chunks for MN-major operands, matching the UMMA layout).
-int make_map(CUtensorMap* map, const float* ptr, long long inner, long long outer, long long ld,
-             int box_inner, int box_outer, bool mn_major) {
-  auto encode = get_encode_fn();
-  if (!encode) return -1;
-  cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld) * 4};
-  cuuint32_t box[2] = {static_cast<cuuint32_t>(box_inner), static_cast<cuuint32_t>(box_outer)};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(ptr), dims, strides,
-                      box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                      mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
-                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+// fp32 tensor map of rank 2 or 4 with a 128-byte swizzle (of 32-byte chunks for
+// MN-major operands, matching the UMMA layout). dims/strides in elements;
+// strides[0] is the stride of dims[1].
+int encode(CUtensorMap* map, const float* ptr, int rank, const long long* dims, const long long* strides,
+           const int* box, bool mn_major) {
+  auto fn = get_encode_fn();
+  if (!fn) return -1;
+  cuuint64_t d[4], st[3];
+  cuuint32_t b[4], e[4] = {1, 1, 1, 1};
+  for (int i = 0; i < rank; ++i) {
+    d[i] = static_cast<cuuint64_t>(dims[i]);
+    b[i] = static_cast<cuuint32_t>(box[i]);
+  }
+  for (int i = 0; i + 1 < rank; ++i) {
+    st[i] = static_cast<cuuint64_t>(strides[i]) * 4;
+    if (st[i] % 16 != 0) return -2;
+  }
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, rank, const_cast<float*>(ptr), d, st, b, e,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? 0 : -2;
 }
 
-template <bool A_MN, bool B_MN>
-void launch(const CUtensorMap& ta, const CUtensorMap& tb, float* C, long long ldc, const float* R,
-            long long ldr, int M, int N, int K, int* err, cudaStream_t stream) {
-  auto kern = gemm_tf32_kernel<A_MN, B_MN>;
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
-  dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM);
-  kern<<<grid, THREADS, SMEM_BYTES, stream>>>(ta, tb, C, ldc, R, ldr, M, N, K, err);
+// 2-D operand: `inner` contiguous elements per row, `outer` rows, `ld` apart.
+int make_map2d(CUtensorMap* map, const float* ptr, long long inner, long long outer, long long ld, int box_inner,
+               int box_outer, bool mn_major) {
+  const long long dims[2] = {inner, outer}, strides[1] = {ld};
+  const int box[2] = {box_inner, box_outer};
+  return encode(map, ptr, 2, dims, strides, box, mn_major);
 }
+
+template <bool A_MN, bool B_MN, int BN, bool BATCHED>
+void launch(const CUtensorMap& ta, const CUtensorMap& tb, float* C, long long ldc, const float* R, long long ldr,
+            int M, int N, int K, int batch, const GemmBatch& bt, int* err, cudaStream_t stream) {
+  using TL = Tile<BN>;
+  auto kern = gemm_tf32_kernel<A_MN, B_MN, BN, BATCHED>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TL::SMEM_BYTES);
+  dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM, batch);
+  kern<<<grid, THREADS, TL::SMEM_BYTES, stream>>>(ta, tb, C, ldc, R, ldr, M, N, K, err, bt);
+}
+
+template <int BN, bool BATCHED>
+void launch_majors(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, float* C, long long ldc,
+                   const float* R, long long ldr, int M, int N, int K, int batch, const GemmBatch& bt, int* err,
+                   cudaStream_t s) {
+  if (!a_mn && !b_mn) launch<false, false, BN, BATCHED>(ta, tb, C, ldc, R, ldr, M, N, K, batch, bt, err, s);
+  else if (!a_mn && b_mn) launch<false, true, BN, BATCHED>(ta, tb, C, ldc, R, ldr, M, N, K, batch, bt, err, s);
+  else if (a_mn && !b_mn) launch<true, false, BN, BATCHED>(ta, tb, C, ldc, R, ldr, M, N, K, batch, bt, err, s);
+  else launch<true, true, BN, BATCHED>(ta, tb, C, ldc, R, ldr, M, N, K, batch, bt, err, s);
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace
 
 const char* gemm_status_string(int status) {
   switch (status) {
     case 0: return "ok";
-    case kGemmBadArgument: return "bad GEMM argument (null pointer or negative size)";
+    case kGemmBadArgument: return "bad GEMM argument (null pointer, negative size or unsupported tile)";
     case kGemmMisaligned: return "GEMM operand not 16-byte aligned or leading dimension not a multiple of 4";
     case kGemmTensorMap: return "cuTensorMapEncodeTiled is unavailable or rejected an operand";
     case kGemmLaunch: return "GEMM kernel launch failed";
@@ -262,25 +329,65 @@ const char* gemm_status_string(int status) {
   }
 }
 
-int gemm_tf32(int M, int N, int K, GemmOperand A, GemmOperand B, float* C, long long ldc,
-              const float* R, long long ldr, int* d_err, cudaStream_t stream) {
+int gemm_tf32(int M, int N, int K, GemmOperand A, GemmOperand B, float* C, long long ldc, const float* R,
+              long long ldr, int* d_err, cudaStream_t stream) {
   if (M < 0 || N < 0 || K < 0 || !C) return kGemmBadArgument;
   if (M == 0 || N == 0) return 0;
   if (K > 0 && (!A.ptr || !B.ptr)) return kGemmBadArgument;
-  auto aligned = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
-  if ((ldc & 3) || !aligned(C) || (R && ((ldr & 3) || !aligned(R)))) return kGemmMisaligned;
+  if ((ldc & 3) || !aligned16(C) || (R && ((ldr & 3) || !aligned16(R)))) return kGemmMisaligned;
+  // Narrow outputs waste less of a 256-wide tile with a 128-wide one.
+  const int bn = N <= 128 ? 128 : 256;
   CUtensorMap ta{}, tb{};
   if (K > 0) {
-    if ((A.ld & 3) || (B.ld & 3) || !aligned(A.ptr) || !aligned(B.ptr)) return kGemmMisaligned;
-    int rc = A.mn_major ? make_map(&ta, A.ptr, M, K, A.ld, 32, BK, true) : make_map(&ta, A.ptr, K, M, A.ld, BK, BM, false);
+    if ((A.ld & 3) || (B.ld & 3) || !aligned16(A.ptr) || !aligned16(B.ptr)) return kGemmMisaligned;
+    int rc = A.mn_major ? make_map2d(&ta, A.ptr, M, K, A.ld, 32, BK, true)
+                        : make_map2d(&ta, A.ptr, K, M, A.ld, BK, BM, false);
     if (rc) return kGemmTensorMap;
-    rc = B.mn_major ? make_map(&tb, B.ptr, N, K, B.ld, 32, BK, true) : make_map(&tb, B.ptr, K, N, B.ld, BK, BN, false);
+    rc = B.mn_major ? make_map2d(&tb, B.ptr, N, K, B.ld, 32, BK, true)
+                    : make_map2d(&tb, B.ptr, K, N, B.ld, BK, bn, false);
     if (rc) return kGemmTensorMap;
   }
-  if (!A.mn_major && !B.mn_major) launch<false, false>(ta, tb, C, ldc, R, ldr, M, N, K, d_err, stream);
-  else if (!A.mn_major && B.mn_major) launch<false, true>(ta, tb, C, ldc, R, ldr, M, N, K, d_err, stream);
-  else if (A.mn_major && !B.mn_major) launch<true, false>(ta, tb, C, ldc, R, ldr, M, N, K, d_err, stream);
-  else launch<true, true>(ta, tb, C, ldc, R, ldr, M, N, K, d_err, stream);
+  const GemmBatch bt{};
+  if (bn == 128)
+    launch_majors<128, false>(A.mn_major, B.mn_major, ta, tb, C, ldc, R, ldr, M, N, K, 1, bt, d_err, stream);
+  else
+    launch_majors<256, false>(A.mn_major, B.mn_major, ta, tb, C, ldc, R, ldr, M, N, K, 1, bt, d_err, stream);
+  return cudaGetLastError() == cudaSuccess ? 0 : kGemmLaunch;
+}
+
+// 4-D operand view (inner, head, row, batch) of a batched GEMM operand.
+static int make_map4d(CUtensorMap* map, const BatchedOperand& o, int box_inner, int box_rows) {
+  const long long dims[4] = {o.inner, o.heads, o.rows, o.batches};
+  const long long strides[3] = {o.head_stride, o.row_stride, o.batch_stride};
+  const int box[4] = {box_inner, 1, box_rows, 1};
+  return encode(map, o.ptr, 4, dims, strides, box, o.mn_major);
+}
+
+int gemm_tf32_batched(int batch, int M, int N, int K, const BatchedOperand& A, const BatchedOperand& B, float* C,
+                      long long ldc, const GemmBatch& bt_in, int bn, int* d_err, cudaStream_t stream) {
+  GemmBatch bt = bt_in;  // operand z -> (batch, head) maps come from the operands
+  bt.a_zdiv = A.zdiv;
+  bt.a_zgroup = A.zgroup;
+  bt.b_zdiv = B.zdiv;
+  bt.b_zgroup = B.zgroup;
+  if (batch < 0 || M < 0 || N < 0 || K <= 0 || !C || !A.ptr || !B.ptr) return kGemmBadArgument;
+  if (batch == 0 || M == 0 || N == 0) return 0;
+  if (bn != 64 && bn != 128 && bn != 256) return kGemmBadArgument;
+  if ((ldc & 3) || !aligned16(C) || !aligned16(A.ptr) || !aligned16(B.ptr)) return kGemmMisaligned;
+  if ((bt.c_sb & 3) || (bt.c_sh & 3) || bt.a_zdiv <= 0 || bt.b_zdiv <= 0 || bt.c_zdiv <= 0 || bt.a_zgroup <= 0 ||
+      bt.b_zgroup <= 0 || bt.c_zgroup <= 0)
+    return kGemmBadArgument;
+  CUtensorMap ta{}, tb{};
+  int rc = A.mn_major ? make_map4d(&ta, A, 32, BK) : make_map4d(&ta, A, BK, BM);
+  if (rc) return kGemmTensorMap;
+  rc = B.mn_major ? make_map4d(&tb, B, 32, BK) : make_map4d(&tb, B, BK, bn);
+  if (rc) return kGemmTensorMap;
+  if (bn == 64)
+    launch_majors<64, true>(A.mn_major, B.mn_major, ta, tb, C, ldc, nullptr, 0, M, N, K, batch, bt, d_err, stream);
+  else if (bn == 128)
+    launch_majors<128, true>(A.mn_major, B.mn_major, ta, tb, C, ldc, nullptr, 0, M, N, K, batch, bt, d_err, stream);
+  else
+    launch_majors<256, true>(A.mn_major, B.mn_major, ta, tb, C, ldc, nullptr, 0, M, N, K, batch, bt, d_err, stream);
   return cudaGetLastError() == cudaSuccess ? 0 : kGemmLaunch;
 }
 

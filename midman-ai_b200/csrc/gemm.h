@@ -20,12 +20,43 @@ enum GemmStatus : int {
   kGemmLaunch = -104,
 };
 
+// Batched products (grid.z = batch). Batch z reads operand X at head
+// (z % X.zdiv) / X.zgroup and batch z / X.zdiv of its 4-D view (the zdiv and
+// zgroup of each BatchedOperand), and writes C at
+// C + (z / c_zdiv) * c_sb + ((z % c_zdiv) / c_zgroup) * c_sh.
+enum GemmCausal : int {
+  kCausalNone = 0,
+  kCausalSkipUpper = 1,  // output tiles entirely above the diagonal (n0 > m0 + 127) are not computed
+  kCausalKBelow = 2,     // the K loop stops at m0 + 128 (keys up to the row block's last query)
+  kCausalKAbove = 3,     // the K loop starts at m0 (queries from the key block's first key on)
+};
+struct GemmBatch {
+  int a_zdiv = 1, a_zgroup = 1, b_zdiv = 1, b_zgroup = 1;
+  long long c_sb = 0, c_sh = 0;
+  int c_zdiv = 1, c_zgroup = 1;
+  int causal = kCausalNone;
+};
+// 4-D view of an operand, extents and strides in elements: `inner` contiguous
+// (K for a K-major operand, M or N for an MN-major one), `rows` the other
+// matrix dimension; heads and batches select the matrix.
+struct BatchedOperand {
+  const float* ptr;
+  bool mn_major;
+  long long inner, heads, rows, batches;
+  long long head_stride, row_stride, batch_stride;
+  int zdiv, zgroup;
+};
+
 // C[m, n] = sum_k A(m, k) B(n, k) (+ R[m, n] if R is not null; R may equal C).
 // Asynchronous on `stream`; a pipeline timeout is reported through d_err.
 int gemm_tf32(int M, int N, int K, GemmOperand A, GemmOperand B, float* C, long long ldc,
               const float* R, long long ldr, int* d_err, cudaStream_t stream);
 
 const char* gemm_status_string(int status);
+
+// The batched form; bn (64, 128 or 256) is the output tile width. No residual.
+int gemm_tf32_batched(int batch, int M, int N, int K, const BatchedOperand& A, const BatchedOperand& B, float* C,
+                      long long ldc, const GemmBatch& bt, int bn, int* d_err, cudaStream_t stream);
 
 }  // namespace mm
 

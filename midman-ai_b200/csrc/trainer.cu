@@ -136,6 +136,18 @@ Trainer::Trainer(const ModelConfig& cfg, int batch, int seq, int precision, int 
   d_partials_ = static_cast<double*>(alloc(kNormBlocks * sizeof(double)));
   d_loss_ = static_cast<double*>(alloc(sizeof(double)));
   d_norm_ = falloc(4);
+  {
+    const int hd = static_cast<int>(cfg.head_dim());
+    const AttnShape shape{batch, seq, static_cast<int>(H), static_cast<int>(cfg.n_kv_heads), hd,
+                          static_cast<long long>(D), static_cast<long long>(KV), static_cast<long long>(KV),
+                          static_cast<long long>(D), 1.0f};
+    attn_tc_ = precision == kPrecisionTF32 && attention_tc_supported(shape);
+    if (attn_tc_) {
+      const uint64_t sz = static_cast<uint64_t>(batch) * H * seq * attention_scores_ld(seq);
+      scores_ = falloc(sz);
+      dscores_ = falloc(sz);
+    }
+  }
   check_cuda(cudaDeviceSynchronize(), "trainer setup");
 }
 

@@ -135,6 +135,10 @@ class Trainer {
   std::vector<void*> allocations_;
   int dx_cur_ = 0;  // which dx_ buffer holds the gradient flowing down
 
+  // Attention on the tensor cores (TF32 mode, head_dim 32/64/128): score buffers.
+  bool attn_tc_ = false;
+  float *scores_ = nullptr, *dscores_ = nullptr;
+
   bool profiling_ = false;
   std::vector<cudaEvent_t> prof_events_;
   struct Pending {

@@ -50,7 +50,10 @@ void Trainer::forward(int B, int T, bool train) {
     rope(a.k, N, T, Hkv, hd, KV, d_cos_, d_sin_, false, stream_);
     const double attn_flops = 2.0 * B * H * static_cast<double>(T) * (T + 1) * hd;  // QK^T and PV, causal half
     int slot = prof_begin();
-    attention_forward(shape, a.q, a.k, a.v, a.o, a.lse, stream_);
+    if (attn_tc_)
+      attention_forward_tc(shape, a.q, a.k, a.v, a.o, a.lse, scores_, stream_);
+    else
+      attention_forward(shape, a.q, a.k, a.v, a.o, a.lse, stream_);
     prof_end(slot, "attention_fwd", attn_flops);
     gemm(N, D, D, a.o, D, false, P_ + bo.o, D, true, a.h, D, a.x, D);
     // out = h + swiglu(mlp_norm(h)) (mlp.rs:20-24)
@@ -108,7 +111,11 @@ void Trainer::backward(int B, int T) {
     gemm(N, D, D, dh, D, false, P_ + bo.o, D, false, do_, D, nullptr, 0);
     gemm(D, D, N, a.o, D, true, dh, D, true, G_ + bo.o, D, nullptr, 0);
     int slot = prof_begin();
-    attention_backward(shape, a.q, a.k, a.v, a.o, a.lse, do_, D, dq_, dk_, dv_, delta_, stream_);
+    if (attn_tc_)
+      attention_backward_tc(shape, a.q, a.k, a.v, a.o, a.lse, do_, D, dq_, dk_, dv_, delta_, scores_, dscores_, tmp_,
+                            stream_);
+    else
+      attention_backward(shape, a.q, a.k, a.v, a.o, a.lse, do_, D, dq_, dk_, dv_, delta_, stream_);
     // dV, dP, dQ, dK: four causal products (the recomputed scores are not counted)
     prof_end(slot, "attention_bwd", 4.0 * B * H * static_cast<double>(T) * (T + 1) * hd);
     rope(dq_, N, T, H, hd, D, d_cos_, d_sin_, true, stream_);

@@ -15,7 +15,8 @@ LIB_PATH = HERE / "lib" / "libmidman_gpu.so"
 
 # Every symbol the public headers declare, grouped by header.
 GPU_SYMBOLS = [
-    "mm_gpu_last_error", "mm_gpu_device_status", "mm_gpu_gemm",
+    "mm_gpu_last_error", "mm_gpu_device_status", "mm_gpu_gemm", "mm_gpu_attention_forward",
+    "mm_gpu_attention_backward",
 ]
 API_SYMBOLS = [
     "midman_abi_version", "midman_alloc", "midman_free", "midman_text_ptr", "midman_text_len",
@@ -53,6 +54,9 @@ def load(path: str | os.PathLike | None = None) -> C.CDLL:
     _sig(lib, "mm_gpu_last_error", C.c_char_p)
     _sig(lib, "mm_gpu_device_status", i32, vp)
     _sig(lib, "mm_gpu_gemm", i32, i32, i32, i32, vp, i64, i32, vp, i64, i32, vp, i64, vp, i64, i32, vp)
+    _sig(lib, "mm_gpu_attention_forward", i32, i32, i32, i32, i32, i32, vp, vp, vp, i64, i64, vp, vp, i32, vp)
+    _sig(lib, "mm_gpu_attention_backward", i32, i32, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp, i64, i64, vp, vp,
+         vp, i32, vp)
     u32, u8p, dp, i32p = C.c_uint32, C.POINTER(C.c_uint8), C.POINTER(C.c_double), C.POINTER(C.c_int32)
     _sig(lib, "midman_abi_version", u32)
     _sig(lib, "midman_alloc", u8p, u32)
@@ -123,6 +127,19 @@ def gemm(a, b, c, *, m, n, k, lda, ldb, ldc, a_mn_major, b_mn_major, r=None, ldr
     return check(load().mm_gpu_gemm(m, n, k, _ptr(a), lda, int(a_mn_major), _ptr(b), ldb,
                                     int(b_mn_major), _ptr(c), ldc, _ptr(r), ldr, precision,
                                     _stream(stream)))
+
+
+def attention_forward(q, k, v, o, lse, *, batch, seq, n_heads, n_kv_heads, head_dim, ldq, ldk, precision=0,
+                      stream=None):
+    return check(load().mm_gpu_attention_forward(batch, seq, n_heads, n_kv_heads, head_dim, _ptr(q), _ptr(k), _ptr(v),
+                                                 ldq, ldk, _ptr(o), _ptr(lse), precision, _stream(stream)))
+
+
+def attention_backward(q, k, v, o, lse, dout, dq, dk, dv, *, batch, seq, n_heads, n_kv_heads, head_dim, ldq, ldk,
+                       precision=0, stream=None):
+    return check(load().mm_gpu_attention_backward(batch, seq, n_heads, n_kv_heads, head_dim, _ptr(q), _ptr(k),
+                                                  _ptr(v), _ptr(o), _ptr(lse), _ptr(dout), ldq, ldk, _ptr(dq),
+                                                  _ptr(dk), _ptr(dv), precision, _stream(stream)))
 
 
 def device_status(stream=None):

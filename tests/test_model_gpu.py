@@ -36,6 +36,8 @@ CASES = {
     "ragged_seq_hd16": (orc.config_array(128, 64, 1, 4, 1, 64, 128), 2, 100, 0.1),
     "hd128": (orc.config_array(128, 256, 1, 2, 1, 64, 96), 2, 80, 0.05),
     "hd64_gqa": (orc.config_array(96, 256, 2, 4, 2, 128, 130), 1, 130, 0.05),
+    # tensor-core attention in TF32 mode: head_dim 32, four query heads per key/value head
+    "hd32_g4_T301": (orc.config_array(64, 128, 1, 4, 1, 64, 301), 1, 301, 0.05),
 }
 
 
