@@ -1,6 +1,6 @@
 """Training-step throughput of the MidMan decoder on B200: tokens/s (fwd + bwd + AdamW).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config large|mid|tiny|smoke]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config large|mid|tiny|smoke|linear|attention]
                     [--precision tf32|3xtf32] [--impl ours|reference]
 
 One process per GPU (torchrun for N > 1); each rank trains its own B x T shard of
@@ -153,6 +153,76 @@ def cpu_baseline(cfg, seq_full, steps=1, warmup=0, threads=None):
                       f"workload's {seq_full} make the CPU's attention share smaller, so this favours the CPU"}
 
 
+LINEAR_SHAPES = [(512, 512), (512, 1408), (1024, 4096), (2048, 5632)]  # configs[1]: (K, N), M = 4096 tokens
+
+
+def run_kernels(args):
+    """configs[1] (isolated Linear fwd+bwd: Y = XW, dX = dY W^T, dW = X^T dY, M = 4096) or configs[2] (causal
+    attention B8 H16 hd64 T1024 fwd+bwd) through the kernel-level C ABI, timed with CUDA events."""
+    import torch
+    import midman_b200 as mm
+    mm.load()
+    torch.cuda.set_device(0)
+    precision = 0 if args.precision == "tf32" else 1
+    g = torch.Generator(device="cuda").manual_seed(0)
+    results = []
+    if args.config == "linear":
+        M = 4096
+        for K, N in LINEAR_SHAPES:
+            x = torch.randn(M, K, device="cuda", generator=g)
+            w = torch.randn(K, N, device="cuda", generator=g)
+            dy = torch.randn(M, N, device="cuda", generator=g)
+            y, dx, dw = torch.empty(M, N, device="cuda"), torch.empty(M, K, device="cuda"), torch.empty(K, N,
+                                                                                                        device="cuda")
+
+            def step():
+                mm.gemm(x, w, y, m=M, n=N, k=K, lda=K, ldb=N, ldc=N, a_mn_major=False, b_mn_major=True,
+                        precision=precision)
+                mm.gemm(dy, w, dx, m=M, n=K, k=N, lda=N, ldb=N, ldc=K, a_mn_major=False, b_mn_major=False,
+                        precision=precision)
+                mm.gemm(x, dy, dw, m=K, n=N, k=M, lda=K, ldb=N, ldc=N, a_mn_major=True, b_mn_major=True,
+                        precision=precision)
+            flops = 3 * 2 * M * K * N
+            results.append(({"K": K, "N": N, "M": M}, flops, step))
+    else:
+        B, H, hd, T = 8, 16, 64, 1024
+        q = torch.randn(B, T, H, hd, device="cuda", generator=g)
+        k = torch.randn(B, T, H, hd, device="cuda", generator=g)
+        v = torch.randn(B, T, H, hd, device="cuda", generator=g)
+        do = torch.randn(B, T, H, hd, device="cuda", generator=g)
+        o, lse = torch.empty_like(q), torch.empty(B, H, T, device="cuda")
+        dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+        kw = dict(batch=B, seq=T, n_heads=H, n_kv_heads=H, head_dim=hd, ldq=H * hd, ldk=H * hd, precision=precision)
+
+        def step():
+            mm.attention_forward(q, k, v, o, lse, **kw)
+            mm.attention_backward(q, k, v, o, lse, do, dq, dk, dv, **kw)
+        flops = 6 * 2 * B * H * (T * T // 2) * hd  # six causal T x T x hd products, no recompute
+        results.append(({"B": B, "H": H, "hd": hd, "T": T}, flops, step))
+    tf32 = tf32_peak_tflops(torch)
+    out = []
+    for shape, flops, step in results:
+        for _ in range(max(3, args.warmup)):
+            step()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(args.steps):
+            step()
+        e.record()
+        e.synchronize()
+        mm.device_status()
+        ms = s.elapsed_time(e) / args.steps
+        out.append({**shape, "ms": ms, "tflops": flops / (ms * 1e-3) / 1e12, "frac_of_cublas_tf32": flops / (ms * 1e-3)
+                    / 1e12 / tf32})
+    line = {"metric": "fwd+bwd TFLOP/s" if args.config == "linear" else "attention fwd+bwd TFLOP/s",
+            "value": statistics.mean(r["tflops"] for r in out), "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "higher_is_better": True, "dtype": args.precision, "data": "synthetic N(0,1)",
+            "config": {"workload": args.config, "shapes": out}, "tf32_peak_cublas": tf32}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def run_reference(args, cfg, B, T, world, rank):
     if rank != 0:
         return 0
@@ -173,12 +243,14 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=8)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--config", default="large", choices=sorted(CONFIGS))
+    ap.add_argument("--config", default="large", choices=sorted(CONFIGS) + ["linear", "attention"])
     ap.add_argument("--precision", default="tf32", choices=["tf32", "3xtf32"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
 
+    if args.config in ("linear", "attention"):
+        return run_kernels(args) if args.impl == "ours" else 0
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
