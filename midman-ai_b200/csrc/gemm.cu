@@ -17,10 +17,12 @@
 // work to the causal part of an attention product (tiles above the diagonal
 // skipped, or the K loop cut at the diagonal).
 //
-// Warp roles (192 threads, one CTA per BM x BN output tile):
+// Warp roles (192 threads; a persistent grid of at most one CTA per SM, each
+// walking BM x BN output tiles with a stride of the grid size):
 //   warp 0      TMA producer (one lane), STAGES-deep ring of A/B stages
-//   warp 1      TMEM allocator + UMMA issuer (one lane)
-//   warps 2..5  epilogue: TMEM -> registers -> global (optionally + R)
+//   warp 1      TMEM allocator + UMMA issuer (one lane), two TMEM accumulators
+//   warps 2..5  epilogue: TMEM -> registers -> global (optionally + R), which
+//               overlaps the UMMAs of the CTA's next tile
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
@@ -48,7 +50,6 @@ struct Tile {
   static constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
   static constexpr int STAGES = SMEM_BUDGET / STAGE_BYTES > 8 ? 8 : SMEM_BUDGET / STAGE_BYTES;
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers, slot, counters*/;
-  static constexpr int TMEM_COLS = BN < 32 ? 32 : BN;
 };
 
 // Byte offset of the 4 KB block that holds MN columns [32j, 32j+32) of an
@@ -73,25 +74,44 @@ __device__ __forceinline__ void load_box(uint32_t dst, const CUtensorMap* map, u
     tma_load_2d(dst, map, bar, x, y);
 }
 
+// Output tile t of this launch: batch, m block, n block (m fastest, so CTAs that
+// run at the same time share B tiles and walk down A), and its K range.
+struct TileInfo {
+  int z, m0, n0, kt_begin, n_k;
+  bool skip;
+};
+
+template <int BN, bool BATCHED>
+__device__ __forceinline__ TileInfo tile_info(int t, int M, int N, int K, const GemmBatch& bt) {
+  const int tm = (M + BM - 1) / BM, tn = (N + BN - 1) / BN;
+  TileInfo ti;
+  ti.z = t / (tm * tn);
+  const int r = t % (tm * tn);
+  ti.m0 = (r % tm) * BM;
+  ti.n0 = (r / tm) * BN;
+  ti.skip = BATCHED && bt.causal == kCausalSkipUpper && ti.n0 > ti.m0 + BM - 1;  // above the diagonal
+  int kt_begin = 0, k_end = K;
+  if (BATCHED && bt.causal == kCausalKBelow) k_end = min(K, ti.m0 + BM);
+  if (BATCHED && bt.causal == kCausalKAbove) kt_begin = ti.m0 / BK;
+  const int kt_end = (k_end + BK - 1) / BK;
+  ti.kt_begin = kt_begin;
+  ti.n_k = kt_end > kt_begin ? kt_end - kt_begin : 0;
+  return ti;
+}
+
+// Persistent: each CTA walks tiles blockIdx.x, blockIdx.x + gridDim.x, ... The
+// TMA/UMMA stage ring runs across tile boundaries, and the accumulator is
+// double-buffered in TMEM, so the epilogue of one tile overlaps the MMAs of the
+// next.
 template <bool A_MN, bool B_MN, int BN, bool BATCHED>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_tf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, float* C,
-                     long long ldc, const float* R, long long ldr, int M, int N, int K, int* err, GemmBatch bt) {
+                     long long ldc, const float* R, long long ldr, int M, int N, int K, int* err, GemmBatch bt,
+                     int total_tiles) {
   using TL = Tile<BN>;
   constexpr int STAGES = TL::STAGES;
   constexpr int STAGE_BYTES = TL::STAGE_BYTES;
-  const int m0 = blockIdx.y * BM;
-  const int n0 = blockIdx.x * BN;
-  if (BATCHED && bt.causal == kCausalSkipUpper && n0 > m0 + BM - 1) return;  // whole tile above the diagonal
-  int kt_begin = 0, k_end = K;
-  if (BATCHED && bt.causal == kCausalKBelow) k_end = min(K, m0 + BM);
-  if (BATCHED && bt.causal == kCausalKAbove) kt_begin = m0 / BK;
-  const int kt_end = (k_end + BK - 1) / BK;
-  const int n_k = kt_end > kt_begin ? kt_end - kt_begin : 0;
-  const int z = blockIdx.z;
-  const int a_zb = BATCHED ? z / bt.a_zdiv : 0, a_zh = BATCHED ? (z % bt.a_zdiv) / bt.a_zgroup : 0;
-  const int b_zb = BATCHED ? z / bt.b_zdiv : 0, b_zh = BATCHED ? (z % bt.b_zdiv) / bt.b_zgroup : 0;
-  if (BATCHED) C += (z / bt.c_zdiv) * bt.c_sb + ((z % bt.c_zdiv) / bt.c_zgroup) * bt.c_sh;
+  constexpr uint32_t ACC_COLS = 2 * BN;  // two accumulators
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
@@ -101,12 +121,14 @@ __global__ void __launch_bounds__(THREADS, 1)
   const uint32_t bar_base = base + STAGES * STAGE_BYTES;
   auto full_bar = [&](int s) { return bar_base + 8u * s; };
   auto empty_bar = [&](int s) { return bar_base + 8u * (STAGES + s); };
-  const uint32_t accum_bar = bar_base + 8u * (2 * STAGES);
-  const uint32_t tmem_slot = bar_base + 8u * (2 * STAGES + 1);
-  uint32_t* tmem_slot_ptr = reinterpret_cast<uint32_t*>(smem + STAGES * STAGE_BYTES + 8 * (2 * STAGES + 1));
+  auto acc_full = [&](int b) { return bar_base + 8u * (2 * STAGES + b); };
+  auto acc_empty = [&](int b) { return bar_base + 8u * (2 * STAGES + 2 + b); };
+  const uint32_t tmem_slot = bar_base + 8u * (2 * STAGES + 4);
+  uint8_t* tail = smem + STAGES * STAGE_BYTES + 8 * (2 * STAGES + 4);
+  uint32_t* tmem_slot_ptr = reinterpret_cast<uint32_t*>(tail);
   // Stages loaded by the producer and consumed by the UMMA issuer; they differ
   // only when a wait timed out, and teardown then drains the difference.
-  int* loads_issued = reinterpret_cast<int*>(smem + STAGES * STAGE_BYTES + 8 * (2 * STAGES + 2));
+  int* loads_issued = reinterpret_cast<int*>(tail + 8);
   int* loads_consumed = loads_issued + 1;
 
   const int warp = threadIdx.x / 32;
@@ -119,114 +141,155 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(full_bar(s), 1);
       mbar_init(empty_bar(s), 1);
     }
-    mbar_init(accum_bar, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(acc_full(b), 1);
+      mbar_init(acc_empty(b), 4);  // one arrival per epilogue warp
+    }
     *loads_issued = 0;
     *loads_consumed = 0;
     fence_barrier_init();
     fence_proxy_async_smem();
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, TL::TMEM_COLS);
+    tmem_alloc(tmem_slot, ACC_COLS);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem_acc = *tmem_slot_ptr;
+  const uint32_t tmem_base = *tmem_slot_ptr;
 
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- TMA producer
-      for (int i = 0; i < n_k; ++i) {
-        const int s = i % STAGES;
-        const int round = i / STAGES;
-        if (round > 0 && !mbar_wait(empty_bar(s), (round - 1) & 1, err, kErrWaitEmpty)) break;
-        const uint32_t sa = base + s * STAGE_BYTES;
-        const uint32_t sb = sa + A_STAGE_BYTES;
-        mbar_arrive_expect_tx(full_bar(s), STAGE_BYTES);
-        const int k0 = (kt_begin + i) * BK;
-        if (!A_MN) {
-          load_box<BATCHED>(sa, &tmA, full_bar(s), k0, m0, a_zh, a_zb);
-        } else {
+      int it = 0;  // stage-ring position, across tiles
+      bool ok = true;
+      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+        const TileInfo ti = tile_info<BN, BATCHED>(t, M, N, K, bt);
+        if (ti.skip) continue;
+        const int a_zb = BATCHED ? ti.z / bt.a_zdiv : 0, a_zh = BATCHED ? (ti.z % bt.a_zdiv) / bt.a_zgroup : 0;
+        const int b_zb = BATCHED ? ti.z / bt.b_zdiv : 0, b_zh = BATCHED ? (ti.z % bt.b_zdiv) / bt.b_zgroup : 0;
+        for (int i = 0; i < ti.n_k; ++i, ++it) {
+          const int s = it % STAGES;
+          const int round = it / STAGES;
+          if (round > 0 && !mbar_wait(empty_bar(s), (round - 1) & 1, err, kErrWaitEmpty)) {
+            ok = false;
+            break;
+          }
+          const uint32_t sa = base + s * STAGE_BYTES;
+          const uint32_t sb = sa + A_STAGE_BYTES;
+          mbar_arrive_expect_tx(full_bar(s), STAGE_BYTES);
+          const int k0 = (ti.kt_begin + i) * BK;
+          if (!A_MN) {
+            load_box<BATCHED>(sa, &tmA, full_bar(s), k0, ti.m0, a_zh, a_zb);
+          } else {
 #pragma unroll
-          for (int j = 0; j < BM / 32; ++j)
-            load_box<BATCHED>(sa + j * MN_BLOCK_BYTES, &tmA, full_bar(s), m0 + 32 * j, k0, a_zh, a_zb);
-        }
-        if (!B_MN) {
-          load_box<BATCHED>(sb, &tmB, full_bar(s), k0, n0, b_zh, b_zb);
-        } else {
+            for (int j = 0; j < BM / 32; ++j)
+              load_box<BATCHED>(sa + j * MN_BLOCK_BYTES, &tmA, full_bar(s), ti.m0 + 32 * j, k0, a_zh, a_zb);
+          }
+          if (!B_MN) {
+            load_box<BATCHED>(sb, &tmB, full_bar(s), k0, ti.n0, b_zh, b_zb);
+          } else {
 #pragma unroll
-          for (int j = 0; j < BN / 32; ++j)
-            load_box<BATCHED>(sb + j * MN_BLOCK_BYTES, &tmB, full_bar(s), n0 + 32 * j, k0, b_zh, b_zb);
+            for (int j = 0; j < BN / 32; ++j)
+              load_box<BATCHED>(sb + j * MN_BLOCK_BYTES, &tmB, full_bar(s), ti.n0 + 32 * j, k0, b_zh, b_zb);
+          }
+          *loads_issued = it + 1;
         }
-        *loads_issued = i + 1;
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- UMMA issuer
       constexpr uint32_t idesc = idesc_tf32(BM, BN, A_MN, B_MN);
-      for (int i = 0; i < n_k; ++i) {
-        const int s = i % STAGES;
-        const int round = i / STAGES;
-        if (!mbar_wait(full_bar(s), round & 1, err, kErrWaitFull)) break;
+      int it = 0, j = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+        const TileInfo ti = tile_info<BN, BATCHED>(t, M, N, K, bt);
+        if (ti.skip) continue;
+        const int buf = j & 1;
+        // the epilogue must have drained this accumulator (tile j - 2)
+        if (j >= 2 && !mbar_wait(acc_empty(buf), ((j >> 1) - 1) & 1, err, kErrWaitAccum)) break;
         tc_fence_after();
-        *loads_consumed = i + 1;
-        const uint32_t sa = base + s * STAGE_BYTES;
-        const uint32_t sb = sa + A_STAGE_BYTES;
+        const uint32_t acc = tmem_base + buf * BN;
+        for (int i = 0; i < ti.n_k; ++i, ++it) {
+          const int s = it % STAGES;
+          const int round = it / STAGES;
+          if (!mbar_wait(full_bar(s), round & 1, err, kErrWaitFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          *loads_consumed = it + 1;
+          const uint32_t sa = base + s * STAGE_BYTES;
+          const uint32_t sb = sa + A_STAGE_BYTES;
 #pragma unroll
-        for (int k = 0; k < BK / 8; ++k) {
-          // K-major: step 8 tf32 = 32 bytes along the swizzled row.
-          // MN-major (32-byte swizzle atoms of 4 K-rows): step 8 K-rows = 1024
-          // bytes; LBO = next 32-wide MN block, SBO = next group of 4 K-rows.
-          const uint64_t adesc = A_MN ? smem_desc(sa + k * 1024, MN_BLOCK_BYTES, 512, kLayoutSw128Base32)
-                                      : smem_desc(sa + k * 32, 16, 1024, kLayoutSw128);
-          const uint64_t bdesc = B_MN ? smem_desc(sb + k * 1024, MN_BLOCK_BYTES, 512, kLayoutSw128Base32)
-                                      : smem_desc(sb + k * 32, 16, 1024, kLayoutSw128);
-          umma_tf32(tmem_acc, adesc, bdesc, idesc, (i | k) != 0 ? 1u : 0u);
+          for (int k = 0; k < BK / 8; ++k) {
+            // K-major: step 8 tf32 = 32 bytes along the swizzled row.
+            // MN-major (32-byte swizzle atoms of 4 K-rows): step 8 K-rows = 1024
+            // bytes; LBO = next 32-wide MN block, SBO = next group of 4 K-rows.
+            const uint64_t adesc = A_MN ? smem_desc(sa + k * 1024, MN_BLOCK_BYTES, 512, kLayoutSw128Base32)
+                                        : smem_desc(sa + k * 32, 16, 1024, kLayoutSw128);
+            const uint64_t bdesc = B_MN ? smem_desc(sb + k * 1024, MN_BLOCK_BYTES, 512, kLayoutSw128Base32)
+                                        : smem_desc(sb + k * 32, 16, 1024, kLayoutSw128);
+            umma_tf32(acc, adesc, bdesc, idesc, (i | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(empty_bar(s));
         }
-        umma_commit(empty_bar(s));
+        umma_commit(acc_full(buf));  // also when the K range is empty: the epilogue writes R or 0
+        ++j;
       }
-      umma_commit(accum_bar);
     }
   } else {
     // ---------------- epilogue: warps 2..5 cover TMEM lane quarters (warp % 4)
     const int quarter = warp & 3;
-    const int row = m0 + quarter * 32 + lane;
-    const bool ok = mbar_wait(accum_bar, 0, err, kErrWaitAccum);
-    tc_fence_after();
-    if (ok && n_k > 0) {
+    int j = 0;
+    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
+      const TileInfo ti = tile_info<BN, BATCHED>(t, M, N, K, bt);
+      if (ti.skip) continue;
+      const int buf = j & 1;
+      if (!mbar_wait(acc_full(buf), (j >> 1) & 1, err, kErrWaitAccum)) break;
+      tc_fence_after();
+      float* Ct = C;
+      if (BATCHED) Ct += (ti.z / bt.c_zdiv) * bt.c_sb + ((ti.z % bt.c_zdiv) / bt.c_zgroup) * bt.c_sh;
+      const int row = ti.m0 + quarter * 32 + lane;
+      if (ti.n_k > 0) {
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem_acc + (static_cast<uint32_t>(quarter * 32) << 16) + c * 32, r);
-        const int col0 = n0 + c * 32;
-        if (row < M && col0 < N) {
-          float* crow = C + static_cast<long long>(row) * ldc;
-          const float* rrow = R ? R + static_cast<long long>(row) * ldr : nullptr;
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tmem_base + buf * BN + (static_cast<uint32_t>(quarter * 32) << 16) + c * 32, r);
+          const int col0 = ti.n0 + c * 32;
+          if (row < M && col0 < N) {
+            float* crow = Ct + static_cast<long long>(row) * ldc;
+            const float* rrow = R ? R + static_cast<long long>(row) * ldr : nullptr;
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const int col = col0 + 4 * j;
-            float4 v = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
-                                   __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
-            if (col + 3 < N) {
-              if (rrow) {
-                const float4 a = *reinterpret_cast<const float4*>(rrow + col);
-                v.x += a.x; v.y += a.y; v.z += a.z; v.w += a.w;
+            for (int q = 0; q < 8; ++q) {
+              const int col = col0 + 4 * q;
+              float4 v = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
+                                     __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]));
+              if (col + 3 < N) {
+                if (rrow) {
+                  const float4 a = *reinterpret_cast<const float4*>(rrow + col);
+                  v.x += a.x; v.y += a.y; v.z += a.z; v.w += a.w;
+                }
+                *reinterpret_cast<float4*>(crow + col) = v;
+              } else {
+                const float vv[4] = {v.x, v.y, v.z, v.w};
+                for (int e = 0; e < 4 && col + e < N; ++e) crow[col + e] = vv[e] + (rrow ? rrow[col + e] : 0.0f);
               }
-              *reinterpret_cast<float4*>(crow + col) = v;
-            } else {
-              const float vv[4] = {v.x, v.y, v.z, v.w};
-              for (int e = 0; e < 4 && col + e < N; ++e)
-                crow[col + e] = vv[e] + (rrow ? rrow[col + e] : 0.0f);
             }
           }
         }
+      } else if (row < M) {
+        // Empty K range: the product is zero, C = R (or 0).
+        for (int col = ti.n0; col < ti.n0 + BN && col < N; ++col)
+          Ct[static_cast<long long>(row) * ldc + col] = R ? R[static_cast<long long>(row) * ldr + col] : 0.0f;
       }
-    } else if (ok && row < M) {
-      // Empty K range: the product is zero, C = R (or 0).
-      for (int col = n0; col < n0 + BN && col < N; ++col)
-        C[static_cast<long long>(row) * ldc + col] = R ? R[static_cast<long long>(row) * ldr + col] : 0.0f;
+      // this warp's reads of the accumulator are complete (tcgen05.wait::ld)
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acc_empty(buf));
+      ++j;
     }
   }
 
@@ -240,11 +303,14 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_acc, TL::TMEM_COLS);
+    tmem_dealloc(tmem_base, ACC_COLS);
   }
   __syncthreads();
 }
 
+}  // namespace
+
+namespace {
 
 // ------------------------------------------------------------------ host side
 
@@ -299,9 +365,21 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, float* C, long long ld
             int M, int N, int K, int batch, const GemmBatch& bt, int* err, cudaStream_t stream) {
   using TL = Tile<BN>;
   auto kern = gemm_tf32_kernel<A_MN, B_MN, BN, BATCHED>;
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TL::SMEM_BYTES);
-  dim3 grid((N + BN - 1) / BN, (M + BM - 1) / BM, batch);
-  kern<<<grid, THREADS, TL::SMEM_BYTES, stream>>>(ta, tb, C, ldc, R, ldr, M, N, K, err, bt);
+  static thread_local int configured_device = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_device != dev) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TL::SMEM_BYTES);
+    configured_device = dev;
+  }
+  const long long tiles = static_cast<long long>((M + BM - 1) / BM) * ((N + BN - 1) / BN) * batch;
+  static thread_local int sms = 0, sms_device = -1;
+  if (sms_device != dev) {
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    sms_device = dev;
+  }
+  const int grid = static_cast<int>(tiles < sms ? tiles : sms);
+  kern<<<grid, THREADS, TL::SMEM_BYTES, stream>>>(ta, tb, C, ldc, R, ldr, M, N, K, err, bt, static_cast<int>(tiles));
 }
 
 template <int BN, bool BATCHED>
