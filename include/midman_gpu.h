@@ -80,6 +80,31 @@ MM_GPU_EXPORT int32_t mm_gpu_attention_backward(int32_t batch, int32_t seq, int3
                                                 int64_t ldk, float *dq, float *dk, float *dv, int32_t precision,
                                                 void *stream);
 
+/* Allocation-free variant of mm_gpu_attention_forward with precision
+ * MM_GPU_TF32 (the tensor-core path; head_dim 32, 64 or 128). No counterpart in
+ * the reference, which has no device memory to manage.
+ *
+ * For callers that cannot let the library call cudaMalloc: a process whose
+ * device memory is fully reserved by its own pool (PyTorch's caching
+ * allocator, a serving arena) would see the allocation fail, and cudaMalloc /
+ * cudaFree can synchronize the device under a caller that overlaps streams.
+ * This call allocates nothing: its score scratch is a fixed 16 MiB array inside
+ * the library (batch * n_heads * seq * round_up(seq, 4) <= 4194304 floats;
+ * larger sizes return MM_GPU_ERR_SHAPE), which every GPU that loads the library
+ * holds until the process exits.
+ *   - The first call on a device looks up that array's device address (once
+ *     per device, with the device current); make it before any stream capture.
+ *   - All calls share the array: calls whose kernels overlap on the GPU (on
+ *     different streams, or from several threads) race on it. Serialize them.
+ *   - device_status: device pointer to one int32 that the caller zeroes; the
+ *     kernels leave it alone unless a pipeline wait timed out, when it receives
+ *     that error code (the codes mm_gpu_device_status reports).
+ * Same operands, layouts and results as mm_gpu_attention_forward. */
+MM_GPU_EXPORT int32_t mm_gpu_attention_forward_noalloc(int32_t batch, int32_t seq, int32_t n_heads,
+                                                       int32_t n_kv_heads, int32_t head_dim, const float *q,
+                                                       const float *k, const float *v, int64_t ldq, int64_t ldk,
+                                                       float *o, float *lse, int32_t *device_status, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -37,6 +37,9 @@ bool attention_tc_supported(const AttnShape& s);
 long long attention_scores_ld(int T);
 void attention_forward_tc(const AttnShape& s, const float* q, const float* k, const float* v, float* o, float* lse,
                           float* S, cudaStream_t stream);
+// The same with the pipeline-timeout flag given by the caller (no library state).
+void attention_forward_tc(const AttnShape& s, const float* q, const float* k, const float* v, float* o, float* lse,
+                          float* S, int* d_err, cudaStream_t stream);
 void attention_backward_tc(const AttnShape& s, const float* q, const float* k, const float* v, const float* o,
                            const float* lse, const float* dout, long long lddo, float* dq, float* dk, float* dv,
                            float* delta, float* S, float* dP, float* tmp, cudaStream_t stream);

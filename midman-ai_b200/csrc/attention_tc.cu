@@ -138,7 +138,11 @@ bool attention_tc_supported(const AttnShape& s) {
 
 void attention_forward_tc(const AttnShape& s, const float* q, const float* k, const float* v, float* o, float* lse,
                           float* S, cudaStream_t stream) {
-  DeviceContext& ctx = device_context();
+  attention_forward_tc(s, q, k, v, o, lse, S, device_context().d_err, stream);
+}
+
+void attention_forward_tc(const AttnShape& s, const float* q, const float* k, const float* v, float* o, float* lse,
+                          float* S, int* d_err, cudaStream_t stream) {
   const int G = s.H / s.Hkv;
   const int BH = s.B * s.H;
   const long long ldS = attention_scores_ld(s.T);
@@ -148,7 +152,7 @@ void attention_forward_tc(const AttnShape& s, const float* q, const float* k, co
   bs.c_sh = static_cast<long long>(s.T) * ldS;
   bs.causal = kCausalSkipUpper;
   check_gemm(gemm_tf32_batched(BH, s.T, s.T, s.hd, heads_view(q, false, s, s.ldq, s.H, 1),
-                               heads_view(k, false, s, s.ldk, s.Hkv, G), S, ldS, bs, 256, ctx.d_err, stream),
+                               heads_view(k, false, s, s.ldk, s.Hkv, G), S, ldS, bs, 256, d_err, stream),
              "attention S = QK^T");
   const long long rows = static_cast<long long>(BH) * s.T;
   softmax_rows_kernel<<<blocks_for(rows * 32), 256, 0, stream>>>(S, ldS, s.T, rows, s.scale, lse);
@@ -160,7 +164,7 @@ void attention_forward_tc(const AttnShape& s, const float* q, const float* k, co
   bo.c_sh = s.hd;
   bo.causal = kCausalKBelow;
   check_gemm(gemm_tf32_batched(BH, s.T, s.hd, s.T, scores_view(S, false, s, ldS),
-                               heads_view(v, true, s, s.ldv, s.Hkv, G), o, s.ldo, bo, tile_for(s.hd), ctx.d_err,
+                               heads_view(v, true, s, s.ldv, s.Hkv, G), o, s.ldo, bo, tile_for(s.hd), d_err,
                                stream),
              "attention O = PV");
 }

@@ -3,7 +3,10 @@
 
 #include <cmath>
 #include <exception>
+#include <mutex>
+#include <stdexcept>
 #include <string>
+#include <vector>
 
 #include "../../include/midman_gpu.h"
 #include "attention.h"
@@ -118,3 +121,69 @@ int32_t mm_gpu_attention_backward(int32_t batch, int32_t seq, int32_t n_heads, i
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------ allocation-free attention forward
+//
+// Some callers cannot let this library call cudaMalloc: a process whose device
+// memory is already fully reserved by its own pool (PyTorch's caching
+// allocator, a serving engine's KV-cache arena) would see the library's
+// allocation fail or push it out of memory, and cudaMalloc/cudaFree can
+// synchronize the whole device, which a caller overlapping work on several
+// streams cannot afford. mm_gpu_attention_forward's tensor-core path needs a
+// score buffer, which it takes from a grow-only arena it allocates on demand;
+// this variant takes it from a fixed array compiled into the library instead.
+namespace {
+
+// Score scratch of the allocation-free forward: batch * n_heads * seq * ld
+// floats (ld = seq rounded up to a multiple of 4), at most 16 MiB. Every GPU
+// that loads the library holds this array until the process exits. Every call
+// shares it and it keeps the last call's contents; nothing in it has to start
+// at zero, because each element a call reads was written earlier in the same
+// call (score tiles above the diagonal are never read).
+constexpr size_t kStaticScoreFloats = size_t(1) << 22;
+static __device__ __align__(256) float g_static_scores[kStaticScoreFloats];
+
+// Device address of g_static_scores per device. In host code the array's name
+// is only a host-side stand-in, so the address is looked up once per device
+// with that device current.
+std::mutex g_static_mu;
+std::vector<float*> g_static_ptr;
+
+float* static_scores(int device) {
+  std::lock_guard<std::mutex> lock(g_static_mu);
+  if (g_static_ptr.size() <= static_cast<size_t>(device)) g_static_ptr.resize(device + 1, nullptr);
+  if (!g_static_ptr[device]) {
+    float* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_static_scores);
+    if (e != cudaSuccess) throw std::runtime_error(std::string("cudaGetSymbolAddress(score scratch): ") +
+                                                   cudaGetErrorString(e));
+    g_static_ptr[device] = p;
+  }
+  return g_static_ptr[device];
+}
+
+}  // namespace
+
+extern "C" int32_t mm_gpu_attention_forward_noalloc(int32_t batch, int32_t seq, int32_t n_heads, int32_t n_kv_heads,
+                                                    int32_t head_dim, const float* q, const float* k, const float* v,
+                                                    int64_t ldq, int64_t ldk, float* o, float* lse,
+                                                    int32_t* device_status, void* stream) {
+  return guarded([&]() -> int32_t {
+    mm::AttnShape s;
+    if (int32_t rc = attention_shape(batch, seq, n_heads, n_kv_heads, head_dim, ldq, ldk, &s)) return rc;
+    if (!q || !k || !v || !o || !lse || !device_status)
+      return fail(MM_GPU_ERR_ARGUMENT, "attention (no-alloc): null pointer");
+    if (!mm::attention_tc_supported(s))
+      return fail(MM_GPU_ERR_SHAPE, "attention (no-alloc): head_dim must be 32, 64 or 128");
+    const size_t need = static_cast<size_t>(batch) * n_heads * seq * mm::attention_scores_ld(seq);
+    if (need > kStaticScoreFloats)
+      return fail(MM_GPU_ERR_SHAPE, "attention (no-alloc): batch * n_heads * seq * round4(seq) = " +
+                                        std::to_string(need) + " floats exceeds the fixed score scratch of " +
+                                        std::to_string(kStaticScoreFloats) + " floats (16 MiB)");
+    int device = 0;
+    const cudaError_t e = cudaGetDevice(&device);
+    if (e != cudaSuccess) return fail(MM_GPU_ERR_DEVICE, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
+    mm::attention_forward_tc(s, q, k, v, o, lse, static_scores(device), device_status, as_stream(stream));
+    return MM_GPU_OK;
+  });
+}

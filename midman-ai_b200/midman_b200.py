@@ -16,7 +16,7 @@ LIB_PATH = HERE / "lib" / "libmidman_gpu.so"
 # Every symbol the public headers declare, grouped by header.
 GPU_SYMBOLS = [
     "mm_gpu_last_error", "mm_gpu_device_status", "mm_gpu_gemm", "mm_gpu_attention_forward",
-    "mm_gpu_attention_backward",
+    "mm_gpu_attention_backward", "mm_gpu_attention_forward_noalloc",
 ]
 API_SYMBOLS = [
     "midman_abi_version", "midman_alloc", "midman_free", "midman_text_ptr", "midman_text_len",
@@ -57,6 +57,8 @@ def load(path: str | os.PathLike | None = None) -> C.CDLL:
     _sig(lib, "mm_gpu_attention_forward", i32, i32, i32, i32, i32, i32, vp, vp, vp, i64, i64, vp, vp, i32, vp)
     _sig(lib, "mm_gpu_attention_backward", i32, i32, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp, i64, i64, vp, vp,
          vp, i32, vp)
+    _sig(lib, "mm_gpu_attention_forward_noalloc", i32, i32, i32, i32, i32, i32, vp, vp, vp, i64, i64, vp, vp, vp,
+         vp)
     u32, u8p, dp, i32p = C.c_uint32, C.POINTER(C.c_uint8), C.POINTER(C.c_double), C.POINTER(C.c_int32)
     _sig(lib, "midman_abi_version", u32)
     _sig(lib, "midman_alloc", u8p, u32)
@@ -140,6 +142,14 @@ def attention_backward(q, k, v, o, lse, dout, dq, dk, dv, *, batch, seq, n_heads
     return check(load().mm_gpu_attention_backward(batch, seq, n_heads, n_kv_heads, head_dim, _ptr(q), _ptr(k),
                                                   _ptr(v), _ptr(o), _ptr(lse), _ptr(dout), ldq, ldk, _ptr(dq),
                                                   _ptr(dk), _ptr(dv), precision, _stream(stream)))
+
+
+def attention_forward_noalloc(q, k, v, o, lse, status, *, batch, seq, n_heads, n_kv_heads, head_dim, ldq, ldk,
+                              stream=None):
+    """TF32 attention forward with the library's fixed score scratch (no device allocation)."""
+    return check(load().mm_gpu_attention_forward_noalloc(batch, seq, n_heads, n_kv_heads, head_dim, _ptr(q), _ptr(k),
+                                                         _ptr(v), ldq, ldk, _ptr(o), _ptr(lse), _ptr(status),
+                                                         _stream(stream)))
 
 
 def device_status(stream=None):
