@@ -175,15 +175,24 @@ def run_kernels(args):
             y, dx, dw = torch.empty(M, N, device="cuda"), torch.empty(M, K, device="cuda"), torch.empty(K, N,
                                                                                                         device="cuda")
 
-            def step():
+            def fwd(x=x, w=w, y=y, K=K, N=N):  # Y = X W (bind this shape's tensors)
                 mm.gemm(x, w, y, m=M, n=N, k=K, lda=K, ldb=N, ldc=N, a_mn_major=False, b_mn_major=True,
                         precision=precision)
+
+            def bwd_x(dy=dy, w=w, dx=dx, K=K, N=N):  # dX = dY W^T
                 mm.gemm(dy, w, dx, m=M, n=K, k=N, lda=N, ldb=N, ldc=K, a_mn_major=False, b_mn_major=False,
                         precision=precision)
+
+            def bwd_w(x=x, dy=dy, dw=dw, K=K, N=N):  # dW = X^T dY
                 mm.gemm(x, dy, dw, m=K, n=N, k=M, lda=K, ldb=N, ldc=N, a_mn_major=True, b_mn_major=True,
                         precision=precision)
+
+            def step(parts=(fwd, bwd_x, bwd_w)):
+                for p in parts:
+                    p()
             flops = 3 * 2 * M * K * N
-            results.append(({"K": K, "N": N, "M": M}, flops, step))
+            results.append(({"K": K, "N": N, "M": M}, flops, step,
+                            {"Y=XW": fwd, "dX=dYW^T": bwd_x, "dW=X^TdY": bwd_w}))
     else:
         B, H, hd, T = 8, 16, 64, 1024
         q = torch.randn(B, T, H, hd, device="cuda", generator=g)
@@ -198,23 +207,29 @@ def run_kernels(args):
             mm.attention_forward(q, k, v, o, lse, **kw)
             mm.attention_backward(q, k, v, o, lse, do, dq, dk, dv, **kw)
         flops = 6 * 2 * B * H * (T * T // 2) * hd  # six causal T x T x hd products, no recompute
-        results.append(({"B": B, "H": H, "hd": hd, "T": T}, flops, step))
+        results.append(({"B": B, "H": H, "hd": hd, "T": T}, flops, step, {}))
     tf32 = tf32_peak_tflops(torch)
-    out = []
-    for shape, flops, step in results:
+    def timed(fn):
         for _ in range(max(3, args.warmup)):
-            step()
+            fn()
         torch.cuda.synchronize()
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
         for _ in range(args.steps):
-            step()
+            fn()
         e.record()
         e.synchronize()
         mm.device_status()
-        ms = s.elapsed_time(e) / args.steps
-        out.append({**shape, "ms": ms, "tflops": flops / (ms * 1e-3) / 1e12, "frac_of_cublas_tf32": flops / (ms * 1e-3)
-                    / 1e12 / tf32})
+        return s.elapsed_time(e) / args.steps
+
+    out = []
+    for shape, flops, step, parts in results:
+        ms = timed(step)
+        row = {**shape, "ms": ms, "tflops": flops / (ms * 1e-3) / 1e12, "frac_of_cublas_tf32": flops / (ms * 1e-3)
+               / 1e12 / tf32}
+        if parts:  # each product alone (a third of the step's FLOPs)
+            row["products"] = {name: round(flops / 3 / (timed(fn) * 1e-3) / 1e12, 1) for name, fn in parts.items()}
+        out.append(row)
     line = {"metric": "fwd+bwd TFLOP/s" if args.config == "linear" else "attention fwd+bwd TFLOP/s",
             "value": statistics.mean(r["tflops"] for r in out), "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
             "warmup": args.warmup, "higher_is_better": True, "dtype": args.precision, "data": "synthetic N(0,1)",

@@ -65,6 +65,15 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int32_t x, int32_t y,
+                                            int32_t z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
+
 template <bool BATCHED>
 __device__ __forceinline__ void load_box(uint32_t dst, const CUtensorMap* map, uint32_t bar, int32_t x, int32_t y,
                                          int32_t zh, int32_t zb) {
@@ -107,7 +116,7 @@ template <bool A_MN, bool B_MN, int BN, bool BATCHED>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_tf32_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, float* C,
                      long long ldc, const float* R, long long ldr, int M, int N, int K, int* err, GemmBatch bt,
-                     int total_tiles) {
+                     int total_tiles, int mn3d) {
   using TL = Tile<BN>;
   constexpr int STAGES = TL::STAGES;
   constexpr int STAGE_BYTES = TL::STAGE_BYTES;
@@ -182,6 +191,8 @@ __global__ void __launch_bounds__(THREADS, 1)
           const int k0 = (ti.kt_begin + i) * BK;
           if (!A_MN) {
             load_box<BATCHED>(sa, &tmA, full_bar(s), k0, ti.m0, a_zh, a_zb);
+          } else if (!BATCHED && (mn3d & 1)) {
+            tma_load_3d(sa, &tmA, full_bar(s), 0, k0, ti.m0 / 32);
           } else {
 #pragma unroll
             for (int j = 0; j < BM / 32; ++j)
@@ -189,6 +200,8 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
           if (!B_MN) {
             load_box<BATCHED>(sb, &tmB, full_bar(s), k0, ti.n0, b_zh, b_zb);
+          } else if (!BATCHED && (mn3d & 2)) {
+            tma_load_3d(sb, &tmB, full_bar(s), 0, k0, ti.n0 / 32);
           } else {
 #pragma unroll
             for (int j = 0; j < BN / 32; ++j)
@@ -360,9 +373,19 @@ int make_map2d(CUtensorMap* map, const float* ptr, long long inner, long long ou
   return encode(map, ptr, 2, dims, strides, box, mn_major);
 }
 
+// MN-major operand (`mn` contiguous elements per K-row, rows `ld` apart) as a
+// 3-D view (32 elements, K-row, 32-wide block): one box of {32, BK, box_mn / 32}
+// lands as box_mn / 32 consecutive 4 KB blocks, the UMMA MN-major layout.
+// Needs mn % 32 == 0 so that no block reads past a row.
+int make_map_mn3d(CUtensorMap* map, const float* ptr, long long mn, long long k, long long ld, int box_mn) {
+  const long long dims[3] = {32, k, mn / 32}, strides[2] = {ld, 32};
+  const int box[3] = {32, BK, box_mn / 32};
+  return encode(map, ptr, 3, dims, strides, box, true);
+}
+
 template <bool A_MN, bool B_MN, int BN, bool BATCHED>
 void launch(const CUtensorMap& ta, const CUtensorMap& tb, float* C, long long ldc, const float* R, long long ldr,
-            int M, int N, int K, int batch, const GemmBatch& bt, int* err, cudaStream_t stream) {
+            int M, int N, int K, int batch, const GemmBatch& bt, int* err, cudaStream_t stream, int mn3d) {
   using TL = Tile<BN>;
   auto kern = gemm_tf32_kernel<A_MN, B_MN, BN, BATCHED>;
   static thread_local int configured_device = -1;
@@ -379,17 +402,17 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, float* C, long long ld
     sms_device = dev;
   }
   const int grid = static_cast<int>(tiles < sms ? tiles : sms);
-  kern<<<grid, THREADS, TL::SMEM_BYTES, stream>>>(ta, tb, C, ldc, R, ldr, M, N, K, err, bt, static_cast<int>(tiles));
+  kern<<<grid, THREADS, TL::SMEM_BYTES, stream>>>(ta, tb, C, ldc, R, ldr, M, N, K, err, bt, static_cast<int>(tiles), mn3d);
 }
 
 template <int BN, bool BATCHED>
 void launch_majors(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, float* C, long long ldc,
                    const float* R, long long ldr, int M, int N, int K, int batch, const GemmBatch& bt, int* err,
-                   cudaStream_t s) {
-  if (!a_mn && !b_mn) launch<false, false, BN, BATCHED>(ta, tb, C, ldc, R, ldr, M, N, K, batch, bt, err, s);
-  else if (!a_mn && b_mn) launch<false, true, BN, BATCHED>(ta, tb, C, ldc, R, ldr, M, N, K, batch, bt, err, s);
-  else if (a_mn && !b_mn) launch<true, false, BN, BATCHED>(ta, tb, C, ldc, R, ldr, M, N, K, batch, bt, err, s);
-  else launch<true, true, BN, BATCHED>(ta, tb, C, ldc, R, ldr, M, N, K, batch, bt, err, s);
+                   cudaStream_t s, int mn3d = 0) {
+  if (!a_mn && !b_mn) launch<false, false, BN, BATCHED>(ta, tb, C, ldc, R, ldr, M, N, K, batch, bt, err, s, mn3d);
+  else if (!a_mn && b_mn) launch<false, true, BN, BATCHED>(ta, tb, C, ldc, R, ldr, M, N, K, batch, bt, err, s, mn3d);
+  else if (a_mn && !b_mn) launch<true, false, BN, BATCHED>(ta, tb, C, ldc, R, ldr, M, N, K, batch, bt, err, s, mn3d);
+  else launch<true, true, BN, BATCHED>(ta, tb, C, ldc, R, ldr, M, N, K, batch, bt, err, s, mn3d);
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -416,20 +439,27 @@ int gemm_tf32(int M, int N, int K, GemmOperand A, GemmOperand B, float* C, long 
   // Narrow outputs waste less of a 256-wide tile with a 128-wide one.
   const int bn = N <= 128 ? 128 : 256;
   CUtensorMap ta{}, tb{};
+  int mn3d = 0;
   if (K > 0) {
     if ((A.ld & 3) || (B.ld & 3) || !aligned16(A.ptr) || !aligned16(B.ptr)) return kGemmMisaligned;
-    int rc = A.mn_major ? make_map2d(&ta, A.ptr, M, K, A.ld, 32, BK, true)
-                        : make_map2d(&ta, A.ptr, K, M, A.ld, BK, BM, false);
+    // MN-major operands whose MN extent is a multiple of 32 load a whole stage in
+    // one 3-D box; otherwise one 2-D box per 32-wide block (zero fill past MN).
+    const bool a3 = A.mn_major && M % 32 == 0, b3 = B.mn_major && N % 32 == 0;
+    int rc = a3 ? make_map_mn3d(&ta, A.ptr, M, K, A.ld, BM)
+             : A.mn_major ? make_map2d(&ta, A.ptr, M, K, A.ld, 32, BK, true)
+                          : make_map2d(&ta, A.ptr, K, M, A.ld, BK, BM, false);
     if (rc) return kGemmTensorMap;
-    rc = B.mn_major ? make_map2d(&tb, B.ptr, N, K, B.ld, 32, BK, true)
-                    : make_map2d(&tb, B.ptr, K, N, B.ld, BK, bn, false);
+    rc = b3 ? make_map_mn3d(&tb, B.ptr, N, K, B.ld, bn)
+         : B.mn_major ? make_map2d(&tb, B.ptr, N, K, B.ld, 32, BK, true)
+                      : make_map2d(&tb, B.ptr, K, N, B.ld, BK, bn, false);
     if (rc) return kGemmTensorMap;
+    mn3d = (a3 ? 1 : 0) | (b3 ? 2 : 0);
   }
   const GemmBatch bt{};
   if (bn == 128)
-    launch_majors<128, false>(A.mn_major, B.mn_major, ta, tb, C, ldc, R, ldr, M, N, K, 1, bt, d_err, stream);
+    launch_majors<128, false>(A.mn_major, B.mn_major, ta, tb, C, ldc, R, ldr, M, N, K, 1, bt, d_err, stream, mn3d);
   else
-    launch_majors<256, false>(A.mn_major, B.mn_major, ta, tb, C, ldc, R, ldr, M, N, K, 1, bt, d_err, stream);
+    launch_majors<256, false>(A.mn_major, B.mn_major, ta, tb, C, ldc, R, ldr, M, N, K, 1, bt, d_err, stream, mn3d);
   return cudaGetLastError() == cudaSuccess ? 0 : kGemmLaunch;
 }
 
