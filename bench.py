@@ -192,7 +192,8 @@ def run_kernels(args):
                     p()
             flops = 3 * 2 * M * K * N
             results.append(({"K": K, "N": N, "M": M}, flops, step,
-                            {"Y=XW": fwd, "dX=dYW^T": bwd_x, "dW=X^TdY": bwd_w}))
+                            {"Y=XW": (fwd, flops / 3), "dX=dYW^T": (bwd_x, flops / 3),
+                             "dW=X^TdY": (bwd_w, flops / 3)}))
     else:
         B, H, hd, T = 8, 16, 64, 1024
         q = torch.randn(B, T, H, hd, device="cuda", generator=g)
@@ -203,11 +204,18 @@ def run_kernels(args):
         dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
         kw = dict(batch=B, seq=T, n_heads=H, n_kv_heads=H, head_dim=hd, ldq=H * hd, ldk=H * hd, precision=precision)
 
-        def step():
+        def fwd():
             mm.attention_forward(q, k, v, o, lse, **kw)
+
+        def bwd():
             mm.attention_backward(q, k, v, o, lse, do, dq, dk, dv, **kw)
+
+        def step():
+            fwd()
+            bwd()
         flops = 6 * 2 * B * H * (T * T // 2) * hd  # six causal T x T x hd products, no recompute
-        results.append(({"B": B, "H": H, "hd": hd, "T": T}, flops, step, {}))
+        results.append(({"B": B, "H": H, "hd": hd, "T": T}, flops, step,
+                        {"forward": (fwd, flops / 3), "backward": (bwd, flops * 2 / 3)}))
     tf32 = tf32_peak_tflops(torch)
     def timed(fn):
         for _ in range(max(3, args.warmup)):
@@ -227,8 +235,8 @@ def run_kernels(args):
         ms = timed(step)
         row = {**shape, "ms": ms, "tflops": flops / (ms * 1e-3) / 1e12, "frac_of_cublas_tf32": flops / (ms * 1e-3)
                / 1e12 / tf32}
-        if parts:  # each product alone (a third of the step's FLOPs)
-            row["products"] = {name: round(flops / 3 / (timed(fn) * 1e-3) / 1e12, 1) for name, fn in parts.items()}
+        if parts:  # TFLOP/s of each part alone
+            row["parts"] = {name: round(f / (timed(fn) * 1e-3) / 1e12, 1) for name, (fn, f) in parts.items()}
         out.append(row)
     line = {"metric": "fwd+bwd TFLOP/s" if args.config == "linear" else "attention fwd+bwd TFLOP/s",
             "value": statistics.mean(r["tflops"] for r in out), "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,

@@ -43,6 +43,11 @@ void attention_forward_tc(const AttnShape& s, const float* q, const float* k, co
 void attention_backward_tc(const AttnShape& s, const float* q, const float* k, const float* v, const float* o,
                            const float* lse, const float* dout, long long lddo, float* dq, float* dk, float* dv,
                            float* delta, float* S, float* dP, float* tmp, cudaStream_t stream);
+// Fused tensor-core forward (flash_tc.cu): scores stay on chip, no scratch.
+// head_dim 32, 64 or 128; row strides multiples of 4; 16-byte aligned pointers.
+bool attention_flash_supported(const AttnShape& s);
+void attention_forward_flash(const AttnShape& s, const float* q, const float* k, const float* v, float* o,
+                             float* lse, int* d_err, cudaStream_t stream);
 // delta[b, h, t] = sum_d dout[t, h, d] * o[t, h, d]
 void attention_delta(const AttnShape& s, const float* o, const float* dout, long long lddo, float* delta,
                      cudaStream_t stream);

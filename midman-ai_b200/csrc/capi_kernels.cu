@@ -84,10 +84,8 @@ int32_t mm_gpu_attention_forward(int32_t batch, int32_t seq, int32_t n_heads, in
     if (int32_t rc = attention_shape(batch, seq, n_heads, n_kv_heads, head_dim, ldq, ldk, &s)) return rc;
     if (!q || !k || !v || !o || !lse) return fail(MM_GPU_ERR_ARGUMENT, "attention: null pointer");
     cudaStream_t st = as_stream(stream);
-    if (precision == MM_GPU_TF32 && mm::attention_tc_supported(s)) {
-      const size_t n = static_cast<size_t>(batch) * n_heads * seq * mm::attention_scores_ld(seq);
-      float* S = static_cast<float*>(mm::device_scratch(n * sizeof(float), st));
-      mm::attention_forward_tc(s, q, k, v, o, lse, S, st);
+    if (precision == MM_GPU_TF32 && mm::attention_flash_supported(s)) {
+      mm::attention_forward_flash(s, q, k, v, o, lse, mm::device_context().d_err, st);
     } else {
       mm::attention_forward(s, q, k, v, o, lse, st);
     }

@@ -1,0 +1,377 @@
+// Fused causal attention forward on the tensor cores (TF32, tcgen05 + TMEM).
+//
+// One CTA per (128-query tile, batch, head). Per block of 64 keys:
+//   S_j = Q K_j^T         tcgen05.mma, A = Q (smem), B = K_j (smem), D in TMEM
+//   P_j = exp(S_j - m)    softmax warps: tcgen05.ld of their own row, online
+//                         max/sum, tcgen05.st of P_j over S_j in TMEM
+//   O  += P_j V_j         tcgen05.mma with A = P_j read from TMEM, B = V_j (smem)
+// so the score matrix never leaves the SM. The running maximum is only moved
+// (and O rescaled in TMEM) when a row's maximum grows by more than 2^8; the
+// final O / l and lse = m + log(l) are exact for any maximum used consistently.
+// Computes what crates/midman-nn/src/attention.rs:79-102 does (scores scaled by
+// 1/sqrt(hd), -1e9 above the diagonal, softmax over keys, P V), with grouped
+// key/value heads read in place rather than expanded by copy.
+//
+// Warp roles (192 threads):
+//   warp 0      TMA producer (one lane): Q once, then a ring of K/V stages
+//   warp 1      TMEM allocator + UMMA issuer (one lane)
+//   warps 2..5  softmax, O rescaling and the epilogue; warp w owns TMEM lanes
+//               32 (w % 4) .. +31, i.e. query rows of that quarter
+// TMEM columns: three S/P buffers of 64 at 0, 64, 128 (S_{j+1} is computed
+// while the softmax works on S_j), O at 192 .. 192 + hd.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdint>
+#include <stdexcept>
+#include <string>
+
+#include "attention.h"
+#include "ptx.cuh"
+#include "tma.h"
+
+namespace mm {
+
+namespace {
+
+constexpr int BQ = 128;    // query rows per CTA = TMEM lanes
+constexpr int BKV = 64;    // keys per block
+constexpr int NSBUF = 3;   // S/P buffers
+constexpr int FTHREADS = 192;
+constexpr uint32_t O_COL = NSBUF * BKV;  // 192
+constexpr float kRescaleLog2 = 8.0f;    // move the running max when it grows by more than 2^8
+
+template <int HD>
+struct FlashCfg {
+  static constexpr int Q_BYTES = BQ * HD * 4;
+  static constexpr int K_BYTES = BKV * HD * 4;
+  static constexpr int STAGE_BYTES = 2 * K_BYTES;  // K and V
+  static constexpr int FIT = (200 * 1024 - Q_BYTES) / STAGE_BYTES;
+  static constexpr int STAGES = FIT > 4 ? 4 : FIT;
+  static constexpr int SMEM = Q_BYTES + STAGES * STAGE_BYTES + 1024 + 256;
+  static constexpr uint32_t TMEM_COLS = O_COL + HD <= 256 ? 256 : 512;
+  static_assert(STAGES >= 2, "flash attention needs two K/V stages");
+};
+
+struct FlashParams {
+  int T, H, G, n_qt, BH;
+  long long ldo;
+  float scale_log2;  // softmax scale * log2(e)
+  float* o;
+  float* lse;
+  int* err;
+};
+
+template <int HD>
+__global__ void __launch_bounds__(FTHREADS, 1)
+    flash_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                     const __grid_constant__ CUtensorMap tmV, FlashParams p) {
+  using Cfg = FlashCfg<HD>;
+  constexpr int STAGES = Cfg::STAGES;
+  // heaviest query tiles (most keys) are scheduled first
+  const int qt = p.n_qt - 1 - static_cast<int>(blockIdx.x) / p.BH;
+  const int bh = static_cast<int>(blockIdx.x) % p.BH;
+  const int b = bh / p.H, h = bh % p.H, hk = h / p.G;
+  const int q0 = qt * BQ;
+  const int kv_end = min(p.T, q0 + BQ);
+  const int n_kv = (kv_end + BKV - 1) / BKV;
+  const int row0 = b * p.T;  // first token row of this sequence
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (base - raw_addr);
+  const uint32_t sQ = base;
+  auto sK = [&](int s) { return base + Cfg::Q_BYTES + s * Cfg::STAGE_BYTES; };
+  auto sV = [&](int s) { return sK(s) + Cfg::K_BYTES; };
+
+  const uint32_t bars = base + Cfg::Q_BYTES + STAGES * Cfg::STAGE_BYTES;
+  const uint32_t q_full = bars;
+  auto k_full = [&](int s) { return bars + 8u * (1 + s); };
+  auto v_full = [&](int s) { return bars + 8u * (1 + STAGES + s); };
+  auto kv_empty = [&](int s) { return bars + 8u * (1 + 2 * STAGES + s); };
+  auto s_full = [&](int bb) { return bars + 8u * (1 + 3 * STAGES + bb); };
+  auto p_full = [&](int bb) { return bars + 8u * (1 + 3 * STAGES + NSBUF + bb); };
+  auto s_free = [&](int bb) { return bars + 8u * (1 + 3 * STAGES + 2 * NSBUF + bb); };
+  const uint32_t o_done = bars + 8u * (1 + 3 * STAGES + 3 * NSBUF);
+  const uint32_t tmem_slot = o_done + 8u;
+  uint8_t* tail = smem + (tmem_slot - base);
+  uint32_t* tmem_slot_ptr = reinterpret_cast<uint32_t*>(tail);
+  // K/V stages loaded by the producer and waited on by the UMMA issuer; they
+  // differ only after a timed-out wait, and teardown then drains the difference.
+  int* kv_issued = reinterpret_cast<int*>(tail + 8);
+  int* kv_consumed = kv_issued + 1;
+  int* q_pending = kv_issued + 2;
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+    mbar_init(q_full, 1);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(k_full(s), 1);
+      mbar_init(v_full(s), 1);
+      mbar_init(kv_empty(s), 1);
+    }
+    for (int bb = 0; bb < NSBUF; ++bb) {
+      mbar_init(s_full(bb), 1);
+      mbar_init(p_full(bb), 4);  // one arrival per softmax warp
+      mbar_init(s_free(bb), 1);
+    }
+    mbar_init(o_done, 1);
+    *kv_issued = 0;
+    *kv_consumed = 0;
+    *q_pending = 0;
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot_ptr;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer
+      *q_pending = 1;
+      mbar_arrive_expect_tx(q_full, Cfg::Q_BYTES);
+      tma_load_3d(sQ, &tmQ, q_full, 0, row0 + q0, h * (HD / 32));
+      for (int j = 0; j < n_kv; ++j) {
+        const int s = j % STAGES, r = j / STAGES;
+        if (r > 0 && !mbar_wait(kv_empty(s), (r - 1) & 1, p.err, kErrWaitEmpty)) break;
+        // rows past this sequence's end belong to the next one (or are zero
+        // fill): they are keys after every query of the tile, always masked
+        mbar_arrive_expect_tx(k_full(s), Cfg::K_BYTES);
+        tma_load_3d(sK(s), &tmK, k_full(s), 0, row0 + j * BKV, hk * (HD / 32));
+        mbar_arrive_expect_tx(v_full(s), Cfg::K_BYTES);
+        tma_load_3d(sV(s), &tmV, v_full(s), 0, row0 + j * BKV, hk * (HD / 32));
+        *kv_issued = j + 1;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- UMMA issuer
+      constexpr uint32_t idesc_s = idesc_tf32(BQ, BKV, false, false);  // Q K-major, K K-major
+      constexpr uint32_t idesc_o = idesc_tf32(BQ, HD, false, true);    // P (TMEM), V MN-major
+      bool ok = mbar_wait(q_full, 0, p.err, kErrWaitFull);
+      if (ok) *q_pending = 0;
+      auto issue_s = [&](int j) -> bool {
+        const int s = j % STAGES, bb = j % NSBUF, u = j / NSBUF;
+        if (!mbar_wait(k_full(s), (j / STAGES) & 1, p.err, kErrWaitFull)) return false;
+        if (u > 0 && !mbar_wait(s_free(bb), (u - 1) & 1, p.err, kErrWaitAccum)) return false;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < HD / 8; ++kk) {
+          const uint32_t off = (kk % 4) * 32u;  // 8 tf32 = 32 bytes along the 128-byte chunk
+          const uint64_t a = smem_desc(sQ + (kk / 4) * (BQ * 128) + off, 16, 1024, kLayoutSw128);
+          const uint64_t bd = smem_desc(sK(s) + (kk / 4) * (BKV * 128) + off, 16, 1024, kLayoutSw128);
+          umma_tf32(tmem + bb * BKV, a, bd, idesc_s, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(s_full(bb));
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      for (int j = 0; ok && j < n_kv; ++j) {
+        if (j + 1 < n_kv && !issue_s(j + 1)) break;
+        const int s = j % STAGES, bb = j % NSBUF;
+        if (!mbar_wait(p_full(bb), (j / NSBUF) & 1, p.err, kErrWaitAccum)) break;
+        if (!mbar_wait(v_full(s), (j / STAGES) & 1, p.err, kErrWaitFull)) break;
+        *kv_consumed = j + 1;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < BKV / 8; ++kk) {
+          // V_j: 32-wide hd blocks of BKV key rows (LBO), 8 key rows per step
+          const uint64_t bd = smem_desc(sV(s) + kk * 1024, BKV * 128, 512, kLayoutSw128Base32);
+          umma_tf32_ts(tmem + O_COL, tmem + bb * BKV + kk * 8, bd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit(kv_empty(s));
+        umma_commit(s_free(bb));
+        umma_commit(o_done);
+      }
+    }
+  } else {
+    // ---------------- softmax + epilogue
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;  // query row within the tile
+    const int q = q0 + row;
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    float m_run = -INFINITY, l_run = 0.0f;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      const int bb = j % NSBUF;
+      if (!mbar_wait(s_full(bb), (j / NSBUF) & 1, p.err, kErrWaitAccum)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t r[2][32];
+      tmem_ld_32x32b_x32(tmem + lane_base + bb * BKV, r[0]);
+      tmem_ld_32x32b_x32(tmem + lane_base + bb * BKV + 32, r[1]);
+      const int kv0 = j * BKV;
+      const bool diag = kv0 + BKV - 1 > q0;  // some key of the block follows some query of the tile
+      float mloc = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 2; ++c)
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          float x = __uint_as_float(r[c][i]) * p.scale_log2;
+          if (diag && kv0 + c * 32 + i > q) x = -INFINITY;
+          r[c][i] = __float_as_uint(x);
+          mloc = fmaxf(mloc, x);
+        }
+      const float m_new = fmaxf(m_run, mloc);
+      if (j == 0) {
+        m_run = m_new;
+      } else {
+        const bool need = m_new > m_run + kRescaleLog2;
+        if (__any_sync(0xffffffffu, need)) {
+          // O holds blocks < j once PV_{j-1} is done; rescale it in place
+          if (!mbar_wait(o_done, (j - 1) & 1, p.err, kErrWaitAccum)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const float alpha = need ? ex2_approx(m_run - m_new) : 1.0f;
+#pragma unroll 1
+          for (int c = 0; c < HD / 32; ++c) {
+            uint32_t o[32];
+            tmem_ld_32x32b_x32(tmem + lane_base + O_COL + c * 32, o);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st_32x32b_x32(tmem + lane_base + O_COL + c * 32, o);
+          }
+          if (need) {
+            l_run *= alpha;
+            m_run = m_new;
+          }
+        }
+      }
+      float lsum = 0.0f;
+#pragma unroll
+      for (int c = 0; c < 2; ++c)
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float e = ex2_approx(__uint_as_float(r[c][i]) - m_run);
+          lsum += e;
+          r[c][i] = __float_as_uint(e);
+        }
+      l_run += lsum;
+      tmem_st_32x32b_x32(tmem + lane_base + bb * BKV, r[0]);
+      tmem_st_32x32b_x32(tmem + lane_base + bb * BKV + 32, r[1]);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full(bb));
+    }
+    if (ok && mbar_wait(o_done, (n_kv - 1) & 1, p.err, kErrWaitAccum)) {
+      tc_fence_after();
+      const float inv = 1.0f / l_run;
+      float* orow = p.o + static_cast<long long>(row0 + q) * p.ldo + static_cast<long long>(h) * HD;
+#pragma unroll 1
+      for (int c = 0; c < HD / 32; ++c) {
+        uint32_t o[32];
+        tmem_ld_32x32b_x32(tmem + lane_base + O_COL + c * 32, o);
+        if (q < p.T) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 4)
+            *reinterpret_cast<float4*>(orow + c * 32 + i) =
+                make_float4(__uint_as_float(o[i]) * inv, __uint_as_float(o[i + 1]) * inv,
+                            __uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);
+        }
+      }
+      if (q < p.T) p.lse[static_cast<long long>(bh) * p.T + q] = (m_run + log2f(l_run)) * 0.69314718055994531f;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    // after a timed-out wait, let every TMA copy still in flight land (bounded)
+    // before the CTA's shared memory is released
+    if (*q_pending) mbar_wait(q_full, 0, p.err, kErrWaitDrain, 1000000000ull);
+    for (int j = *kv_consumed; j < *kv_issued; ++j) {
+      const int s = j % STAGES;
+      if (!mbar_wait(k_full(s), (j / STAGES) & 1, p.err, kErrWaitDrain, 1000000000ull)) break;
+      if (!mbar_wait(v_full(s), (j / STAGES) & 1, p.err, kErrWaitDrain, 1000000000ull)) break;
+    }
+  }
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, Cfg::TMEM_COLS);
+  }
+  __syncthreads();
+}
+
+bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
+
+// Token-major operand [rows, ld] whose head `hh` occupies columns hh*HD ..: a
+// 3-D view (32 columns, token row, 32-column block) so one box brings a whole
+// row tile of one head, laid out as hd/32 consecutive 128-byte-wide chunks.
+void head_map(CUtensorMap* map, const float* ptr, long long rows, long long ld, int heads, int hd, int box_rows,
+              bool mn_major) {
+  const long long dims[3] = {32, rows, static_cast<long long>(heads) * hd / 32};
+  const long long strides[2] = {ld, 32};
+  const int box[3] = {32, box_rows, hd / 32};
+  if (encode_tensor_map(map, ptr, 3, dims, strides, box, mn_major))
+    throw std::runtime_error("flash attention: tensor map rejected");
+}
+
+template <int HD>
+void launch_flash(const AttnShape& s, const float* q, const float* k, const float* v, float* o, float* lse,
+                  int* d_err, cudaStream_t stream) {
+  using Cfg = FlashCfg<HD>;
+  const long long rows = static_cast<long long>(s.B) * s.T;
+  CUtensorMap tq, tk, tv;
+  head_map(&tq, q, rows, s.ldq, s.H, HD, BQ, false);
+  head_map(&tk, k, rows, s.ldk, s.Hkv, HD, BKV, false);
+  head_map(&tv, v, rows, s.ldv, s.Hkv, HD, BKV, true);
+  static thread_local int configured = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured != dev) {
+    cudaFuncSetAttribute(flash_fwd_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
+    configured = dev;
+  }
+  FlashParams p;
+  p.T = s.T;
+  p.H = s.H;
+  p.G = s.H / s.Hkv;
+  p.n_qt = (s.T + BQ - 1) / BQ;
+  p.BH = s.B * s.H;
+  p.ldo = s.ldo;
+  p.scale_log2 = s.scale * 1.4426950408889634f;
+  p.o = o;
+  p.lse = lse;
+  p.err = d_err;
+  const long long grid = static_cast<long long>(p.n_qt) * p.BH;
+  flash_fwd_kernel<HD><<<static_cast<unsigned>(grid), FTHREADS, Cfg::SMEM, stream>>>(tq, tk, tv, p);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) throw std::runtime_error(std::string("flash attention launch: ") + cudaGetErrorString(e));
+}
+
+}  // namespace
+
+bool attention_flash_supported(const AttnShape& s) {
+  return (s.hd == 32 || s.hd == 64 || s.hd == 128) && s.ldq % 4 == 0 && s.ldk % 4 == 0 && s.ldv % 4 == 0 &&
+         s.ldo % 4 == 0;
+}
+
+void attention_forward_flash(const AttnShape& s, const float* q, const float* k, const float* v, float* o,
+                             float* lse, int* d_err, cudaStream_t stream) {
+  if (!attention_flash_supported(s) || !aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(o))
+    throw std::runtime_error("flash attention: unsupported head_dim, stride or alignment");
+  switch (s.hd) {
+    case 32: launch_flash<32>(s, q, k, v, o, lse, d_err, stream); break;
+    case 64: launch_flash<64>(s, q, k, v, o, lse, d_err, stream); break;
+    default: launch_flash<128>(s, q, k, v, o, lse, d_err, stream); break;
+  }
+}
+
+}  // namespace mm

@@ -33,6 +33,7 @@
 
 #include "gemm.h"
 #include "ptx.cuh"
+#include "tma.h"
 
 namespace mm {
 
@@ -62,15 +63,6 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
       "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(h), "r"(y), "r"(b)
-      : "memory");
-}
-
-__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int32_t x, int32_t y,
-                                            int32_t z) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y), "r"(z)
       : "memory");
 }
 
@@ -348,8 +340,9 @@ int encode(CUtensorMap* map, const float* ptr, int rank, const long long* dims, 
            const int* box, bool mn_major) {
   auto fn = get_encode_fn();
   if (!fn) return -1;
-  cuuint64_t d[4], st[3];
-  cuuint32_t b[4], e[4] = {1, 1, 1, 1};
+  if (rank < 2 || rank > 5) return -2;
+  cuuint64_t d[5], st[4];
+  cuuint32_t b[5], e[5] = {1, 1, 1, 1, 1};
   for (int i = 0; i < rank; ++i) {
     d[i] = static_cast<cuuint64_t>(dims[i]);
     b[i] = static_cast<cuuint32_t>(box[i]);
@@ -364,6 +357,15 @@ int encode(CUtensorMap* map, const float* ptr, int rank, const long long* dims, 
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? 0 : -2;
 }
+
+}  // namespace
+
+int encode_tensor_map(CUtensorMap* map, const float* ptr, int rank, const long long* dims, const long long* strides,
+                      const int* box, bool mn_major) {
+  return encode(map, ptr, rank, dims, strides, box, mn_major);
+}
+
+namespace {
 
 // 2-D operand: `inner` contiguous elements per row, `outer` rows, `ld` apart.
 int make_map2d(CUtensorMap* map, const float* ptr, long long inner, long long outer, long long ld, int box_inner,

@@ -50,8 +50,8 @@ void Trainer::forward(int B, int T, bool train) {
     rope(a.k, N, T, Hkv, hd, KV, d_cos_, d_sin_, false, stream_);
     const double attn_flops = 2.0 * B * H * static_cast<double>(T) * (T + 1) * hd;  // QK^T and PV, causal half
     int slot = prof_begin();
-    if (attn_tc_)
-      attention_forward_tc(shape, a.q, a.k, a.v, a.o, a.lse, scores_, stream_);
+    if (attn_tc_)  // fused: the scores stay on chip
+      attention_forward_flash(shape, a.q, a.k, a.v, a.o, a.lse, device_context().d_err, stream_);
     else
       attention_forward(shape, a.q, a.k, a.v, a.o, a.lse, stream_);
     prof_end(slot, "attention_fwd", attn_flops);
