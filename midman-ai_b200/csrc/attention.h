@@ -48,6 +48,11 @@ void attention_backward_tc(const AttnShape& s, const float* q, const float* k, c
 bool attention_flash_supported(const AttnShape& s);
 void attention_forward_flash(const AttnShape& s, const float* q, const float* k, const float* v, float* o,
                              float* lse, int* d_err, cudaStream_t stream);
+// Fused tensor-core backward (flash_bwd.cu): writes delta (B*H*T floats) and
+// dq, dk, dv (dk/dv summed over each key head's group); no score buffers.
+void attention_backward_flash(const AttnShape& s, const float* q, const float* k, const float* v, const float* o,
+                              const float* lse, const float* dout, long long lddo, float* dq, float* dk, float* dv,
+                              float* delta, int* d_err, cudaStream_t stream);
 // delta[b, h, t] = sum_d dout[t, h, d] * o[t, h, d]
 void attention_delta(const AttnShape& s, const float* o, const float* dout, long long lddo, float* delta,
                      cudaStream_t stream);

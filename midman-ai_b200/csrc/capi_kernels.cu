@@ -104,12 +104,9 @@ int32_t mm_gpu_attention_backward(int32_t batch, int32_t seq, int32_t n_heads, i
       return fail(MM_GPU_ERR_ARGUMENT, "attention: null pointer");
     cudaStream_t st = as_stream(stream);
     const size_t rows = static_cast<size_t>(batch) * n_heads * seq;
-    if (precision == MM_GPU_TF32 && mm::attention_tc_supported(s)) {
-      const size_t n = rows * mm::attention_scores_ld(seq);
-      const size_t tmp = static_cast<size_t>(batch) * seq * n_heads * head_dim;
-      float* ws = static_cast<float*>(mm::device_scratch((2 * n + tmp + rows) * sizeof(float), st));
-      mm::attention_backward_tc(s, q, k, v, o, lse, dout, ldq, dq, dk, dv, ws + 2 * n + tmp, ws, ws + n, ws + 2 * n,
-                                st);
+    if (precision == MM_GPU_TF32 && mm::attention_flash_supported(s)) {
+      float* delta = static_cast<float*>(mm::device_scratch(rows * sizeof(float), st));
+      mm::attention_backward_flash(s, q, k, v, o, lse, dout, ldq, dq, dk, dv, delta, mm::device_context().d_err, st);
     } else {
       float* delta = static_cast<float*>(mm::device_scratch(rows * sizeof(float), st));
       mm::attention_backward(s, q, k, v, o, lse, dout, ldq, dq, dk, dv, delta, st);

@@ -1,0 +1,637 @@
+// Fused causal attention backward on the tensor cores (TF32, tcgen05 + TMEM).
+//
+// The backward of attention.rs:79-102 (the reference differentiates it through
+// its autograd tape), split FA2-style into two kernels that never write a
+// score-sized buffer:
+//
+//   flash_bwd_kv  one CTA per (128-key tile, batch, key/value head); loops over
+//                 the group's query heads and the query blocks (32 queries) at
+//                 or after the tile's first key. Per block, lanes = keys:
+//                   S^T  = K Q^T          A = K (smem), B = Q (smem, K-major)
+//                   dP^T = V dO^T         A = V (TMEM),  B = dO (smem, K-major)
+//                   P = exp(S*scale - lse), dS = P (dP - delta) * scale  (softmax warps)
+//                   dV  += P^T-rows dO    A = P  (TMEM), B = dO (smem, MN-major)
+//                   dK  += dS^T-rows Q    A = dS (TMEM), B = Q  (smem, MN-major)
+//                 dK and dV of the key/value head accumulate in TMEM over the
+//                 whole group, so grouped-query heads need no reduction pass.
+//   flash_bwd_q   one CTA per (128-query tile, batch, head); loops over key
+//                 blocks (32 keys) up to the diagonal. Lanes = queries:
+//                   S  = Q K^T            A = Q (smem),  B = K (smem, K-major)
+//                   dP = dO V^T           A = dO (TMEM), B = V (smem, K-major)
+//                   dS = P (dP - delta) * scale
+//                   dQ += dS K            A = dS (TMEM), B = K (smem, MN-major)
+//
+// An fp32 [rows, hd] tile serves as a K-major operand (hd contracted) with the
+// 16-byte-atom 128-byte swizzle and as an MN-major operand (hd the output
+// dimension) only with the 32-byte-atom swizzle, so those tiles are loaded
+// twice, once per layout. delta = rowsum(dO * O) comes from attention_delta.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdint>
+#include <stdexcept>
+#include <string>
+
+#include "attention.h"
+#include "ptx.cuh"
+#include "tma.h"
+
+namespace mm {
+
+namespace {
+
+constexpr int TILE = 128;  // lanes: keys (kv kernel) or queries (q kernel)
+constexpr int BLK = 32;    // streamed queries (kv kernel) or keys (q kernel) per step
+constexpr int BTHREADS = 192;
+constexpr float kLog2e = 1.4426950408889634f;
+
+struct BwdParams {
+  int T, H, Hkv, G, n_tiles, BHx;  // BHx = B * heads the grid runs over
+  long long ld_in;                 // row stride of the operand loaded into TMEM (v or dout)
+  long long ld_out;                // row stride of the outputs
+  long long ld_out2;               // dv (kv kernel)
+  const float* tm_src;             // that operand
+  const float* lse;
+  const float* delta;
+  float* out;   // dk (kv kernel) or dq (q kernel)
+  float* out2;  // dv (kv kernel)
+  float scale, scale_log2;
+  int* err;
+};
+
+template <int HD>
+struct BwdCfg {
+  static constexpr int TILE_BYTES = TILE * HD * 4;  // resident K (kv) or Q (q)
+  static constexpr int BLK_BYTES = BLK * HD * 4;    // one streamed tile
+  // kv kernel streams Q, dO (K-major) and Q, dO (MN-major); q kernel K, V (K-major) and K (MN-major)
+  static constexpr int KV_STAGE = 4 * BLK_BYTES;
+  static constexpr int Q_STAGE = 3 * BLK_BYTES;
+  static constexpr int KV_STAGES_FIT = (210 * 1024 - TILE_BYTES) / KV_STAGE;
+  static constexpr int Q_STAGES_FIT = (210 * 1024 - TILE_BYTES) / Q_STAGE;
+  static constexpr int KV_STAGES = KV_STAGES_FIT > 4 ? 4 : KV_STAGES_FIT;
+  static constexpr int Q_STAGES = Q_STAGES_FIT > 4 ? 4 : Q_STAGES_FIT;
+  static constexpr int KV_SMEM = TILE_BYTES + KV_STAGES * KV_STAGE + 1024 + 256;
+  static constexpr int Q_SMEM = TILE_BYTES + Q_STAGES * Q_STAGE + 1024 + 256;
+  // TMEM: 2 x (S/P, dP/dS) buffers of BLK columns, then the TMEM-resident
+  // operand and the accumulators, hd columns each
+  static constexpr uint32_t BUF_COLS = 4 * BLK;      // 128
+  static constexpr uint32_t OPND_COL = BUF_COLS;     // V (kv) or dO (q)
+  static constexpr uint32_t ACC_COL = BUF_COLS + HD; // dV (kv) or dQ (q)
+  static constexpr uint32_t ACC2_COL = ACC_COL + HD; // dK (kv)
+  static constexpr uint32_t TMEM_COLS = 512;
+  static_assert(KV_STAGES >= 2 && Q_STAGES >= 2, "backward needs two stages");
+  static_assert(ACC2_COL + HD <= TMEM_COLS, "TMEM budget");
+};
+
+__device__ __forceinline__ uint32_t s_col(int bb) { return bb * 2 * BLK; }       // S / P
+__device__ __forceinline__ uint32_t dp_col(int bb) { return bb * 2 * BLK + BLK; } // dP / dS
+
+// Barrier block shared by both kernels (offsets in 8-byte slots).
+template <int STAGES>
+struct Bars {
+  uint32_t base;
+  __device__ uint32_t tile_full() const { return base; }
+  __device__ uint32_t full(int s) const { return base + 8u * (1 + s); }
+  __device__ uint32_t empty(int s) const { return base + 8u * (1 + STAGES + s); }
+  __device__ uint32_t s_full(int bb) const { return base + 8u * (1 + 2 * STAGES + bb); }
+  __device__ uint32_t p_full(int bb) const { return base + 8u * (3 + 2 * STAGES + bb); }
+  __device__ uint32_t s_free(int bb) const { return base + 8u * (5 + 2 * STAGES + bb); }
+  __device__ uint32_t opnd_ready() const { return base + 8u * (7 + 2 * STAGES); }
+  __device__ uint32_t acc_done() const { return base + 8u * (8 + 2 * STAGES); }
+  __device__ uint32_t slot() const { return base + 8u * (9 + 2 * STAGES); }
+  __device__ void init() const {
+    mbar_init(tile_full(), 1);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full(s), 1);
+      mbar_init(empty(s), 1);
+    }
+    for (int bb = 0; bb < 2; ++bb) {
+      mbar_init(s_full(bb), 1);
+      mbar_init(p_full(bb), 4);
+      mbar_init(s_free(bb), 1);
+    }
+    mbar_init(opnd_ready(), 4);
+    mbar_init(acc_done(), 1);
+  }
+};
+
+// K-major descriptor of contraction step kk (8 tf32) in a tile of `rows` rows
+// stored as 128-byte chunks of 32 elements (chunk stride rows * 128 bytes).
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t tile, int rows, int kk) {
+  return smem_desc(tile + (kk / 4) * (rows * 128) + (kk % 4) * 32, 16, 1024, kLayoutSw128);
+}
+// MN-major descriptor of contraction step kk (8 rows) in a BLK-row tile stored
+// as 32-column blocks of BLK rows (block stride BLK * 128 bytes).
+__device__ __forceinline__ uint64_t mnmajor_desc(uint32_t tile, int kk) {
+  return smem_desc(tile + kk * 1024, BLK * 128, 512, kLayoutSw128Base32);
+}
+
+// Copies row `row` (HD floats at src, or zeros when !valid) into TMEM columns
+// [col, col + HD) of this thread's lane.
+template <int HD>
+__device__ __forceinline__ void row_to_tmem(const float* src, bool valid, uint32_t taddr) {
+#pragma unroll 1
+  for (int c = 0; c < HD / 32; ++c) {
+    uint32_t r[32];
+#pragma unroll
+    for (int i = 0; i < 32; i += 4) {
+      float4 v = valid ? *reinterpret_cast<const float4*>(src + c * 32 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+      r[i] = __float_as_uint(v.x);
+      r[i + 1] = __float_as_uint(v.y);
+      r[i + 2] = __float_as_uint(v.z);
+      r[i + 3] = __float_as_uint(v.w);
+    }
+    tmem_st_32x32b_x32(taddr + c * 32, r);
+  }
+}
+
+// Writes TMEM columns [col, col + HD) of this thread's lane, times `mul`, to dst.
+template <int HD>
+__device__ __forceinline__ void tmem_to_row(uint32_t taddr, float* dst, bool valid, float mul) {
+#pragma unroll 1
+  for (int c = 0; c < HD / 32; ++c) {
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(taddr + c * 32, r);
+    if (valid) {
+#pragma unroll
+      for (int i = 0; i < 32; i += 4)
+        *reinterpret_cast<float4*>(dst + c * 32 + i) =
+            make_float4(__uint_as_float(r[i]) * mul, __uint_as_float(r[i + 1]) * mul,
+                        __uint_as_float(r[i + 2]) * mul, __uint_as_float(r[i + 3]) * mul);
+    }
+  }
+}
+
+// out[i] = src[i] * mul for the first n_valid of 32 consecutive floats, 0 past them.
+__device__ __forceinline__ void load32(const float* src, int n_valid, float mul, float (&out)[32]) {
+  if (n_valid >= 32 && (reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
+#pragma unroll
+    for (int i = 0; i < 32; i += 4) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(src + i));
+      out[i] = v.x * mul;
+      out[i + 1] = v.y * mul;
+      out[i + 2] = v.z * mul;
+      out[i + 3] = v.w * mul;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) out[i] = i < n_valid ? __ldg(src + i) * mul : 0.0f;
+  }
+}
+
+// Shared-memory tail after the barriers: TMEM address slot and pipeline counters.
+struct Tail {
+  uint32_t tmem;
+  int pad;
+  int issued, consumed, tile_pending;
+};
+
+template <int STAGES>
+__device__ __forceinline__ void drain(const Bars<STAGES>& bars, Tail* tl, int* err) {
+  if (tl->tile_pending) mbar_wait(bars.tile_full(), 0, err, kErrWaitDrain, 1000000000ull);
+  for (int t = tl->consumed; t < tl->issued; ++t)
+    if (!mbar_wait(bars.full(t % STAGES), (t / STAGES) & 1, err, kErrWaitDrain, 1000000000ull)) break;
+}
+
+// ------------------------------------------------------------------ dK, dV
+template <int HD>
+__global__ void __launch_bounds__(BTHREADS, 1)
+    flash_bwd_kv_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmQk,
+                        const __grid_constant__ CUtensorMap tmDOk, const __grid_constant__ CUtensorMap tmQm,
+                        const __grid_constant__ CUtensorMap tmDOm, BwdParams p) {
+  using Cfg = BwdCfg<HD>;
+  constexpr int STAGES = Cfg::KV_STAGES;
+  constexpr int BB = Cfg::BLK_BYTES;
+  const int kt = static_cast<int>(blockIdx.x) / p.BHx;  // low key tiles see the most queries: first
+  const int bhk = static_cast<int>(blockIdx.x) % p.BHx;
+  const int b = bhk / p.Hkv, hk = bhk % p.Hkv;
+  const int k0 = kt * TILE;
+  const int row0 = b * p.T;
+  const int n_q = (p.T - k0 + BLK - 1) / BLK;  // query blocks from the tile's first key on
+  const int n_steps = p.G * n_q;
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  const uint32_t sK = base;
+  auto stage = [&](int s) { return base + Cfg::TILE_BYTES + s * Cfg::KV_STAGE; };
+  const Bars<STAGES> bars{base + Cfg::TILE_BYTES + STAGES * Cfg::KV_STAGE};
+  Tail* tl = reinterpret_cast<Tail*>(smem_raw + (bars.slot() - raw_addr));
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmQk);
+    tma_prefetch_desc(&tmDOk);
+    tma_prefetch_desc(&tmQm);
+    tma_prefetch_desc(&tmDOm);
+    bars.init();
+    tl->issued = tl->consumed = tl->tile_pending = 0;
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 1) {
+    tmem_alloc(bars.slot(), Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tl->tmem;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer: the key tile, then Q / dO blocks in both layouts
+      tl->tile_pending = 1;
+      mbar_arrive_expect_tx(bars.tile_full(), Cfg::TILE_BYTES);
+      tma_load_3d(sK, &tmK, bars.tile_full(), 0, row0 + k0, hk * (HD / 32));
+      for (int t = 0; t < n_steps; ++t) {
+        const int s = t % STAGES, r = t / STAGES;
+        if (r > 0 && !mbar_wait(bars.empty(s), (r - 1) & 1, p.err, kErrWaitEmpty)) break;
+        const int h = hk * p.G + t / n_q;
+        const int qrow = row0 + k0 + (t % n_q) * BLK;  // rows past the sequence are masked
+        const int xb = h * (HD / 32);
+        const uint32_t st = stage(s);
+        mbar_arrive_expect_tx(bars.full(s), Cfg::KV_STAGE);
+        tma_load_3d(st, &tmQk, bars.full(s), 0, qrow, xb);
+        tma_load_3d(st + BB, &tmDOk, bars.full(s), 0, qrow, xb);
+        tma_load_3d(st + 2 * BB, &tmQm, bars.full(s), 0, qrow, xb);
+        tma_load_3d(st + 3 * BB, &tmDOm, bars.full(s), 0, qrow, xb);
+        tl->issued = t + 1;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- UMMA issuer
+      constexpr uint32_t idesc_s = idesc_tf32(TILE, BLK, false, false);
+      constexpr uint32_t idesc_g = idesc_tf32(TILE, HD, false, true);
+      bool ok = mbar_wait(bars.tile_full(), 0, p.err, kErrWaitFull);
+      if (ok) tl->tile_pending = 0;
+      ok = ok && mbar_wait(bars.opnd_ready(), 0, p.err, kErrWaitAccum);
+      auto issue_s = [&](int t) -> bool {
+        const int s = t % STAGES, bb = t & 1, u = t >> 1;
+        if (!mbar_wait(bars.full(s), (t / STAGES) & 1, p.err, kErrWaitFull)) return false;
+        tl->consumed = t + 1;
+        if (u > 0 && !mbar_wait(bars.s_free(bb), (u - 1) & 1, p.err, kErrWaitAccum)) return false;
+        tc_fence_after();
+        const uint32_t st = stage(s);
+#pragma unroll
+        for (int kk = 0; kk < HD / 8; ++kk)  // S^T = K Q^T
+          umma_tf32(tmem + s_col(bb), kmajor_desc(sK, TILE, kk), kmajor_desc(st, BLK, kk), idesc_s,
+                    kk > 0 ? 1u : 0u);
+#pragma unroll
+        for (int kk = 0; kk < HD / 8; ++kk)  // dP^T = V dO^T, V in TMEM
+          umma_tf32_ts(tmem + dp_col(bb), tmem + Cfg::OPND_COL + kk * 8, kmajor_desc(st + BB, BLK, kk), idesc_s,
+                       kk > 0 ? 1u : 0u);
+        umma_commit(bars.s_full(bb));
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      for (int t = 0; ok && t < n_steps; ++t) {
+        if (t + 1 < n_steps && !issue_s(t + 1)) break;
+        const int s = t % STAGES, bb = t & 1;
+        if (!mbar_wait(bars.p_full(bb), (t >> 1) & 1, p.err, kErrWaitAccum)) break;
+        tc_fence_after();
+        const uint32_t st = stage(s);
+#pragma unroll
+        for (int kk = 0; kk < BLK / 8; ++kk) {
+          const uint32_t acc = (t > 0 || kk > 0) ? 1u : 0u;
+          umma_tf32_ts(tmem + Cfg::ACC_COL, tmem + s_col(bb) + kk * 8, mnmajor_desc(st + 3 * BB, kk), idesc_g,
+                       acc);  // dV += P dO
+          umma_tf32_ts(tmem + Cfg::ACC2_COL, tmem + dp_col(bb) + kk * 8, mnmajor_desc(st + 2 * BB, kk), idesc_g,
+                       acc);  // dK += dS Q
+        }
+        umma_commit(bars.empty(s));
+        umma_commit(bars.s_free(bb));
+      }
+      umma_commit(bars.acc_done());
+    }
+  } else {
+    // ---------------- V into TMEM, softmax gradient, epilogue (lane = key)
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const int key = k0 + row;
+    const bool key_ok = key < p.T;
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    row_to_tmem<HD>(p.tm_src + static_cast<long long>(row0 + key) * p.ld_in + static_cast<long long>(hk) * HD,
+                    key_ok, tmem + lane_base + Cfg::OPND_COL);
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bars.opnd_ready());
+    bool ok = true;
+    for (int t = 0; t < n_steps; ++t) {
+      const int bb = t & 1;
+      const int h = hk * p.G + t / n_q;
+      const int qs = k0 + (t % n_q) * BLK;
+      const long long lrow = (static_cast<long long>(b) * p.H + h) * p.T;
+      float l2[32], dl[32];
+      load32(p.lse + lrow + qs, p.T - qs, kLog2e, l2);
+      load32(p.delta + lrow + qs, p.T - qs, 1.0f, dl);
+      if (!mbar_wait(bars.s_full(bb), (t >> 1) & 1, p.err, kErrWaitAccum)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t sv[32], dv[32];
+      tmem_ld_32x32b_x32(tmem + lane_base + s_col(bb), sv);
+      tmem_ld_32x32b_x32(tmem + lane_base + dp_col(bb), dv);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int q = qs + i;
+        const bool keep = q < p.T && key <= q;
+        const float pv = keep ? ex2_approx(fmaf(__uint_as_float(sv[i]), p.scale_log2, -l2[i])) : 0.0f;
+        sv[i] = __float_as_uint(pv);
+        dv[i] = __float_as_uint(pv * (__uint_as_float(dv[i]) - dl[i]) * p.scale);
+      }
+      tmem_st_32x32b_x32(tmem + lane_base + s_col(bb), sv);
+      tmem_st_32x32b_x32(tmem + lane_base + dp_col(bb), dv);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bars.p_full(bb));
+    }
+    if (ok && mbar_wait(bars.acc_done(), 0, p.err, kErrWaitAccum)) {
+      tc_fence_after();
+      const long long r = row0 + key;
+      tmem_to_row<HD>(tmem + lane_base + Cfg::ACC_COL, p.out2 + r * p.ld_out2 + static_cast<long long>(hk) * HD,
+                      key_ok, 1.0f);
+      tmem_to_row<HD>(tmem + lane_base + Cfg::ACC2_COL, p.out + r * p.ld_out + static_cast<long long>(hk) * HD,
+                      key_ok, 1.0f);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0) drain(bars, tl, p.err);
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, Cfg::TMEM_COLS);
+  }
+  __syncthreads();
+}
+
+// ------------------------------------------------------------------ dQ
+template <int HD>
+__global__ void __launch_bounds__(BTHREADS, 1)
+    flash_bwd_q_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKk,
+                       const __grid_constant__ CUtensorMap tmVk, const __grid_constant__ CUtensorMap tmKm,
+                       BwdParams p) {
+  using Cfg = BwdCfg<HD>;
+  constexpr int STAGES = Cfg::Q_STAGES;
+  constexpr int BB = Cfg::BLK_BYTES;
+  const int qt = p.n_tiles - 1 - static_cast<int>(blockIdx.x) / p.BHx;  // most keys first
+  const int bh = static_cast<int>(blockIdx.x) % p.BHx;
+  const int b = bh / p.H, h = bh % p.H, hk = h / p.G;
+  const int q0 = qt * TILE;
+  const int row0 = b * p.T;
+  const int n_kv = (min(p.T, q0 + TILE) + BLK - 1) / BLK;
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  const uint32_t sQ = base;
+  auto stage = [&](int s) { return base + Cfg::TILE_BYTES + s * Cfg::Q_STAGE; };
+  const Bars<STAGES> bars{base + Cfg::TILE_BYTES + STAGES * Cfg::Q_STAGE};
+  Tail* tl = reinterpret_cast<Tail*>(smem_raw + (bars.slot() - raw_addr));
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmKk);
+    tma_prefetch_desc(&tmVk);
+    tma_prefetch_desc(&tmKm);
+    bars.init();
+    tl->issued = tl->consumed = tl->tile_pending = 0;
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 1) {
+    tmem_alloc(bars.slot(), Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tl->tmem;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer: the query tile, then K (both layouts) and V blocks
+      tl->tile_pending = 1;
+      mbar_arrive_expect_tx(bars.tile_full(), Cfg::TILE_BYTES);
+      tma_load_3d(sQ, &tmQ, bars.tile_full(), 0, row0 + q0, h * (HD / 32));
+      for (int j = 0; j < n_kv; ++j) {
+        const int s = j % STAGES, r = j / STAGES;
+        if (r > 0 && !mbar_wait(bars.empty(s), (r - 1) & 1, p.err, kErrWaitEmpty)) break;
+        const int krow = row0 + j * BLK;  // keys past the sequence follow every query: masked
+        const int xb = hk * (HD / 32);
+        const uint32_t st = stage(s);
+        mbar_arrive_expect_tx(bars.full(s), Cfg::Q_STAGE);
+        tma_load_3d(st, &tmKk, bars.full(s), 0, krow, xb);
+        tma_load_3d(st + BB, &tmVk, bars.full(s), 0, krow, xb);
+        tma_load_3d(st + 2 * BB, &tmKm, bars.full(s), 0, krow, xb);
+        tl->issued = j + 1;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- UMMA issuer
+      constexpr uint32_t idesc_s = idesc_tf32(TILE, BLK, false, false);
+      constexpr uint32_t idesc_g = idesc_tf32(TILE, HD, false, true);
+      bool ok = mbar_wait(bars.tile_full(), 0, p.err, kErrWaitFull);
+      if (ok) tl->tile_pending = 0;
+      ok = ok && mbar_wait(bars.opnd_ready(), 0, p.err, kErrWaitAccum);
+      auto issue_s = [&](int j) -> bool {
+        const int s = j % STAGES, bb = j & 1, u = j >> 1;
+        if (!mbar_wait(bars.full(s), (j / STAGES) & 1, p.err, kErrWaitFull)) return false;
+        tl->consumed = j + 1;
+        if (u > 0 && !mbar_wait(bars.s_free(bb), (u - 1) & 1, p.err, kErrWaitAccum)) return false;
+        tc_fence_after();
+        const uint32_t st = stage(s);
+#pragma unroll
+        for (int kk = 0; kk < HD / 8; ++kk)  // S = Q K^T
+          umma_tf32(tmem + s_col(bb), kmajor_desc(sQ, TILE, kk), kmajor_desc(st, BLK, kk), idesc_s,
+                    kk > 0 ? 1u : 0u);
+#pragma unroll
+        for (int kk = 0; kk < HD / 8; ++kk)  // dP = dO V^T, dO in TMEM
+          umma_tf32_ts(tmem + dp_col(bb), tmem + Cfg::OPND_COL + kk * 8, kmajor_desc(st + BB, BLK, kk), idesc_s,
+                       kk > 0 ? 1u : 0u);
+        umma_commit(bars.s_full(bb));
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      for (int j = 0; ok && j < n_kv; ++j) {
+        if (j + 1 < n_kv && !issue_s(j + 1)) break;
+        const int s = j % STAGES, bb = j & 1;
+        if (!mbar_wait(bars.p_full(bb), (j >> 1) & 1, p.err, kErrWaitAccum)) break;
+        tc_fence_after();
+        const uint32_t st = stage(s);
+#pragma unroll
+        for (int kk = 0; kk < BLK / 8; ++kk)  // dQ += dS K
+          umma_tf32_ts(tmem + Cfg::ACC_COL, tmem + dp_col(bb) + kk * 8, mnmajor_desc(st + 2 * BB, kk), idesc_g,
+                       (j > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(bars.empty(s));
+        umma_commit(bars.s_free(bb));
+      }
+      umma_commit(bars.acc_done());
+    }
+  } else {
+    // ---------------- dO into TMEM, softmax gradient, epilogue (lane = query)
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const int q = q0 + row;
+    const bool q_ok = q < p.T;
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    row_to_tmem<HD>(p.tm_src + static_cast<long long>(row0 + q) * p.ld_in + static_cast<long long>(h) * HD, q_ok,
+                    tmem + lane_base + Cfg::OPND_COL);
+    const long long li = static_cast<long long>(bh) * p.T + q;
+    const float lse2 = q_ok ? p.lse[li] * kLog2e : 0.0f;
+    const float dlt = q_ok ? p.delta[li] : 0.0f;
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bars.opnd_ready());
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      const int bb = j & 1;
+      if (!mbar_wait(bars.s_full(bb), (j >> 1) & 1, p.err, kErrWaitAccum)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t sv[32], dv[32];
+      tmem_ld_32x32b_x32(tmem + lane_base + s_col(bb), sv);
+      tmem_ld_32x32b_x32(tmem + lane_base + dp_col(bb), dv);
+      const int kb = j * BLK;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const bool keep = q_ok && kb + i <= q;
+        const float pv = keep ? ex2_approx(fmaf(__uint_as_float(sv[i]), p.scale_log2, -lse2)) : 0.0f;
+        dv[i] = __float_as_uint(pv * (__uint_as_float(dv[i]) - dlt) * p.scale);
+      }
+      tmem_st_32x32b_x32(tmem + lane_base + dp_col(bb), dv);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bars.p_full(bb));
+    }
+    if (ok && mbar_wait(bars.acc_done(), 0, p.err, kErrWaitAccum)) {
+      tc_fence_after();
+      tmem_to_row<HD>(tmem + lane_base + Cfg::ACC_COL,
+                      p.out + static_cast<long long>(row0 + q) * p.ld_out + static_cast<long long>(h) * HD, q_ok,
+                      1.0f);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0) drain(bars, tl, p.err);
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, Cfg::TMEM_COLS);
+  }
+  __syncthreads();
+}
+
+bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
+
+// Token-major operand [rows, ld]: 3-D view (32 columns, token row, 32-column
+// block) whose box brings `box_rows` rows of one head as hd/32 chunks.
+void head_map(CUtensorMap* map, const float* ptr, long long rows, long long ld, int heads, int hd, int box_rows,
+              bool mn_major) {
+  const long long dims[3] = {32, rows, static_cast<long long>(heads) * hd / 32};
+  const long long strides[2] = {ld, 32};
+  const int box[3] = {32, box_rows, hd / 32};
+  if (encode_tensor_map(map, ptr, 3, dims, strides, box, mn_major))
+    throw std::runtime_error("flash attention backward: tensor map rejected");
+}
+
+template <class K>
+void set_smem(K kern, int bytes) {
+  const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess)
+    throw std::runtime_error(std::string("flash attention backward: shared memory size: ") + cudaGetErrorString(e));
+}
+
+// At least this much dynamic shared memory, so that one CTA (holding all 512
+// TMEM columns) runs per SM and no second CTA waits in tcgen05.alloc.
+constexpr int kMinSmem = 120 * 1024;
+
+template <int HD>
+void launch_bwd(const AttnShape& s, const float* q, const float* k, const float* v, const float* lse,
+                const float* dout, long long lddo, float* dq, float* dk, float* dv, const float* delta, int* d_err,
+                cudaStream_t stream) {
+  using Cfg = BwdCfg<HD>;
+  const long long rows = static_cast<long long>(s.B) * s.T;
+  const int n_tiles = (s.T + TILE - 1) / TILE;
+  BwdParams p{};
+  p.T = s.T;
+  p.H = s.H;
+  p.Hkv = s.Hkv;
+  p.G = s.H / s.Hkv;
+  p.n_tiles = n_tiles;
+  p.lse = lse;
+  p.delta = delta;
+  p.scale = s.scale;
+  p.scale_log2 = s.scale * kLog2e;
+  p.err = d_err;
+
+  {  // dK, dV
+    CUtensorMap tk, tqk, tdok, tqm, tdom;
+    head_map(&tk, k, rows, s.ldk, s.Hkv, HD, TILE, false);
+    head_map(&tqk, q, rows, s.ldq, s.H, HD, BLK, false);
+    head_map(&tdok, dout, rows, lddo, s.H, HD, BLK, false);
+    head_map(&tqm, q, rows, s.ldq, s.H, HD, BLK, true);
+    head_map(&tdom, dout, rows, lddo, s.H, HD, BLK, true);
+    BwdParams pk = p;
+    pk.BHx = s.B * s.Hkv;
+    pk.ld_in = s.ldv;
+    pk.tm_src = v;
+    pk.out = dk;
+    pk.ld_out = s.ldk;
+    pk.out2 = dv;
+    pk.ld_out2 = s.ldv;
+    const int smem = Cfg::KV_SMEM > kMinSmem ? Cfg::KV_SMEM : kMinSmem;
+    set_smem(flash_bwd_kv_kernel<HD>, smem);
+    const long long grid = static_cast<long long>(n_tiles) * pk.BHx;
+    flash_bwd_kv_kernel<HD><<<static_cast<unsigned>(grid), BTHREADS, smem, stream>>>(tk, tqk, tdok, tqm, tdom, pk);
+  }
+  {  // dQ
+    CUtensorMap tq, tkk, tvk, tkm;
+    head_map(&tq, q, rows, s.ldq, s.H, HD, TILE, false);
+    head_map(&tkk, k, rows, s.ldk, s.Hkv, HD, BLK, false);
+    head_map(&tvk, v, rows, s.ldv, s.Hkv, HD, BLK, false);
+    head_map(&tkm, k, rows, s.ldk, s.Hkv, HD, BLK, true);
+    BwdParams pq = p;
+    pq.BHx = s.B * s.H;
+    pq.ld_in = lddo;
+    pq.tm_src = dout;
+    pq.out = dq;
+    pq.ld_out = s.ldq;
+    const int smem = Cfg::Q_SMEM > kMinSmem ? Cfg::Q_SMEM : kMinSmem;
+    set_smem(flash_bwd_q_kernel<HD>, smem);
+    const long long grid = static_cast<long long>(n_tiles) * pq.BHx;
+    flash_bwd_q_kernel<HD><<<static_cast<unsigned>(grid), BTHREADS, smem, stream>>>(tq, tkk, tvk, tkm, pq);
+  }
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess)
+    throw std::runtime_error(std::string("flash attention backward launch: ") + cudaGetErrorString(e));
+}
+
+}  // namespace
+
+void attention_backward_flash(const AttnShape& s, const float* q, const float* k, const float* v, const float* o,
+                              const float* lse, const float* dout, long long lddo, float* dq, float* dk, float* dv,
+                              float* delta, int* d_err, cudaStream_t stream) {
+  if (!attention_flash_supported(s) || lddo % 4 != 0 || !aligned16(q) || !aligned16(k) || !aligned16(v) ||
+      !aligned16(dout) || !aligned16(dq) || !aligned16(dk) || !aligned16(dv))
+    throw std::runtime_error("flash attention backward: unsupported head_dim, stride or alignment");
+  attention_delta(s, o, dout, lddo, delta, stream);
+  switch (s.hd) {
+    case 32: launch_bwd<32>(s, q, k, v, lse, dout, lddo, dq, dk, dv, delta, d_err, stream); break;
+    case 64: launch_bwd<64>(s, q, k, v, lse, dout, lddo, dq, dk, dv, delta, d_err, stream); break;
+    default: launch_bwd<128>(s, q, k, v, lse, dout, lddo, dq, dk, dv, delta, d_err, stream); break;
+  }
+}
+
+}  // namespace mm

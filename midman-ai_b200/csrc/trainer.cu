@@ -141,12 +141,8 @@ Trainer::Trainer(const ModelConfig& cfg, int batch, int seq, int precision, int 
     const AttnShape shape{batch, seq, static_cast<int>(H), static_cast<int>(cfg.n_kv_heads), hd,
                           static_cast<long long>(D), static_cast<long long>(KV), static_cast<long long>(KV),
                           static_cast<long long>(D), 1.0f};
-    attn_tc_ = precision == kPrecisionTF32 && attention_tc_supported(shape);
-    if (attn_tc_) {
-      const uint64_t sz = static_cast<uint64_t>(batch) * H * seq * attention_scores_ld(seq);
-      scores_ = falloc(sz);
-      dscores_ = falloc(sz);
-    }
+    // TF32: fused tensor-core attention (no score buffers); 3xTF32: FP32 flash kernels
+    attn_tc_ = precision == kPrecisionTF32 && attention_flash_supported(shape);
   }
   check_cuda(cudaDeviceSynchronize(), "trainer setup");
 }

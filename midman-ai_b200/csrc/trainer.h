@@ -137,7 +137,6 @@ class Trainer {
 
   // Attention on the tensor cores (TF32 mode, head_dim 32/64/128): score buffers.
   bool attn_tc_ = false;
-  float *scores_ = nullptr, *dscores_ = nullptr;
 
   bool profiling_ = false;
   std::vector<cudaEvent_t> prof_events_;

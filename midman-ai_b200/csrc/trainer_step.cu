@@ -112,8 +112,8 @@ void Trainer::backward(int B, int T) {
     gemm(D, D, N, a.o, D, true, dh, D, true, G_ + bo.o, D, nullptr, 0);
     int slot = prof_begin();
     if (attn_tc_)
-      attention_backward_tc(shape, a.q, a.k, a.v, a.o, a.lse, do_, D, dq_, dk_, dv_, delta_, scores_, dscores_, tmp_,
-                            stream_);
+      attention_backward_flash(shape, a.q, a.k, a.v, a.o, a.lse, do_, D, dq_, dk_, dv_, delta_, device_context().d_err,
+                               stream_);
     else
       attention_backward(shape, a.q, a.k, a.v, a.o, a.lse, do_, D, dq_, dk_, dv_, delta_, stream_);
     // dV, dP, dQ, dK: four causal products (the recomputed scores are not counted)
