@@ -246,6 +246,13 @@ def run_kernels(args):
     return 0
 
 
+def gemm_shapes(prof, steps, top=10):
+    """The slowest GEMM shapes of the profiled steps: [shape "MxNxK AB", launches/step, ms/step, TFLOP/s]."""
+    rows = sorted(prof.items(), key=lambda kv: -kv[1]["ms"])[:top]
+    return [[k, v["launches"] // steps, round(v["ms"] / steps, 3), round(v["flops"] / (v["ms"] * 1e-3) / 1e12, 1)]
+            for k, v in rows if v["ms"] > 0]
+
+
 def run_reference(args, cfg, B, T, world, rank):
     if rank != 0:
         return 0
@@ -402,6 +409,7 @@ def main():
                          "step_tflops": fpt * B * T * args.steps / (ms * 1e-3) / 1e12 / world,
                          "step_frac": fpt * B * T * args.steps / (ms * 1e-3) / 1e12 / world / tf32,
                          "time_share": kernel_share,
+                         "gemm_shapes": gemm_shapes(desc.get("profile_gemm", {}), args.steps),
                          "measured": f"CUDA events around each launch in a second run of the same {args.steps} "
                                      f"steps ({prof_ms / args.steps:.2f} ms/step with the events)"},
             "e2e": {"value": e2e, "unit": "tokens/s", "h2d_bytes_per_step": int((5 * B * T + 1) * 4),

@@ -679,6 +679,15 @@ int32_t midman_train_describe(uint32_t handle) {
       w.end_object();
     }
     w.end_object();
+    w.key("profile_gemm").begin_object();
+    for (const auto& e : t.trainer->gemm_profile()) {
+      w.key(e.first).begin_object();
+      w.key("launches").integer(e.second.launches);
+      w.key("ms").number(e.second.ms);
+      w.key("flops").number(e.second.flops);
+      w.end_object();
+    }
+    w.end_object();
     w.key("tensors").begin_array();
     for (const TensorInfo& ti : L.tensors) {
       w.begin_object();

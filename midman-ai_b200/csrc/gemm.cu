@@ -50,7 +50,8 @@ struct Tile {
   static constexpr int B_STAGE_BYTES = BN * BK * 4;
   static constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
   static constexpr int STAGES = SMEM_BUDGET / STAGE_BYTES > 8 ? 8 : SMEM_BUDGET / STAGE_BYTES;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers, slot, counters*/;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers, slot, counters*/ +
+                                    4 * 32 * 32 * 4 /*epilogue staging, one 32x32 tile per epilogue warp*/;
 };
 
 // Byte offset of the 4 KB block that holds MN columns [32j, 32j+32) of an
@@ -248,6 +249,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else {
     // ---------------- epilogue: warps 2..5 cover TMEM lane quarters (warp % 4)
     const int quarter = warp & 3;
+    float4* stage_tile = reinterpret_cast<float4*>(smem + STAGES * STAGE_BYTES + 256) + quarter * 256;
     int j = 0;
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
       const TileInfo ti = tile_info<BN, BATCHED>(t, M, N, K, bt);
@@ -257,43 +259,82 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc_fence_after();
       float* Ct = C;
       if (BATCHED) Ct += (ti.z / bt.c_zdiv) * bt.c_sb + ((ti.z % bt.c_zdiv) / bt.c_zgroup) * bt.c_sh;
-      const int row = ti.m0 + quarter * 32 + lane;
+      const int wrow0 = ti.m0 + quarter * 32;  // this warp's 32 rows
+      bool released = false;
       if (ti.n_k > 0) {
+        // Each 32-column slice goes TMEM -> registers (lane = row) -> this warp's
+        // staging tile -> global with 8 lanes per row, so every R load and C
+        // store instruction covers four whole 128-byte row segments. The
+        // residual of slice c + 1 is loaded before slice c is stored (slices
+        // are disjoint, so this holds when R aliases C).
+        const int sub = lane & 7, rsub = lane >> 3;
+        float4 rnext[8];
+        auto load_r = [&](int c) {
+          const int col = ti.n0 + c * 32 + 4 * sub;
+#pragma unroll
+          for (int it = 0; it < 8; ++it) {
+            const int row = wrow0 + it * 4 + rsub;
+            rnext[it] = (col + 3 < N && row < M)
+                            ? *reinterpret_cast<const float4*>(R + static_cast<long long>(row) * ldr + col)
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+        };
+        if (R) load_r(0);
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
           uint32_t r[32];
           tmem_ld_32x32b_x32(tmem_base + buf * BN + (static_cast<uint32_t>(quarter * 32) << 16) + c * 32, r);
-          const int col0 = ti.n0 + c * 32;
-          if (row < M && col0 < N) {
-            float* crow = Ct + static_cast<long long>(row) * ldc;
-            const float* rrow = R ? R + static_cast<long long>(row) * ldr : nullptr;
+          if (c == BN / 32 - 1) {  // the accumulator is free for the tile after next
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acc_empty(buf));
+            released = true;
+          }
+          // 4-float granules, XOR-swizzled by row: conflict-free both ways
 #pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              const int col = col0 + 4 * q;
-              float4 v = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
-                                     __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]));
-              if (col + 3 < N) {
-                if (rrow) {
-                  const float4 a = *reinterpret_cast<const float4*>(rrow + col);
-                  v.x += a.x; v.y += a.y; v.z += a.z; v.w += a.w;
-                }
-                *reinterpret_cast<float4*>(crow + col) = v;
-              } else {
-                const float vv[4] = {v.x, v.y, v.z, v.w};
-                for (int e = 0; e < 4 && col + e < N; ++e) crow[col + e] = vv[e] + (rrow ? rrow[col + e] : 0.0f);
-              }
+          for (int g = 0; g < 8; ++g)
+            stage_tile[lane * 8 + (g ^ (lane & 7))] =
+                make_float4(__uint_as_float(r[4 * g]), __uint_as_float(r[4 * g + 1]), __uint_as_float(r[4 * g + 2]),
+                            __uint_as_float(r[4 * g + 3]));
+          __syncwarp();
+          float4 v[8];
+#pragma unroll
+          for (int it = 0; it < 8; ++it) {
+            const int rr = it * 4 + rsub;
+            v[it] = stage_tile[rr * 8 + (sub ^ (rr & 7))];
+            if (R) {
+              v[it].x += rnext[it].x; v[it].y += rnext[it].y; v[it].z += rnext[it].z; v[it].w += rnext[it].w;
             }
           }
+          if (R && c + 1 < BN / 32) load_r(c + 1);
+          const int col = ti.n0 + c * 32 + 4 * sub;
+#pragma unroll
+          for (int it = 0; it < 8; ++it) {
+            const int row = wrow0 + it * 4 + rsub;
+            if (row >= M || col >= N) continue;
+            float* cp = Ct + static_cast<long long>(row) * ldc + col;
+            if (col + 3 < N) {
+              *reinterpret_cast<float4*>(cp) = v[it];
+            } else {  // ragged right edge: the residual was not prefetched
+              const float* rp = R ? R + static_cast<long long>(row) * ldr + col : nullptr;
+              const float vv[4] = {v[it].x, v[it].y, v[it].z, v[it].w};
+              for (int e = 0; e < 4 && col + e < N; ++e) cp[e] = vv[e] + (rp ? rp[e] : 0.0f);
+            }
+          }
+          __syncwarp();  // before the next slice overwrites the staging tile
         }
-      } else if (row < M) {
+      } else {
         // Empty K range: the product is zero, C = R (or 0).
-        for (int col = ti.n0; col < ti.n0 + BN && col < N; ++col)
-          Ct[static_cast<long long>(row) * ldc + col] = R ? R[static_cast<long long>(row) * ldr + col] : 0.0f;
+        const int row = wrow0 + lane;
+        if (row < M)
+          for (int col = ti.n0; col < ti.n0 + BN && col < N; ++col)
+            Ct[static_cast<long long>(row) * ldc + col] = R ? R[static_cast<long long>(row) * ldr + col] : 0.0f;
       }
-      // this warp's reads of the accumulator are complete (tcgen05.wait::ld)
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(acc_empty(buf));
+      if (!released) {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(acc_empty(buf));
+      }
       ++j;
     }
   }
@@ -385,6 +426,17 @@ int make_map_mn3d(CUtensorMap* map, const float* ptr, long long mn, long long k,
   return encode(map, ptr, 3, dims, strides, box, true);
 }
 
+int device_sms() {
+  static thread_local int sms = 0, sms_device = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (sms_device != dev) {
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    sms_device = dev;
+  }
+  return sms;
+}
+
 template <bool A_MN, bool B_MN, int BN, bool BATCHED>
 void launch(const CUtensorMap& ta, const CUtensorMap& tb, float* C, long long ldc, const float* R, long long ldr,
             int M, int N, int K, int batch, const GemmBatch& bt, int* err, cudaStream_t stream, int mn3d) {
@@ -398,11 +450,7 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, float* C, long long ld
     configured_device = dev;
   }
   const long long tiles = static_cast<long long>((M + BM - 1) / BM) * ((N + BN - 1) / BN) * batch;
-  static thread_local int sms = 0, sms_device = -1;
-  if (sms_device != dev) {
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    sms_device = dev;
-  }
+  const int sms = device_sms();
   const int grid = static_cast<int>(tiles < sms ? tiles : sms);
   kern<<<grid, THREADS, TL::SMEM_BYTES, stream>>>(ta, tb, C, ldc, R, ldr, M, N, K, err, bt, static_cast<int>(tiles), mn3d);
 }
@@ -438,8 +486,10 @@ int gemm_tf32(int M, int N, int K, GemmOperand A, GemmOperand B, float* C, long 
   if (M == 0 || N == 0) return 0;
   if (K > 0 && (!A.ptr || !B.ptr)) return kGemmBadArgument;
   if ((ldc & 3) || !aligned16(C) || (R && ((ldr & 3) || !aligned16(R)))) return kGemmMisaligned;
-  // Narrow outputs waste less of a 256-wide tile with a 128-wide one.
-  const int bn = N <= 128 ? 128 : 256;
+  // Narrow outputs waste less of a 256-wide tile with a 128-wide one, and so do
+  // products whose 256-wide tiles would leave half of the SMs idle.
+  const long long tiles256 = static_cast<long long>((M + BM - 1) / BM) * ((N + 255) / 256);
+  const int bn = (N <= 128 || 2 * tiles256 <= device_sms()) ? 128 : 256;
   CUtensorMap ta{}, tb{};
   int mn3d = 0;
   if (K > 0) {

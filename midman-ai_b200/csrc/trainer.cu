@@ -237,6 +237,7 @@ void Trainer::upload_batch(const int32_t* inputs, const int32_t* targets, int B,
 void Trainer::set_profile(bool on) {
   profiling_ = on;
   profile_.clear();
+  gemm_profile_.clear();
   pending_.clear();
   prof_next_ = 0;
 }
@@ -254,27 +255,35 @@ int Trainer::prof_begin() {
   return slot;
 }
 
-void Trainer::prof_end(int slot, const char* cls, double flops) {
+void Trainer::prof_end(int slot, const char* cls, double flops, std::string shape) {
   if (slot < 0) return;
   check_cuda(cudaEventRecord(prof_events_[slot + 1], stream_), "profile event");
-  pending_.push_back({slot, cls, flops});
+  pending_.push_back({slot, cls, flops, std::move(shape)});
 }
+
+namespace {
+void accumulate(std::vector<std::pair<std::string, Trainer::ProfileEntry>>& v, const std::string& key, float ms,
+                double flops) {
+  auto it = v.begin();
+  for (; it != v.end(); ++it)
+    if (it->first == key) break;
+  if (it == v.end()) {
+    v.push_back({key, Trainer::ProfileEntry{}});
+    it = v.end() - 1;
+  }
+  it->second.launches += 1;
+  it->second.ms += ms;
+  it->second.flops += flops;
+}
+}  // namespace
 
 // Called after the stream has synchronized.
 void Trainer::prof_collect() {
   for (const Pending& p : pending_) {
     float ms = 0.0f;
     check_cuda(cudaEventElapsedTime(&ms, prof_events_[p.slot], prof_events_[p.slot + 1]), "profile elapsed");
-    auto it = profile_.begin();
-    for (; it != profile_.end(); ++it)
-      if (it->first == p.cls) break;
-    if (it == profile_.end()) {
-      profile_.push_back({p.cls, ProfileEntry{}});
-      it = profile_.end() - 1;
-    }
-    it->second.launches += 1;
-    it->second.ms += ms;
-    it->second.flops += p.flops;
+    accumulate(profile_, p.cls, ms, p.flops);
+    if (!p.shape.empty()) accumulate(gemm_profile_, p.shape, ms, p.flops);
   }
   pending_.clear();
   prof_next_ = 0;
@@ -289,7 +298,10 @@ void Trainer::gemm(int M, int N, int K, const float* A, long long lda, bool a_mn
                                               : gemm_3xtf32(M, N, K, a, b, C, ldc, R, ldr, ctx.d_err, stream_);
   if (rc) throw std::runtime_error(std::string("GEMM: ") + gemm_status_string(rc));
   launches_ += precision_ == kPrecisionTF32 ? 1 : 5;
-  prof_end(slot, precision_ == kPrecisionTF32 ? "gemm_tf32" : "gemm_3xtf32", 2.0 * M * N * K);
+  if (slot >= 0)
+    prof_end(slot, precision_ == kPrecisionTF32 ? "gemm_tf32" : "gemm_3xtf32", 2.0 * M * N * K,
+             std::to_string(M) + "x" + std::to_string(N) + "x" + std::to_string(K) + (a_mn ? " M" : " K") +
+                 (b_mn ? "M" : "K"));
 }
 
 void Trainer::check_device(const char* where) {

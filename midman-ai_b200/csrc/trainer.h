@@ -82,6 +82,8 @@ class Trainer {
   };
   void set_profile(bool on);
   const std::vector<std::pair<std::string, ProfileEntry>>& profile() const { return profile_; }
+  // The GEMM class split by shape and operand majors ("MxNxK AB").
+  const std::vector<std::pair<std::string, ProfileEntry>>& gemm_profile() const { return gemm_profile_; }
 
  private:
   void forward(int B, int T, bool train);
@@ -94,7 +96,7 @@ class Trainer {
   void allreduce_grads_range(uint64_t offset, uint64_t n);
   void check_device(const char* where);
   int prof_begin();
-  void prof_end(int slot, const char* cls, double flops);
+  void prof_end(int slot, const char* cls, double flops, std::string shape = {});
   void prof_collect();
 
   ModelConfig cfg_;
@@ -144,7 +146,9 @@ class Trainer {
     int slot;
     std::string cls;
     double flops;
+    std::string shape;  // GEMMs: "MxNxK AB" (A/B: K = K-major, M = MN-major)
   };
+  std::vector<std::pair<std::string, ProfileEntry>> gemm_profile_;
   std::vector<Pending> pending_;
   int prof_next_ = 0;
   std::vector<std::pair<std::string, ProfileEntry>> profile_;
