@@ -43,7 +43,7 @@ namespace {
 
 constexpr int TILE = 128;  // lanes: keys (kv kernel) or queries (q kernel)
 constexpr int BLK = 32;    // streamed queries (kv kernel) or keys (q kernel) per step
-constexpr int BTHREADS = 192;
+constexpr int BTHREADS = 320;  // producer, UMMA issuer, two softmax warpgroups
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct BwdParams {
@@ -84,8 +84,10 @@ struct BwdCfg {
   static_assert(ACC2_COL + HD <= TMEM_COLS, "TMEM budget");
 };
 
-__device__ __forceinline__ uint32_t s_col(int bb) { return bb * 2 * BLK; }       // S / P
-__device__ __forceinline__ uint32_t dp_col(int bb) { return bb * 2 * BLK + BLK; } // dP / dS
+__device__ __forceinline__ uint32_t s_col_of(int bb, int blk) { return bb * 2 * blk; }         // S / P
+__device__ __forceinline__ uint32_t dp_col_of(int bb, int blk) { return bb * 2 * blk + blk; }  // dP / dS
+__device__ __forceinline__ uint32_t s_col(int bb) { return s_col_of(bb, BLK); }
+__device__ __forceinline__ uint32_t dp_col(int bb) { return dp_col_of(bb, BLK); }
 
 // Barrier block shared by both kernels (offsets in 8-byte slots).
 template <int STAGES>
@@ -111,7 +113,7 @@ struct Bars {
       mbar_init(p_full(bb), 4);
       mbar_init(s_free(bb), 1);
     }
-    mbar_init(opnd_ready(), 4);
+    mbar_init(opnd_ready(), 8);  // every softmax warp
     mbar_init(acc_done(), 1);
   }
 };
@@ -127,12 +129,12 @@ __device__ __forceinline__ uint64_t mnmajor_desc(uint32_t tile, int kk) {
   return smem_desc(tile + kk * 1024, BLK * 128, 512, kLayoutSw128Base32);
 }
 
-// Copies row `row` (HD floats at src, or zeros when !valid) into TMEM columns
-// [col, col + HD) of this thread's lane.
+// Copies 32-column chunks c0, c0 + 2, ... of a row (HD floats at src, or zeros
+// when !valid) into the same TMEM columns of this thread's lane.
 template <int HD>
-__device__ __forceinline__ void row_to_tmem(const float* src, bool valid, uint32_t taddr) {
+__device__ __forceinline__ void row_to_tmem(const float* src, bool valid, uint32_t taddr, int c0) {
 #pragma unroll 1
-  for (int c = 0; c < HD / 32; ++c) {
+  for (int c = c0; c < HD / 32; c += 2) {
     uint32_t r[32];
 #pragma unroll
     for (int i = 0; i < 32; i += 4) {
@@ -146,11 +148,13 @@ __device__ __forceinline__ void row_to_tmem(const float* src, bool valid, uint32
   }
 }
 
-// Writes TMEM columns [col, col + HD) of this thread's lane, times `mul`, to dst.
+// Writes 32-column chunks c0, c0 + step, ... of this thread's TMEM lane, times
+// `mul`, to the same columns of dst.
 template <int HD>
-__device__ __forceinline__ void tmem_to_row(uint32_t taddr, float* dst, bool valid, float mul) {
+__device__ __forceinline__ void tmem_to_row(uint32_t taddr, float* dst, bool valid, float mul, int c0 = 0,
+                                            int step = 1) {
 #pragma unroll 1
-  for (int c = 0; c < HD / 32; ++c) {
+  for (int c = c0; c < HD / 32; c += step) {
     uint32_t r[32];
     tmem_ld_32x32b_x32(taddr + c * 32, r);
     if (valid) {
@@ -187,8 +191,8 @@ struct Tail {
   int issued, consumed, tile_pending;
 };
 
-template <int STAGES>
-__device__ __forceinline__ void drain(const Bars<STAGES>& bars, Tail* tl, int* err) {
+template <int STAGES, class B>
+__device__ __forceinline__ void drain(const B& bars, Tail* tl, int* err) {
   if (tl->tile_pending) mbar_wait(bars.tile_full(), 0, err, kErrWaitDrain, 1000000000ull);
   for (int t = tl->consumed; t < tl->issued; ++t)
     if (!mbar_wait(bars.full(t % STAGES), (t / STAGES) & 1, err, kErrWaitDrain, 1000000000ull)) break;
@@ -309,20 +313,23 @@ __global__ void __launch_bounds__(BTHREADS, 1)
       umma_commit(bars.acc_done());
     }
   } else {
-    // ---------------- V into TMEM, softmax gradient, epilogue (lane = key)
+    // ---------------- V into TMEM, softmax gradient, epilogue (lane = key).
+    // Steps carry no state from one to the next, so warpgroup grp (warps 2-5,
+    // 6-9) takes the steps t = grp mod 2, which use S/dP buffer grp.
+    const int grp = (warp - 2) >> 2;
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     const int key = k0 + row;
     const bool key_ok = key < p.T;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     row_to_tmem<HD>(p.tm_src + static_cast<long long>(row0 + key) * p.ld_in + static_cast<long long>(hk) * HD,
-                    key_ok, tmem + lane_base + Cfg::OPND_COL);
+                    key_ok, tmem + lane_base + Cfg::OPND_COL, grp);
     tc_fence_before();
     __syncwarp();
     if (lane == 0) mbar_arrive(bars.opnd_ready());
     bool ok = true;
-    for (int t = 0; t < n_steps; ++t) {
-      const int bb = t & 1;
+    for (int t = grp; t < n_steps; t += 2) {
+      const int bb = grp;
       const int h = hk * p.G + t / n_q;
       const int qs = k0 + (t % n_q) * BLK;
       const long long lrow = (static_cast<long long>(b) * p.H + h) * p.T;
@@ -354,16 +361,18 @@ __global__ void __launch_bounds__(BTHREADS, 1)
     if (ok && mbar_wait(bars.acc_done(), 0, p.err, kErrWaitAccum)) {
       tc_fence_after();
       const long long r = row0 + key;
-      tmem_to_row<HD>(tmem + lane_base + Cfg::ACC_COL, p.out2 + r * p.ld_out2 + static_cast<long long>(hk) * HD,
-                      key_ok, 1.0f);
-      tmem_to_row<HD>(tmem + lane_base + Cfg::ACC2_COL, p.out + r * p.ld_out + static_cast<long long>(hk) * HD,
-                      key_ok, 1.0f);
+      if (grp == 0)
+        tmem_to_row<HD>(tmem + lane_base + Cfg::ACC_COL, p.out2 + r * p.ld_out2 + static_cast<long long>(hk) * HD,
+                        key_ok, 1.0f);
+      else
+        tmem_to_row<HD>(tmem + lane_base + Cfg::ACC2_COL, p.out + r * p.ld_out + static_cast<long long>(hk) * HD,
+                        key_ok, 1.0f);
     }
   }
 
   tc_fence_before();
   __syncthreads();
-  if (threadIdx.x == 0) drain(bars, tl, p.err);
+  if (threadIdx.x == 0) drain<STAGES>(bars, tl, p.err);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, Cfg::TMEM_COLS);
@@ -478,14 +487,16 @@ __global__ void __launch_bounds__(BTHREADS, 1)
       umma_commit(bars.acc_done());
     }
   } else {
-    // ---------------- dO into TMEM, softmax gradient, epilogue (lane = query)
+    // ---------------- dO into TMEM, softmax gradient, epilogue (lane = query);
+    // warpgroup grp takes the key blocks j = grp mod 2 (S/dP buffer grp)
+    const int grp = (warp - 2) >> 2;
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     const int q = q0 + row;
     const bool q_ok = q < p.T;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
     row_to_tmem<HD>(p.tm_src + static_cast<long long>(row0 + q) * p.ld_in + static_cast<long long>(h) * HD, q_ok,
-                    tmem + lane_base + Cfg::OPND_COL);
+                    tmem + lane_base + Cfg::OPND_COL, grp);
     const long long li = static_cast<long long>(bh) * p.T + q;
     const float lse2 = q_ok ? p.lse[li] * kLog2e : 0.0f;
     const float dlt = q_ok ? p.delta[li] : 0.0f;
@@ -493,8 +504,8 @@ __global__ void __launch_bounds__(BTHREADS, 1)
     __syncwarp();
     if (lane == 0) mbar_arrive(bars.opnd_ready());
     bool ok = true;
-    for (int j = 0; j < n_kv; ++j) {
-      const int bb = j & 1;
+    for (int j = grp; j < n_kv; j += 2) {
+      const int bb = grp;
       if (!mbar_wait(bars.s_full(bb), (j >> 1) & 1, p.err, kErrWaitAccum)) {
         ok = false;
         break;
@@ -519,13 +530,13 @@ __global__ void __launch_bounds__(BTHREADS, 1)
       tc_fence_after();
       tmem_to_row<HD>(tmem + lane_base + Cfg::ACC_COL,
                       p.out + static_cast<long long>(row0 + q) * p.ld_out + static_cast<long long>(h) * HD, q_ok,
-                      1.0f);
+                      1.0f, grp, 2);
     }
   }
 
   tc_fence_before();
   __syncthreads();
-  if (threadIdx.x == 0) drain(bars, tl, p.err);
+  if (threadIdx.x == 0) drain<STAGES>(bars, tl, p.err);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, Cfg::TMEM_COLS);
@@ -533,15 +544,446 @@ __global__ void __launch_bounds__(BTHREADS, 1)
   __syncthreads();
 }
 
+// ------------------------------------------------------------------ CTA pairs
+// The same two kernels with a cluster of two CTAs per 256-row tile (keys for
+// dK/dV, queries for dQ). The leader issues every UMMA with M = 256
+// (cta_group::2); the streamed operand of every product is split between the
+// pair (half of its rows for the K-major use, half of the hd columns for the
+// MN-major use), so the pair reads each streamed block from L2 once.
+constexpr int PBLK_KV = 32;  // queries per step of the dK/dV pair kernel (UMMA N; 16 rows per CTA)
+constexpr int PBLK_Q = 64;   // keys per step of the dQ pair kernel (UMMA N; 32 rows per CTA)
+
+template <int HD>
+struct PairBwdCfg {
+  static constexpr int TILE_BYTES = TILE * HD * 4;
+  static constexpr int KV_HALF_K = (PBLK_KV / 2) * HD * 4;  // Q or dO rows, K-major
+  static constexpr int KV_HALF_M = PBLK_KV * (HD / 2) * 4;  // Q or dO hd/2 columns, MN-major
+  static constexpr int KV_STAGE = 2 * KV_HALF_K + 2 * KV_HALF_M;
+  static constexpr int Q_HALF_K = (PBLK_Q / 2) * HD * 4;    // K or V rows, K-major
+  static constexpr int Q_HALF_M = PBLK_Q * (HD / 2) * 4;    // K hd/2 columns, MN-major
+  static constexpr int Q_STAGE = 2 * Q_HALF_K + Q_HALF_M;
+  static constexpr int KV_FIT = (210 * 1024 - TILE_BYTES) / KV_STAGE;
+  static constexpr int Q_FIT = (210 * 1024 - TILE_BYTES) / Q_STAGE;
+  static constexpr int KV_STAGES = KV_FIT > 4 ? 4 : KV_FIT;
+  static constexpr int Q_STAGES = Q_FIT > 4 ? 4 : Q_FIT;
+  static constexpr int KV_SMEM = TILE_BYTES + KV_STAGES * KV_STAGE + 1024 + 256;
+  static constexpr int Q_SMEM = TILE_BYTES + Q_STAGES * Q_STAGE + 1024 + 256;
+  // TMEM: S (or P) and dP (or dS) buffers, two of each, then the TMEM operand
+  // (V or dO) and the accumulators
+  static constexpr uint32_t KV_OPND = 4 * PBLK_KV, KV_DV = KV_OPND + HD, KV_DK = KV_DV + HD;
+  static constexpr uint32_t Q_OPND = 4 * PBLK_Q, Q_DQ = Q_OPND + HD;
+  static constexpr uint32_t TMEM_COLS = 512;
+  static_assert(KV_DK + HD <= TMEM_COLS && Q_DQ + HD <= TMEM_COLS, "TMEM budget");
+  static_assert(KV_STAGES >= 2 && Q_STAGES >= 2, "two stages");
+};
+
+// Barriers of a pair kernel. Those the UMMA issuer waits on are used in the
+// leader only; stage-empty, S-full and accumulator-done ones receive commits
+// multicast to both CTAs.
+template <int STAGES>
+struct PairBars {
+  uint32_t base;
+  __device__ uint32_t tile_full() const { return base; }
+  __device__ uint32_t full(int s) const { return base + 8u * (1 + s); }
+  __device__ uint32_t empty(int s) const { return base + 8u * (1 + STAGES + s); }
+  __device__ uint32_t s_full(int bb) const { return base + 8u * (1 + 2 * STAGES + bb); }
+  __device__ uint32_t p_full(int bb) const { return base + 8u * (3 + 2 * STAGES + bb); }
+  __device__ uint32_t s_free(int bb) const { return base + 8u * (5 + 2 * STAGES + bb); }
+  __device__ uint32_t opnd_ready() const { return base + 8u * (7 + 2 * STAGES); }
+  __device__ uint32_t acc_done() const { return base + 8u * (8 + 2 * STAGES); }
+  __device__ uint32_t slot() const { return base + 8u * (9 + 2 * STAGES); }
+  __device__ void init() const {
+    mbar_init(tile_full(), 1);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full(s), 1);
+      mbar_init(empty(s), 1);
+    }
+    for (int bb = 0; bb < 2; ++bb) {
+      mbar_init(s_full(bb), 1);
+      mbar_init(p_full(bb), 8);  // one warpgroup of each CTA
+      mbar_init(s_free(bb), 1);
+    }
+    mbar_init(opnd_ready(), 16);  // every softmax warp of both CTAs
+    mbar_init(acc_done(), 1);
+  }
+};
+
+// MN-major descriptor of step kk (8 rows) in a tile of `rows`-row 32-column blocks.
+__device__ __forceinline__ uint64_t mnmajor_desc_rows(uint32_t tile, int rows, int kk) {
+  return smem_desc(tile + kk * 1024, rows * 128, 512, kLayoutSw128Base32);
+}
+
+template <int STAGES>
+__device__ __forceinline__ void pair_teardown(bool leader, const PairBars<STAGES>& bars, Tail* tl, int* err,
+                                              int warp, uint32_t tmem) {
+  tc_fence_before();
+  cluster_sync();  // both CTAs are done with their TMEM and with each other's barriers
+  if (leader && threadIdx.x == 0) drain<STAGES>(bars, tl, err);
+  cluster_sync();  // the pair's copies in flight (after a timeout) have landed
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, 512);
+  }
+}
+
+// ---------------- dK, dV (pair of 128-key tiles)
+template <int HD>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(BTHREADS, 1)
+    flash_bwd_kv_pair_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmQk,
+                             const __grid_constant__ CUtensorMap tmDOk, const __grid_constant__ CUtensorMap tmQm,
+                             const __grid_constant__ CUtensorMap tmDOm, BwdParams p) {
+  using Cfg = PairBwdCfg<HD>;
+  constexpr int STAGES = Cfg::KV_STAGES;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = static_cast<int>(blockIdx.x) / 2;
+  const int kt = pair / p.BHx;  // low key tiles see the most queries: first
+  const int bhk = pair % p.BHx;
+  const int b = bhk / p.Hkv, hk = bhk % p.Hkv;
+  const int k0 = kt * 2 * TILE;
+  const int my_k0 = k0 + static_cast<int>(rank) * TILE;
+  const int row0 = b * p.T;
+  const int n_q = (p.T - k0 + PBLK_KV - 1) / PBLK_KV;
+  const int n_steps = p.G * n_q;
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  const uint32_t sK = base;
+  auto stage = [&](int s) { return base + Cfg::TILE_BYTES + s * Cfg::KV_STAGE; };
+  const PairBars<STAGES> bars{base + Cfg::TILE_BYTES + STAGES * Cfg::KV_STAGE};
+  Tail* tl = reinterpret_cast<Tail*>(smem_raw + (bars.slot() - raw_addr));
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmQk);
+    tma_prefetch_desc(&tmDOk);
+    tma_prefetch_desc(&tmQm);
+    tma_prefetch_desc(&tmDOm);
+    bars.init();
+    tl->issued = tl->consumed = tl->tile_pending = 0;
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(bars.slot(), Cfg::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem = tl->tmem;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer (both CTAs): completions land on the leader's barriers
+      if (leader) {
+        tl->tile_pending = 1;
+        mbar_arrive_expect_tx(bars.tile_full(), 2 * Cfg::TILE_BYTES);
+      }
+      tma_load_3d_pair(sK, &tmK, mapa_shared(bars.tile_full(), 0), 0, row0 + my_k0, hk * (HD / 32));
+      for (int t = 0; t < n_steps; ++t) {
+        const int s = t % STAGES, r = t / STAGES;
+        if (r > 0 && !mbar_wait(bars.empty(s), (r - 1) & 1, p.err, kErrWaitEmpty)) break;
+        if (leader) mbar_arrive_expect_tx(bars.full(s), 2 * Cfg::KV_STAGE);
+        const int h = hk * p.G + t / n_q;
+        const int qrow = row0 + k0 + (t % n_q) * PBLK_KV;  // rows past the sequence are masked
+        const int xb = h * (HD / 32);
+        const uint32_t st = stage(s);
+        const uint32_t fb = mapa_shared(bars.full(s), 0);
+        const int half = static_cast<int>(rank) * (PBLK_KV / 2);
+        tma_load_3d_pair(st, &tmQk, fb, 0, qrow + half, xb);
+        tma_load_3d_pair(st + Cfg::KV_HALF_K, &tmDOk, fb, 0, qrow + half, xb);
+        const int xm = xb + static_cast<int>(rank) * (HD / 64);
+        tma_load_3d_pair(st + 2 * Cfg::KV_HALF_K, &tmQm, fb, 0, qrow, xm);
+        tma_load_3d_pair(st + 2 * Cfg::KV_HALF_K + Cfg::KV_HALF_M, &tmDOm, fb, 0, qrow, xm);
+        tl->issued = t + 1;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ---------------- UMMA issuer (leader only), M = 256 keys across the pair
+      constexpr uint32_t idesc_s = idesc_tf32(2 * TILE, PBLK_KV, false, false);
+      constexpr uint32_t idesc_g = idesc_tf32(2 * TILE, HD, false, true);
+      bool ok = mbar_wait(bars.tile_full(), 0, p.err, kErrWaitFull);
+      if (ok) tl->tile_pending = 0;
+      ok = ok && mbar_wait_cluster(bars.opnd_ready(), 0, p.err, kErrWaitAccum);
+      auto issue_s = [&](int t) -> bool {
+        const int s = t % STAGES, bb = t & 1, u = t >> 1;
+        if (!mbar_wait(bars.full(s), (t / STAGES) & 1, p.err, kErrWaitFull)) return false;
+        tl->consumed = t + 1;
+        if (u > 0 && !mbar_wait(bars.s_free(bb), (u - 1) & 1, p.err, kErrWaitAccum)) return false;
+        tc_fence_after();
+        const uint32_t st = stage(s);
+#pragma unroll
+        for (int kk = 0; kk < HD / 8; ++kk)  // S^T = K Q^T
+          umma_tf32_pair(tmem + s_col_of(bb, PBLK_KV), kmajor_desc(sK, TILE, kk),
+                         kmajor_desc(st, PBLK_KV / 2, kk), idesc_s, kk > 0 ? 1u : 0u);
+#pragma unroll
+        for (int kk = 0; kk < HD / 8; ++kk)  // dP^T = V dO^T, V in TMEM
+          umma_tf32_ts_pair(tmem + dp_col_of(bb, PBLK_KV), tmem + Cfg::KV_OPND + kk * 8,
+                            kmajor_desc(st + Cfg::KV_HALF_K, PBLK_KV / 2, kk), idesc_s, kk > 0 ? 1u : 0u);
+        umma_commit_pair(bars.s_full(bb), 0x3);
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      for (int t = 0; ok && t < n_steps; ++t) {
+        if (t + 1 < n_steps && !issue_s(t + 1)) break;
+        const int s = t % STAGES, bb = t & 1;
+        if (!mbar_wait_cluster(bars.p_full(bb), (t >> 1) & 1, p.err, kErrWaitAccum)) break;
+        tc_fence_after();
+        const uint32_t st = stage(s);
+#pragma unroll
+        for (int kk = 0; kk < PBLK_KV / 8; ++kk) {
+          const uint32_t acc = (t > 0 || kk > 0) ? 1u : 0u;
+          umma_tf32_ts_pair(tmem + Cfg::KV_DV, tmem + s_col_of(bb, PBLK_KV) + kk * 8,
+                            mnmajor_desc_rows(st + 2 * Cfg::KV_HALF_K + Cfg::KV_HALF_M, PBLK_KV, kk), idesc_g,
+                            acc);  // dV += P dO
+          umma_tf32_ts_pair(tmem + Cfg::KV_DK, tmem + dp_col_of(bb, PBLK_KV) + kk * 8,
+                            mnmajor_desc_rows(st + 2 * Cfg::KV_HALF_K, PBLK_KV, kk), idesc_g, acc);  // dK += dS Q
+        }
+        umma_commit_pair(bars.empty(s), 0x3);
+        umma_commit_pair(bars.s_free(bb), 0x1);
+      }
+      umma_commit_pair(bars.acc_done(), 0x3);
+    }
+  } else {
+    // ---------------- V into TMEM, softmax gradient, epilogue (lane = key);
+    // warpgroup grp takes the steps t = grp mod 2 (buffers grp)
+    const int grp = (warp - 2) >> 2;
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const int key = my_k0 + row;
+    const bool key_ok = key < p.T;
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    row_to_tmem<HD>(p.tm_src + static_cast<long long>(row0 + key) * p.ld_in + static_cast<long long>(hk) * HD,
+                    key_ok, tmem + lane_base + Cfg::KV_OPND, grp);
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive_remote(mapa_shared(bars.opnd_ready(), 0));
+    const uint32_t p_full_lead = mapa_shared(bars.p_full(grp), 0);
+    bool ok = true;
+    for (int t = grp; t < n_steps; t += 2) {
+      const int h = hk * p.G + t / n_q;
+      const int qs = k0 + (t % n_q) * PBLK_KV;
+      const long long lrow = (static_cast<long long>(b) * p.H + h) * p.T;
+      float l2[32], dl[32];
+      load32(p.lse + lrow + qs, p.T - qs, kLog2e, l2);
+      load32(p.delta + lrow + qs, p.T - qs, 1.0f, dl);
+      if (!mbar_wait(bars.s_full(grp), (t >> 1) & 1, p.err, kErrWaitAccum)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t sv[32], dv[32];
+      tmem_ld_32x32b_x32(tmem + lane_base + s_col_of(grp, PBLK_KV), sv);
+      tmem_ld_32x32b_x32(tmem + lane_base + dp_col_of(grp, PBLK_KV), dv);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int q = qs + i;
+        const bool keep = q < p.T && key <= q;
+        const float pv = keep ? ex2_approx(fmaf(__uint_as_float(sv[i]), p.scale_log2, -l2[i])) : 0.0f;
+        sv[i] = __float_as_uint(pv);
+        dv[i] = __float_as_uint(pv * (__uint_as_float(dv[i]) - dl[i]) * p.scale);
+      }
+      tmem_st_32x32b_x32(tmem + lane_base + s_col_of(grp, PBLK_KV), sv);
+      tmem_st_32x32b_x32(tmem + lane_base + dp_col_of(grp, PBLK_KV), dv);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(p_full_lead);
+    }
+    if (ok && mbar_wait(bars.acc_done(), 0, p.err, kErrWaitAccum)) {
+      tc_fence_after();
+      const long long r = row0 + key;
+      if (grp == 0)
+        tmem_to_row<HD>(tmem + lane_base + Cfg::KV_DV, p.out2 + r * p.ld_out2 + static_cast<long long>(hk) * HD,
+                        key_ok, 1.0f);
+      else
+        tmem_to_row<HD>(tmem + lane_base + Cfg::KV_DK, p.out + r * p.ld_out + static_cast<long long>(hk) * HD,
+                        key_ok, 1.0f);
+    }
+  }
+  pair_teardown<STAGES>(leader, bars, tl, p.err, warp, tmem);
+}
+
+// ---------------- dQ (pair of 128-query tiles)
+template <int HD>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(BTHREADS, 1)
+    flash_bwd_q_pair_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKk,
+                            const __grid_constant__ CUtensorMap tmVk, const __grid_constant__ CUtensorMap tmKm,
+                            BwdParams p) {
+  using Cfg = PairBwdCfg<HD>;
+  constexpr int STAGES = Cfg::Q_STAGES;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = static_cast<int>(blockIdx.x) / 2;
+  const int qt = p.n_tiles - 1 - pair / p.BHx;  // most keys first
+  const int bh = pair % p.BHx;
+  const int b = bh / p.H, h = bh % p.H, hk = h / p.G;
+  const int q0 = qt * 2 * TILE;
+  const int my_q0 = q0 + static_cast<int>(rank) * TILE;
+  const int row0 = b * p.T;
+  const int n_kv = (min(p.T, q0 + 2 * TILE) + PBLK_Q - 1) / PBLK_Q;
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  const uint32_t sQ = base;
+  auto stage = [&](int s) { return base + Cfg::TILE_BYTES + s * Cfg::Q_STAGE; };
+  const PairBars<STAGES> bars{base + Cfg::TILE_BYTES + STAGES * Cfg::Q_STAGE};
+  Tail* tl = reinterpret_cast<Tail*>(smem_raw + (bars.slot() - raw_addr));
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmKk);
+    tma_prefetch_desc(&tmVk);
+    tma_prefetch_desc(&tmKm);
+    bars.init();
+    tl->issued = tl->consumed = tl->tile_pending = 0;
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(bars.slot(), Cfg::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem = tl->tmem;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer (both CTAs)
+      if (leader) {
+        tl->tile_pending = 1;
+        mbar_arrive_expect_tx(bars.tile_full(), 2 * Cfg::TILE_BYTES);
+      }
+      tma_load_3d_pair(sQ, &tmQ, mapa_shared(bars.tile_full(), 0), 0, row0 + my_q0, h * (HD / 32));
+      for (int j = 0; j < n_kv; ++j) {
+        const int s = j % STAGES, r = j / STAGES;
+        if (r > 0 && !mbar_wait(bars.empty(s), (r - 1) & 1, p.err, kErrWaitEmpty)) break;
+        if (leader) mbar_arrive_expect_tx(bars.full(s), 2 * Cfg::Q_STAGE);
+        const int krow = row0 + j * PBLK_Q;  // keys past the sequence follow every query: masked
+        const int xb = hk * (HD / 32);
+        const uint32_t st = stage(s);
+        const uint32_t fb = mapa_shared(bars.full(s), 0);
+        const int half = static_cast<int>(rank) * (PBLK_Q / 2);
+        tma_load_3d_pair(st, &tmKk, fb, 0, krow + half, xb);
+        tma_load_3d_pair(st + Cfg::Q_HALF_K, &tmVk, fb, 0, krow + half, xb);
+        tma_load_3d_pair(st + 2 * Cfg::Q_HALF_K, &tmKm, fb, 0, krow, xb + static_cast<int>(rank) * (HD / 64));
+        tl->issued = j + 1;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ---------------- UMMA issuer (leader only), M = 256 queries across the pair
+      constexpr uint32_t idesc_s = idesc_tf32(2 * TILE, PBLK_Q, false, false);
+      constexpr uint32_t idesc_g = idesc_tf32(2 * TILE, HD, false, true);
+      bool ok = mbar_wait(bars.tile_full(), 0, p.err, kErrWaitFull);
+      if (ok) tl->tile_pending = 0;
+      ok = ok && mbar_wait_cluster(bars.opnd_ready(), 0, p.err, kErrWaitAccum);
+      auto issue_s = [&](int j) -> bool {
+        const int s = j % STAGES, bb = j & 1, u = j >> 1;
+        if (!mbar_wait(bars.full(s), (j / STAGES) & 1, p.err, kErrWaitFull)) return false;
+        tl->consumed = j + 1;
+        if (u > 0 && !mbar_wait(bars.s_free(bb), (u - 1) & 1, p.err, kErrWaitAccum)) return false;
+        tc_fence_after();
+        const uint32_t st = stage(s);
+#pragma unroll
+        for (int kk = 0; kk < HD / 8; ++kk)  // S = Q K^T
+          umma_tf32_pair(tmem + s_col_of(bb, PBLK_Q), kmajor_desc(sQ, TILE, kk), kmajor_desc(st, PBLK_Q / 2, kk),
+                         idesc_s, kk > 0 ? 1u : 0u);
+#pragma unroll
+        for (int kk = 0; kk < HD / 8; ++kk)  // dP = dO V^T, dO in TMEM
+          umma_tf32_ts_pair(tmem + dp_col_of(bb, PBLK_Q), tmem + Cfg::Q_OPND + kk * 8,
+                            kmajor_desc(st + Cfg::Q_HALF_K, PBLK_Q / 2, kk), idesc_s, kk > 0 ? 1u : 0u);
+        umma_commit_pair(bars.s_full(bb), 0x3);
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      for (int j = 0; ok && j < n_kv; ++j) {
+        if (j + 1 < n_kv && !issue_s(j + 1)) break;
+        const int s = j % STAGES, bb = j & 1;
+        if (!mbar_wait_cluster(bars.p_full(bb), (j >> 1) & 1, p.err, kErrWaitAccum)) break;
+        tc_fence_after();
+        const uint32_t st = stage(s);
+#pragma unroll
+        for (int kk = 0; kk < PBLK_Q / 8; ++kk)  // dQ += dS K
+          umma_tf32_ts_pair(tmem + Cfg::Q_DQ, tmem + dp_col_of(bb, PBLK_Q) + kk * 8,
+                            mnmajor_desc_rows(st + 2 * Cfg::Q_HALF_K, PBLK_Q, kk), idesc_g,
+                            (j > 0 || kk > 0) ? 1u : 0u);
+        umma_commit_pair(bars.empty(s), 0x3);
+        umma_commit_pair(bars.s_free(bb), 0x1);
+      }
+      umma_commit_pair(bars.acc_done(), 0x3);
+    }
+  } else {
+    // ---------------- dO into TMEM, softmax gradient, epilogue (lane = query);
+    // warpgroup grp takes the key blocks j = grp mod 2
+    const int grp = (warp - 2) >> 2;
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const int q = my_q0 + row;
+    const bool q_ok = q < p.T;
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    row_to_tmem<HD>(p.tm_src + static_cast<long long>(row0 + q) * p.ld_in + static_cast<long long>(h) * HD, q_ok,
+                    tmem + lane_base + Cfg::Q_OPND, grp);
+    const long long li = static_cast<long long>(bh) * p.T + q;
+    const float lse2 = q_ok ? p.lse[li] * kLog2e : 0.0f;
+    const float dlt = q_ok ? p.delta[li] : 0.0f;
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive_remote(mapa_shared(bars.opnd_ready(), 0));
+    const uint32_t p_full_lead = mapa_shared(bars.p_full(grp), 0);
+    bool ok = true;
+    for (int j = grp; j < n_kv; j += 2) {
+      if (!mbar_wait(bars.s_full(grp), (j >> 1) & 1, p.err, kErrWaitAccum)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < PBLK_Q / 32; ++c) {
+        uint32_t sv[32], dv[32];
+        tmem_ld_32x32b_x32(tmem + lane_base + s_col_of(grp, PBLK_Q) + c * 32, sv);
+        tmem_ld_32x32b_x32(tmem + lane_base + dp_col_of(grp, PBLK_Q) + c * 32, dv);
+        const int kb = j * PBLK_Q + c * 32;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const bool keep = q_ok && kb + i <= q;
+          const float pv = keep ? ex2_approx(fmaf(__uint_as_float(sv[i]), p.scale_log2, -lse2)) : 0.0f;
+          dv[i] = __float_as_uint(pv * (__uint_as_float(dv[i]) - dlt) * p.scale);
+        }
+        tmem_st_32x32b_x32(tmem + lane_base + dp_col_of(grp, PBLK_Q) + c * 32, dv);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(p_full_lead);
+    }
+    if (ok && mbar_wait(bars.acc_done(), 0, p.err, kErrWaitAccum)) {
+      tc_fence_after();
+      tmem_to_row<HD>(tmem + lane_base + Cfg::Q_DQ,
+                      p.out + static_cast<long long>(row0 + q) * p.ld_out + static_cast<long long>(h) * HD, q_ok,
+                      1.0f, grp, 2);
+    }
+  }
+  pair_teardown<STAGES>(leader, bars, tl, p.err, warp, tmem);
+}
+
 bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
 
 // Token-major operand [rows, ld]: 3-D view (32 columns, token row, 32-column
 // block) whose box brings `box_rows` rows of one head as hd/32 chunks.
 void head_map(CUtensorMap* map, const float* ptr, long long rows, long long ld, int heads, int hd, int box_rows,
-              bool mn_major) {
+              bool mn_major, int box_blocks = 0) {
   const long long dims[3] = {32, rows, static_cast<long long>(heads) * hd / 32};
   const long long strides[2] = {ld, 32};
-  const int box[3] = {32, box_rows, hd / 32};
+  const int box[3] = {32, box_rows, box_blocks ? box_blocks : hd / 32};
   if (encode_tensor_map(map, ptr, 3, dims, strides, box, mn_major))
     throw std::runtime_error("flash attention backward: tensor map rejected");
 }
@@ -618,6 +1060,65 @@ void launch_bwd(const AttnShape& s, const float* q, const float* k, const float*
     throw std::runtime_error(std::string("flash attention backward launch: ") + cudaGetErrorString(e));
 }
 
+template <int HD>
+void launch_bwd_pair(const AttnShape& s, const float* q, const float* k, const float* v, const float* lse,
+                     const float* dout, long long lddo, float* dq, float* dk, float* dv, const float* delta,
+                     int* d_err, cudaStream_t stream) {
+  using Cfg = PairBwdCfg<HD>;
+  const long long rows = static_cast<long long>(s.B) * s.T;
+  const int n_pairs = (s.T + 2 * TILE - 1) / (2 * TILE);
+  BwdParams p{};
+  p.T = s.T;
+  p.H = s.H;
+  p.Hkv = s.Hkv;
+  p.G = s.H / s.Hkv;
+  p.n_tiles = n_pairs;
+  p.lse = lse;
+  p.delta = delta;
+  p.scale = s.scale;
+  p.scale_log2 = s.scale * kLog2e;
+  p.err = d_err;
+  {  // dK, dV
+    CUtensorMap tk, tqk, tdok, tqm, tdom;
+    head_map(&tk, k, rows, s.ldk, s.Hkv, HD, TILE, false);
+    head_map(&tqk, q, rows, s.ldq, s.H, HD, PBLK_KV / 2, false);
+    head_map(&tdok, dout, rows, lddo, s.H, HD, PBLK_KV / 2, false);
+    head_map(&tqm, q, rows, s.ldq, s.H, HD, PBLK_KV, true, HD / 64);
+    head_map(&tdom, dout, rows, lddo, s.H, HD, PBLK_KV, true, HD / 64);
+    BwdParams pk = p;
+    pk.BHx = s.B * s.Hkv;
+    pk.ld_in = s.ldv;
+    pk.tm_src = v;
+    pk.out = dk;
+    pk.ld_out = s.ldk;
+    pk.out2 = dv;
+    pk.ld_out2 = s.ldv;
+    set_smem(flash_bwd_kv_pair_kernel<HD>, Cfg::KV_SMEM);
+    const long long grid = 2ll * n_pairs * pk.BHx;
+    flash_bwd_kv_pair_kernel<HD>
+        <<<static_cast<unsigned>(grid), BTHREADS, Cfg::KV_SMEM, stream>>>(tk, tqk, tdok, tqm, tdom, pk);
+  }
+  {  // dQ
+    CUtensorMap tq, tkk, tvk, tkm;
+    head_map(&tq, q, rows, s.ldq, s.H, HD, TILE, false);
+    head_map(&tkk, k, rows, s.ldk, s.Hkv, HD, PBLK_Q / 2, false);
+    head_map(&tvk, v, rows, s.ldv, s.Hkv, HD, PBLK_Q / 2, false);
+    head_map(&tkm, k, rows, s.ldk, s.Hkv, HD, PBLK_Q, true, HD / 64);
+    BwdParams pq = p;
+    pq.BHx = s.B * s.H;
+    pq.ld_in = lddo;
+    pq.tm_src = dout;
+    pq.out = dq;
+    pq.ld_out = s.ldq;
+    set_smem(flash_bwd_q_pair_kernel<HD>, Cfg::Q_SMEM);
+    const long long grid = 2ll * n_pairs * pq.BHx;
+    flash_bwd_q_pair_kernel<HD><<<static_cast<unsigned>(grid), BTHREADS, Cfg::Q_SMEM, stream>>>(tq, tkk, tvk, tkm, pq);
+  }
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess)
+    throw std::runtime_error(std::string("flash attention backward launch: ") + cudaGetErrorString(e));
+}
+
 }  // namespace
 
 void attention_backward_flash(const AttnShape& s, const float* q, const float* k, const float* v, const float* o,
@@ -629,8 +1130,8 @@ void attention_backward_flash(const AttnShape& s, const float* q, const float* k
   attention_delta(s, o, dout, lddo, delta, stream);
   switch (s.hd) {
     case 32: launch_bwd<32>(s, q, k, v, lse, dout, lddo, dq, dk, dv, delta, d_err, stream); break;
-    case 64: launch_bwd<64>(s, q, k, v, lse, dout, lddo, dq, dk, dv, delta, d_err, stream); break;
-    default: launch_bwd<128>(s, q, k, v, lse, dout, lddo, dq, dk, dv, delta, d_err, stream); break;
+    case 64: launch_bwd_pair<64>(s, q, k, v, lse, dout, lddo, dq, dk, dv, delta, d_err, stream); break;
+    default: launch_bwd_pair<128>(s, q, k, v, lse, dout, lddo, dq, dk, dv, delta, d_err, stream); break;
   }
 }
 

@@ -38,7 +38,7 @@ namespace {
 constexpr int BQ = 128;    // query rows per CTA = TMEM lanes
 constexpr int BKV = 64;    // keys per block
 constexpr int NSBUF = 3;   // S/P buffers
-constexpr int FTHREADS = 192;
+constexpr int FTHREADS = 320;  // producer, UMMA issuer, two softmax warpgroups
 constexpr uint32_t O_COL = NSBUF * BKV;  // 192
 constexpr float kRescaleLog2 = 8.0f;    // move the running max when it grows by more than 2^8
 
@@ -49,8 +49,8 @@ struct FlashCfg {
   static constexpr int STAGE_BYTES = 2 * K_BYTES;  // K and V
   static constexpr int FIT = (200 * 1024 - Q_BYTES) / STAGE_BYTES;
   static constexpr int STAGES = FIT > 4 ? 4 : FIT;
-  static constexpr int SMEM = Q_BYTES + STAGES * STAGE_BYTES + 1024 + 256;
-  static constexpr uint32_t TMEM_COLS = O_COL + HD <= 256 ? 256 : 512;
+  static constexpr int SMEM = Q_BYTES + STAGES * STAGE_BYTES + 1024 + 256 + 2048 /*group exchange*/;
+  static constexpr uint32_t TMEM_COLS = O_COL + 2 * HD <= 256 ? 256 : 512;  // O of each warpgroup
   static_assert(STAGES >= 2, "flash attention needs two K/V stages");
 };
 
@@ -94,8 +94,8 @@ __global__ void __launch_bounds__(FTHREADS, 1)
   auto s_full = [&](int bb) { return bars + 8u * (1 + 3 * STAGES + bb); };
   auto p_full = [&](int bb) { return bars + 8u * (1 + 3 * STAGES + NSBUF + bb); };
   auto s_free = [&](int bb) { return bars + 8u * (1 + 3 * STAGES + 2 * NSBUF + bb); };
-  const uint32_t o_done = bars + 8u * (1 + 3 * STAGES + 3 * NSBUF);
-  const uint32_t tmem_slot = o_done + 8u;
+  auto o_done = [&](int g) { return bars + 8u * (1 + 3 * STAGES + 3 * NSBUF + g); };
+  const uint32_t tmem_slot = bars + 8u * (3 + 3 * STAGES + 3 * NSBUF);
   uint8_t* tail = smem + (tmem_slot - base);
   uint32_t* tmem_slot_ptr = reinterpret_cast<uint32_t*>(tail);
   // K/V stages loaded by the producer and waited on by the UMMA issuer; they
@@ -122,7 +122,8 @@ __global__ void __launch_bounds__(FTHREADS, 1)
       mbar_init(p_full(bb), 4);  // one arrival per softmax warp
       mbar_init(s_free(bb), 1);
     }
-    mbar_init(o_done, 1);
+    mbar_init(o_done(0), 1);
+    mbar_init(o_done(1), 1);
     *kv_issued = 0;
     *kv_consumed = 0;
     *q_pending = 0;
@@ -190,22 +191,28 @@ __global__ void __launch_bounds__(FTHREADS, 1)
         for (int kk = 0; kk < BKV / 8; ++kk) {
           // V_j: 32-wide hd blocks of BKV key rows (LBO), 8 key rows per step
           const uint64_t bd = smem_desc(sV(s) + kk * 1024, BKV * 128, 512, kLayoutSw128Base32);
-          umma_tf32_ts(tmem + O_COL, tmem + bb * BKV + kk * 8, bd, idesc_o, (j > 0 || kk > 0) ? 1u : 0u);
+          umma_tf32_ts(tmem + O_COL + (j & 1) * HD, tmem + bb * BKV + kk * 8, bd, idesc_o,
+                       (j > 1 || kk > 0) ? 1u : 0u);
         }
         umma_commit(kv_empty(s));
         umma_commit(s_free(bb));
-        umma_commit(o_done);
+        umma_commit(o_done(j & 1));
       }
     }
   } else {
-    // ---------------- softmax + epilogue
+    // ---------------- softmax + epilogue. Warpgroup grp (warps 2-5, 6-9) takes
+    // the key blocks j = grp mod 2 with its own running max / sum and its own
+    // O accumulator; the two partial results are merged at the end.
+    const int grp = (warp - 2) >> 2;
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;  // query row within the tile
     const int q = q0 + row;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t o_col = O_COL + grp * HD;
     float m_run = -INFINITY, l_run = 0.0f;
     bool ok = true;
-    for (int j = 0; j < n_kv; ++j) {
+    int k = 0;  // blocks this group has processed
+    for (int j = grp; j < n_kv; j += 2, ++k) {
       const int bb = j % NSBUF;
       if (!mbar_wait(s_full(bb), (j / NSBUF) & 1, p.err, kErrWaitAccum)) {
         ok = false;
@@ -217,7 +224,7 @@ __global__ void __launch_bounds__(FTHREADS, 1)
       tmem_ld_32x32b_x32(tmem + lane_base + bb * BKV + 32, r[1]);
       const int kv0 = j * BKV;
       const bool diag = kv0 + BKV - 1 > q0;  // some key of the block follows some query of the tile
-      float mloc = -INFINITY;
+      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
       for (int c = 0; c < 2; ++c)
 #pragma unroll
@@ -225,16 +232,16 @@ __global__ void __launch_bounds__(FTHREADS, 1)
           float x = __uint_as_float(r[c][i]) * p.scale_log2;
           if (diag && kv0 + c * 32 + i > q) x = -INFINITY;
           r[c][i] = __float_as_uint(x);
-          mloc = fmaxf(mloc, x);
+          mx[i & 3] = fmaxf(mx[i & 3], x);
         }
-      const float m_new = fmaxf(m_run, mloc);
-      if (j == 0) {
+      const float m_new = fmaxf(m_run, fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])));
+      if (k == 0) {
         m_run = m_new;
       } else {
         const bool need = m_new > m_run + kRescaleLog2;
         if (__any_sync(0xffffffffu, need)) {
-          // O holds blocks < j once PV_{j-1} is done; rescale it in place
-          if (!mbar_wait(o_done, (j - 1) & 1, p.err, kErrWaitAccum)) {
+          // this group's O holds its blocks before j once their PV is done
+          if (!mbar_wait(o_done(grp), (k - 1) & 1, p.err, kErrWaitAccum)) {
             ok = false;
             break;
           }
@@ -243,10 +250,10 @@ __global__ void __launch_bounds__(FTHREADS, 1)
 #pragma unroll 1
           for (int c = 0; c < HD / 32; ++c) {
             uint32_t o[32];
-            tmem_ld_32x32b_x32(tmem + lane_base + O_COL + c * 32, o);
+            tmem_ld_32x32b_x32(tmem + lane_base + o_col + c * 32, o);
 #pragma unroll
             for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            tmem_st_32x32b_x32(tmem + lane_base + O_COL + c * 32, o);
+            tmem_st_32x32b_x32(tmem + lane_base + o_col + c * 32, o);
           }
           if (need) {
             l_run *= alpha;
@@ -254,39 +261,64 @@ __global__ void __launch_bounds__(FTHREADS, 1)
           }
         }
       }
-      float lsum = 0.0f;
+      // a row with every key so far masked (possible for a group's blocks past
+      // the diagonal) keeps m = -inf: exponentiate against 0 so that P = 0
+      const float mref = m_run == -INFINITY ? 0.0f : m_run;
+      float ls[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
       for (int c = 0; c < 2; ++c)
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          const float e = ex2_approx(__uint_as_float(r[c][i]) - m_run);
-          lsum += e;
+          const float e = ex2_approx(__uint_as_float(r[c][i]) - mref);
+          ls[i & 3] += e;
           r[c][i] = __float_as_uint(e);
         }
-      l_run += lsum;
+      l_run += (ls[0] + ls[1]) + (ls[2] + ls[3]);
       tmem_st_32x32b_x32(tmem + lane_base + bb * BKV, r[0]);
       tmem_st_32x32b_x32(tmem + lane_base + bb * BKV + 32, r[1]);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full(bb));
     }
-    if (ok && mbar_wait(o_done, (n_kv - 1) & 1, p.err, kErrWaitAccum)) {
-      tc_fence_after();
-      const float inv = 1.0f / l_run;
+    if (ok && k > 0 && !mbar_wait(o_done(grp), (k - 1) & 1, p.err, kErrWaitAccum)) ok = false;
+    // publish (m, l) of this group's rows, then merge with the other group's
+    // after the 256 bytes of barriers and counters: [group][m | l][row]
+    float* xch = reinterpret_cast<float*>(smem + Cfg::Q_BYTES + STAGES * Cfg::STAGE_BYTES + 256);
+    xch[grp * 256 + row] = m_run;
+    xch[grp * 256 + 128 + row] = l_run;
+    tc_fence_before();
+    asm volatile("bar.sync 1, 256;" ::: "memory");  // the eight softmax warps
+    tc_fence_after();
+    const float m_o = xch[(1 - grp) * 256 + row], l_o = xch[(1 - grp) * 256 + 128 + row];
+    if (ok) {
+      const float m0 = grp == 0 ? m_run : m_o, l0 = grp == 0 ? l_run : l_o;
+      const float m1 = grp == 0 ? m_o : m_run, l1 = grp == 0 ? l_o : l_run;
+      const float m = fmaxf(m0, m1);
+      const float a0 = l0 > 0.0f ? ex2_approx(m0 - m) : 0.0f;  // a group without blocks has l = 0
+      const float a1 = l1 > 0.0f ? ex2_approx(m1 - m) : 0.0f;
+      const float l = (a0 > 0.0f ? l0 * a0 : 0.0f) + (a1 > 0.0f ? l1 * a1 : 0.0f);
+      const float inv = 1.0f / l;
+      const float w0 = a0 * inv, w1 = a1 * inv;
       float* orow = p.o + static_cast<long long>(row0 + q) * p.ldo + static_cast<long long>(h) * HD;
 #pragma unroll 1
-      for (int c = 0; c < HD / 32; ++c) {
-        uint32_t o[32];
-        tmem_ld_32x32b_x32(tmem + lane_base + O_COL + c * 32, o);
+      for (int c = grp; c < HD / 32; c += 2) {  // each group writes alternate 32-column chunks
+        uint32_t o0[32], o1[32];
+        tmem_ld_32x32b_x32(tmem + lane_base + O_COL + c * 32, o0);
+        tmem_ld_32x32b_x32(tmem + lane_base + O_COL + HD + c * 32, o1);
         if (q < p.T) {
 #pragma unroll
-          for (int i = 0; i < 32; i += 4)
-            *reinterpret_cast<float4*>(orow + c * 32 + i) =
-                make_float4(__uint_as_float(o[i]) * inv, __uint_as_float(o[i + 1]) * inv,
-                            __uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);
+          for (int i = 0; i < 32; i += 4) {
+            float v[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              v[e] = (a0 > 0.0f ? __uint_as_float(o0[i + e]) * w0 : 0.0f) +
+                     (a1 > 0.0f ? __uint_as_float(o1[i + e]) * w1 : 0.0f);
+            *reinterpret_cast<float4*>(orow + c * 32 + i) = make_float4(v[0], v[1], v[2], v[3]);
+          }
         }
       }
-      if (q < p.T) p.lse[static_cast<long long>(bh) * p.T + q] = (m_run + log2f(l_run)) * 0.69314718055994531f;
+      if (grp == 0 && q < p.T)
+        p.lse[static_cast<long long>(bh) * p.T + q] = (m + log2f(l)) * 0.69314718055994531f;
     }
   }
 
@@ -307,6 +339,308 @@ __global__ void __launch_bounds__(FTHREADS, 1)
     tmem_dealloc(tmem, Cfg::TMEM_COLS);
   }
   __syncthreads();
+}
+
+// ------------------------------------------------------------------ CTA pairs
+// Two CTAs of a cluster share one 256-query block: CTA r holds query rows
+// q0 + 128 r ... For every 128-key block each CTA loads half of K_j (64 keys)
+// and half of V_j (hd / 2 columns), so the pair reads each K/V block from L2
+// once where two single CTAs read it twice. The leader (rank 0) issues every
+// UMMA with M = 256 (cta_group::2): S_j = Q K_j^T (N = 128 keys) and
+// O += P_j V_j (N = hd, P_j read from each CTA's own TMEM). Barriers the
+// UMMA issuer waits on live in the leader; the commits that release stages,
+// S buffers and O reach both CTAs.
+constexpr int PQ = 128;   // query rows per CTA (a pair: 256)
+constexpr int PKV = 128;  // keys per block = N of the S product
+
+template <int HD>
+struct PairCfg {
+  static constexpr int Q_BYTES = PQ * HD * 4;
+  static constexpr int K_BYTES = (PKV / 2) * HD * 4;  // this CTA's 64 keys of K_j
+  static constexpr int V_BYTES = PKV * (HD / 2) * 4;  // this CTA's hd/2 columns of V_j
+  static constexpr int STAGE_BYTES = K_BYTES + V_BYTES;
+  static constexpr int FIT = (200 * 1024 - Q_BYTES) / STAGE_BYTES;
+  static constexpr int STAGES = FIT > 4 ? 4 : FIT;
+  static constexpr int SMEM = Q_BYTES + STAGES * STAGE_BYTES + 1024 + 256 + 2048 /*group exchange*/;
+  static constexpr uint32_t O_COL = 2 * PKV;  // two S/P buffers, then O of each warpgroup
+  static constexpr uint32_t TMEM_COLS = 512;
+  static_assert(O_COL + 2 * HD <= TMEM_COLS, "TMEM budget");
+  static_assert(STAGES >= 2, "two K/V stages");
+};
+
+template <int HD>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(FTHREADS, 1)
+    flash_fwd_pair_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                          const __grid_constant__ CUtensorMap tmV, FlashParams p) {
+  using Cfg = PairCfg<HD>;
+  constexpr int STAGES = Cfg::STAGES;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = static_cast<int>(blockIdx.x) / 2;
+  const int qt = p.n_qt - 1 - pair / p.BH;  // heaviest 256-query blocks first
+  const int bh = pair % p.BH;
+  const int b = bh / p.H, h = bh % p.H, hk = h / p.G;
+  const int q0 = qt * 2 * PQ;
+  const int my_q0 = q0 + static_cast<int>(rank) * PQ;
+  const int n_kv = (min(p.T, q0 + 2 * PQ) + PKV - 1) / PKV;
+  const int row0 = b * p.T;
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (base - raw_addr);
+  const uint32_t sQ = base;
+  auto sK = [&](int s) { return base + Cfg::Q_BYTES + s * Cfg::STAGE_BYTES; };
+  auto sV = [&](int s) { return sK(s) + Cfg::K_BYTES; };
+  const uint32_t bars = base + Cfg::Q_BYTES + STAGES * Cfg::STAGE_BYTES;
+  const uint32_t q_full = bars;
+  auto k_full = [&](int s) { return bars + 8u * (1 + s); };
+  auto v_full = [&](int s) { return bars + 8u * (1 + STAGES + s); };
+  auto kv_empty = [&](int s) { return bars + 8u * (1 + 2 * STAGES + s); };
+  auto s_full = [&](int bb) { return bars + 8u * (1 + 3 * STAGES + bb); };
+  auto p_full = [&](int bb) { return bars + 8u * (3 + 3 * STAGES + bb); };
+  auto s_free = [&](int bb) { return bars + 8u * (5 + 3 * STAGES + bb); };
+  auto o_done = [&](int g) { return bars + 8u * (7 + 3 * STAGES + g); };
+  const uint32_t tmem_slot = bars + 8u * (9 + 3 * STAGES);
+  uint8_t* tail = smem + (tmem_slot - base);
+  uint32_t* tmem_slot_ptr = reinterpret_cast<uint32_t*>(tail);
+  int* kv_issued = reinterpret_cast<int*>(tail + 8);
+  int* kv_consumed = kv_issued + 1;
+  int* q_pending = kv_issued + 2;
+  float* xch = reinterpret_cast<float*>(smem + Cfg::Q_BYTES + STAGES * Cfg::STAGE_BYTES + 256);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+    mbar_init(q_full, 1);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(k_full(s), 1);
+      mbar_init(v_full(s), 1);
+      mbar_init(kv_empty(s), 1);
+    }
+    for (int bb = 0; bb < 2; ++bb) {
+      mbar_init(s_full(bb), 1);
+      mbar_init(p_full(bb), 8);  // four softmax warps in each CTA
+      mbar_init(s_free(bb), 1);
+      mbar_init(o_done(bb), 1);
+    }
+    *kv_issued = 0;
+    *kv_consumed = 0;
+    *q_pending = 0;
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // both CTAs' barriers initialised and TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot_ptr;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer (both CTAs); completions land on the leader's barriers
+      if (leader) {
+        *q_pending = 1;
+        mbar_arrive_expect_tx(q_full, 2 * Cfg::Q_BYTES);
+      }
+      tma_load_3d_pair(sQ, &tmQ, mapa_shared(q_full, 0), 0, row0 + my_q0, h * (HD / 32));
+      for (int j = 0; j < n_kv; ++j) {
+        const int s = j % STAGES, r = j / STAGES;
+        if (r > 0 && !mbar_wait(kv_empty(s), (r - 1) & 1, p.err, kErrWaitEmpty)) break;
+        if (leader) {
+          mbar_arrive_expect_tx(k_full(s), 2 * Cfg::K_BYTES);
+          mbar_arrive_expect_tx(v_full(s), 2 * Cfg::V_BYTES);
+        }
+        // keys past this sequence's end follow every query of the pair: masked
+        tma_load_3d_pair(sK(s), &tmK, mapa_shared(k_full(s), 0), 0, row0 + j * PKV + static_cast<int>(rank) * (PKV / 2),
+                         hk * (HD / 32));
+        tma_load_3d_pair(sV(s), &tmV, mapa_shared(v_full(s), 0), 0, row0 + j * PKV,
+                         hk * (HD / 32) + static_cast<int>(rank) * (HD / 64));
+        *kv_issued = j + 1;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ---------------- UMMA issuer (leader only), M = 256 across the pair
+      constexpr uint32_t idesc_s = idesc_tf32(2 * PQ, PKV, false, false);
+      constexpr uint32_t idesc_o = idesc_tf32(2 * PQ, HD, false, true);
+      bool ok = mbar_wait(q_full, 0, p.err, kErrWaitFull);
+      if (ok) *q_pending = 0;
+      auto issue_s = [&](int j) -> bool {
+        const int s = j % STAGES, bb = j & 1, u = j >> 1;
+        if (!mbar_wait(k_full(s), (j / STAGES) & 1, p.err, kErrWaitFull)) return false;
+        if (u > 0 && !mbar_wait(s_free(bb), (u - 1) & 1, p.err, kErrWaitAccum)) return false;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < HD / 8; ++kk) {
+          const uint32_t off = (kk % 4) * 32u;  // 8 tf32 = 32 bytes along the 128-byte chunk
+          const uint64_t a = smem_desc(sQ + (kk / 4) * (PQ * 128) + off, 16, 1024, kLayoutSw128);
+          const uint64_t bd = smem_desc(sK(s) + (kk / 4) * ((PKV / 2) * 128) + off, 16, 1024, kLayoutSw128);
+          umma_tf32_pair(tmem + bb * PKV, a, bd, idesc_s, kk > 0 ? 1u : 0u);
+        }
+        umma_commit_pair(s_full(bb), 0x3);
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      for (int j = 0; ok && j < n_kv; ++j) {
+        if (j + 1 < n_kv && !issue_s(j + 1)) break;
+        const int s = j % STAGES, bb = j & 1;
+        if (!mbar_wait_cluster(p_full(bb), (j >> 1) & 1, p.err, kErrWaitAccum)) break;
+        if (!mbar_wait(v_full(s), (j / STAGES) & 1, p.err, kErrWaitFull)) break;
+        *kv_consumed = j + 1;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < PKV / 8; ++kk) {
+          // this CTA's half of V_j: 32-wide hd blocks of PKV key rows (LBO), 8 key rows per step
+          const uint64_t bd = smem_desc(sV(s) + kk * 1024, PKV * 128, 512, kLayoutSw128Base32);
+          umma_tf32_ts_pair(tmem + Cfg::O_COL + (j & 1) * HD, tmem + bb * PKV + kk * 8, bd, idesc_o,
+                            (j > 1 || kk > 0) ? 1u : 0u);
+        }
+        umma_commit_pair(kv_empty(s), 0x3);
+        umma_commit_pair(s_free(bb), 0x1);
+        umma_commit_pair(o_done(j & 1), 0x3);
+      }
+    }
+  } else {
+    // ---------------- softmax + epilogue (both CTAs): warpgroup grp takes the
+    // blocks j = grp mod 2, which use S/P buffer grp and O accumulator grp
+    const int grp = (warp - 2) >> 2;
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const int q = my_q0 + row;
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t s_col = grp * PKV;
+    const uint32_t o_col = Cfg::O_COL + grp * HD;
+    const uint32_t p_full_lead = mapa_shared(p_full(grp), 0);
+    float m_run = -INFINITY, l_run = 0.0f;
+    bool ok = true;
+    int k = 0;
+    for (int j = grp; j < n_kv; j += 2, ++k) {
+      if (!mbar_wait(s_full(grp), k & 1, p.err, kErrWaitAccum)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t r[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(tmem + lane_base + s_col + c * 32, r[c]);
+      const int kv0 = j * PKV;
+      const bool diag = kv0 + PKV - 1 > my_q0;
+      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          float x = __uint_as_float(r[c][i]) * p.scale_log2;
+          if (diag && kv0 + c * 32 + i > q) x = -INFINITY;
+          r[c][i] = __float_as_uint(x);
+          mx[i & 3] = fmaxf(mx[i & 3], x);
+        }
+      const float m_new = fmaxf(m_run, fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])));
+      if (k == 0) {
+        m_run = m_new;
+      } else {
+        const bool need = m_new > m_run + kRescaleLog2;
+        if (__any_sync(0xffffffffu, need)) {
+          if (!mbar_wait(o_done(grp), (k - 1) & 1, p.err, kErrWaitAccum)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const float alpha = need ? ex2_approx(m_run - m_new) : 1.0f;
+#pragma unroll 1
+          for (int c = 0; c < HD / 32; ++c) {
+            uint32_t o[32];
+            tmem_ld_32x32b_x32(tmem + lane_base + o_col + c * 32, o);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st_32x32b_x32(tmem + lane_base + o_col + c * 32, o);
+          }
+          if (need) {
+            l_run *= alpha;
+            m_run = m_new;
+          }
+        }
+      }
+      const float mref = m_run == -INFINITY ? 0.0f : m_run;
+      float ls[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float e = ex2_approx(__uint_as_float(r[c][i]) - mref);
+          ls[i & 3] += e;
+          r[c][i] = __float_as_uint(e);
+        }
+      l_run += (ls[0] + ls[1]) + (ls[2] + ls[3]);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tmem_st_32x32b_x32(tmem + lane_base + s_col + c * 32, r[c]);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(p_full_lead);
+    }
+    if (ok && k > 0 && !mbar_wait(o_done(grp), (k - 1) & 1, p.err, kErrWaitAccum)) ok = false;
+    xch[grp * 256 + row] = m_run;
+    xch[grp * 256 + 128 + row] = l_run;
+    tc_fence_before();
+    asm volatile("bar.sync 1, 256;" ::: "memory");  // the eight softmax warps of this CTA
+    tc_fence_after();
+    const float m_o = xch[(1 - grp) * 256 + row], l_o = xch[(1 - grp) * 256 + 128 + row];
+    if (ok) {
+      const float m0 = grp == 0 ? m_run : m_o, l0 = grp == 0 ? l_run : l_o;
+      const float m1 = grp == 0 ? m_o : m_run, l1 = grp == 0 ? l_o : l_run;
+      const float m = fmaxf(m0, m1);
+      const float a0 = l0 > 0.0f ? ex2_approx(m0 - m) : 0.0f;
+      const float a1 = l1 > 0.0f ? ex2_approx(m1 - m) : 0.0f;
+      const float l = (a0 > 0.0f ? l0 * a0 : 0.0f) + (a1 > 0.0f ? l1 * a1 : 0.0f);
+      const float inv = 1.0f / l;
+      const float w0 = a0 * inv, w1 = a1 * inv;
+      float* orow = p.o + static_cast<long long>(row0 + q) * p.ldo + static_cast<long long>(h) * HD;
+#pragma unroll 1
+      for (int c = grp; c < HD / 32; c += 2) {
+        uint32_t o0[32], o1[32];
+        tmem_ld_32x32b_x32(tmem + lane_base + Cfg::O_COL + c * 32, o0);
+        tmem_ld_32x32b_x32(tmem + lane_base + Cfg::O_COL + HD + c * 32, o1);
+        if (q < p.T) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 4) {
+            float v[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              v[e] = (a0 > 0.0f ? __uint_as_float(o0[i + e]) * w0 : 0.0f) +
+                     (a1 > 0.0f ? __uint_as_float(o1[i + e]) * w1 : 0.0f);
+            *reinterpret_cast<float4*>(orow + c * 32 + i) = make_float4(v[0], v[1], v[2], v[3]);
+          }
+        }
+      }
+      if (grp == 0 && q < p.T)
+        p.lse[static_cast<long long>(bh) * p.T + q] = (m + log2f(l)) * 0.69314718055994531f;
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync();  // both CTAs are done with their TMEM and with each other's barriers
+  if (leader && threadIdx.x == 0) {
+    // after a timed-out wait, let every TMA copy of the pair still in flight
+    // land (bounded) before either CTA's shared memory is released
+    if (*q_pending) mbar_wait(q_full, 0, p.err, kErrWaitDrain, 1000000000ull);
+    for (int j = *kv_consumed; j < *kv_issued; ++j) {
+      const int s = j % STAGES;
+      if (!mbar_wait(k_full(s), (j / STAGES) & 1, p.err, kErrWaitDrain, 1000000000ull)) break;
+      if (!mbar_wait(v_full(s), (j / STAGES) & 1, p.err, kErrWaitDrain, 1000000000ull)) break;
+    }
+  }
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, Cfg::TMEM_COLS);
+  }
 }
 
 bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
@@ -356,6 +690,41 @@ void launch_flash(const AttnShape& s, const float* q, const float* k, const floa
   if (e != cudaSuccess) throw std::runtime_error(std::string("flash attention launch: ") + cudaGetErrorString(e));
 }
 
+template <int HD>
+void launch_flash_pair(const AttnShape& s, const float* q, const float* k, const float* v, float* o, float* lse,
+                       int* d_err, cudaStream_t stream) {
+  using Cfg = PairCfg<HD>;
+  const long long rows = static_cast<long long>(s.B) * s.T;
+  CUtensorMap tq, tk, tv;
+  head_map(&tq, q, rows, s.ldq, s.H, HD, PQ, false);
+  head_map(&tk, k, rows, s.ldk, s.Hkv, HD, PKV / 2, false);
+  {  // V: each CTA of a pair takes hd/2 columns of all PKV keys
+    const long long dims[3] = {32, rows, static_cast<long long>(s.Hkv) * HD / 32};
+    const long long strides[2] = {s.ldv, 32};
+    const int box[3] = {32, PKV, HD / 64};
+    if (encode_tensor_map(&tv, v, 3, dims, strides, box, true))
+      throw std::runtime_error("flash attention: tensor map rejected");
+  }
+  const cudaError_t a =
+      cudaFuncSetAttribute(flash_fwd_pair_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
+  if (a != cudaSuccess) throw std::runtime_error(std::string("flash attention smem: ") + cudaGetErrorString(a));
+  FlashParams p;
+  p.T = s.T;
+  p.H = s.H;
+  p.G = s.H / s.Hkv;
+  p.n_qt = (s.T + 2 * PQ - 1) / (2 * PQ);
+  p.BH = s.B * s.H;
+  p.ldo = s.ldo;
+  p.scale_log2 = s.scale * 1.4426950408889634f;
+  p.o = o;
+  p.lse = lse;
+  p.err = d_err;
+  const long long grid = 2ll * p.n_qt * p.BH;
+  flash_fwd_pair_kernel<HD><<<static_cast<unsigned>(grid), FTHREADS, Cfg::SMEM, stream>>>(tq, tk, tv, p);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) throw std::runtime_error(std::string("flash attention launch: ") + cudaGetErrorString(e));
+}
+
 }  // namespace
 
 bool attention_flash_supported(const AttnShape& s) {
@@ -369,8 +738,8 @@ void attention_forward_flash(const AttnShape& s, const float* q, const float* k,
     throw std::runtime_error("flash attention: unsupported head_dim, stride or alignment");
   switch (s.hd) {
     case 32: launch_flash<32>(s, q, k, v, o, lse, d_err, stream); break;
-    case 64: launch_flash<64>(s, q, k, v, o, lse, d_err, stream); break;
-    default: launch_flash<128>(s, q, k, v, o, lse, d_err, stream); break;
+    case 64: launch_flash_pair<64>(s, q, k, v, o, lse, d_err, stream); break;
+    default: launch_flash_pair<128>(s, q, k, v, o, lse, d_err, stream); break;
   }
 }
 
