@@ -288,6 +288,9 @@ def main():
     if args.impl == "reference":
         return run_reference(args, cfg, B, T, world, rank)
 
+    # NCCL's version banner (printed at NCCL_DEBUG=VERSION) would land on stdout beside the JSON line
+    if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
+        os.environ["NCCL_DEBUG"] = "WARN"
     import torch
     import midman_b200 as mm
     torch.cuda.set_device(local)
