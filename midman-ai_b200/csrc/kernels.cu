@@ -7,6 +7,7 @@
 
 #include <cfloat>
 #include <cmath>
+#include <cstdint>
 #include <stdexcept>
 
 #include "kernels.h"
@@ -59,6 +60,8 @@ int grid_for(long long n, int per_thread = 4) {
   return static_cast<int>(b);
 }
 
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
 void check_launch(const char* what) {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) throw std::runtime_error(std::string(what) + ": " + cudaGetErrorString(e));
@@ -89,26 +92,38 @@ __global__ void embedding_bwd_kernel(const int32_t* __restrict__ uniq, const int
 }
 
 // ---------------------------------------------------------------- RMSNorm
+// One block per row; the row stays in registers (G float4 per thread) between
+// the sum of squares and the scaled write.
+template <int G>
 __global__ void rmsnorm_fwd_kernel(const float* __restrict__ x, const float* __restrict__ w, int dim, float eps,
                                    float* __restrict__ y, float* __restrict__ rstd) {
   __shared__ float red[32];
   const long long r = blockIdx.x;
+  const int nv = dim / 4;
   const float4* xr = reinterpret_cast<const float4*>(x + r * dim);
   const float4* w4 = reinterpret_cast<const float4*>(w);
   float4* yr = reinterpret_cast<float4*>(y + r * dim);
+  float4 v[G];
   float ss = 0.0f;
-  for (int j = threadIdx.x; j < dim / 4; j += blockDim.x) {
-    const float4 v = xr[j];
-    ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const int j = threadIdx.x + g * blockDim.x;
+    v[g] = j < nv ? xr[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+    ss += v[g].x * v[g].x + v[g].y * v[g].y + v[g].z * v[g].z + v[g].w * v[g].w;
   }
   ss = block_sum(ss, red);
   // mean_axis = sum * (1/len) (ops_reduce.rs:87-90), + eps, ^(-1/2)
   const float t = ss * (1.0f / static_cast<float>(dim)) + eps;
   const float inv = 1.0f / sqrtf(t);
   if (threadIdx.x == 0) rstd[r] = inv;
-  for (int j = threadIdx.x; j < dim / 4; j += blockDim.x) {
-    const float4 v = xr[j], g = w4[j];
-    yr[j] = make_float4((v.x * inv) * g.x, (v.y * inv) * g.y, (v.z * inv) * g.z, (v.w * inv) * g.w);
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const int j = threadIdx.x + g * blockDim.x;
+    if (j < nv) {
+      const float4 gw = w4[j];
+      yr[j] = make_float4((v[g].x * inv) * gw.x, (v[g].y * inv) * gw.y, (v[g].z * inv) * gw.z,
+                          (v[g].w * inv) * gw.w);
+    }
   }
 }
 
@@ -132,20 +147,28 @@ __global__ void rmsnorm_bwd_kernel(const float* __restrict__ x, const float* __r
     wv[g] = j < nv ? w4[j] : make_float4(0.f, 0.f, 0.f, 0.f);
   }
   const float inv_dim = 1.0f / static_cast<float>(dim);
-  for (int r = r0; r < r1; ++r) {
+  // x and dy of row r + 1 are loaded while row r is reduced and written
+  float4 xv[G], gv[G], xn[G], gn[G];
+  auto load_row = [&](int r, float4 (&xa)[G], float4 (&ga)[G]) {
     const float4* xr = reinterpret_cast<const float4*>(x + static_cast<long long>(r) * dim);
     const float4* gr = reinterpret_cast<const float4*>(dy + static_cast<long long>(r) * dim);
-    float4 xv[G], gv[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const int j = threadIdx.x + g * blockDim.x;
+      xa[g] = j < nv ? xr[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+      ga[g] = j < nv ? gr[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  };
+  if (r0 < r1) load_row(r0, xv, gv);
+  for (int r = r0; r < r1; ++r) {
+    if (r + 1 < r1) load_row(r + 1, xn, gn);
     float dot = 0.0f;
 #pragma unroll
     for (int g = 0; g < G; ++g) {
       const int j = threadIdx.x + g * blockDim.x;
-      if (j < nv) {
-        xv[g] = xr[j];
-        gv[g] = gr[j];
+      if (j < nv)
         dot += (gv[g].x * wv[g].x) * xv[g].x + (gv[g].y * wv[g].y) * xv[g].y + (gv[g].z * wv[g].z) * xv[g].z +
                (gv[g].w * wv[g].w) * xv[g].w;
-      }
     }
     dot = block_sum(dot, red);
     const float inv = rstd[r];
@@ -172,6 +195,11 @@ __global__ void rmsnorm_bwd_kernel(const float* __restrict__ x, const float* __r
         acc[g].w += gv[g].w * (xv[g].w * inv);
       }
     }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      xv[g] = xn[g];
+      gv[g] = gn[g];
+    }
   }
   float4* out = reinterpret_cast<float4*>(ws + static_cast<long long>(blockIdx.x) * dim);
 #pragma unroll
@@ -181,16 +209,38 @@ __global__ void rmsnorm_bwd_kernel(const float* __restrict__ x, const float* __r
   }
 }
 
-// dw[j] = sum over blocks of the partials, in block order.
+// dw[j] = sum over the blocks' partial rows. A block owns 32 columns; warp w
+// sums rows w, w + 8, ... with four interleaved accumulators (coalesced
+// 128-byte row segments), and the eight warp sums are added in warp order, so
+// the result does not depend on timing.
 __global__ void column_sum_kernel(const float* __restrict__ ws, int nblk, int dim, float* __restrict__ dw) {
-  const int j = blockIdx.x * blockDim.x + threadIdx.x;
-  if (j >= dim) return;
-  float s = 0.0f;
-  for (int b = 0; b < nblk; ++b) s += ws[static_cast<long long>(b) * dim + j];
-  dw[j] = s;
+  __shared__ float part[8][32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int j = blockIdx.x * 32 + lane;
+  float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
+  if (j < dim) {
+    const float* col = ws + j;
+    const long long st = static_cast<long long>(dim);
+    int b = warp;
+    for (; b + 24 < nblk; b += 32) {
+      a0 += col[b * st];
+      a1 += col[(b + 8) * st];
+      a2 += col[(b + 16) * st];
+      a3 += col[(b + 24) * st];
+    }
+    for (; b < nblk; b += 8) a0 += col[b * st];
+  }
+  part[warp][lane] = (a0 + a1) + (a2 + a3);
+  __syncthreads();
+  if (warp == 0 && j < dim) {
+    float s = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) s += part[w][lane];
+    dw[j] = s;
+  }
 }
 
-int rmsnorm_bwd_blocks(int rows) { return rows < 296 ? rows : 296; }
+int rmsnorm_bwd_blocks(int rows) { return rows < 592 ? rows : 592; }
 
 // ---------------------------------------------------------------- RoPE
 __global__ void rope_kernel(float* x, int rows, int T, int heads, int half, long long ld,
@@ -212,6 +262,30 @@ __global__ void rope_kernel(float* x, int rows, int T, int heads, int half, long
   }
 }
 
+// Four consecutive i per thread (half % 4 == 0, 16-byte aligned rows and tables).
+__global__ void rope4_kernel(float* x, int rows, int T, int heads, int half, long long ld,
+                             const float* __restrict__ cos_t, const float* __restrict__ sin_t, float sign) {
+  const int q4 = half / 4;
+  const long long total = static_cast<long long>(rows) * heads * q4;
+  for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int i = static_cast<int>(idx % q4) * 4;
+    const long long rh = idx / q4;
+    const int h = static_cast<int>(rh % heads);
+    const long long r = rh / heads;
+    const int t = static_cast<int>(r % T);
+    float* v = x + r * ld + static_cast<long long>(h) * 2 * half;
+    const float4 c = *reinterpret_cast<const float4*>(cos_t + static_cast<long long>(t) * half + i);
+    const float4 sn = *reinterpret_cast<const float4*>(sin_t + static_cast<long long>(t) * half + i);
+    const float4 a = *reinterpret_cast<const float4*>(v + i), b = *reinterpret_cast<const float4*>(v + i + half);
+    const float s0 = sign * sn.x, s1 = sign * sn.y, s2 = sign * sn.z, s3 = sign * sn.w;
+    *reinterpret_cast<float4*>(v + i) =
+        make_float4(a.x * c.x - b.x * s0, a.y * c.y - b.y * s1, a.z * c.z - b.z * s2, a.w * c.w - b.w * s3);
+    *reinterpret_cast<float4*>(v + i + half) =
+        make_float4(b.x * c.x + a.x * s0, b.y * c.y + a.y * s1, b.z * c.z + a.z * s2, b.w * c.w + a.w * s3);
+  }
+}
+
 // ---------------------------------------------------------------- SwiGLU
 __device__ __forceinline__ float sigmoidf_ref(float x) { return 1.0f / (1.0f + expf(-x)); }
 
@@ -221,6 +295,39 @@ __global__ void swiglu_fwd_kernel(const float* __restrict__ g, const float* __re
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
     const float x = g[i];
     act[i] = (x * sigmoidf_ref(x)) * u[i];  // silu (ops_elementwise.rs:355-364) then mul
+  }
+}
+
+// The same arithmetic per element, four elements per thread with 128-bit accesses.
+__device__ __forceinline__ float silu_mul(float x, float up) { return (x * sigmoidf_ref(x)) * up; }
+
+__global__ void swiglu_fwd4_kernel(const float4* __restrict__ g, const float4* __restrict__ u,
+                                   float4* __restrict__ act, long long n4) {
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n4;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const float4 x = g[i], up = u[i];
+    act[i] = make_float4(silu_mul(x.x, up.x), silu_mul(x.y, up.y), silu_mul(x.z, up.z), silu_mul(x.w, up.w));
+  }
+}
+
+__device__ __forceinline__ void swiglu_grad1(float x, float up, float d, float& dg, float& du) {
+  const float s = sigmoidf_ref(x);
+  const float silu = x * s;
+  dg = (d * up) * (s * (1.0f + x * (1.0f - s)));
+  du = d * silu;
+}
+
+__global__ void swiglu_bwd4_kernel(float4* g, float4* u, const float4* __restrict__ dact, long long n4) {
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n4;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const float4 x = g[i], up = u[i], d = dact[i];
+    float4 dg, du;
+    swiglu_grad1(x.x, up.x, d.x, dg.x, du.x);
+    swiglu_grad1(x.y, up.y, d.y, dg.y, du.y);
+    swiglu_grad1(x.z, up.z, d.z, dg.z, du.z);
+    swiglu_grad1(x.w, up.w, d.w, dg.w, du.w);
+    g[i] = dg;
+    u[i] = du;
   }
 }
 
@@ -254,13 +361,27 @@ __global__ void cross_entropy_kernel(float* logits, long long ld, const int32_t*
   const long long r = blockIdx.x;
   float* z = logits + r * ld;
   MaxSum acc{-INFINITY, 0.0f};
-  for (int j = threadIdx.x; j < vocab; j += blockDim.x) {
-    const float v = z[j];
-    if (v > acc.m) {
-      acc.s = (acc.m == -INFINITY ? 0.0f : acc.s * expf(acc.m - v)) + 1.0f;
-      acc.m = v;
-    } else {
-      acc.s += expf(v - acc.m);
+  const bool vec = (vocab & 3) == 0 && (ld & 3) == 0 && (reinterpret_cast<uintptr_t>(logits) & 15u) == 0;
+  if (vec) {  // four logits per step: one max update, then four exponentials against it
+    const float4* z4 = reinterpret_cast<const float4*>(z);
+    for (int j = threadIdx.x; j < vocab / 4; j += blockDim.x) {
+      const float4 v = z4[j];
+      const float m4 = fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w));
+      if (m4 > acc.m) {
+        acc.s = acc.m == -INFINITY ? 0.0f : acc.s * expf(acc.m - m4);
+        acc.m = m4;
+      }
+      acc.s += (expf(v.x - acc.m) + expf(v.y - acc.m)) + (expf(v.z - acc.m) + expf(v.w - acc.m));
+    }
+  } else {
+    for (int j = threadIdx.x; j < vocab; j += blockDim.x) {
+      const float v = z[j];
+      if (v > acc.m) {
+        acc.s = (acc.m == -INFINITY ? 0.0f : acc.s * expf(acc.m - v)) + 1.0f;
+        acc.m = v;
+      } else {
+        acc.s += expf(v - acc.m);
+      }
     }
   }
 #pragma unroll
@@ -292,10 +413,26 @@ __global__ void cross_entropy_kernel(float* logits, long long ld, const int32_t*
   __syncthreads();
   const float mx = row_max, sum = row_sum;
   const int t = targets[r];
-  for (int j = threadIdx.x; j < vocab; j += blockDim.x) {
-    float d = expf(z[j] - mx) / sum * grad_scale;  // ops_reduce.rs:266-270
-    if (j == t) d -= grad_scale;
-    z[j] = d;
+  if (vec) {
+    float4* z4 = reinterpret_cast<float4*>(z);
+    for (int j = threadIdx.x; j < vocab / 4; j += blockDim.x) {
+      const float4 v = z4[j];
+      float4 d = make_float4(expf(v.x - mx) / sum * grad_scale, expf(v.y - mx) / sum * grad_scale,
+                             expf(v.z - mx) / sum * grad_scale, expf(v.w - mx) / sum * grad_scale);
+      if ((t >> 2) == j) {
+        if ((t & 3) == 0) d.x -= grad_scale;
+        if ((t & 3) == 1) d.y -= grad_scale;
+        if ((t & 3) == 2) d.z -= grad_scale;
+        if ((t & 3) == 3) d.w -= grad_scale;
+      }
+      z4[j] = d;
+    }
+  } else {
+    for (int j = threadIdx.x; j < vocab; j += blockDim.x) {
+      float d = expf(z[j] - mx) / sum * grad_scale;  // ops_reduce.rs:266-270
+      if (j == t) d -= grad_scale;
+      z[j] = d;
+    }
   }
 }
 
@@ -378,7 +515,17 @@ void embedding_backward(const int32_t* uniq, const int32_t* offsets, const int32
 void rmsnorm_forward(const float* x, const float* w, int rows, int dim, float eps, float* y, float* rstd,
                      cudaStream_t s) {
   if (rows <= 0) return;
-  rmsnorm_fwd_kernel<<<rows, kThreads, 0, s>>>(x, w, dim, eps, y, rstd);
+  const int groups = (dim / 4 + kThreads - 1) / kThreads;
+  if (groups <= 1)
+    rmsnorm_fwd_kernel<1><<<rows, kThreads, 0, s>>>(x, w, dim, eps, y, rstd);
+  else if (groups <= 2)
+    rmsnorm_fwd_kernel<2><<<rows, kThreads, 0, s>>>(x, w, dim, eps, y, rstd);
+  else if (groups <= 4)
+    rmsnorm_fwd_kernel<4><<<rows, kThreads, 0, s>>>(x, w, dim, eps, y, rstd);
+  else if (groups <= 8)
+    rmsnorm_fwd_kernel<8><<<rows, kThreads, 0, s>>>(x, w, dim, eps, y, rstd);
+  else
+    throw std::runtime_error("rmsnorm_forward: d_model above 8192 is not supported");
   check_launch("rmsnorm_forward");
 }
 
@@ -401,7 +548,7 @@ void rmsnorm_backward(const float* x, const float* w, const float* rstd, const f
   else
     throw std::runtime_error("rmsnorm_backward: d_model above 8192 is not supported");
   check_launch("rmsnorm_backward");
-  column_sum_kernel<<<(dim + 255) / 256, 256, 0, s>>>(ws, nblk, dim, dw);
+  column_sum_kernel<<<(dim + 31) / 32, 256, 0, s>>>(ws, nblk, dim, dw);
   check_launch("rmsnorm_backward(column sum)");
 }
 
@@ -409,20 +556,35 @@ void rope(float* x, int rows, int T, int heads, int hd, long long ld, const floa
           bool backward, cudaStream_t s) {
   const long long total = static_cast<long long>(rows) * heads * (hd / 2);
   if (total <= 0) return;
-  rope_kernel<<<grid_for(total, 1), kThreads, 0, s>>>(x, rows, T, heads, hd / 2, ld, cos_t, sin_t,
-                                                       backward ? -1.0f : 1.0f);
+  const bool vec = (hd / 2) % 4 == 0 && ld % 4 == 0 && aligned16(x) && aligned16(cos_t) && aligned16(sin_t);
+  if (vec)
+    rope4_kernel<<<grid_for(total / 4, 2), kThreads, 0, s>>>(x, rows, T, heads, hd / 2, ld, cos_t, sin_t,
+                                                           backward ? -1.0f : 1.0f);
+  else
+    rope_kernel<<<grid_for(total, 1), kThreads, 0, s>>>(x, rows, T, heads, hd / 2, ld, cos_t, sin_t,
+                                                         backward ? -1.0f : 1.0f);
   check_launch("rope");
 }
 
 void swiglu_forward(const float* g, const float* u, float* act, long long n, cudaStream_t s) {
   if (n <= 0) return;
-  swiglu_fwd_kernel<<<grid_for(n, 4), kThreads, 0, s>>>(g, u, act, n);
+  if (n % 4 == 0 && aligned16(g) && aligned16(u) && aligned16(act))
+    swiglu_fwd4_kernel<<<grid_for(n / 4, 2), kThreads, 0, s>>>(reinterpret_cast<const float4*>(g),
+                                                               reinterpret_cast<const float4*>(u),
+                                                               reinterpret_cast<float4*>(act), n / 4);
+  else
+    swiglu_fwd_kernel<<<grid_for(n, 4), kThreads, 0, s>>>(g, u, act, n);
   check_launch("swiglu_forward");
 }
 
 void swiglu_backward(float* g, float* u, const float* dact, long long n, cudaStream_t s) {
   if (n <= 0) return;
-  swiglu_bwd_kernel<<<grid_for(n, 4), kThreads, 0, s>>>(g, u, dact, n);
+  if (n % 4 == 0 && aligned16(g) && aligned16(u) && aligned16(dact))
+    swiglu_bwd4_kernel<<<grid_for(n / 4, 2), kThreads, 0, s>>>(reinterpret_cast<float4*>(g),
+                                                               reinterpret_cast<float4*>(u),
+                                                               reinterpret_cast<const float4*>(dact), n / 4);
+  else
+    swiglu_bwd_kernel<<<grid_for(n, 4), kThreads, 0, s>>>(g, u, dact, n);
   check_launch("swiglu_backward");
 }
 

@@ -62,7 +62,7 @@ void Trainer::forward(int B, int T, bool train) {
     gemm(N, F, D, a.xn2, D, false, P_ + bo.up, F, true, a.u, F, nullptr, 0);
     swiglu_forward(a.g, a.u, a.act, static_cast<long long>(N) * F, stream_);
     gemm(N, D, F, a.act, F, false, P_ + bo.down, D, true, next_x, D, a.h, D);
-    launches_ += 7;
+    launches_ += 6;  // two RMSNorms, two RoPEs, attention, SwiGLU (GEMMs are counted in gemm())
   }
   rmsnorm_forward(x_final_, P_ + layout_.final_norm, N, D, eps, xf_, rstdf_, stream_);
   launches_ += 1;
@@ -127,7 +127,7 @@ void Trainer::backward(int B, int T) {
     gemm(D, KV, N, a.xn1, D, true, dk_, KV, true, G_ + bo.k, KV, nullptr, 0);
     gemm(D, KV, N, a.xn1, D, true, dv_, KV, true, G_ + bo.v, KV, nullptr, 0);
     rmsnorm_backward(a.x, P_ + bo.attn_norm, a.rstd1, dxn_, N, D, dx, dh, G_ + bo.attn_norm, norm_ws_, stream_);
-    launches_ += 12;
+    launches_ += 10;  // SwiGLU, two RMSNorm backwards (2 kernels each), attention backward (3), two RoPEs
     if (world_ > 1) {
       // This layer's gradients are final: average them while the next layer's
       // backward runs (a bucket per layer, in reverse parameter order).
