@@ -101,6 +101,100 @@ __device__ __forceinline__ TileInfo tile_info(int t, int M, int N, int K, const 
   return ti;
 }
 
+// Epilogue of one warp for its 32 rows (starting at wrow0) of a BM x BN tile:
+// the accumulator slice at TMEM address `acc` (lane = row) goes through the
+// warp's staging tile to C (+ R). As soon as the last TMEM slice is loaded the
+// warp arrives on `release_bar` (in the pair's leader CTA when `remote`), which
+// frees the accumulator for the tile after next.
+__device__ __forceinline__ void release(uint32_t bar, bool remote) {
+  if (remote)
+    mbar_arrive_remote(bar);
+  else
+    mbar_arrive(bar);
+}
+
+template <int BN>
+__device__ __forceinline__ void store_tile(uint32_t acc, bool has_k, float4* stage_tile, int wrow0, int n0, float* Ct,
+                                           long long ldc, const float* R, long long ldr, int M, int N,
+                                           uint32_t release_bar, bool remote) {
+  const int lane = threadIdx.x % 32;
+  bool released = false;
+  if (has_k) {
+    // Each 32-column slice goes TMEM -> registers (lane = row) -> this warp's
+    // staging tile -> global with 8 lanes per row, so every R load and C
+    // store instruction covers four whole 128-byte row segments. The
+    // residual of slice c + 1 is loaded before slice c is stored (slices
+    // are disjoint, so this holds when R aliases C).
+    const int sub = lane & 7, rsub = lane >> 3;
+    float4 rnext[8];
+    auto load_r = [&](int c) {
+      const int col = n0 + c * 32 + 4 * sub;
+#pragma unroll
+      for (int it = 0; it < 8; ++it) {
+        const int row = wrow0 + it * 4 + rsub;
+        rnext[it] = (col + 3 < N && row < M)
+                        ? *reinterpret_cast<const float4*>(R + static_cast<long long>(row) * ldr + col)
+                        : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    };
+    if (R) load_r(0);
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(acc + c * 32, r);
+      if (c == BN / 32 - 1) {  // the accumulator is free for the tile after next
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) release(release_bar, remote);
+        released = true;
+      }
+      // 4-float granules, XOR-swizzled by row: conflict-free both ways
+#pragma unroll
+      for (int g = 0; g < 8; ++g)
+        stage_tile[lane * 8 + (g ^ (lane & 7))] =
+            make_float4(__uint_as_float(r[4 * g]), __uint_as_float(r[4 * g + 1]), __uint_as_float(r[4 * g + 2]),
+                        __uint_as_float(r[4 * g + 3]));
+      __syncwarp();
+      float4 v[8];
+#pragma unroll
+      for (int it = 0; it < 8; ++it) {
+        const int rr = it * 4 + rsub;
+        v[it] = stage_tile[rr * 8 + (sub ^ (rr & 7))];
+        if (R) {
+          v[it].x += rnext[it].x; v[it].y += rnext[it].y; v[it].z += rnext[it].z; v[it].w += rnext[it].w;
+        }
+      }
+      if (R && c + 1 < BN / 32) load_r(c + 1);
+      const int col = n0 + c * 32 + 4 * sub;
+#pragma unroll
+      for (int it = 0; it < 8; ++it) {
+        const int row = wrow0 + it * 4 + rsub;
+        if (row >= M || col >= N) continue;
+        float* cp = Ct + static_cast<long long>(row) * ldc + col;
+        if (col + 3 < N) {
+          *reinterpret_cast<float4*>(cp) = v[it];
+        } else {  // ragged right edge: the residual was not prefetched
+          const float* rp = R ? R + static_cast<long long>(row) * ldr + col : nullptr;
+          const float vv[4] = {v[it].x, v[it].y, v[it].z, v[it].w};
+          for (int e = 0; e < 4 && col + e < N; ++e) cp[e] = vv[e] + (rp ? rp[e] : 0.0f);
+        }
+      }
+      __syncwarp();  // before the next slice overwrites the staging tile
+    }
+  } else {
+    // Empty K range: the product is zero, C = R (or 0).
+    const int row = wrow0 + lane;
+    if (row < M)
+      for (int col = n0; col < n0 + BN && col < N; ++col)
+        Ct[static_cast<long long>(row) * ldc + col] = R ? R[static_cast<long long>(row) * ldr + col] : 0.0f;
+  }
+  if (!released) {
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) release(release_bar, remote);
+  }
+}
+
 // Persistent: each CTA walks tiles blockIdx.x, blockIdx.x + gridDim.x, ... The
 // TMA/UMMA stage ring runs across tile boundaries, and the accumulator is
 // double-buffered in TMEM, so the epilogue of one tile overlaps the MMAs of the
@@ -259,82 +353,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc_fence_after();
       float* Ct = C;
       if (BATCHED) Ct += (ti.z / bt.c_zdiv) * bt.c_sb + ((ti.z % bt.c_zdiv) / bt.c_zgroup) * bt.c_sh;
-      const int wrow0 = ti.m0 + quarter * 32;  // this warp's 32 rows
-      bool released = false;
-      if (ti.n_k > 0) {
-        // Each 32-column slice goes TMEM -> registers (lane = row) -> this warp's
-        // staging tile -> global with 8 lanes per row, so every R load and C
-        // store instruction covers four whole 128-byte row segments. The
-        // residual of slice c + 1 is loaded before slice c is stored (slices
-        // are disjoint, so this holds when R aliases C).
-        const int sub = lane & 7, rsub = lane >> 3;
-        float4 rnext[8];
-        auto load_r = [&](int c) {
-          const int col = ti.n0 + c * 32 + 4 * sub;
-#pragma unroll
-          for (int it = 0; it < 8; ++it) {
-            const int row = wrow0 + it * 4 + rsub;
-            rnext[it] = (col + 3 < N && row < M)
-                            ? *reinterpret_cast<const float4*>(R + static_cast<long long>(row) * ldr + col)
-                            : make_float4(0.f, 0.f, 0.f, 0.f);
-          }
-        };
-        if (R) load_r(0);
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(tmem_base + buf * BN + (static_cast<uint32_t>(quarter * 32) << 16) + c * 32, r);
-          if (c == BN / 32 - 1) {  // the accumulator is free for the tile after next
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(acc_empty(buf));
-            released = true;
-          }
-          // 4-float granules, XOR-swizzled by row: conflict-free both ways
-#pragma unroll
-          for (int g = 0; g < 8; ++g)
-            stage_tile[lane * 8 + (g ^ (lane & 7))] =
-                make_float4(__uint_as_float(r[4 * g]), __uint_as_float(r[4 * g + 1]), __uint_as_float(r[4 * g + 2]),
-                            __uint_as_float(r[4 * g + 3]));
-          __syncwarp();
-          float4 v[8];
-#pragma unroll
-          for (int it = 0; it < 8; ++it) {
-            const int rr = it * 4 + rsub;
-            v[it] = stage_tile[rr * 8 + (sub ^ (rr & 7))];
-            if (R) {
-              v[it].x += rnext[it].x; v[it].y += rnext[it].y; v[it].z += rnext[it].z; v[it].w += rnext[it].w;
-            }
-          }
-          if (R && c + 1 < BN / 32) load_r(c + 1);
-          const int col = ti.n0 + c * 32 + 4 * sub;
-#pragma unroll
-          for (int it = 0; it < 8; ++it) {
-            const int row = wrow0 + it * 4 + rsub;
-            if (row >= M || col >= N) continue;
-            float* cp = Ct + static_cast<long long>(row) * ldc + col;
-            if (col + 3 < N) {
-              *reinterpret_cast<float4*>(cp) = v[it];
-            } else {  // ragged right edge: the residual was not prefetched
-              const float* rp = R ? R + static_cast<long long>(row) * ldr + col : nullptr;
-              const float vv[4] = {v[it].x, v[it].y, v[it].z, v[it].w};
-              for (int e = 0; e < 4 && col + e < N; ++e) cp[e] = vv[e] + (rp ? rp[e] : 0.0f);
-            }
-          }
-          __syncwarp();  // before the next slice overwrites the staging tile
-        }
-      } else {
-        // Empty K range: the product is zero, C = R (or 0).
-        const int row = wrow0 + lane;
-        if (row < M)
-          for (int col = ti.n0; col < ti.n0 + BN && col < N; ++col)
-            Ct[static_cast<long long>(row) * ldc + col] = R ? R[static_cast<long long>(row) * ldr + col] : 0.0f;
-      }
-      if (!released) {
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(acc_empty(buf));
-      }
+      store_tile<BN>(tmem_base + buf * BN + (static_cast<uint32_t>(quarter * 32) << 16), ti.n_k > 0, stage_tile,
+                     ti.m0 + quarter * 32, ti.n0, Ct, ldc, R, ldr, M, N, acc_empty(buf), false);
       ++j;
     }
   }
@@ -352,6 +372,175 @@ __global__ void __launch_bounds__(THREADS, 1)
     tmem_dealloc(tmem_base, ACC_COLS);
   }
   __syncthreads();
+}
+
+// ------------------------------------------------------------------ CTA pairs
+// A cluster of two CTAs computes 256 x 256 output tiles: CTA r loads rows
+// m0 + 128 r of A and rows n0 + 128 r of B (its half of the UMMA's N), the
+// leader issues M = 256 cta_group::2 UMMAs, and each CTA's TMEM holds the
+// accumulator of its 128 rows. Per stage a CTA loads 32 KB (16 KB of A, 16 KB
+// of B) for the same MMA work per SM that costs a single CTA 48 KB (A plus a
+// 256-wide B), so the ring is deeper (6 stages) and L2 serves a third less.
+constexpr int PBN = 256;
+constexpr int P_B_BYTES = (PBN / 2) * BK * 4;  // 16 KB
+constexpr int P_STAGE = A_STAGE_BYTES + P_B_BYTES;
+constexpr int P_STAGES = 6;
+constexpr int P_SMEM = P_STAGES * P_STAGE + 1024 + 256 + 4 * 32 * 32 * 4;
+
+template <bool A_MN, bool B_MN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, float* C,
+                     long long ldc, const float* R, long long ldr, int M, int N, int K, int* err, int total_tiles,
+                     int mn3d) {
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = static_cast<int>(blockIdx.x) / 2, npairs = static_cast<int>(gridDim.x) / 2;
+  const int tm = (M + 2 * BM - 1) / (2 * BM);
+  const int n_k = (K + BK - 1) / BK;
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (base - raw_addr);
+  const uint32_t bar_base = base + P_STAGES * P_STAGE;
+  auto full_bar = [&](int s) { return bar_base + 8u * s; };
+  auto empty_bar = [&](int s) { return bar_base + 8u * (P_STAGES + s); };
+  auto acc_full = [&](int b) { return bar_base + 8u * (2 * P_STAGES + b); };
+  auto acc_empty = [&](int b) { return bar_base + 8u * (2 * P_STAGES + 2 + b); };
+  const uint32_t tmem_slot = bar_base + 8u * (2 * P_STAGES + 4);
+  uint8_t* tail = smem + P_STAGES * P_STAGE + 8 * (2 * P_STAGES + 4);
+  uint32_t* tmem_slot_ptr = reinterpret_cast<uint32_t*>(tail);
+  int* loads_issued = reinterpret_cast<int*>(tail + 8);
+  int* loads_consumed = loads_issued + 1;
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    for (int s = 0; s < P_STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(acc_full(b), 1);
+      mbar_init(acc_empty(b), 8);  // four epilogue warps in each CTA
+    }
+    *loads_issued = 0;
+    *loads_consumed = 0;
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, 2 * PBN);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot_ptr;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer (both CTAs); completions land on the leader's barriers
+      int it = 0;
+      bool ok = true;
+      for (int t = pair; t < total_tiles && ok; t += npairs) {
+        const int my_m0 = (t % tm) * 2 * BM + static_cast<int>(rank) * BM;
+        const int my_n0 = (t / tm) * PBN + static_cast<int>(rank) * (PBN / 2);
+        for (int i = 0; i < n_k; ++i, ++it) {
+          const int s = it % P_STAGES, round = it / P_STAGES;
+          if (round > 0 && !mbar_wait(empty_bar(s), (round - 1) & 1, err, kErrWaitEmpty)) {
+            ok = false;
+            break;
+          }
+          if (leader) mbar_arrive_expect_tx(full_bar(s), 2 * P_STAGE);
+          const uint32_t fb = mapa_shared(full_bar(s), 0);
+          const uint32_t sa = base + s * P_STAGE, sb = sa + A_STAGE_BYTES;
+          const int k0 = i * BK;
+          if (!A_MN) {
+            tma_load_2d_pair(sa, &tmA, fb, k0, my_m0);
+          } else if (mn3d & 1) {
+            tma_load_3d_pair(sa, &tmA, fb, 0, k0, my_m0 / 32);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BM / 32; ++j) tma_load_2d_pair(sa + j * MN_BLOCK_BYTES, &tmA, fb, my_m0 + 32 * j, k0);
+          }
+          if (!B_MN) {
+            tma_load_2d_pair(sb, &tmB, fb, k0, my_n0);
+          } else if (mn3d & 2) {
+            tma_load_3d_pair(sb, &tmB, fb, 0, k0, my_n0 / 32);
+          } else {
+#pragma unroll
+            for (int j = 0; j < PBN / 64; ++j) tma_load_2d_pair(sb + j * MN_BLOCK_BYTES, &tmB, fb, my_n0 + 32 * j, k0);
+          }
+          *loads_issued = it + 1;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ---------------- UMMA issuer (leader only), M = 256 across the pair
+      constexpr uint32_t idesc = idesc_tf32(2 * BM, PBN, A_MN, B_MN);
+      int it = 0, j = 0;
+      bool ok = true;
+      for (int t = pair; t < total_tiles && ok; t += npairs) {
+        const int buf = j & 1;
+        if (j >= 2 && !mbar_wait_cluster(acc_empty(buf), ((j >> 1) - 1) & 1, err, kErrWaitAccum)) break;
+        tc_fence_after();
+        const uint32_t acc = tmem_base + buf * PBN;
+        for (int i = 0; i < n_k; ++i, ++it) {
+          const int s = it % P_STAGES, round = it / P_STAGES;
+          if (!mbar_wait(full_bar(s), round & 1, err, kErrWaitFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          *loads_consumed = it + 1;
+          const uint32_t sa = base + s * P_STAGE, sb = sa + A_STAGE_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 8; ++k) {
+            const uint64_t adesc = A_MN ? smem_desc(sa + k * 1024, MN_BLOCK_BYTES, 512, kLayoutSw128Base32)
+                                        : smem_desc(sa + k * 32, 16, 1024, kLayoutSw128);
+            const uint64_t bdesc = B_MN ? smem_desc(sb + k * 1024, MN_BLOCK_BYTES, 512, kLayoutSw128Base32)
+                                        : smem_desc(sb + k * 32, 16, 1024, kLayoutSw128);
+            umma_tf32_pair(acc, adesc, bdesc, idesc, (i | k) != 0 ? 1u : 0u);
+          }
+          umma_commit_pair(empty_bar(s), 0x3);
+        }
+        umma_commit_pair(acc_full(buf), 0x3);
+        ++j;
+      }
+    }
+  } else {
+    // ---------------- epilogue (both CTAs): this CTA's 128 rows, all 256 columns
+    const int quarter = warp & 3;
+    float4* stage_tile = reinterpret_cast<float4*>(smem + P_STAGES * P_STAGE + 256) + quarter * 256;
+    int j = 0;
+    for (int t = pair; t < total_tiles; t += npairs) {
+      const int buf = j & 1;
+      if (!mbar_wait(acc_full(buf), (j >> 1) & 1, err, kErrWaitAccum)) break;
+      tc_fence_after();
+      const int my_m0 = (t % tm) * 2 * BM + static_cast<int>(rank) * BM;
+      store_tile<PBN>(tmem_base + buf * PBN + (static_cast<uint32_t>(quarter * 32) << 16), true, stage_tile,
+                      my_m0 + quarter * 32, (t / tm) * PBN, C, ldc, R, ldr, M, N, mapa_shared(acc_empty(buf), 0),
+                      true);
+      ++j;
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync();  // both CTAs are done with their TMEM and with each other's barriers
+  if (leader && threadIdx.x == 0) {
+    // after a timed-out wait, let the pair's copies in flight land (bounded)
+    for (int i = *loads_consumed; i < *loads_issued; ++i)
+      if (!mbar_wait(full_bar(i % P_STAGES), (i / P_STAGES) & 1, err, kErrWaitDrain, 1000000000ull)) break;
+  }
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, 2 * PBN);
+  }
 }
 
 }  // namespace
@@ -465,6 +654,23 @@ void launch_majors(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMa
   else launch<true, true, BN, BATCHED>(ta, tb, C, ldc, R, ldr, M, N, K, batch, bt, err, s, mn3d);
 }
 
+template <bool A_MN, bool B_MN>
+void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, float* C, long long ldc, const float* R, long long ldr,
+                 int M, int N, int K, int* err, cudaStream_t stream, int mn3d) {
+  auto kern = gemm_pair_kernel<A_MN, B_MN>;
+  static thread_local int configured_device = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_device != dev) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM);
+    configured_device = dev;
+  }
+  const long long tiles = static_cast<long long>((M + 2 * BM - 1) / (2 * BM)) * ((N + PBN - 1) / PBN);
+  const int pairs = device_sms() / 2;
+  const int grid = 2 * static_cast<int>(tiles < pairs ? tiles : pairs);
+  kern<<<grid, THREADS, P_SMEM, stream>>>(ta, tb, C, ldc, R, ldr, M, N, K, err, static_cast<int>(tiles), mn3d);
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace
@@ -486,10 +692,13 @@ int gemm_tf32(int M, int N, int K, GemmOperand A, GemmOperand B, float* C, long 
   if (M == 0 || N == 0) return 0;
   if (K > 0 && (!A.ptr || !B.ptr)) return kGemmBadArgument;
   if ((ldc & 3) || !aligned16(C) || (R && ((ldr & 3) || !aligned16(R)))) return kGemmMisaligned;
-  // Narrow outputs waste less of a 256-wide tile with a 128-wide one, and so do
-  // products whose 256-wide tiles would leave half of the SMs idle.
+  // 256 x 256 tiles on CTA pairs when they fill the SMs; otherwise single CTAs
+  // with 128 x 256 tiles, or 128 x 128 ones for narrow outputs and for products
+  // whose 256-wide tiles would leave half of the SMs idle.
   const long long tiles256 = static_cast<long long>((M + BM - 1) / BM) * ((N + 255) / 256);
-  const int bn = (N <= 128 || 2 * tiles256 <= device_sms()) ? 128 : 256;
+  const long long pair_tiles = static_cast<long long>((M + 2 * BM - 1) / (2 * BM)) * ((N + PBN - 1) / PBN);
+  const bool use_pair = K > 0 && N > 128 && 2 * pair_tiles >= device_sms();
+  const int bn = use_pair ? PBN : (N <= 128 || 2 * tiles256 <= device_sms()) ? 128 : 256;
   CUtensorMap ta{}, tb{};
   int mn3d = 0;
   if (K > 0) {
@@ -501,11 +710,19 @@ int gemm_tf32(int M, int N, int K, GemmOperand A, GemmOperand B, float* C, long 
              : A.mn_major ? make_map2d(&ta, A.ptr, M, K, A.ld, 32, BK, true)
                           : make_map2d(&ta, A.ptr, K, M, A.ld, BK, BM, false);
     if (rc) return kGemmTensorMap;
-    rc = b3 ? make_map_mn3d(&tb, B.ptr, N, K, B.ld, bn)
+    const int b_box = use_pair ? PBN / 2 : bn;  // a pair's CTA loads half of B's tile
+    rc = b3 ? make_map_mn3d(&tb, B.ptr, N, K, B.ld, b_box)
          : B.mn_major ? make_map2d(&tb, B.ptr, N, K, B.ld, 32, BK, true)
-                      : make_map2d(&tb, B.ptr, K, N, B.ld, BK, bn, false);
+                      : make_map2d(&tb, B.ptr, K, N, B.ld, BK, b_box, false);
     if (rc) return kGemmTensorMap;
     mn3d = (a3 ? 1 : 0) | (b3 ? 2 : 0);
+  }
+  if (use_pair) {
+    if (!A.mn_major && !B.mn_major) launch_pair<false, false>(ta, tb, C, ldc, R, ldr, M, N, K, d_err, stream, mn3d);
+    else if (!A.mn_major) launch_pair<false, true>(ta, tb, C, ldc, R, ldr, M, N, K, d_err, stream, mn3d);
+    else if (!B.mn_major) launch_pair<true, false>(ta, tb, C, ldc, R, ldr, M, N, K, d_err, stream, mn3d);
+    else launch_pair<true, true>(ta, tb, C, ldc, R, ldr, M, N, K, d_err, stream, mn3d);
+    return cudaGetLastError() == cudaSuccess ? 0 : kGemmLaunch;
   }
   const GemmBatch bt{};
   if (bn == 128)

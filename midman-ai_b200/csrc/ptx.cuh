@@ -150,6 +150,16 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
+// 2-D tile load of one CTA of a pair (cta_group::2, no multicast); see below.
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar, int32_t x,
+                                                 int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
+      : "memory");
+}
+
 // 3-D tile load of one CTA of a pair (cta_group::2, no multicast): the bytes
 // land in this CTA's shared memory and complete on the mbarrier at `bar`, a
 // shared::cluster address in the pair's leader CTA.

@@ -35,8 +35,10 @@ def rel_l2(got, want):
     return ((got.double() - want).norm() / want.norm().clamp_min(1e-300)).item()
 
 
+# The last three run on CTA pairs (256 x 256 tiles): ragged M and N (2-D boxes for
+# MN-major operands whose extent is not a multiple of 32), ragged K.
 SHAPES = [(128, 256, 32), (256, 512, 512), (300, 344, 200), (64, 8, 12), (1000, 1032, 1000),
-          (4096, 1408, 512)]
+          (4096, 1408, 512), (2200, 2340, 300), (2304, 4096, 64)]
 MAJORS = [(False, True), (False, False), (True, True), (True, False)]
 
 
