@@ -709,7 +709,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(BTHREADS, 1)
       constexpr uint32_t idesc_g = idesc_tf32(2 * TILE, HD, false, true);
       bool ok = mbar_wait(bars.tile_full(), 0, p.err, kErrWaitFull);
       if (ok) tl->tile_pending = 0;
-      ok = ok && mbar_wait_cluster(bars.opnd_ready(), 0, p.err, kErrWaitAccum);
+      ok = ok && mbar_wait(bars.opnd_ready(), 0, p.err, kErrWaitAccum);
       auto issue_s = [&](int t) -> bool {
         const int s = t % STAGES, bb = t & 1, u = t >> 1;
         if (!mbar_wait(bars.full(s), (t / STAGES) & 1, p.err, kErrWaitFull)) return false;
@@ -732,7 +732,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(BTHREADS, 1)
       for (int t = 0; ok && t < n_steps; ++t) {
         if (t + 1 < n_steps && !issue_s(t + 1)) break;
         const int s = t % STAGES, bb = t & 1;
-        if (!mbar_wait_cluster(bars.p_full(bb), (t >> 1) & 1, p.err, kErrWaitAccum)) break;
+        if (!mbar_wait(bars.p_full(bb), (t >> 1) & 1, p.err, kErrWaitAccum)) break;
         tc_fence_after();
         const uint32_t st = stage(s);
 #pragma unroll
@@ -777,19 +777,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(BTHREADS, 1)
         break;
       }
       tc_fence_after();
-      uint32_t sv[32], dv[32];
-      tmem_ld_32x32b_x32(tmem + lane_base + s_col_of(grp, PBLK_KV), sv);
-      tmem_ld_32x32b_x32(tmem + lane_base + dp_col_of(grp, PBLK_KV), dv);
+      // S^T and dP^T of this buffer are adjacent: columns [0, 32) and [32, 64)
+      uint32_t sd[64];
+      tmem_ld_32x32b_x64(tmem + lane_base + s_col_of(grp, PBLK_KV), sd);
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
         const int q = qs + i;
         const bool keep = q < p.T && key <= q;
-        const float pv = keep ? ex2_approx(fmaf(__uint_as_float(sv[i]), p.scale_log2, -l2[i])) : 0.0f;
-        sv[i] = __float_as_uint(pv);
-        dv[i] = __float_as_uint(pv * (__uint_as_float(dv[i]) - dl[i]) * p.scale);
+        const float pv = keep ? ex2_approx(fmaf(__uint_as_float(sd[i]), p.scale_log2, -l2[i])) : 0.0f;
+        sd[i] = __float_as_uint(pv);
+        sd[32 + i] = __float_as_uint(pv * (__uint_as_float(sd[32 + i]) - dl[i]) * p.scale);
       }
-      tmem_st_32x32b_x32(tmem + lane_base + s_col_of(grp, PBLK_KV), sv);
-      tmem_st_32x32b_x32(tmem + lane_base + dp_col_of(grp, PBLK_KV), dv);
+      tmem_st_32x32b_x64(tmem + lane_base + s_col_of(grp, PBLK_KV), sd);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(p_full_lead);
@@ -886,7 +885,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(BTHREADS, 1)
       constexpr uint32_t idesc_g = idesc_tf32(2 * TILE, HD, false, true);
       bool ok = mbar_wait(bars.tile_full(), 0, p.err, kErrWaitFull);
       if (ok) tl->tile_pending = 0;
-      ok = ok && mbar_wait_cluster(bars.opnd_ready(), 0, p.err, kErrWaitAccum);
+      ok = ok && mbar_wait(bars.opnd_ready(), 0, p.err, kErrWaitAccum);
       auto issue_s = [&](int j) -> bool {
         const int s = j % STAGES, bb = j & 1, u = j >> 1;
         if (!mbar_wait(bars.full(s), (j / STAGES) & 1, p.err, kErrWaitFull)) return false;
@@ -909,7 +908,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(BTHREADS, 1)
       for (int j = 0; ok && j < n_kv; ++j) {
         if (j + 1 < n_kv && !issue_s(j + 1)) break;
         const int s = j % STAGES, bb = j & 1;
-        if (!mbar_wait_cluster(bars.p_full(bb), (j >> 1) & 1, p.err, kErrWaitAccum)) break;
+        if (!mbar_wait(bars.p_full(bb), (j >> 1) & 1, p.err, kErrWaitAccum)) break;
         tc_fence_after();
         const uint32_t st = stage(s);
 #pragma unroll
@@ -947,19 +946,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(BTHREADS, 1)
         break;
       }
       tc_fence_after();
+      {
+        // S and dP of this buffer are adjacent: columns [0, 64) and [64, 128)
+        uint32_t sd[2 * PBLK_Q];
+        tmem_ld_32x32b_x128(tmem + lane_base + s_col_of(grp, PBLK_Q), sd);
+        const int kb = j * PBLK_Q;
+        uint32_t ds[PBLK_Q];
 #pragma unroll
-      for (int c = 0; c < PBLK_Q / 32; ++c) {
-        uint32_t sv[32], dv[32];
-        tmem_ld_32x32b_x32(tmem + lane_base + s_col_of(grp, PBLK_Q) + c * 32, sv);
-        tmem_ld_32x32b_x32(tmem + lane_base + dp_col_of(grp, PBLK_Q) + c * 32, dv);
-        const int kb = j * PBLK_Q + c * 32;
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
+        for (int i = 0; i < PBLK_Q; ++i) {
           const bool keep = q_ok && kb + i <= q;
-          const float pv = keep ? ex2_approx(fmaf(__uint_as_float(sv[i]), p.scale_log2, -lse2)) : 0.0f;
-          dv[i] = __float_as_uint(pv * (__uint_as_float(dv[i]) - dlt) * p.scale);
+          const float pv = keep ? ex2_approx(fmaf(__uint_as_float(sd[i]), p.scale_log2, -lse2)) : 0.0f;
+          ds[i] = __float_as_uint(pv * (__uint_as_float(sd[PBLK_Q + i]) - dlt) * p.scale);
         }
-        tmem_st_32x32b_x32(tmem + lane_base + dp_col_of(grp, PBLK_Q) + c * 32, dv);
+        tmem_st_32x32b_x64(tmem + lane_base + dp_col_of(grp, PBLK_Q), ds);
       }
       tc_fence_before();
       __syncwarp();

@@ -491,7 +491,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(FTHREADS, 1)
       for (int j = 0; ok && j < n_kv; ++j) {
         if (j + 1 < n_kv && !issue_s(j + 1)) break;
         const int s = j % STAGES, bb = j & 1;
-        if (!mbar_wait_cluster(p_full(bb), (j >> 1) & 1, p.err, kErrWaitAccum)) break;
+        if (!mbar_wait(p_full(bb), (j >> 1) & 1, p.err, kErrWaitAccum)) break;
         if (!mbar_wait(v_full(s), (j / STAGES) & 1, p.err, kErrWaitFull)) break;
         *kv_consumed = j + 1;
         tc_fence_after();
@@ -527,21 +527,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(FTHREADS, 1)
         break;
       }
       tc_fence_after();
-      uint32_t r[4][32];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_ld_32x32b_x32(tmem + lane_base + s_col + c * 32, r[c]);
+      uint32_t r[PKV];
+      tmem_ld_32x32b_x128(tmem + lane_base + s_col, r);
       const int kv0 = j * PKV;
       const bool diag = kv0 + PKV - 1 > my_q0;
       float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          float x = __uint_as_float(r[c][i]) * p.scale_log2;
-          if (diag && kv0 + c * 32 + i > q) x = -INFINITY;
-          r[c][i] = __float_as_uint(x);
-          mx[i & 3] = fmaxf(mx[i & 3], x);
-        }
+      for (int i = 0; i < PKV; ++i) {
+        float x = __uint_as_float(r[i]) * p.scale_log2;
+        if (diag && kv0 + i > q) x = -INFINITY;
+        r[i] = __float_as_uint(x);
+        mx[i & 3] = fmaxf(mx[i & 3], x);
+      }
       const float m_new = fmaxf(m_run, fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])));
       if (k == 0) {
         m_run = m_new;
@@ -571,16 +568,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(FTHREADS, 1)
       const float mref = m_run == -INFINITY ? 0.0f : m_run;
       float ls[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-      for (int c = 0; c < 4; ++c)
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float e = ex2_approx(__uint_as_float(r[c][i]) - mref);
-          ls[i & 3] += e;
-          r[c][i] = __float_as_uint(e);
-        }
+      for (int i = 0; i < PKV; ++i) {
+        const float e = ex2_approx(__uint_as_float(r[i]) - mref);
+        ls[i & 3] += e;
+        r[i] = __float_as_uint(e);
+      }
       l_run += (ls[0] + ls[1]) + (ls[2] + ls[3]);
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tmem_st_32x32b_x32(tmem + lane_base + s_col + c * 32, r[c]);
+      tmem_st_32x32b_x128(tmem + lane_base + s_col, r);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(p_full_lead);

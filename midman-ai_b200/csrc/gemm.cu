@@ -486,7 +486,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       bool ok = true;
       for (int t = pair; t < total_tiles && ok; t += npairs) {
         const int buf = j & 1;
-        if (j >= 2 && !mbar_wait_cluster(acc_empty(buf), ((j >> 1) - 1) & 1, err, kErrWaitAccum)) break;
+        if (j >= 2 && !mbar_wait(acc_empty(buf), ((j >> 1) - 1) & 1, err, kErrWaitAccum)) break;
         tc_fence_after();
         const uint32_t acc = tmem_base + buf * PBN;
         for (int i = 0; i < n_k; ++i, ++it) {
