@@ -118,6 +118,12 @@ struct Bars {
   }
 };
 
+// Byte offset of contraction step kk (8 tf32) in a K-major tile of `rows` rows
+// stored as 128-byte chunks of 32 elements (chunk stride rows * 128 bytes).
+__host__ __device__ constexpr uint32_t kchunk_off(int rows, int kk) {
+  return static_cast<uint32_t>((kk / 4) * (rows * 128) + (kk % 4) * 32);
+}
+
 // K-major descriptor of contraction step kk (8 tf32) in a tile of `rows` rows
 // stored as 128-byte chunks of 32 elements (chunk stride rows * 128 bytes).
 __device__ __forceinline__ uint64_t kmajor_desc(uint32_t tile, int rows, int kk) {
@@ -588,10 +594,14 @@ struct PairBars {
   __device__ uint32_t empty(int s) const { return base + 8u * (1 + STAGES + s); }
   __device__ uint32_t s_full(int bb) const { return base + 8u * (1 + 2 * STAGES + bb); }
   __device__ uint32_t p_full(int bb) const { return base + 8u * (3 + 2 * STAGES + bb); }
+  // S (P) part and dP (dS) part of buffer bb no longer read by an UMMA: freed
+  // separately, so the next product into one part overlaps the UMMAs still
+  // reading the other
   __device__ uint32_t s_free(int bb) const { return base + 8u * (5 + 2 * STAGES + bb); }
-  __device__ uint32_t opnd_ready() const { return base + 8u * (7 + 2 * STAGES); }
-  __device__ uint32_t acc_done() const { return base + 8u * (8 + 2 * STAGES); }
-  __device__ uint32_t slot() const { return base + 8u * (9 + 2 * STAGES); }
+  __device__ uint32_t dp_free(int bb) const { return base + 8u * (7 + 2 * STAGES + bb); }
+  __device__ uint32_t opnd_ready() const { return base + 8u * (9 + 2 * STAGES); }
+  __device__ uint32_t acc_done() const { return base + 8u * (10 + 2 * STAGES); }
+  __device__ uint32_t slot() const { return base + 8u * (11 + 2 * STAGES); }
   __device__ void init() const {
     mbar_init(tile_full(), 1);
     for (int s = 0; s < STAGES; ++s) {
@@ -602,6 +612,7 @@ struct PairBars {
       mbar_init(s_full(bb), 1);
       mbar_init(p_full(bb), 8);  // one warpgroup of each CTA
       mbar_init(s_free(bb), 1);
+      mbar_init(dp_free(bb), 1);
     }
     mbar_init(opnd_ready(), 16);  // every softmax warp of both CTAs
     mbar_init(acc_done(), 1);
@@ -707,6 +718,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(BTHREADS, 1)
       // ---------------- UMMA issuer (leader only), M = 256 keys across the pair
       constexpr uint32_t idesc_s = idesc_tf32(2 * TILE, PBLK_KV, false, false);
       constexpr uint32_t idesc_g = idesc_tf32(2 * TILE, HD, false, true);
+      const uint64_t dk0 = kmajor_desc(sK, TILE, 0);
       bool ok = mbar_wait(bars.tile_full(), 0, p.err, kErrWaitFull);
       if (ok) tl->tile_pending = 0;
       ok = ok && mbar_wait(bars.opnd_ready(), 0, p.err, kErrWaitAccum);
@@ -717,14 +729,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(BTHREADS, 1)
         if (u > 0 && !mbar_wait(bars.s_free(bb), (u - 1) & 1, p.err, kErrWaitAccum)) return false;
         tc_fence_after();
         const uint32_t st = stage(s);
+        const uint64_t dq0 = kmajor_desc(st, PBLK_KV / 2, 0), ddo0 = kmajor_desc(st + Cfg::KV_HALF_K, PBLK_KV / 2, 0);
 #pragma unroll
         for (int kk = 0; kk < HD / 8; ++kk)  // S^T = K Q^T
-          umma_tf32_pair(tmem + s_col_of(bb, PBLK_KV), kmajor_desc(sK, TILE, kk),
-                         kmajor_desc(st, PBLK_KV / 2, kk), idesc_s, kk > 0 ? 1u : 0u);
+          umma_tf32_pair(tmem + s_col_of(bb, PBLK_KV), desc_add(dk0, kchunk_off(TILE, kk)),
+                         desc_add(dq0, kchunk_off(PBLK_KV / 2, kk)), idesc_s, kk > 0 ? 1u : 0u);
+        if (u > 0 && !mbar_wait(bars.dp_free(bb), (u - 1) & 1, p.err, kErrWaitAccum)) return false;
+        tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < HD / 8; ++kk)  // dP^T = V dO^T, V in TMEM
           umma_tf32_ts_pair(tmem + dp_col_of(bb, PBLK_KV), tmem + Cfg::KV_OPND + kk * 8,
-                            kmajor_desc(st + Cfg::KV_HALF_K, PBLK_KV / 2, kk), idesc_s, kk > 0 ? 1u : 0u);
+                            desc_add(ddo0, kchunk_off(PBLK_KV / 2, kk)), idesc_s, kk > 0 ? 1u : 0u);
         umma_commit_pair(bars.s_full(bb), 0x3);
         return true;
       };
@@ -735,17 +750,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(BTHREADS, 1)
         if (!mbar_wait(bars.p_full(bb), (t >> 1) & 1, p.err, kErrWaitAccum)) break;
         tc_fence_after();
         const uint32_t st = stage(s);
+        const uint64_t ddom0 = mnmajor_desc_rows(st + 2 * Cfg::KV_HALF_K + Cfg::KV_HALF_M, PBLK_KV, 0);
+        const uint64_t dqm0 = mnmajor_desc_rows(st + 2 * Cfg::KV_HALF_K, PBLK_KV, 0);
 #pragma unroll
-        for (int kk = 0; kk < PBLK_KV / 8; ++kk) {
-          const uint32_t acc = (t > 0 || kk > 0) ? 1u : 0u;
-          umma_tf32_ts_pair(tmem + Cfg::KV_DV, tmem + s_col_of(bb, PBLK_KV) + kk * 8,
-                            mnmajor_desc_rows(st + 2 * Cfg::KV_HALF_K + Cfg::KV_HALF_M, PBLK_KV, kk), idesc_g,
-                            acc);  // dV += P dO
-          umma_tf32_ts_pair(tmem + Cfg::KV_DK, tmem + dp_col_of(bb, PBLK_KV) + kk * 8,
-                            mnmajor_desc_rows(st + 2 * Cfg::KV_HALF_K, PBLK_KV, kk), idesc_g, acc);  // dK += dS Q
-        }
-        umma_commit_pair(bars.empty(s), 0x3);
+        for (int kk = 0; kk < PBLK_KV / 8; ++kk)  // dV += P dO
+          umma_tf32_ts_pair(tmem + Cfg::KV_DV, tmem + s_col_of(bb, PBLK_KV) + kk * 8, desc_add(ddom0, kk * 1024),
+                            idesc_g, (t > 0 || kk > 0) ? 1u : 0u);
         umma_commit_pair(bars.s_free(bb), 0x1);
+#pragma unroll
+        for (int kk = 0; kk < PBLK_KV / 8; ++kk)  // dK += dS Q
+          umma_tf32_ts_pair(tmem + Cfg::KV_DK, tmem + dp_col_of(bb, PBLK_KV) + kk * 8, desc_add(dqm0, kk * 1024),
+                            idesc_g, (t > 0 || kk > 0) ? 1u : 0u);
+        umma_commit_pair(bars.dp_free(bb), 0x1);
+        umma_commit_pair(bars.empty(s), 0x3);
       }
       umma_commit_pair(bars.acc_done(), 0x3);
     }
@@ -883,6 +900,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(BTHREADS, 1)
       // ---------------- UMMA issuer (leader only), M = 256 queries across the pair
       constexpr uint32_t idesc_s = idesc_tf32(2 * TILE, PBLK_Q, false, false);
       constexpr uint32_t idesc_g = idesc_tf32(2 * TILE, HD, false, true);
+      const uint64_t dqt0 = kmajor_desc(sQ, TILE, 0);
       bool ok = mbar_wait(bars.tile_full(), 0, p.err, kErrWaitFull);
       if (ok) tl->tile_pending = 0;
       ok = ok && mbar_wait(bars.opnd_ready(), 0, p.err, kErrWaitAccum);
@@ -890,17 +908,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(BTHREADS, 1)
         const int s = j % STAGES, bb = j & 1, u = j >> 1;
         if (!mbar_wait(bars.full(s), (j / STAGES) & 1, p.err, kErrWaitFull)) return false;
         tl->consumed = j + 1;
-        if (u > 0 && !mbar_wait(bars.s_free(bb), (u - 1) & 1, p.err, kErrWaitAccum)) return false;
+        // the S part was last read by the softmax of block j - 2, whose p_full
+        // this thread has already waited for; the dP part by dQ(j - 2)
         tc_fence_after();
         const uint32_t st = stage(s);
+        const uint64_t dkk0 = kmajor_desc(st, PBLK_Q / 2, 0), dvk0 = kmajor_desc(st + Cfg::Q_HALF_K, PBLK_Q / 2, 0);
 #pragma unroll
         for (int kk = 0; kk < HD / 8; ++kk)  // S = Q K^T
-          umma_tf32_pair(tmem + s_col_of(bb, PBLK_Q), kmajor_desc(sQ, TILE, kk), kmajor_desc(st, PBLK_Q / 2, kk),
-                         idesc_s, kk > 0 ? 1u : 0u);
+          umma_tf32_pair(tmem + s_col_of(bb, PBLK_Q), desc_add(dqt0, kchunk_off(TILE, kk)),
+                         desc_add(dkk0, kchunk_off(PBLK_Q / 2, kk)), idesc_s, kk > 0 ? 1u : 0u);
+        if (u > 0 && !mbar_wait(bars.dp_free(bb), (u - 1) & 1, p.err, kErrWaitAccum)) return false;
+        tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < HD / 8; ++kk)  // dP = dO V^T, dO in TMEM
           umma_tf32_ts_pair(tmem + dp_col_of(bb, PBLK_Q), tmem + Cfg::Q_OPND + kk * 8,
-                            kmajor_desc(st + Cfg::Q_HALF_K, PBLK_Q / 2, kk), idesc_s, kk > 0 ? 1u : 0u);
+                            desc_add(dvk0, kchunk_off(PBLK_Q / 2, kk)), idesc_s, kk > 0 ? 1u : 0u);
         umma_commit_pair(bars.s_full(bb), 0x3);
         return true;
       };
@@ -911,13 +933,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(BTHREADS, 1)
         if (!mbar_wait(bars.p_full(bb), (j >> 1) & 1, p.err, kErrWaitAccum)) break;
         tc_fence_after();
         const uint32_t st = stage(s);
+        const uint64_t dkm0 = mnmajor_desc_rows(st + 2 * Cfg::Q_HALF_K, PBLK_Q, 0);
 #pragma unroll
         for (int kk = 0; kk < PBLK_Q / 8; ++kk)  // dQ += dS K
-          umma_tf32_ts_pair(tmem + Cfg::Q_DQ, tmem + dp_col_of(bb, PBLK_Q) + kk * 8,
-                            mnmajor_desc_rows(st + 2 * Cfg::Q_HALF_K, PBLK_Q, kk), idesc_g,
-                            (j > 0 || kk > 0) ? 1u : 0u);
+          umma_tf32_ts_pair(tmem + Cfg::Q_DQ, tmem + dp_col_of(bb, PBLK_Q) + kk * 8, desc_add(dkm0, kk * 1024),
+                            idesc_g, (j > 0 || kk > 0) ? 1u : 0u);
+        umma_commit_pair(bars.dp_free(bb), 0x1);
         umma_commit_pair(bars.empty(s), 0x3);
-        umma_commit_pair(bars.s_free(bb), 0x1);
       }
       umma_commit_pair(bars.acc_done(), 0x3);
     }

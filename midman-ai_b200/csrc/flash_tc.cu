@@ -470,6 +470,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(FTHREADS, 1)
       // ---------------- UMMA issuer (leader only), M = 256 across the pair
       constexpr uint32_t idesc_s = idesc_tf32(2 * PQ, PKV, false, false);
       constexpr uint32_t idesc_o = idesc_tf32(2 * PQ, HD, false, true);
+      const uint64_t dq0 = smem_desc(sQ, 16, 1024, kLayoutSw128);
       bool ok = mbar_wait(q_full, 0, p.err, kErrWaitFull);
       if (ok) *q_pending = 0;
       auto issue_s = [&](int j) -> bool {
@@ -477,12 +478,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(FTHREADS, 1)
         if (!mbar_wait(k_full(s), (j / STAGES) & 1, p.err, kErrWaitFull)) return false;
         if (u > 0 && !mbar_wait(s_free(bb), (u - 1) & 1, p.err, kErrWaitAccum)) return false;
         tc_fence_after();
+        const uint64_t dk0 = smem_desc(sK(s), 16, 1024, kLayoutSw128);
 #pragma unroll
         for (int kk = 0; kk < HD / 8; ++kk) {
           const uint32_t off = (kk % 4) * 32u;  // 8 tf32 = 32 bytes along the 128-byte chunk
-          const uint64_t a = smem_desc(sQ + (kk / 4) * (PQ * 128) + off, 16, 1024, kLayoutSw128);
-          const uint64_t bd = smem_desc(sK(s) + (kk / 4) * ((PKV / 2) * 128) + off, 16, 1024, kLayoutSw128);
-          umma_tf32_pair(tmem + bb * PKV, a, bd, idesc_s, kk > 0 ? 1u : 0u);
+          umma_tf32_pair(tmem + bb * PKV, desc_add(dq0, (kk / 4) * (PQ * 128) + off),
+                         desc_add(dk0, (kk / 4) * ((PKV / 2) * 128) + off), idesc_s, kk > 0 ? 1u : 0u);
         }
         umma_commit_pair(s_full(bb), 0x3);
         return true;
@@ -495,13 +496,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(FTHREADS, 1)
         if (!mbar_wait(v_full(s), (j / STAGES) & 1, p.err, kErrWaitFull)) break;
         *kv_consumed = j + 1;
         tc_fence_after();
+        // this CTA's half of V_j: 32-wide hd blocks of PKV key rows (LBO), 8 key rows per step
+        const uint64_t dv0 = smem_desc(sV(s), PKV * 128, 512, kLayoutSw128Base32);
 #pragma unroll
-        for (int kk = 0; kk < PKV / 8; ++kk) {
-          // this CTA's half of V_j: 32-wide hd blocks of PKV key rows (LBO), 8 key rows per step
-          const uint64_t bd = smem_desc(sV(s) + kk * 1024, PKV * 128, 512, kLayoutSw128Base32);
-          umma_tf32_ts_pair(tmem + Cfg::O_COL + (j & 1) * HD, tmem + bb * PKV + kk * 8, bd, idesc_o,
-                            (j > 1 || kk > 0) ? 1u : 0u);
-        }
+        for (int kk = 0; kk < PKV / 8; ++kk)
+          umma_tf32_ts_pair(tmem + Cfg::O_COL + (j & 1) * HD, tmem + bb * PKV + kk * 8, desc_add(dv0, kk * 1024),
+                            idesc_o, (j > 1 || kk > 0) ? 1u : 0u);
         umma_commit_pair(kv_empty(s), 0x3);
         umma_commit_pair(s_free(bb), 0x1);
         umma_commit_pair(o_done(j & 1), 0x3);

@@ -333,6 +333,12 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo_bytes,
   return d;
 }
 
+// `d` advanced by `bytes` inside the same tile: the start address is the low
+// 14-bit field (in 16-byte units) and shared memory is below 256 KB, so a plain
+// add never carries into the other fields. Lets a UMMA loop build each step's
+// descriptors with one add from a base computed once.
+__device__ __forceinline__ uint64_t desc_add(uint64_t d, uint32_t bytes) { return d + (bytes >> 4); }
+
 // Instruction descriptor for kind::tf32 with an f32 accumulator.
 __host__ __device__ constexpr uint32_t idesc_tf32(int m, int n, bool a_mn_major, bool b_mn_major) {
   return (1u << 4)                                   // D format: f32
