@@ -195,14 +195,16 @@ def run_kernels(args):
                             {"Y=XW": (fwd, flops / 3), "dX=dYW^T": (bwd_x, flops / 3),
                              "dW=X^TdY": (bwd_w, flops / 3)}))
     else:
-        B, H, hd, T = 8, 16, 64, 1024
+        # configs[2] (B8 H16 hd64 T1024), or with attention-large the attention of configs[4]'s layers
+        B, H, Hkv, hd, T = (8, 16, 16, 64, 1024) if args.config == "attention" else (4, 16, 8, 128, 2048)
         q = torch.randn(B, T, H, hd, device="cuda", generator=g)
-        k = torch.randn(B, T, H, hd, device="cuda", generator=g)
-        v = torch.randn(B, T, H, hd, device="cuda", generator=g)
+        k = torch.randn(B, T, Hkv, hd, device="cuda", generator=g)
+        v = torch.randn(B, T, Hkv, hd, device="cuda", generator=g)
         do = torch.randn(B, T, H, hd, device="cuda", generator=g)
         o, lse = torch.empty_like(q), torch.empty(B, H, T, device="cuda")
         dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
-        kw = dict(batch=B, seq=T, n_heads=H, n_kv_heads=H, head_dim=hd, ldq=H * hd, ldk=H * hd, precision=precision)
+        kw = dict(batch=B, seq=T, n_heads=H, n_kv_heads=Hkv, head_dim=hd, ldq=H * hd, ldk=Hkv * hd,
+                  precision=precision)
 
         def fwd():
             mm.attention_forward(q, k, v, o, lse, **kw)
@@ -214,7 +216,7 @@ def run_kernels(args):
             fwd()
             bwd()
         flops = 6 * 2 * B * H * (T * T // 2) * hd  # six causal T x T x hd products, no recompute
-        results.append(({"B": B, "H": H, "hd": hd, "T": T}, flops, step,
+        results.append(({"B": B, "H": H, "Hkv": Hkv, "hd": hd, "T": T}, flops, step,
                         {"forward": (fwd, flops / 3), "backward": (bwd, flops * 2 / 3)}))
     tf32 = tf32_peak_tflops(torch)
     def timed(fn):
@@ -246,6 +248,9 @@ def run_kernels(args):
     return 0
 
 
+GEMM_TRAFFIC_BYTES = 462e6  # see the roofline entry below
+
+
 def gemm_shapes(prof, steps, top=10):
     """The slowest GEMM shapes of the profiled steps: [shape "MxNxK AB", launches/step, ms/step, TFLOP/s]."""
     rows = sorted(prof.items(), key=lambda kv: -kv[1]["ms"])[:top]
@@ -273,13 +278,13 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=8)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--config", default="large", choices=sorted(CONFIGS) + ["linear", "attention"])
+    ap.add_argument("--config", default="large", choices=sorted(CONFIGS) + ["linear", "attention", "attention-large"])
     ap.add_argument("--precision", default="tf32", choices=["tf32", "3xtf32"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
 
-    if args.config in ("linear", "attention"):
+    if args.config in ("linear", "attention", "attention-large"):
         return run_kernels(args) if args.impl == "ours" else 0
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -408,7 +413,12 @@ def main():
                          "frac": (achieved / tf32) if achieved else None,
                          "peak_source": "cuBLAS TF32 GEMM 8192^3 measured in this run (MEASURED_PEAKS.json has "
                                         f"bf16 only: {peaks.get('bf16_tflops')} TF/s burst)",
-                         "traffic": None, "kernel_launches": g["launches"],
+                         # DRAM read+write bytes per GEMM launch, averaged over one step's 423 GEMM launches
+                         # of this command under ncu (one-pass launch list; measured, not computed here)
+                         "traffic": GEMM_TRAFFIC_BYTES if args.config == "large" and precision == 0 else None,
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, large preset step, "
+                                           "mean over the step's GEMM launches",
+                         "kernel_launches": g["launches"],
                          "step_tflops": fpt * B * T * args.steps / (ms * 1e-3) / 1e12 / world,
                          "step_frac": fpt * B * T * args.steps / (ms * 1e-3) / 1e12 / world / tf32,
                          "time_share": kernel_share,
