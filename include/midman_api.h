@@ -165,6 +165,34 @@ MIDMAN_EXPORT int32_t midman_batcher_synthetic(uint32_t token_seed, uint32_t voc
 MIDMAN_EXPORT int32_t midman_batcher_next(uint32_t handle, int32_t *inputs, int32_t *targets);
 MIDMAN_EXPORT int32_t midman_batcher_destroy(uint32_t handle);
 
+/* ---- Training state files (crates/midman-training/src/state.rs:45-288 with the
+ * safetensors container of crates/midman-checkpoint/src/safetensors.rs). A file
+ * written here is the reference's state file: the same tensor names
+ * (param/<name>, adamw.m/<name>, adamw.v/<name>), metadata (format,
+ * state_version, step, epoch, position and the twelve train.* settings of
+ * config.rs:113-131) and byte layout, so a GPU run resumes a CPU state and the
+ * other way round. The data-order seed, epoch and position belong to the caller's
+ * batcher; the global batch size is batch * world of midman_train_create. */
+
+/* Writes <path>.tmp and renames it over path (safetensors.rs:224-253). */
+MIDMAN_EXPORT int32_t midman_train_save(uint32_t handle, const uint8_t *path, uint32_t path_len,
+                                        uint32_t data_seed_lo, uint32_t data_seed_hi, uint64_t epoch,
+                                        uint64_t position);
+/* Loads weights, both moments and the step count after every check of
+ * load_state (state.rs:176-288) and AdamW::restore (adamw.rs:95-130); nothing
+ * changes unless the whole load succeeds. Text: {"step","epoch","position"}.
+ * Errors: MIDMAN_ERR_OTHER for a file that is not a valid state file (format,
+ * version, header), MIDMAN_ERR_ARGUMENT for a state that does not fit the run
+ * (settings, missing or extra tensors, bad moments), MIDMAN_ERR_SHAPE for a
+ * tensor of another shape. */
+MIDMAN_EXPORT int32_t midman_train_restore(uint32_t handle, const uint8_t *path, uint32_t path_len,
+                                           uint32_t data_seed_lo, uint32_t data_seed_hi);
+/* Reads and checks a safetensors file (TensorFile::from_bytes,
+ * safetensors.rs:270-353; and progress_of, state.rs:125-173, when its format
+ * entry says it is a training state) without a GPU. Text: {"metadata",
+ * "tensors":[{"name","shape","data_offsets"}], "progress" (training states)}. */
+MIDMAN_EXPORT int32_t midman_state_inspect(const uint8_t *path, uint32_t path_len);
+
 #ifdef __cplusplus
 }
 #endif

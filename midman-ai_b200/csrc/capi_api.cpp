@@ -17,6 +17,7 @@
 #include "../../include/midman_api.h"
 #include "host.h"
 #include "json.h"
+#include "state.h"
 #include "trainer.h"
 
 namespace {
@@ -100,6 +101,9 @@ int32_t run(F&& body) {
   } catch (const DeviceError& e) {
     set_error(e.what());
     return MIDMAN_ERR_DEVICE;
+  } catch (const StateShapeError& e) {
+    set_error(e.what());
+    return MIDMAN_ERR_SHAPE;
   } catch (const std::bad_alloc&) {
     set_error("internal error: out of host memory");
     return MIDMAN_ERR_PANIC;
@@ -657,6 +661,115 @@ int32_t midman_train_load(uint32_t handle, const float* values, uint64_t len) {
       throw ArgumentError("expected " + std::to_string(t.trainer->layout().total) + " values, got " +
                           std::to_string(len));
     t.trainer->load_params(values);
+    return MIDMAN_OK;
+  });
+}
+
+namespace {
+std::string path_from(const uint8_t* path, uint32_t len) {
+  if (!path || len == 0) throw ArgumentError("the path must not be empty");
+  return std::string(reinterpret_cast<const char*>(path), len);
+}
+
+// TrainConfig of this run (config.rs:16-41): the global batch, the schedule and
+// AdamW settings it was created with, and the data-order seed of its batcher.
+TrainSettings settings_of(const Train& t, uint32_t seed_lo, uint32_t seed_hi) {
+  TrainSettings s;
+  s.batch_size = static_cast<uint64_t>(t.trainer->batch()) * static_cast<uint64_t>(t.trainer->world());
+  s.seq_len = static_cast<uint64_t>(t.trainer->seq());
+  s.seed = (static_cast<uint64_t>(seed_hi) << 32) | seed_lo;
+  s.max_lr = t.hyper.max_lr;
+  s.min_lr = t.hyper.min_lr;
+  s.warmup_steps = t.hyper.warmup;
+  s.total_steps = t.hyper.total;
+  s.beta1 = t.hyper.beta1;
+  s.beta2 = t.hyper.beta2;
+  s.eps = adam_of(t.hyper).eps;
+  s.weight_decay = t.hyper.weight_decay;
+  s.clip_norm = t.hyper.clip_norm;
+  return s;
+}
+
+std::vector<StateParam> state_params(const ParamLayout& L) {
+  std::vector<StateParam> out;
+  for (const TensorInfo& ti : L.tensors) {
+    StateParam p;
+    p.name = ti.name;
+    for (auto d : ti.shape) p.shape.push_back(static_cast<uint64_t>(d));
+    p.offset = ti.offset;
+    p.count = ti.numel;
+    out.push_back(std::move(p));
+  }
+  return out;
+}
+
+void write_progress(JsonWriter& w, const Progress& p) {
+  w.begin_object();
+  w.key("step").integer(p.step);
+  w.key("epoch").integer(p.epoch);
+  w.key("position").integer(p.position);
+  w.end_object();
+}
+}  // namespace
+
+int32_t midman_train_save(uint32_t handle, const uint8_t* path, uint32_t path_len, uint32_t data_seed_lo,
+                          uint32_t data_seed_hi, uint64_t epoch, uint64_t position) {
+  return run([&] {
+    Train& t = train_ref(handle);
+    const std::string file = path_from(path, path_len);
+    Progress p;
+    p.step = t.step;
+    p.epoch = epoch;
+    p.position = position;
+    save_state(file, state_params(t.trainer->layout()), p, settings_of(t, data_seed_lo, data_seed_hi),
+               [&](int which, uint64_t offset, uint64_t n, float* out) { t.trainer->read_tensor(offset, n, out, which); });
+    return MIDMAN_OK;
+  });
+}
+
+int32_t midman_train_restore(uint32_t handle, const uint8_t* path, uint32_t path_len, uint32_t data_seed_lo,
+                             uint32_t data_seed_hi) {
+  return run([&] {
+    Train& t = train_ref(handle);
+    const std::string file = path_from(path, path_len);
+    const ParamLayout& L = t.trainer->layout();
+    LoadedState st = load_state(file, state_params(L), L.total, settings_of(t, data_seed_lo, data_seed_hi));
+    t.trainer->restore(st.params.data(), st.m.empty() ? nullptr : st.m.data(), st.v.empty() ? nullptr : st.v.data(),
+                       st.progress.step);
+    t.step = st.progress.step;
+    JsonWriter w;
+    write_progress(w, st.progress);
+    set_text(w.finish());
+    return MIDMAN_OK;
+  });
+}
+
+int32_t midman_state_inspect(const uint8_t* path, uint32_t path_len) {
+  return run([&] {
+    const SafeFile f = load_safetensors(path_from(path, path_len));
+    JsonWriter w;
+    w.begin_object();
+    w.key("metadata").begin_object();
+    for (const auto& [k, v] : f.metadata) w.key(k).string(v);
+    w.end_object();
+    w.key("tensors").begin_array();
+    for (const SafeTensor& t : f.tensors) {
+      w.begin_object();
+      w.key("name").string(t.name);
+      w.key("shape").begin_array();
+      for (auto d : t.shape) w.integer(d);
+      w.end_array();
+      w.key("data_offsets").begin_array().integer(t.begin).integer(t.end).end_array();
+      w.end_object();
+    }
+    w.end_array();
+    const auto fmt = f.metadata.find("format");
+    if (fmt != f.metadata.end() && fmt->second == "midman-training-state") {  // its header entries must hold
+      w.key("progress");
+      write_progress(w, progress_of(f.metadata));
+    }
+    w.end_object();
+    set_text(w.finish());
     return MIDMAN_OK;
   });
 }

@@ -173,6 +173,17 @@ void Trainer::load_params(const float* host) {
   check_cuda(cudaStreamSynchronize(stream_), "load params");
 }
 
+void Trainer::restore(const float* params, const float* m, const float* v, uint64_t adam_steps) {
+  const size_t bytes = layout_.total * 4;
+  check_cuda(cudaMemcpyAsync(P_, params, bytes, cudaMemcpyHostToDevice, stream_), "restore params");
+  if (m) check_cuda(cudaMemcpyAsync(M_, m, bytes, cudaMemcpyHostToDevice, stream_), "restore moments");
+  else check_cuda(cudaMemsetAsync(M_, 0, bytes, stream_), "restore moments");
+  if (v) check_cuda(cudaMemcpyAsync(V_, v, bytes, cudaMemcpyHostToDevice, stream_), "restore moments");
+  else check_cuda(cudaMemsetAsync(V_, 0, bytes, stream_), "restore moments");
+  check_cuda(cudaStreamSynchronize(stream_), "restore");
+  adam_steps_ = adam_steps;
+}
+
 void Trainer::read_params(float* host) { read_tensor(0, layout_.total, host, 0); }
 void Trainer::read_grads(float* host) { read_tensor(0, layout_.total, host, 1); }
 

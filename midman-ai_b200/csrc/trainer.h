@@ -41,6 +41,7 @@ class Trainer {
   const ParamLayout& layout() const { return layout_; }
   int batch() const { return batch_; }
   int seq() const { return seq_; }
+  int world() const { return world_; }
   uint64_t adam_steps() const { return adam_steps_; }
   cudaStream_t stream() const { return stream_; }
 
@@ -50,7 +51,10 @@ class Trainer {
   void read_params(float* host);
   void read_grads(float* host);
   void read_moments(float* m, float* v);
-  void read_tensor(uint64_t offset, uint64_t n, float* host, int which /*0 params, 1 grads*/);
+  void read_tensor(uint64_t offset, uint64_t n, float* host, int which /*0 params, 1 grads, 2 m, 3 v*/);
+  // Replaces parameters, both AdamW moments (null: zeros, for a run before its
+  // first step) and the optimizer's step count, as a resumed run (state.rs:176-288).
+  void restore(const float* params, const float* m, const float* v, uint64_t adam_steps);
 
   // One full step on host token ids (batch*seq each). lr from the caller's schedule.
   StepOut train_step(const int32_t* inputs, const int32_t* targets, float lr, const AdamHyper& h);

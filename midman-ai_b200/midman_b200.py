@@ -27,7 +27,8 @@ API_SYMBOLS = [
     "midman_train_stage", "midman_train_step_staged", "midman_train_loss_and_grads", "midman_train_read",
     "midman_train_load", "midman_train_describe", "midman_train_eval", "midman_train_destroy",
     "midman_train_stream", "midman_train_profile", "midman_batcher_create", "midman_batcher_synthetic",
-    "midman_batcher_next", "midman_batcher_destroy",
+    "midman_batcher_next", "midman_batcher_destroy", "midman_train_save", "midman_train_restore",
+    "midman_state_inspect",
 ]
 STATUS = {0: "OK", 1: "STOPPED", -1: "ARGUMENT", -2: "CONFIG", -3: "SHAPE", -4: "INDEX", -5: "OTHER",
           -6: "DEVICE", -99: "PANIC"}
@@ -97,6 +98,9 @@ def load(path: str | os.PathLike | None = None) -> C.CDLL:
     _sig(lib, "midman_batcher_synthetic", i32, u32, u32, C.c_uint64, u32, u32, u32, u32)
     _sig(lib, "midman_batcher_next", i32, u32, i32p, i32p)
     _sig(lib, "midman_batcher_destroy", i32, u32)
+    _sig(lib, "midman_train_save", i32, u32, u8p, u32, u32, u32, C.c_uint64, C.c_uint64)
+    _sig(lib, "midman_train_restore", i32, u32, u8p, u32, u32, u32)
+    _sig(lib, "midman_state_inspect", i32, u8p, u32)
     _lib = lib
     return lib
 
@@ -202,6 +206,18 @@ def _dp(a):
 
 def _ip(a):
     return a.ctypes.data_as(C.POINTER(C.c_int32))
+
+
+def _path_bytes(path):
+    raw = str(path).encode()
+    return (C.c_uint8 * len(raw)).from_buffer_copy(raw) if raw else None
+
+
+def state_inspect(path) -> dict:
+    """midman_state_inspect: the checked header of a safetensors (state) file."""
+    b = _path_bytes(path)
+    api(load().midman_state_inspect(b, len(b) if b is not None else 0))
+    return _json.loads(text())
 
 
 def config_array(vocab, d_model, n_layers, n_heads, n_kv_heads, d_ff, max_seq_len, rope_theta=10000.0,
@@ -352,6 +368,17 @@ class Trainer:
 
     def profile(self, enable: bool):
         api(load().midman_train_profile(self.h, int(enable)))
+
+    def save(self, path, data_seed: int = 0, epoch: int = 0, position: int = 0):
+        """Writes the run's state file (param/*, adamw.m/*, adamw.v/* and the run's metadata)."""
+        b = _path_bytes(path)
+        api(load().midman_train_save(self.h, b, len(b), data_seed & 0xFFFFFFFF, data_seed >> 32, epoch, position))
+
+    def restore(self, path, data_seed: int = 0) -> dict:
+        """Loads a state file into this run; returns its progress {step, epoch, position}."""
+        b = _path_bytes(path)
+        api(load().midman_train_restore(self.h, b, len(b), data_seed & 0xFFFFFFFF, data_seed >> 32))
+        return _json.loads(text())
 
     def close(self):
         if self.h:

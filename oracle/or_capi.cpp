@@ -195,6 +195,17 @@ void or_adamw_moments(void* op, float* m, float* v) {
   std::memcpy(m, o->m.data(), o->m.size() * sizeof(float));
   std::memcpy(v, o->v.data(), o->v.size() * sizeof(float));
 }
+// AdamW::restore (adamw.rs:95-130) for the whole flat vector: steps and both
+// moments; refuses non-finite m and negative or non-finite v (returns -1).
+int or_adamw_restore(void* op, uint64_t steps, const float* m, const float* v) {
+  AdamW* o = static_cast<AdamW*>(op);
+  for (size_t i = 0; i < o->m.size(); ++i)
+    if (!std::isfinite(m[i]) || !std::isfinite(v[i]) || v[i] < 0.0f) return -1;
+  std::memcpy(o->m.data(), m, o->m.size() * sizeof(float));
+  std::memcpy(o->v.data(), v, o->v.size() * sizeof(float));
+  o->steps = steps;
+  return 0;
+}
 
 }  // extern "C"
 

@@ -69,6 +69,7 @@ def lib() -> C.CDLL:
     sig("or_adamw_step", i32, vp, vp, P(f32), f32)
     sig("or_adamw_steps", u64, vp)
     sig("or_adamw_moments", None, vp, P(f32), P(f32))
+    sig("or_adamw_restore", i32, vp, u64, P(f32), P(f32))
     sig("or_train_update", i32, vp, vp, P(C.c_int32), P(C.c_int32), i32, i32, f32, f32, P(f32))
     sig("or_batcher_new", vp, P(C.c_uint32), sz, i32, i32, u64)
     sig("or_batcher_free", None, vp)
@@ -336,6 +337,18 @@ class AdamW:
         v = np.zeros(self.model.n, np.float32)
         lib().or_adamw_moments(self.h, _p(m, C.c_float), _p(v, C.c_float))
         return m, v
+
+    @property
+    def steps(self) -> int:
+        return int(lib().or_adamw_steps(self.h))
+
+    def restore(self, steps: int, m: np.ndarray, v: np.ndarray):
+        """AdamW::restore (adamw.rs:95-130) of the flat moments."""
+        m = np.ascontiguousarray(m, np.float32)
+        v = np.ascontiguousarray(v, np.float32)
+        assert m.size == self.model.n and v.size == self.model.n
+        if lib().or_adamw_restore(self.h, steps, _p(m, C.c_float), _p(v, C.c_float)) != 0:
+            raise ValueError("adamw: moments are not finite or a second moment is negative")
 
 
 def train_update(model: Model, opt: AdamW, inputs, targets, batch, seq, clip_norm, lr):
