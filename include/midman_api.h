@@ -165,6 +165,46 @@ MIDMAN_EXPORT int32_t midman_batcher_synthetic(uint32_t token_seed, uint32_t voc
 MIDMAN_EXPORT int32_t midman_batcher_next(uint32_t handle, int32_t *inputs, int32_t *targets);
 MIDMAN_EXPORT int32_t midman_batcher_destroy(uint32_t handle);
 
+/* ---- Token shards (crates/midman-data/src/shard.rs) and the input pipeline.
+ * A .mmtokens file: 32-byte header (MMTOKENS, version 1, token width 2 or 4,
+ * vocabulary size, end-of-text id, u64 token count), little-endian ids, SHA-256
+ * of everything before it. The readers refuse a file for the reasons of
+ * TokenShard::from_bytes (shard.rs:137-219) with MIDMAN_ERR_OTHER. */
+
+/* Text: {"vocab_size","eos","tokens","token_width"}. Needs no GPU. */
+MIDMAN_EXPORT int32_t midman_shard_inspect(const uint8_t *path, uint32_t path_len);
+/* TokenShard::load (shard.rs:255-262): as midman_shard_inspect, and the first
+ * min(capacity, tokens) ids into `tokens`. */
+MIDMAN_EXPORT int32_t midman_shard_read(const uint8_t *path, uint32_t path_len, uint32_t *tokens,
+                                        uint64_t capacity);
+/* TokenShard::new + save (shard.rs:59-82, :113-135, :221-253): the file of these
+ * ids, written to `path`.tmp, synced, renamed over `path`. A vocabulary of 0, an
+ * end-of-text id or an id not below the vocabulary is MIDMAN_ERR_ARGUMENT. */
+MIDMAN_EXPORT int32_t midman_shard_write(const uint8_t *path, uint32_t path_len, uint32_t vocab_size,
+                                         uint32_t eos, const uint32_t *tokens, uint64_t n);
+/* SHA-256 (FIPS 180-4) of n bytes into digest[32] (crates/midman-data/src/hash.rs:
+ * the checksum shards end with). */
+MIDMAN_EXPORT int32_t midman_sha256(const uint8_t *data, uint64_t n, uint8_t *digest);
+/* A batcher over the sequences of these shards (paths separated by '\n'),
+ * Sequences::new + Batcher::new (batch.rs:38-70, :113-170): windows of seq+1
+ * tokens that never cross from one shard to the next, all shards with one
+ * vocabulary and end-of-text id. Returns the handle (> 0) or an error. */
+MIDMAN_EXPORT int32_t midman_batcher_open(const uint8_t *paths, uint32_t paths_len, uint32_t seq, uint32_t batch,
+                                          uint32_t seed_lo, uint32_t seed_hi);
+/* Batcher::seek (batch.rs:191-210): the next batch is the one a continuous run
+ * would take after batches_done batches of this epoch. Text: {"epoch",
+ * "position","sequences"}. */
+MIDMAN_EXPORT int32_t midman_batcher_seek(uint32_t handle, uint64_t epoch, uint64_t batches_done);
+/* Trainer::step (trainer.rs:162-183) `steps` times with batches from the batcher,
+ * which gives the global batch (batch * world rows of seq tokens); this rank
+ * trains rows [rank * batch, (rank + 1) * batch). The host takes and prepares
+ * the next batch (checks, pinned copy, embedding index) while the GPU runs the
+ * current step; its ids cross to the device after that step. Floats:
+ * [loss, grad_norm, lr] per completed step. A step that fails leaves the
+ * weights, moments, step count and the batcher's place as they were
+ * (MIDMAN_STOPPED). Text: {"epoch","position","sequences"} of the batcher. */
+MIDMAN_EXPORT int32_t midman_train_run(uint32_t handle, uint32_t batcher, uint32_t steps);
+
 /* ---- Training state files (crates/midman-training/src/state.rs:45-288 with the
  * safetensors container of crates/midman-checkpoint/src/safetensors.rs). A file
  * written here is the reference's state file: the same tensor names

@@ -8,6 +8,7 @@
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
+#include <exception>
 #include <memory>
 #include <stdexcept>
 #include <string>
@@ -17,6 +18,7 @@
 #include "../../include/midman_api.h"
 #include "host.h"
 #include "json.h"
+#include "shard.h"
 #include "state.h"
 #include "trainer.h"
 
@@ -101,6 +103,9 @@ int32_t run(F&& body) {
   } catch (const DeviceError& e) {
     set_error(e.what());
     return MIDMAN_ERR_DEVICE;
+  } catch (const ShardError& e) {
+    set_error(e.what());
+    return MIDMAN_ERR_OTHER;
   } catch (const StateShapeError& e) {
     set_error(e.what());
     return MIDMAN_ERR_SHAPE;
@@ -876,6 +881,168 @@ int32_t midman_batcher_next(uint32_t handle, int32_t* inputs, int32_t* targets) 
     w.key("epoch").integer(at.first);
     w.key("index").integer(at.second);
     w.key("sequences").integer(g.batchers[handle - 1]->sequences());
+    w.end_object();
+    set_text(w.finish());
+    return MIDMAN_OK;
+  });
+}
+
+namespace {
+Batcher& batcher_ref(uint32_t handle) {
+  if (handle == 0 || handle > g.batchers.size() || !g.batchers[handle - 1])
+    throw ArgumentError(std::to_string(handle) + " is not a live batcher handle");
+  return *g.batchers[handle - 1];
+}
+
+void write_place(JsonWriter& w, const Batcher& b) {
+  w.key("epoch").integer(b.epoch());
+  w.key("position").integer(b.position());
+  w.key("sequences").integer(b.sequences());
+}
+}  // namespace
+
+// TokenShard::load (shard.rs:255-262) and the header fields; the first `capacity` ids into `tokens`.
+static int32_t shard_read(const uint8_t* path, uint32_t path_len, uint32_t* tokens, uint64_t capacity) {
+  return run([&] {
+    if (!tokens && capacity) throw ArgumentError("tokens must not be null");
+    const TokenShard sh = load_token_shard(path_from(path, path_len));
+    const uint64_t n = std::min<uint64_t>(capacity, sh.tokens.size());
+    if (n) std::memcpy(tokens, sh.tokens.data(), n * 4);
+    JsonWriter w;
+    w.begin_object();
+    w.key("vocab_size").integer(sh.vocab_size);
+    w.key("eos").integer(sh.eos);
+    w.key("tokens").integer(sh.tokens.size());
+    w.key("token_width").integer(sh.vocab_size <= 65536 ? 2 : 4);
+    w.end_object();
+    set_text(w.finish());
+    return MIDMAN_OK;
+  });
+}
+
+int32_t midman_sha256(const uint8_t* data, uint64_t n, uint8_t* digest) {
+  return run([&] {
+    if ((!data && n) || !digest) throw ArgumentError("data and digest must not be null");
+    const std::array<uint8_t, 32> d = sha256(data, n);
+    std::memcpy(digest, d.data(), d.size());
+    return MIDMAN_OK;
+  });
+}
+
+int32_t midman_shard_write(const uint8_t* path, uint32_t path_len, uint32_t vocab_size, uint32_t eos,
+                           const uint32_t* tokens, uint64_t n) {
+  return run([&] {
+    if (!tokens && n) throw ArgumentError("tokens must not be null");
+    save_token_shard(path_from(path, path_len), vocab_size, eos, tokens, n);
+    return MIDMAN_OK;
+  });
+}
+
+int32_t midman_shard_read(const uint8_t* path, uint32_t path_len, uint32_t* tokens, uint64_t capacity) {
+  return shard_read(path, path_len, tokens, capacity);
+}
+
+int32_t midman_shard_inspect(const uint8_t* path, uint32_t path_len) {
+  return shard_read(path, path_len, nullptr, 0);
+}
+
+int32_t midman_batcher_open(const uint8_t* paths, uint32_t paths_len, uint32_t seq, uint32_t batch,
+                            uint32_t seed_lo, uint32_t seed_hi) {
+  return run([&]() -> int32_t {
+    const std::string all = path_from(paths, paths_len);
+    std::vector<std::vector<uint32_t>> shards;
+    uint32_t vocab = 0, eos = 0;
+    size_t start = 0;
+    while (start <= all.size()) {
+      size_t end = all.find('\n', start);
+      if (end == std::string::npos) end = all.size();
+      if (end > start) {
+        TokenShard sh = load_token_shard(all.substr(start, end - start));
+        if (!shards.empty() && (sh.vocab_size != vocab || sh.eos != eos))  // batch.rs:45-58
+          throw ArgumentError("shard " + std::to_string(shards.size()) + " has vocabulary size " +
+                              std::to_string(sh.vocab_size) + " and end-of-text " + std::to_string(sh.eos) +
+                              ", but shard 0 has " + std::to_string(vocab) + " and " + std::to_string(eos));
+        vocab = sh.vocab_size;
+        eos = sh.eos;
+        shards.push_back(std::move(sh.tokens));
+      }
+      start = end + 1;
+    }
+    if (shards.empty()) throw ArgumentError("no shard paths given");
+    auto b = std::make_unique<Batcher>(std::move(shards), vocab, static_cast<int>(seq), static_cast<int>(batch),
+                                       (static_cast<uint64_t>(seed_hi) << 32) | seed_lo);
+    return static_cast<int32_t>(insert(g.batchers, std::move(b)));
+  });
+}
+
+int32_t midman_batcher_seek(uint32_t handle, uint64_t epoch, uint64_t batches_done) {
+  return run([&] {
+    Batcher& b = batcher_ref(handle);
+    b.seek(epoch, batches_done);
+    JsonWriter w;
+    w.begin_object();
+    write_place(w, b);
+    w.end_object();
+    set_text(w.finish());
+    return MIDMAN_OK;
+  });
+}
+
+int32_t midman_train_run(uint32_t handle, uint32_t batcher, uint32_t steps) {
+  return run([&]() -> int32_t {
+    Train& t = train_ref(handle);
+    Batcher& b = batcher_ref(batcher);
+    Trainer& tr = *t.trainer;
+    const int B = tr.batch(), T = tr.seq(), W = tr.world(), r = tr.rank();
+    if (b.batch() != static_cast<size_t>(B) * W || b.seq() != static_cast<size_t>(T))
+      throw ArgumentError("the batcher gives batches of " + std::to_string(b.batch()) + " x " +
+                          std::to_string(b.seq()) + " but the run takes " + std::to_string(B) + " x " +
+                          std::to_string(W) + " ranks x " + std::to_string(T));
+    const size_t rows = static_cast<size_t>(B) * T;
+    std::vector<int32_t> in(rows * W), tg(rows * W);
+    std::pair<uint64_t, uint64_t> before[2];
+    // Takes the next global batch and prepares this rank's rows in a staging slot;
+    // remembers where the batcher was, to put it back if the step fails.
+    auto take = [&](int slot) {
+      before[slot] = {b.epoch(), b.position()};
+      b.next(in.data(), tg.data());
+      tr.prepare_batch(in.data() + r * rows, tg.data() + r * rows, B, T, slot);
+    };
+    auto put_back = [&](int slot) { b.seek(before[slot].first, before[slot].second); };
+    try {
+      take(0);
+    } catch (...) {
+      put_back(0);
+      throw;
+    }
+    tr.upload_prepared(0, B, T, true);
+    for (uint32_t s = 0; s < steps; ++s) {
+      const int cur = s & 1, nxt = cur ^ 1;
+      const float lr = schedule_lr(t.hyper.max_lr, t.hyper.min_lr, t.hyper.warmup, t.hyper.total, t.step);
+      tr.launch_step(lr, adam_of(t.hyper));
+      // the host takes and prepares the next batch while the GPU runs this step
+      std::exception_ptr next_failed;
+      if (s + 1 < steps) {
+        try {
+          take(nxt);
+        } catch (...) {
+          next_failed = std::current_exception();
+        }
+      }
+      const StepOut out = tr.collect_step();
+      if (record_step(t, out, lr) != MIDMAN_OK) {  // trainer.rs:162-183: nothing of this step stays
+        put_back(cur);
+        return MIDMAN_STOPPED;
+      }
+      if (next_failed) {
+        put_back(nxt);
+        std::rethrow_exception(next_failed);
+      }
+      if (s + 1 < steps) tr.upload_prepared(nxt, B, T, true);
+    }
+    JsonWriter w;
+    w.begin_object();
+    write_place(w, b);
     w.end_object();
     set_text(w.finish());
     return MIDMAN_OK;

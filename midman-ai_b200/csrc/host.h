@@ -90,15 +90,24 @@ void rope_tables(uint64_t head_dim, uint64_t max_seq_len, float theta, std::vect
 class Batcher {
  public:
   Batcher(std::vector<uint32_t> tokens, uint32_t vocab, int seq, int batch, uint64_t seed);
+  // Sequences::new (batch.rs:38-70) over several shards: windows never cross
+  // from one shard to the next.
+  Batcher(std::vector<std::vector<uint32_t>> shards, uint32_t vocab, int seq, int batch, uint64_t seed);
   size_t sequences() const { return count_; }
   size_t batches_per_epoch() const { return count_ / batch_; }
+  size_t batch() const { return batch_; }
+  size_t seq() const { return seq_; }
+  uint64_t epoch() const { return epoch_; }
+  size_t position() const { return next_; }  // batches of the epoch handed out (batch.rs:186-189)
   // Writes batch * seq inputs and targets (int32). Returns (epoch, index) of the batch.
   std::pair<uint64_t, uint64_t> next(int32_t* inputs, int32_t* targets);
   void seek(uint64_t epoch, uint64_t done);
 
  private:
   void permute();
-  std::vector<uint32_t> tokens_;
+  const uint32_t* window(uint64_t index) const;  // Sequences::window (batch.rs:96-106)
+  std::vector<std::vector<uint32_t>> shards_;
+  std::vector<size_t> ends_;  // sequences in each shard and all the shards before it
   uint32_t vocab_;
   size_t seq_, batch_, count_;
   uint64_t seed_, epoch_ = 0;

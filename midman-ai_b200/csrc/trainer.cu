@@ -97,7 +97,8 @@ Trainer::Trainer(const ModelConfig& cfg, int batch, int seq, int precision, int 
   d_off_ = static_cast<int32_t*>(alloc((N + 1) * 4));
   d_pos_ = static_cast<int32_t*>(alloc(N * 4));
   d_pred_ = static_cast<int32_t*>(alloc(N * 4));
-  check_cuda(cudaMallocHost(&h_pinned_, (5 * N + 1) * sizeof(int32_t)), "pinned ids");
+  for (int slot = 0; slot < 2; ++slot)
+    check_cuda(cudaMallocHost(&h_pinned_[slot], (5 * N + 1) * sizeof(int32_t)), "pinned ids");
   check_cuda(cudaMallocHost(&h_out_, 64), "pinned out");
 
   acts_.resize(cfg.n_layers);
@@ -151,7 +152,8 @@ Trainer::~Trainer() {
   if (stream_) cudaStreamSynchronize(stream_);
   if (comm_stream_) cudaStreamSynchronize(comm_stream_);
   for (void* p : allocations_) cudaFree(p);
-  if (h_pinned_) cudaFreeHost(h_pinned_);
+  for (int32_t* p : h_pinned_)
+    if (p) cudaFreeHost(p);
   if (h_out_) cudaFreeHost(h_out_);
   for (auto e : layer_done_) cudaEventDestroy(e);
   for (auto e : prof_events_) cudaEventDestroy(e);
@@ -201,13 +203,13 @@ void Trainer::read_moments(float* m, float* v) {
 
 // Groups token positions by id, positions ascending within each id, so the
 // embedding gradient adds rows in the reference's order (ops_shape.rs:262-272).
-void Trainer::build_embedding_csr(const int32_t* inputs, int N) {
+void Trainer::build_embedding_csr(const int32_t* inputs, int N, int slot) {
   std::vector<std::pair<int32_t, int32_t>> order(N);
   for (int i = 0; i < N; ++i) order[i] = {inputs[i], i};
   std::sort(order.begin(), order.end());
-  int32_t* uniq = h_pinned_ + 2 * N;
-  int32_t* offs = h_pinned_ + 3 * N;
-  int32_t* pos = h_pinned_ + 4 * N + 1;
+  int32_t* uniq = h_pinned_[slot] + 2 * N;
+  int32_t* offs = h_pinned_[slot] + 3 * N;
+  int32_t* pos = h_pinned_[slot] + 4 * N + 1;
   int nu = 0;
   for (int i = 0; i < N; ++i) {
     if (i == 0 || order[i].first != order[i - 1].first) {
@@ -218,10 +220,17 @@ void Trainer::build_embedding_csr(const int32_t* inputs, int N) {
     pos[i] = order[i].second;
   }
   offs[nu] = N;
-  n_uniq_ = nu;
+  n_uniq_slot_[slot] = nu;
 }
 
 void Trainer::upload_batch(const int32_t* inputs, const int32_t* targets, int B, int T) {
+  // The previous step's copies out of slot 0 have finished: each step ends with
+  // a synchronizing read of its results.
+  prepare_batch(inputs, targets, B, T, 0);
+  upload_prepared(0, B, T, targets != nullptr);
+}
+
+void Trainer::prepare_batch(const int32_t* inputs, const int32_t* targets, int B, int T, int slot) {
   const int N = B * T;
   if (N > batch_ * seq_) throw std::invalid_argument("batch larger than the trainer's capacity");
   if (static_cast<uint64_t>(T) > cfg_.max_seq_len) throw std::invalid_argument("sequence longer than max_seq_len");
@@ -233,16 +242,21 @@ void Trainer::upload_batch(const int32_t* inputs, const int32_t* targets, int B,
       throw std::out_of_range("target class " + std::to_string(targets[i]) + " is out of range for vocab " +
                               std::to_string(cfg_.vocab));
   }
-  // The previous step's copies out of the staging buffer have finished (each
-  // step ends with a synchronizing read of its results).
-  std::memcpy(h_pinned_, inputs, N * 4);
-  if (targets) std::memcpy(h_pinned_ + N, targets, N * 4);
-  build_embedding_csr(inputs, N);
-  check_cuda(cudaMemcpyAsync(d_ids_, h_pinned_, N * 4, cudaMemcpyHostToDevice, stream_), "ids");
-  if (targets) check_cuda(cudaMemcpyAsync(d_tgt_, h_pinned_ + N, N * 4, cudaMemcpyHostToDevice, stream_), "targets");
-  check_cuda(cudaMemcpyAsync(d_uniq_, h_pinned_ + 2 * N, n_uniq_ * 4, cudaMemcpyHostToDevice, stream_), "uniq");
-  check_cuda(cudaMemcpyAsync(d_off_, h_pinned_ + 3 * N, (n_uniq_ + 1) * 4, cudaMemcpyHostToDevice, stream_), "offs");
-  check_cuda(cudaMemcpyAsync(d_pos_, h_pinned_ + 4 * N + 1, N * 4, cudaMemcpyHostToDevice, stream_), "pos");
+  int32_t* h = h_pinned_[slot];
+  std::memcpy(h, inputs, N * 4);
+  if (targets) std::memcpy(h + N, targets, N * 4);
+  build_embedding_csr(inputs, N, slot);
+}
+
+void Trainer::upload_prepared(int slot, int B, int T, bool with_targets) {
+  const int N = B * T;
+  const int32_t* h = h_pinned_[slot];
+  n_uniq_ = n_uniq_slot_[slot];
+  check_cuda(cudaMemcpyAsync(d_ids_, h, N * 4, cudaMemcpyHostToDevice, stream_), "ids");
+  if (with_targets) check_cuda(cudaMemcpyAsync(d_tgt_, h + N, N * 4, cudaMemcpyHostToDevice, stream_), "targets");
+  check_cuda(cudaMemcpyAsync(d_uniq_, h + 2 * N, n_uniq_ * 4, cudaMemcpyHostToDevice, stream_), "uniq");
+  check_cuda(cudaMemcpyAsync(d_off_, h + 3 * N, (n_uniq_ + 1) * 4, cudaMemcpyHostToDevice, stream_), "offs");
+  check_cuda(cudaMemcpyAsync(d_pos_, h + 4 * N + 1, N * 4, cudaMemcpyHostToDevice, stream_), "pos");
 }
 
 void Trainer::set_profile(bool on) {

@@ -42,6 +42,7 @@ class Trainer {
   int batch() const { return batch_; }
   int seq() const { return seq_; }
   int world() const { return world_; }
+  int rank() const { return rank_; }
   uint64_t adam_steps() const { return adam_steps_; }
   cudaStream_t stream() const { return stream_; }
 
@@ -93,10 +94,24 @@ class Trainer {
   void forward(int B, int T, bool train);
   void backward(int B, int T);
   void upload_batch(const int32_t* inputs, const int32_t* targets, int B, int T);
-  void build_embedding_csr(const int32_t* inputs, int N);
+  StepOut finish_collect(bool update);
+  void finish_launch(float lr, const AdamHyper& h, bool update);
+  void build_embedding_csr(const int32_t* inputs, int N, int slot);
   void gemm(int M, int N, int K, const float* A, long long lda, bool a_mn, const float* B, long long ldb, bool b_mn,
             float* C, long long ldc, const float* R, long long ldr);
   StepOut finish_step(float lr, const AdamHyper& h, bool update);
+
+ public:
+  // The step split for a host that prepares the next batch while the GPU runs
+  // this one: prepare_batch (host only: checks, pinned copy, embedding CSR) into
+  // staging slot 0 or 1, upload_prepared (H2D on the step's stream), then
+  // launch_step (no wait) and collect_step (waits, returns the results).
+  void prepare_batch(const int32_t* inputs, const int32_t* targets, int B, int T, int slot);
+  void upload_prepared(int slot, int B, int T, bool with_targets);
+  void launch_step(float lr, const AdamHyper& h);
+  StepOut collect_step();
+
+ private:
   void allreduce_grads_range(uint64_t offset, uint64_t n);
   void check_device(const char* where);
   int prof_begin();
@@ -121,8 +136,9 @@ class Trainer {
 
   // token ids and the embedding-gradient CSR
   int32_t *d_ids_ = nullptr, *d_tgt_ = nullptr, *d_uniq_ = nullptr, *d_off_ = nullptr, *d_pos_ = nullptr;
-  int n_uniq_ = 0;
-  int32_t* h_pinned_ = nullptr;  // staging: ids, targets, uniq, offsets, positions
+  int n_uniq_ = 0;                            // distinct ids of the batch on the device
+  int32_t* h_pinned_[2] = {nullptr, nullptr};  // two staging slots: ids, targets, uniq, offsets, positions
+  int n_uniq_slot_[2] = {0, 0};
   std::vector<int32_t> h_ids_copy_;
 
   // saved activations, one set per layer

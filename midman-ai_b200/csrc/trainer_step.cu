@@ -154,6 +154,11 @@ void Trainer::backward(int B, int T) {
 }
 
 StepOut Trainer::finish_step(float lr, const AdamHyper& h, bool update) {
+  finish_launch(lr, h, update);
+  return finish_collect(update);
+}
+
+void Trainer::finish_launch(float lr, const AdamHyper& h, bool update) {
   sumsq_partials(G_, static_cast<long long>(layout_.total), d_partials_, stream_);
   finish_norm(d_partials_, d_loss_, h.clip_norm, d_norm_, stream_);
   launches_ += 2;
@@ -169,6 +174,9 @@ StepOut Trainer::finish_step(float lr, const AdamHyper& h, bool update) {
   }
   check_cuda(cudaMemcpyAsync(h_out_, d_loss_, sizeof(double), cudaMemcpyDeviceToHost, stream_), "loss D2H");
   check_cuda(cudaMemcpyAsync(h_out_ + 2, d_norm_, 3 * sizeof(float), cudaMemcpyDeviceToHost, stream_), "norm D2H");
+}
+
+StepOut Trainer::finish_collect(bool update) {
   check_device("training step");  // synchronizes the stream
   if (profiling_) prof_collect();
   double loss;
@@ -186,6 +194,11 @@ void Trainer::stage_batch(const int32_t* inputs, const int32_t* targets) {
 }
 
 StepOut Trainer::step_staged(float lr, const AdamHyper& h) {
+  launch_step(lr, h);
+  return collect_step();
+}
+
+void Trainer::launch_step(float lr, const AdamHyper& h) {
   if (!(std::isfinite(lr) && lr >= 0.0f)) throw std::invalid_argument("lr must be finite and not negative");
   const int N = batch_ * seq_;
   forward(batch_, seq_, true);
@@ -194,8 +207,10 @@ StepOut Trainer::step_staged(float lr, const AdamHyper& h) {
   mean_loss(row_loss_, N, d_loss_, stream_);
   launches_ += 2;
   backward(batch_, seq_);
-  return finish_step(lr, h, true);
+  finish_launch(lr, h, true);
 }
+
+StepOut Trainer::collect_step() { return finish_collect(true); }
 
 StepOut Trainer::train_step(const int32_t* inputs, const int32_t* targets, float lr, const AdamHyper& h) {
   stage_batch(inputs, targets);

@@ -28,7 +28,8 @@ API_SYMBOLS = [
     "midman_train_load", "midman_train_describe", "midman_train_eval", "midman_train_destroy",
     "midman_train_stream", "midman_train_profile", "midman_batcher_create", "midman_batcher_synthetic",
     "midman_batcher_next", "midman_batcher_destroy", "midman_train_save", "midman_train_restore",
-    "midman_state_inspect",
+    "midman_state_inspect", "midman_shard_inspect", "midman_batcher_open", "midman_batcher_seek", "midman_train_run",
+    "midman_shard_read", "midman_shard_write", "midman_sha256",
 ]
 STATUS = {0: "OK", 1: "STOPPED", -1: "ARGUMENT", -2: "CONFIG", -3: "SHAPE", -4: "INDEX", -5: "OTHER",
           -6: "DEVICE", -99: "PANIC"}
@@ -101,6 +102,13 @@ def load(path: str | os.PathLike | None = None) -> C.CDLL:
     _sig(lib, "midman_train_save", i32, u32, u8p, u32, u32, u32, C.c_uint64, C.c_uint64)
     _sig(lib, "midman_train_restore", i32, u32, u8p, u32, u32, u32)
     _sig(lib, "midman_state_inspect", i32, u8p, u32)
+    _sig(lib, "midman_shard_inspect", i32, u8p, u32)
+    _sig(lib, "midman_batcher_open", i32, u8p, u32, u32, u32, u32, u32)
+    _sig(lib, "midman_batcher_seek", i32, u32, C.c_uint64, C.c_uint64)
+    _sig(lib, "midman_train_run", i32, u32, u32, u32)
+    _sig(lib, "midman_shard_read", i32, u8p, u32, C.POINTER(C.c_uint32), C.c_uint64)
+    _sig(lib, "midman_shard_write", i32, u8p, u32, u32, u32, C.POINTER(C.c_uint32), C.c_uint64)
+    _sig(lib, "midman_sha256", i32, u8p, C.c_uint64, u8p)
     _lib = lib
     return lib
 
@@ -211,6 +219,38 @@ def _ip(a):
 def _path_bytes(path):
     raw = str(path).encode()
     return (C.c_uint8 * len(raw)).from_buffer_copy(raw) if raw else None
+
+
+def shard_inspect(path) -> dict:
+    """midman_shard_inspect: {vocab_size, eos, tokens, token_width} of a checked .mmtokens file."""
+    b = _path_bytes(path)
+    api(load().midman_shard_inspect(b, len(b) if b is not None else 0))
+    return _json.loads(text())
+
+
+def shard_read(path):
+    """midman_shard_read: (header dict, uint32 ids) of a checked .mmtokens file."""
+    info = shard_inspect(path)
+    out = _np.zeros(info["tokens"], _np.uint32)
+    b = _path_bytes(path)
+    api(load().midman_shard_read(b, len(b), out.ctypes.data_as(C.POINTER(C.c_uint32)), out.size))
+    return _json.loads(text()), out
+
+
+def shard_write(path, vocab_size: int, eos: int, tokens):
+    """midman_shard_write: TokenShard::new + save."""
+    t = _np.ascontiguousarray(tokens, _np.uint32)
+    b = _path_bytes(path)
+    api(load().midman_shard_write(b, len(b) if b is not None else 0, vocab_size, eos,
+                                  t.ctypes.data_as(C.POINTER(C.c_uint32)), t.size))
+
+
+def sha256(data: bytes) -> bytes:
+    """midman_sha256."""
+    buf = (C.c_uint8 * max(len(data), 1)).from_buffer_copy(data or b"\0")
+    out = (C.c_uint8 * 32)()
+    api(load().midman_sha256(buf, len(data), out))
+    return bytes(out)
 
 
 def state_inspect(path) -> dict:
@@ -369,6 +409,12 @@ class Trainer:
     def profile(self, enable: bool):
         api(load().midman_train_profile(self.h, int(enable)))
 
+    def run(self, batcher, steps: int):
+        """midman_train_run: (records [n, 3], status, batcher place)."""
+        st = api(load().midman_train_run(self.h, batcher.h, steps), ok=(0, 1))
+        rec = floats().reshape(-1, 3)
+        return rec, st, (_json.loads(text()) if st == 0 else None)
+
     def save(self, path, data_seed: int = 0, epoch: int = 0, position: int = 0):
         """Writes the run's state file (param/*, adamw.m/*, adamw.v/* and the run's metadata)."""
         b = _path_bytes(path)
@@ -387,12 +433,16 @@ class Trainer:
 
 
 class Batcher:
-    """midman_batcher_*: the reference's Sequences + Batcher over one shard."""
+    """midman_batcher_*: the reference's Sequences + Batcher over token ids, synthetic ids or shard files."""
 
-    def __init__(self, tokens=None, *, vocab, seq, batch, seed=0, synthetic_tokens=None, token_seed=0):
+    def __init__(self, tokens=None, *, vocab=0, seq, batch, seed=0, synthetic_tokens=None, token_seed=0,
+                 shards=None):
         L = load()
         s_lo, s_hi = seed & 0xFFFFFFFF, (seed >> 32) & 0xFFFFFFFF
-        if tokens is not None:
+        if shards is not None:
+            b = _path_bytes("\n".join(str(p) for p in shards))
+            st = L.midman_batcher_open(b, len(b) if b is not None else 0, seq, batch, s_lo, s_hi)
+        elif tokens is not None:
             self._tok = _np.ascontiguousarray(tokens, _np.uint32)
             st = L.midman_batcher_create(self._tok.ctypes.data_as(C.POINTER(C.c_uint32)), self._tok.size, vocab,
                                          seq, batch, s_lo, s_hi)
@@ -408,6 +458,10 @@ class Batcher:
         api(load().midman_batcher_next(self.h, _ip(i), _ip(t)))
         meta = _json.loads(text())
         return i, t, meta["epoch"], meta["index"]
+
+    def seek(self, epoch: int, batches_done: int) -> dict:
+        api(load().midman_batcher_seek(self.h, epoch, batches_done))
+        return _json.loads(text())
 
     def close(self):
         if self.h:

@@ -19,9 +19,11 @@ struct AdamW {
   std::vector<char> decay;  // per element: parameter has rank >= 2 (adamw.rs:197)
 };
 
-// Sequences over one shard + Batcher (crates/midman-data/src/batch.rs:45-248).
+// Sequences over shards + Batcher (crates/midman-data/src/batch.rs:38-248).
 struct Batcher {
-  std::vector<uint32_t> tokens;
+  std::vector<uint32_t> tokens;  // the shards one after another
+  std::vector<size_t> starts;    // where each shard begins in `tokens`
+  std::vector<size_t> ends;      // sequences in each shard and the ones before (batch.rs:61-68)
   size_t seq, batch, count;
   uint64_t seed, epoch = 0;
   size_t next = 0;
@@ -32,6 +34,12 @@ struct Batcher {
     Rng r(seed);
     Rng f = r.fork(epoch);
     f.shuffle(order);
+  }
+  const uint32_t* window(size_t index) const {  // batch.rs:96-106
+    size_t shard = 0;
+    while (ends[shard] <= index) ++shard;
+    const size_t before = shard == 0 ? 0 : ends[shard - 1];
+    return tokens.data() + starts[shard] + (index - before) * seq;
   }
 };
 
@@ -281,13 +289,21 @@ int or_train_update(void* mp, void* op, const int32_t* inputs, const int32_t* ta
   return or_adamw_step(op, mp, grads.data(), lr);
 }
 
-void* or_batcher_new(const uint32_t* tokens, size_t n, int seq, int batch, uint64_t seed) {
+void* or_batcher_new_shards(const uint32_t* tokens, const size_t* lens, size_t n_shards, int seq, int batch,
+                            uint64_t seed) {
   if (seq <= 0 || batch <= 0) return nullptr;
   Batcher* b = new Batcher;
-  b->tokens.assign(tokens, tokens + n);
   b->seq = seq;
   b->batch = batch;
-  b->count = n > static_cast<size_t>(seq) ? (n - 1) / seq : 0;  // batch.rs:63-67
+  b->count = 0;
+  size_t at = 0;
+  for (size_t i = 0; i < n_shards; ++i) {
+    b->starts.push_back(at);
+    b->tokens.insert(b->tokens.end(), tokens + at, tokens + at + lens[i]);
+    if (lens[i] > static_cast<size_t>(seq)) b->count += (lens[i] - 1) / seq;  // batch.rs:63-67
+    b->ends.push_back(b->count);
+    at += lens[i];
+  }
   b->seed = seed;
   if (b->count < b->batch) {
     delete b;
@@ -295,6 +311,9 @@ void* or_batcher_new(const uint32_t* tokens, size_t n, int seq, int batch, uint6
   }
   b->permute();
   return b;
+}
+void* or_batcher_new(const uint32_t* tokens, size_t n, int seq, int batch, uint64_t seed) {
+  return or_batcher_new_shards(tokens, &n, 1, seq, batch, seed);
 }
 void or_batcher_free(void* b) { delete static_cast<Batcher*>(b); }
 size_t or_batcher_num_sequences(void* b) { return static_cast<Batcher*>(b)->count; }
@@ -307,8 +326,7 @@ void or_batcher_next(void* bp, int32_t* inputs, int32_t* targets, uint64_t* epoc
     b->permute();
   }
   for (size_t r = 0; r < b->batch; ++r) {
-    const size_t s = b->order[b->next * b->batch + r];
-    const uint32_t* w = b->tokens.data() + s * b->seq;
+    const uint32_t* w = b->window(b->order[b->next * b->batch + r]);
     for (size_t t = 0; t < b->seq; ++t) {
       inputs[r * b->seq + t] = static_cast<int32_t>(w[t]);
       targets[r * b->seq + t] = static_cast<int32_t>(w[t + 1]);

@@ -72,6 +72,7 @@ def lib() -> C.CDLL:
     sig("or_adamw_restore", i32, vp, u64, P(f32), P(f32))
     sig("or_train_update", i32, vp, vp, P(C.c_int32), P(C.c_int32), i32, i32, f32, f32, P(f32))
     sig("or_batcher_new", vp, P(C.c_uint32), sz, i32, i32, u64)
+    sig("or_batcher_new_shards", vp, P(C.c_uint32), P(sz), sz, i32, i32, u64)
     sig("or_batcher_free", None, vp)
     sig("or_batcher_num_sequences", sz, vp)
     sig("or_batcher_next", None, vp, P(C.c_int32), P(C.c_int32), P(u64), P(u64))
@@ -362,10 +363,16 @@ def train_update(model: Model, opt: AdamW, inputs, targets, batch, seq, clip_nor
 
 
 class Batcher:
-    def __init__(self, tokens, seq, batch, seed):
+    def __init__(self, tokens, seq, batch, seed, shard_lengths=None):
+        """tokens: one shard, or the shards one after another with their lengths in shard_lengths."""
         self.tok = np.ascontiguousarray(tokens, np.uint32)
         self.seq, self.batch = seq, batch
-        self.h = lib().or_batcher_new(_p(self.tok, C.c_uint32), self.tok.size, seq, batch, seed)
+        if shard_lengths is None:
+            self.h = lib().or_batcher_new(_p(self.tok, C.c_uint32), self.tok.size, seq, batch, seed)
+        else:
+            lens = (C.c_size_t * len(shard_lengths))(*shard_lengths)
+            self.h = lib().or_batcher_new_shards(_p(self.tok, C.c_uint32), lens, len(shard_lengths), seq, batch,
+                                                 seed)
         if not self.h:
             raise ValueError("fewer sequences than one batch")
 
