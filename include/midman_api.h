@@ -204,6 +204,15 @@ MIDMAN_EXPORT int32_t midman_batcher_seek(uint32_t handle, uint64_t epoch, uint6
  * weights, moments, step count and the batcher's place as they were
  * (MIDMAN_STOPPED). Text: {"epoch","position","sequences"} of the batcher. */
 MIDMAN_EXPORT int32_t midman_train_run(uint32_t handle, uint32_t batcher, uint32_t steps);
+/* Trainer::evaluate (trainer.rs:209-262) over held-out shard files (paths
+ * separated by '\n'), windows of the run's seq: batches of the run's global batch
+ * (or all the sequences, if fewer), row k of the `rows` taken is sequence
+ * k * len / rows, at most max_batches batches; no gradients, the weights are
+ * untouched. Shards of another vocabulary than the model's, max_batches 0 or no
+ * sequence: MIDMAN_ERR_ARGUMENT. Floats: [loss]; text {"loss","batches","tokens"}.
+ * Under data parallelism every rank evaluates all rows (no collective). */
+MIDMAN_EXPORT int32_t midman_train_evaluate(uint32_t handle, const uint8_t *paths, uint32_t paths_len,
+                                            uint64_t max_batches);
 
 /* ---- Training state files (crates/midman-training/src/state.rs:45-288 with the
  * safetensors container of crates/midman-checkpoint/src/safetensors.rs). A file

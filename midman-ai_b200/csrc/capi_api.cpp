@@ -946,32 +946,100 @@ int32_t midman_shard_inspect(const uint8_t* path, uint32_t path_len) {
   return shard_read(path, path_len, nullptr, 0);
 }
 
+namespace {
+struct ShardSet {
+  std::vector<std::vector<uint32_t>> shards;
+  uint32_t vocab = 0, eos = 0;
+};
+
+// The shard files named in `paths` ('\n'-separated), checked to share one
+// vocabulary and end-of-text id (Sequences::new, batch.rs:45-58).
+ShardSet load_shards(const uint8_t* paths, uint32_t paths_len) {
+  const std::string all = path_from(paths, paths_len);
+  ShardSet set;
+  size_t start = 0;
+  while (start <= all.size()) {
+    size_t end = all.find('\n', start);
+    if (end == std::string::npos) end = all.size();
+    if (end > start) {
+      TokenShard sh = load_token_shard(all.substr(start, end - start));
+      if (!set.shards.empty() && (sh.vocab_size != set.vocab || sh.eos != set.eos))
+        throw ArgumentError("shard " + std::to_string(set.shards.size()) + " has vocabulary size " +
+                            std::to_string(sh.vocab_size) + " and end-of-text " + std::to_string(sh.eos) +
+                            ", but shard 0 has " + std::to_string(set.vocab) + " and " + std::to_string(set.eos));
+      set.vocab = sh.vocab_size;
+      set.eos = sh.eos;
+      set.shards.push_back(std::move(sh.tokens));
+    }
+    start = end + 1;
+  }
+  return set;
+}
+}  // namespace
+
 int32_t midman_batcher_open(const uint8_t* paths, uint32_t paths_len, uint32_t seq, uint32_t batch,
                             uint32_t seed_lo, uint32_t seed_hi) {
   return run([&]() -> int32_t {
-    const std::string all = path_from(paths, paths_len);
-    std::vector<std::vector<uint32_t>> shards;
-    uint32_t vocab = 0, eos = 0;
-    size_t start = 0;
-    while (start <= all.size()) {
-      size_t end = all.find('\n', start);
-      if (end == std::string::npos) end = all.size();
-      if (end > start) {
-        TokenShard sh = load_token_shard(all.substr(start, end - start));
-        if (!shards.empty() && (sh.vocab_size != vocab || sh.eos != eos))  // batch.rs:45-58
-          throw ArgumentError("shard " + std::to_string(shards.size()) + " has vocabulary size " +
-                              std::to_string(sh.vocab_size) + " and end-of-text " + std::to_string(sh.eos) +
-                              ", but shard 0 has " + std::to_string(vocab) + " and " + std::to_string(eos));
-        vocab = sh.vocab_size;
-        eos = sh.eos;
-        shards.push_back(std::move(sh.tokens));
-      }
-      start = end + 1;
-    }
-    if (shards.empty()) throw ArgumentError("no shard paths given");
-    auto b = std::make_unique<Batcher>(std::move(shards), vocab, static_cast<int>(seq), static_cast<int>(batch),
-                                       (static_cast<uint64_t>(seed_hi) << 32) | seed_lo);
+    ShardSet set = load_shards(paths, paths_len);
+    if (set.shards.empty()) throw ArgumentError("no shard paths given");
+    auto b = std::make_unique<Batcher>(std::move(set.shards), set.vocab, static_cast<int>(seq),
+                                       static_cast<int>(batch), (static_cast<uint64_t>(seed_hi) << 32) | seed_lo);
     return static_cast<int32_t>(insert(g.batchers, std::move(b)));
+  });
+}
+
+int32_t midman_train_evaluate(uint32_t handle, const uint8_t* paths, uint32_t paths_len, uint64_t max_batches) {
+  return run([&] {
+    Train& t = train_ref(handle);
+    Trainer& tr = *t.trainer;
+    const ShardSet set = load_shards(paths, paths_len);
+    const size_t seq = static_cast<size_t>(tr.seq());
+    const size_t global_batch = static_cast<size_t>(tr.batch()) * tr.world();
+    const Sequences data(set.shards, static_cast<int>(seq));
+    // trainer.rs:218-235: the data must fit the run and the model
+    if (!set.shards.empty() && set.vocab != tr.config().vocab)
+      throw ArgumentError("the evaluation data has a vocabulary of " + std::to_string(set.vocab) + " and the model " +
+                          std::to_string(tr.config().vocab));
+    if (set.shards.empty())
+      throw ArgumentError("the evaluation data has no vocabulary and the model " + std::to_string(tr.config().vocab));
+    if (max_batches == 0 || data.size() == 0) throw ArgumentError("nothing to evaluate");
+    // trainer.rs:236-261: batches of the run's size (or all there is), rows at even
+    // distances through the sequences; the loss is the mean of the batch losses in f64.
+    const size_t batch = std::min(global_batch, data.size());
+    const size_t batches = std::min<uint64_t>(max_batches, data.size() / batch);
+    const size_t rows = batches * batch;
+    const size_t chunk = static_cast<size_t>(tr.batch());  // this rank's capacity in rows
+    std::vector<int32_t> in(chunk * seq), tg(chunk * seq);
+    double total = 0.0;
+    for (size_t b = 0; b < batches; ++b) {
+      // a batch larger than one rank's capacity (data parallel) is taken in chunks and
+      // recombined as the token-weighted mean of the chunk losses
+      double batch_loss = 0.0;
+      for (size_t r0 = 0; r0 < batch; r0 += chunk) {
+        const size_t n = std::min(chunk, batch - r0);
+        for (size_t r = 0; r < n; ++r) {
+          const size_t at = static_cast<size_t>((static_cast<unsigned __int128>(b * batch + r0 + r) * data.size()) / rows);
+          const uint32_t* w = data.window(at);
+          for (size_t j = 0; j < seq; ++j) {
+            in[r * seq + j] = static_cast<int32_t>(w[j]);
+            tg[r * seq + j] = static_cast<int32_t>(w[j + 1]);
+          }
+        }
+        const float l = tr.eval(in.data(), tg.data(), static_cast<int>(n), static_cast<int>(seq), nullptr);
+        batch_loss = n == batch ? static_cast<double>(l) : batch_loss + static_cast<double>(l) * n / batch;
+      }
+      total += static_cast<double>(static_cast<float>(batch_loss));
+    }
+    const float loss = static_cast<float>(total / static_cast<double>(batches));
+    g.floats.push_back(loss);
+    JsonWriter w;
+    w.begin_object();
+    w.key("loss").number(loss);
+    w.key("batches").integer(batches);
+    w.key("tokens").integer(rows * seq);
+    w.end_object();
+    set_text(w.finish());
+    return MIDMAN_OK;
   });
 }
 

@@ -289,29 +289,34 @@ void rope_tables(uint64_t head_dim, uint64_t max_seq_len, float theta, std::vect
 Batcher::Batcher(std::vector<uint32_t> tokens, uint32_t vocab, int seq, int batch, uint64_t seed)
     : Batcher(std::vector<std::vector<uint32_t>>{std::move(tokens)}, vocab, seq, batch, seed) {}
 
-Batcher::Batcher(std::vector<std::vector<uint32_t>> shards, uint32_t vocab, int seq, int batch, uint64_t seed)
-    : shards_(std::move(shards)), vocab_(vocab), seq_(seq), batch_(batch), seed_(seed) {
+Sequences::Sequences(std::vector<std::vector<uint32_t>> shards, int seq) : shards_(std::move(shards)), seq_(seq) {
   if (seq <= 0) throw std::invalid_argument("a sequence must have at least one token");
-  if (batch <= 0) throw std::invalid_argument("a batch must have at least one sequence");
-  count_ = 0;
+  size_t total = 0;
   for (const auto& shard : shards_) {
-    for (uint32_t t : shard)
-      if (t >= vocab_) throw std::out_of_range("token id " + std::to_string(t) + " is out of range for vocab " +
-                                               std::to_string(vocab_));
-    if (shard.size() > seq_) count_ += (shard.size() - 1) / seq_;  // batch.rs:63-67
-    ends_.push_back(count_);
+    if (shard.size() > seq_) total += (shard.size() - 1) / seq_;  // batch.rs:63-67
+    ends_.push_back(total);
   }
-  if (count_ < batch_)
-    throw std::invalid_argument("there are " + std::to_string(count_) + " sequences, fewer than one batch of " +
-                                std::to_string(batch_));
-  permute();
 }
 
-const uint32_t* Batcher::window(uint64_t index) const {
+const uint32_t* Sequences::window(uint64_t index) const {
   // the first shard whose running count passes `index`
   const size_t shard = std::upper_bound(ends_.begin(), ends_.end(), static_cast<size_t>(index)) - ends_.begin();
   const size_t before = shard == 0 ? 0 : ends_[shard - 1];
   return shards_[shard].data() + (index - before) * seq_;
+}
+
+Batcher::Batcher(std::vector<std::vector<uint32_t>> shards, uint32_t vocab, int seq, int batch, uint64_t seed)
+    : data_(std::move(shards), seq), vocab_(vocab), seq_(seq), batch_(batch), seed_(seed) {
+  if (batch <= 0) throw std::invalid_argument("a batch must have at least one sequence");
+  for (const auto& shard : data_.shards())
+    for (uint32_t t : shard)
+      if (t >= vocab_) throw std::out_of_range("token id " + std::to_string(t) + " is out of range for vocab " +
+                                               std::to_string(vocab_));
+  count_ = data_.size();
+  if (count_ < batch_)
+    throw std::invalid_argument("there are " + std::to_string(count_) + " sequences, fewer than one batch of " +
+                                std::to_string(batch_));
+  permute();
 }
 
 // batch.rs:244-248: Rng(seed).fork(epoch).shuffle(0..n)
@@ -331,7 +336,7 @@ std::pair<uint64_t, uint64_t> Batcher::next(int32_t* inputs, int32_t* targets) {
     permute();
   }
   for (size_t r = 0; r < batch_; ++r) {
-    const uint32_t* w = window(order_[next_ * batch_ + r]);
+    const uint32_t* w = data_.window(order_[next_ * batch_ + r]);
     for (size_t t = 0; t < seq_; ++t) {
       inputs[r * seq_ + t] = static_cast<int32_t>(w[t]);
       targets[r * seq_ + t] = static_cast<int32_t>(w[t + 1]);

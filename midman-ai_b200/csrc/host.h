@@ -87,6 +87,22 @@ void rope_tables(uint64_t head_dim, uint64_t max_seq_len, float theta, std::vect
 
 // Sequences over one token shard (windows of seq + 1 tokens every seq tokens)
 // and the seeded Batcher (crates/midman-data/src/batch.rs:45-248).
+// Sequences (batch.rs:29-107): windows of seq + 1 tokens every seq tokens of each
+// shard; a window never crosses from one shard to the next.
+class Sequences {
+ public:
+  Sequences(std::vector<std::vector<uint32_t>> shards, int seq);
+  size_t size() const { return ends_.empty() ? 0 : ends_.back(); }
+  size_t seq() const { return seq_; }
+  const std::vector<std::vector<uint32_t>>& shards() const { return shards_; }
+  const uint32_t* window(uint64_t index) const;  // Sequences::window (batch.rs:96-106); index < size()
+
+ private:
+  std::vector<std::vector<uint32_t>> shards_;
+  std::vector<size_t> ends_;  // sequences in each shard and all the shards before it
+  size_t seq_;
+};
+
 class Batcher {
  public:
   Batcher(std::vector<uint32_t> tokens, uint32_t vocab, int seq, int batch, uint64_t seed);
@@ -105,9 +121,7 @@ class Batcher {
 
  private:
   void permute();
-  const uint32_t* window(uint64_t index) const;  // Sequences::window (batch.rs:96-106)
-  std::vector<std::vector<uint32_t>> shards_;
-  std::vector<size_t> ends_;  // sequences in each shard and all the shards before it
+  Sequences data_;
   uint32_t vocab_;
   size_t seq_, batch_, count_;
   uint64_t seed_, epoch_ = 0;

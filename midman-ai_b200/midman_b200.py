@@ -29,7 +29,7 @@ API_SYMBOLS = [
     "midman_train_stream", "midman_train_profile", "midman_batcher_create", "midman_batcher_synthetic",
     "midman_batcher_next", "midman_batcher_destroy", "midman_train_save", "midman_train_restore",
     "midman_state_inspect", "midman_shard_inspect", "midman_batcher_open", "midman_batcher_seek", "midman_train_run",
-    "midman_shard_read", "midman_shard_write", "midman_sha256",
+    "midman_shard_read", "midman_shard_write", "midman_sha256", "midman_train_evaluate",
 ]
 STATUS = {0: "OK", 1: "STOPPED", -1: "ARGUMENT", -2: "CONFIG", -3: "SHAPE", -4: "INDEX", -5: "OTHER",
           -6: "DEVICE", -99: "PANIC"}
@@ -109,6 +109,7 @@ def load(path: str | os.PathLike | None = None) -> C.CDLL:
     _sig(lib, "midman_shard_read", i32, u8p, u32, C.POINTER(C.c_uint32), C.c_uint64)
     _sig(lib, "midman_shard_write", i32, u8p, u32, u32, u32, C.POINTER(C.c_uint32), C.c_uint64)
     _sig(lib, "midman_sha256", i32, u8p, C.c_uint64, u8p)
+    _sig(lib, "midman_train_evaluate", i32, u32, u8p, u32, C.c_uint64)
     _lib = lib
     return lib
 
@@ -414,6 +415,12 @@ class Trainer:
         st = api(load().midman_train_run(self.h, batcher.h, steps), ok=(0, 1))
         rec = floats().reshape(-1, 3)
         return rec, st, (_json.loads(text()) if st == 0 else None)
+
+    def evaluate(self, shards, max_batches: int) -> dict:
+        """midman_train_evaluate: {loss, batches, tokens} over held-out shard files."""
+        b = _path_bytes("\n".join(str(p) for p in shards))
+        api(load().midman_train_evaluate(self.h, b, len(b) if b is not None else 0, max_batches))
+        return _json.loads(text())
 
     def save(self, path, data_seed: int = 0, epoch: int = 0, position: int = 0):
         """Writes the run's state file (param/*, adamw.m/*, adamw.v/* and the run's metadata)."""

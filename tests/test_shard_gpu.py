@@ -134,3 +134,59 @@ def test_the_batcher_must_fit_the_run(mm, tmp_path):
     assert np.array_equal(got[0], want[0]) and got[2:] == want[2:]
     for h in (t, wrong, fresh):
         h.close()
+
+
+def test_evaluation_is_the_mean_loss_on_evenly_spread_sequences(mm, tmp_path):
+    # trainer.rs:485-514, through midman_train_evaluate over held-out shard files
+    lengths = [300, 95, 210]
+    paths = shards(tmp_path, lengths, seed=4)
+    t = trainer(mm)
+    for x, y in [(np.arange(B * T) % 64, (np.arange(B * T) * 7) % 64)]:
+        t.step(x, y)
+    before = t.params().copy()
+    report = t.evaluate(paths, 3)
+    assert report["batches"] == 3 and report["tokens"] == 3 * B * T
+    assert t.evaluate(paths, 3) == report  # the same call gives the same number
+    assert np.array_equal(bits(t.params()), bits(before))  # and does not train
+    # by hand: row k of the rows taken is sequence k * len / rows, mean of the batch losses in f64
+    tokens = np.concatenate([ts_tokens(p) for p in paths])
+    starts = np.cumsum([0] + lengths[:-1])
+    windows = [(s + j * T) for s, n in zip(starts, lengths) if n > T for j in range((n - 1) // T)]
+    rows = 3 * B
+    oracle_model = orc.Model(CFG, seed=0)
+    oracle_model.params = t.params()
+    total, total_oracle = 0.0, 0.0
+    for b in range(3):
+        at = [windows[(b * B + r) * len(windows) // rows] for r in range(B)]
+        x = np.concatenate([tokens[a:a + T] for a in at]).astype(np.int32)
+        y = np.concatenate([tokens[a + 1:a + T + 1] for a in at]).astype(np.int32)
+        total += float(np.float32(t.eval(x, y, B, T)))
+        total_oracle += oracle_model.loss(x, y, B, T)
+    assert np.float32(report["loss"]) == np.float32(total / 3)
+    assert abs(report["loss"] - total_oracle / 3) <= 1e-5 * abs(total_oracle / 3)
+    # more batches than the data holds is cut to what it holds
+    small = tmp_path / "small.mmtokens"
+    small.write_bytes(ts.to_bytes(64, 11, np.ones(5 * T + 1, np.uint32)))
+    r = t.evaluate([small], 100)
+    assert (r["batches"], r["tokens"]) == (5 // B, (5 // B) * B * T)
+    one = tmp_path / "one.mmtokens"
+    one.write_bytes(ts.to_bytes(64, 11, np.ones(T + 1, np.uint32)))  # one sequence: a batch of one row
+    r = t.evaluate([one], 4)
+    assert (r["batches"], r["tokens"]) == (1, T)
+    t.close()
+
+
+def test_evaluation_refuses_what_does_not_fit(mm, tmp_path):
+    # trainer.rs:517-527
+    t = trainer(mm)
+    paths = shards(tmp_path, [300], seed=5)
+    other_vocab = tmp_path / "v.mmtokens"
+    other_vocab.write_bytes(ts.to_bytes(65, 0, np.ones(100, np.uint32)))
+    empty = tmp_path / "e.mmtokens"
+    empty.write_bytes(ts.to_bytes(64, 0, np.ones(T, np.uint32)))  # shorter than one window
+    for args, mention in [((paths, 0), "nothing"), (([other_vocab], 2), "vocabulary"), (([empty], 2), "nothing"),
+                          (([], 2), "empty")]:
+        with pytest.raises(mm.MidmanError) as e:
+            t.evaluate(*args)
+        assert e.value.status == -1 and mention in e.value.message, (args, e.value.message)
+    t.close()
