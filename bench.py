@@ -282,6 +282,8 @@ def main():
     ap.add_argument("--precision", default="tf32", choices=["tf32", "3xtf32"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--optimizer", default="replicated", choices=["replicated", "sharded"],
+                    help="sharded: ZeRO-1, each rank keeps and updates 1/N of the AdamW state (N > 1)")
     args = ap.parse_args()
 
     if args.config in ("linear", "attention", "attention-large"):
@@ -326,6 +328,8 @@ def main():
                            beta1=0.9, beta2=0.95)
     trainer = mm.Trainer(mm.config_array(*cfg), hyper, seed=0, batch=B, seq=T, precision=precision, world=world,
                          rank=rank, nccl_id=nccl_id)
+    if args.optimizer == "sharded":
+        trainer.shard_optimizer(True)
     stream = torch.cuda.ExternalStream(trainer.stream())
 
     def barrier():
@@ -405,7 +409,7 @@ def main():
             "scaling": "weak", "vs_baseline": None, "dtype": "tf32" if precision == 0 else "3xtf32",
             "data": "synthetic uniform token ids (Rng(0).below(vocab)), seeded init",
             "config": {"workload": args.config, "preset": list(cfg), "batch_per_gpu": B, "global_batch": B * world,
-                       "seq_len": T, "parallelism": f"dp{world}",
+                       "seq_len": T, "parallelism": f"dp{world}", "optimizer": args.optimizer,
                        "l2": "no flush: the step's working set (weights, moments, activations) is far above the "
                              "126 MB L2"},
             "loss_first_last": [float(rec[0, 0]), float(rec[-1, 0])],

@@ -204,6 +204,22 @@ MIDMAN_EXPORT int32_t midman_batcher_seek(uint32_t handle, uint64_t epoch, uint6
  * weights, moments, step count and the batcher's place as they were
  * (MIDMAN_STOPPED). Text: {"epoch","position","sequences"} of the batcher. */
 MIDMAN_EXPORT int32_t midman_train_run(uint32_t handle, uint32_t batcher, uint32_t steps);
+/* Optimizer-state sharding (ZeRO stage 1; no counterpart in the reference, whose
+ * trainer is one process). enable != 0: rank r keeps the AdamW moments of one
+ * contiguous range of the flat parameter vector (1/world of them); each step
+ * reduces every gradient bucket to its owners (ncclReduce) instead of
+ * all-reducing it, takes the global norm from the ranks' shares of the fixed
+ * sum-of-squares grid (the same number as unsharded), updates its own range and
+ * broadcasts it, the next forward waiting bucket by bucket. The step's results
+ * match the unsharded step's to rounding (NCCL's reduce and all-reduce may add in
+ * other orders). While on: reading moments (midman_train_read 2/3) and
+ * midman_train_save are collective (every rank calls them; rank 0 alone writes the
+ * file); gradients after a step are whole only on the owner's range, so
+ * midman_train_read 1 is refused until midman_train_loss_and_grads. enable == 0
+ * gathers the moments back (collective). Text: {"sharding": {"optimizer",
+ * "world","rank","ranges":[[begin,end]...],"buckets":[[begin,end]...]}}; the
+ * same object appears in midman_train_describe. */
+MIDMAN_EXPORT int32_t midman_train_shard_optimizer(uint32_t handle, uint32_t enable);
 /* Trainer::evaluate (trainer.rs:209-262) over held-out shard files (paths
  * separated by '\n'), windows of the run's seq: batches of the run's global batch
  * (or all the sequences, if fewer), row k of the `rows` taken is sequence

@@ -708,6 +708,31 @@ std::vector<StateParam> state_params(const ParamLayout& L) {
   return out;
 }
 
+// "sharding": {"optimizer": bool, "ranges": [[begin, end] per rank], "buckets": [[begin, end]...]}
+void write_sharding(JsonWriter& w, const Trainer& tr) {
+  w.key("sharding").begin_object();
+  w.key("optimizer").boolean(tr.optimizer_sharded());
+  w.key("world").integer(tr.world());
+  w.key("rank").integer(tr.rank());
+  w.key("ranges").begin_array();
+  for (int r = 0; r < tr.world(); ++r) {
+    w.begin_array();
+    w.integer(tr.shard_begin(r));
+    w.integer(tr.shard_end(r));
+    w.end_array();
+  }
+  w.end_array();
+  w.key("buckets").begin_array();
+  for (const auto& b : tr.buckets()) {
+    w.begin_array();
+    w.integer(b.first);
+    w.integer(b.second);
+    w.end_array();
+  }
+  w.end_array();
+  w.end_object();
+}
+
 void write_progress(JsonWriter& w, const Progress& p) {
   w.begin_object();
   w.key("step").integer(p.step);
@@ -726,8 +751,38 @@ int32_t midman_train_save(uint32_t handle, const uint8_t* path, uint32_t path_le
     p.step = t.step;
     p.epoch = epoch;
     p.position = position;
-    save_state(file, state_params(t.trainer->layout()), p, settings_of(t, data_seed_lo, data_seed_hi),
-               [&](int which, uint64_t offset, uint64_t n, float* out) { t.trainer->read_tensor(offset, n, out, which); });
+    Trainer& tr = *t.trainer;
+    if (tr.optimizer_sharded() && tr.world() > 1) {
+      // collective: every rank gathers the moments from their owners; rank 0 writes
+      const uint64_t total = tr.layout().total;
+      std::vector<float> m(total), v(total);
+      tr.read_tensor(0, total, m.data(), 2);
+      tr.read_tensor(0, total, v.data(), 3);
+      if (tr.rank() != 0) return MIDMAN_OK;
+      save_state(file, state_params(tr.layout()), p, settings_of(t, data_seed_lo, data_seed_hi),
+                 [&](int which, uint64_t offset, uint64_t n, float* out) {
+                   if (which == 2 || which == 3)
+                     std::memcpy(out, (which == 2 ? m : v).data() + offset, n * 4);
+                   else
+                     tr.read_tensor(offset, n, out, which);
+                 });
+      return MIDMAN_OK;
+    }
+    save_state(file, state_params(tr.layout()), p, settings_of(t, data_seed_lo, data_seed_hi),
+               [&](int which, uint64_t offset, uint64_t n, float* out) { tr.read_tensor(offset, n, out, which); });
+    return MIDMAN_OK;
+  });
+}
+
+int32_t midman_train_shard_optimizer(uint32_t handle, uint32_t enable) {
+  return run([&] {
+    Train& t = train_ref(handle);
+    t.trainer->shard_optimizer(enable != 0);
+    JsonWriter w;
+    w.begin_object();
+    write_sharding(w, *t.trainer);
+    w.end_object();
+    set_text(w.finish());
     return MIDMAN_OK;
   });
 }
@@ -788,6 +843,7 @@ int32_t midman_train_describe(uint32_t handle) {
     w.key("params").integer(L.total);
     w.key("steps").integer(t.step);
     w.key("kernel_launches").integer(t.trainer->kernel_launches());
+    write_sharding(w, *t.trainer);
     w.key("profile").begin_object();
     for (const auto& e : t.trainer->profile()) {
       w.key(e.first).begin_object();

@@ -52,16 +52,24 @@ struct AdamChunk {
   int decay;  // parameter has rank >= 2
 };
 // Partial sums of g^2 in f64 (fixed grid: deterministic). partials: kNormBlocks doubles.
+// Block b reduces elements [b * norm_block_elems(n), (b + 1) * norm_block_elems(n)) ∩ [0, n);
+// with [lo, hi) given, blocks whose range is not inside it write 0 (a data-parallel
+// rank's share of the grid: summed over ranks, the partials are the whole grid's).
 constexpr int kNormBlocks = 1184;  // 8 x 148 SMs
-void sumsq_partials(const float* g, long long n, double* partials, cudaStream_t s);
+__host__ __device__ inline long long norm_block_elems(long long n) {
+  return ((n + kNormBlocks - 1) / kNormBlocks + 3) & ~3ll;
+}
+void sumsq_partials(const float* g, long long n, double* partials, cudaStream_t s, long long lo = 0,
+                    long long hi = -1);
 // status[0..]: finishes the norm from the partials, applies the reference's clip
 // rule and writes [norm (f32), clip factor, ok flag] into `norm_out` (device).
 void finish_norm(const double* partials, const double* loss, float max_norm, float* norm_out, cudaStream_t s);
 // One AdamW step over every chunk, skipped entirely when norm_out says the loss or
-// the norm was not finite. Gradients are scaled by the clip factor first.
+// the norm was not finite. Gradients are scaled by the clip factor first. m and v
+// hold the moments of the flat elements from mv_base on (chunks lie inside them).
 void adamw_step(const AdamChunk* chunks, int n_chunks, float* p, const float* g, float* m, float* v,
-                const float* norm_out, float lr, float beta1, float beta2, float eps, float weight_decay,
-                float step_size, float bias2_sqrt, cudaStream_t s);
+                long long mv_base, const float* norm_out, float lr, float beta1, float beta2, float eps,
+                float weight_decay, float step_size, float bias2_sqrt, cudaStream_t s);
 // Per-tensor sum of squares in f64 (for per-parameter statistics).
 void tensor_sumsq(const float* x, long long n, double* out, cudaStream_t s);
 

@@ -36,14 +36,16 @@ __device__ __forceinline__ double block_sum_d(double v, double* red) {
   return warp_sum_d(t);
 }
 
-__global__ void sumsq_kernel(const float* __restrict__ g, long long n, double* __restrict__ partials) {
+__global__ void sumsq_kernel(const float* __restrict__ g, long long n, double* __restrict__ partials, long long lo,
+                             long long hi) {
   __shared__ double red[32];
   // Each block reduces one contiguous range; ranges start on 4-element boundaries.
-  const long long per = ((n + gridDim.x - 1) / gridDim.x + 3) & ~3ll;
+  // A block whose range is not inside [lo, hi) writes 0 (another rank's share).
+  const long long per = norm_block_elems(n);
   const long long beg = per * blockIdx.x;
   const long long end = beg + per < n ? beg + per : n;
   double s = 0.0;
-  if (beg < end) {
+  if (beg < end && beg >= lo && end <= hi) {
     const long long nvec = (end - beg) / 4;
     const float4* g4 = reinterpret_cast<const float4*>(g + beg);
     for (long long j = threadIdx.x; j < nvec; j += blockDim.x) {
@@ -73,23 +75,28 @@ __global__ void finish_norm_kernel(const double* __restrict__ partials, int n, c
 }
 
 // One block per chunk (a chunk never spans two parameters).
+// m and v hold the moments of elements [mv_base, ...) of the flat vector (the whole
+// vector, or one rank's share of it under optimizer-state sharding).
 __global__ void adamw_kernel(const AdamChunk* __restrict__ chunks, float* __restrict__ p, const float* __restrict__ g,
-                             float* __restrict__ m, float* __restrict__ v, const float* __restrict__ norm_out,
-                             float lr, float beta1, float beta2, float eps, float wd, float step_size,
-                             float bias2_sqrt) {
+                             float* __restrict__ m, float* __restrict__ v, long long mv_base,
+                             const float* __restrict__ norm_out, float lr, float beta1, float beta2, float eps,
+                             float wd, float step_size, float bias2_sqrt) {
   if (norm_out[2] == 0.0f) return;  // a rejected step changes nothing
   const float factor = norm_out[1];
   const AdamChunk c = chunks[blockIdx.x];
   const float decay = c.decay ? 1.0f - lr * wd : 1.0f;
   const float omb1 = 1.0f - beta1, omb2 = 1.0f - beta2;
   const long long base = c.offset;
+  m += base - mv_base;
+  v += base - mv_base;
   for (int i = threadIdx.x * 4; i < c.length; i += blockDim.x * 4) {
     const long long k = base + i;
+    const long long km = i;  // index into m and v
     if (i + 3 < c.length) {
       float4 x = *reinterpret_cast<float4*>(p + k);
       float4 gg = *reinterpret_cast<const float4*>(g + k);
-      float4 mm_ = *reinterpret_cast<float4*>(m + k);
-      float4 vv = *reinterpret_cast<float4*>(v + k);
+      float4 mm_ = *reinterpret_cast<float4*>(m + km);
+      float4 vv = *reinterpret_cast<float4*>(v + km);
       float* xs = &x.x;
       float* gs = &gg.x;
       float* ms = &mm_.x;
@@ -103,18 +110,18 @@ __global__ void adamw_kernel(const AdamChunk* __restrict__ chunks, float* __rest
         xs[e] -= step_size * ms[e] / (sqrtf(vs[e]) / bias2_sqrt + eps);
       }
       *reinterpret_cast<float4*>(p + k) = x;
-      *reinterpret_cast<float4*>(m + k) = mm_;
-      *reinterpret_cast<float4*>(v + k) = vv;
+      *reinterpret_cast<float4*>(m + km) = mm_;
+      *reinterpret_cast<float4*>(v + km) = vv;
     } else {
       for (int e = 0; e < 4 && i + e < c.length; ++e) {
         const float gr = g[k + e] * factor;
         float x = p[k + e] * decay;
-        const float mn = beta1 * m[k + e] + omb1 * gr;
-        const float vn = beta2 * v[k + e] + omb2 * gr * gr;
+        const float mn = beta1 * m[km + e] + omb1 * gr;
+        const float vn = beta2 * v[km + e] + omb2 * gr * gr;
         x -= step_size * mn / (sqrtf(vn) / bias2_sqrt + eps);
         p[k + e] = x;
-        m[k + e] = mn;
-        v[k + e] = vn;
+        m[km + e] = mn;
+        v[km + e] = vn;
       }
     }
   }
@@ -135,8 +142,8 @@ void check(const char* what) {
 
 }  // namespace
 
-void sumsq_partials(const float* g, long long n, double* partials, cudaStream_t s) {
-  sumsq_kernel<<<kNormBlocks, 256, 0, s>>>(g, n, partials);
+void sumsq_partials(const float* g, long long n, double* partials, cudaStream_t s, long long lo, long long hi) {
+  sumsq_kernel<<<kNormBlocks, 256, 0, s>>>(g, n, partials, lo, hi < 0 ? n : hi);
   check("sumsq_partials");
 }
 
@@ -146,11 +153,11 @@ void finish_norm(const double* partials, const double* loss, float max_norm, flo
 }
 
 void adamw_step(const AdamChunk* chunks, int n_chunks, float* p, const float* g, float* m, float* v,
-                const float* norm_out, float lr, float beta1, float beta2, float eps, float weight_decay,
-                float step_size, float bias2_sqrt, cudaStream_t s) {
+                long long mv_base, const float* norm_out, float lr, float beta1, float beta2, float eps,
+                float weight_decay, float step_size, float bias2_sqrt, cudaStream_t s) {
   if (n_chunks <= 0) return;
-  adamw_kernel<<<n_chunks, 256, 0, s>>>(chunks, p, g, m, v, norm_out, lr, beta1, beta2, eps, weight_decay, step_size,
-                                        bias2_sqrt);
+  adamw_kernel<<<n_chunks, 256, 0, s>>>(chunks, p, g, m, v, mv_base, norm_out, lr, beta1, beta2, eps, weight_decay,
+                                        step_size, bias2_sqrt);
   check("adamw_step");
 }
 

@@ -54,7 +54,15 @@ Trainer::Trainer(const ModelConfig& cfg, int batch, int seq, int precision, int 
     layer_done_.resize(cfg.n_layers + 1);
     for (auto& e : layer_done_) check_cuda(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "event");
     check_cuda(cudaEventCreateWithFlags(&comm_done_, cudaEventDisableTiming), "event");
+    gathered_.resize(cfg.n_layers + 2);
+    for (auto& e : gathered_) check_cuda(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "event");
+    check_cuda(cudaEventCreateWithFlags(&update_done_, cudaEventDisableTiming), "event");
   }
+  // gradient buckets in forward order: embedding, blocks, final norm (+ untied head)
+  buckets_.push_back({layout_.embed, layout_.embed + cfg.vocab * cfg.d_model});
+  for (const BlockOffsets& bo : layout_.blocks)
+    buckets_.push_back({bo.attn_norm, bo.down + cfg.d_ff * cfg.d_model});
+  buckets_.push_back({layout_.final_norm, layout_.total});
 
   auto alloc = [&](size_t bytes) {
     void* p = nullptr;
@@ -72,15 +80,12 @@ Trainer::Trainer(const ModelConfig& cfg, int batch, int seq, int precision, int 
   check_cuda(cudaMemset(M_, 0, total * 4), "memset");
   check_cuda(cudaMemset(V_, 0, total * 4), "memset");
 
-  // AdamW chunks: never across a parameter boundary; decay for rank >= 2 (adamw.rs:197).
-  std::vector<AdamChunk> chunks;
-  for (const TensorInfo& t : layout_.tensors)
-    for (uint64_t o = 0; o < t.numel; o += 16384)
-      chunks.push_back({static_cast<long long>(t.offset + o), static_cast<int>(std::min<uint64_t>(16384, t.numel - o)),
-                        t.shape.size() >= 2 ? 1 : 0});
-  n_chunks_ = static_cast<int>(chunks.size());
-  d_chunks_ = static_cast<AdamChunk*>(alloc(chunks.size() * sizeof(AdamChunk)));
-  check_cuda(cudaMemcpy(d_chunks_, chunks.data(), chunks.size() * sizeof(AdamChunk), cudaMemcpyHostToDevice), "chunks");
+  {
+    uint64_t n = 0;
+    for (const TensorInfo& t : layout_.tensors) n += (t.numel + 16383) / 16384;
+    d_chunks_ = static_cast<AdamChunk*>(alloc(std::max<uint64_t>(n, 1) * sizeof(AdamChunk)));
+  }
+  build_chunks();
 
   std::vector<float> cs, sn;
   rope_tables(cfg.head_dim(), cfg.max_seq_len, cfg.rope_theta, cs, sn);
@@ -156,6 +161,8 @@ Trainer::~Trainer() {
     if (p) cudaFreeHost(p);
   if (h_out_) cudaFreeHost(h_out_);
   for (auto e : layer_done_) cudaEventDestroy(e);
+  for (auto e : gathered_) cudaEventDestroy(e);
+  if (update_done_) cudaEventDestroy(update_done_);
   for (auto e : prof_events_) cudaEventDestroy(e);
   if (comm_done_) cudaEventDestroy(comm_done_);
   if (comm_) nccl().CommDestroy(static_cast<ncclComm_t>(comm_));
@@ -170,18 +177,109 @@ void Trainer::init_params(HostRng& rng, float init_std, int threads) {
   load_params(host.data());
 }
 
+// AdamW chunks of the range this rank updates: never across a parameter
+// boundary, at most 16,384 elements; decay for rank >= 2 tensors (adamw.rs:197).
+void Trainer::build_chunks() {
+  const uint64_t lo = shard_begin(rank_), hi = shard_end(rank_);
+  std::vector<AdamChunk> chunks;
+  for (const TensorInfo& t : layout_.tensors) {
+    const uint64_t b = std::max(lo, t.offset), e = std::min(hi, t.offset + t.numel);
+    for (uint64_t o = b; o < e; o += 16384)
+      chunks.push_back({static_cast<long long>(o), static_cast<int>(std::min<uint64_t>(16384, e - o)),
+                        t.shape.size() >= 2 ? 1 : 0});
+  }
+  n_chunks_ = static_cast<int>(chunks.size());
+  if (n_chunks_)
+    check_cuda(cudaMemcpy(d_chunks_, chunks.data(), chunks.size() * sizeof(AdamChunk), cudaMemcpyHostToDevice),
+               "chunks");
+}
+
+void Trainer::shard_optimizer(bool on) {
+  if (on == zero1_) return;
+  wait_params(-1);
+  check_cuda(cudaStreamSynchronize(stream_), "shard optimizer");
+  const uint64_t total = layout_.total;
+  auto replace = [&](float*& buf, float* fresh) {
+    allocations_.erase(std::find(allocations_.begin(), allocations_.end(), static_cast<void*>(buf)));
+    check_cuda(cudaFree(buf), "cudaFree");
+    buf = fresh;
+    allocations_.push_back(fresh);
+  };
+  auto falloc = [&](uint64_t n) {
+    void* p = nullptr;
+    check_cuda(cudaMalloc(&p, std::max<uint64_t>(n * 4, 256)), "cudaMalloc");
+    return static_cast<float*>(p);
+  };
+  if (on) {
+    // ranges end on blocks of the fixed norm grid, so each block's partial is one rank's
+    const uint64_t per = static_cast<uint64_t>(norm_block_elems(static_cast<long long>(total)));
+    bounds_.assign(world_ + 1, total);
+    for (int r = 0; r < world_; ++r)
+      bounds_[r] = std::min<uint64_t>(total, per * ((static_cast<uint64_t>(kNormBlocks) * r) / world_));
+    const uint64_t lo = bounds_[rank_], n = bounds_[rank_ + 1] - lo;
+    float* m = falloc(n);
+    float* v = falloc(n);
+    check_cuda(cudaMemcpy(m, M_ + lo, n * 4, cudaMemcpyDeviceToDevice), "shard moments");
+    check_cuda(cudaMemcpy(v, V_ + lo, n * 4, cudaMemcpyDeviceToDevice), "shard moments");
+    replace(M_, m);
+    replace(V_, v);
+    zero1_ = true;
+  } else {
+    float* m = falloc(total);
+    float* v = falloc(total);
+    gather_moment(2, 0, total, m);
+    gather_moment(3, 0, total, v);
+    check_cuda(cudaStreamSynchronize(stream_), "gather moments");
+    replace(M_, m);
+    replace(V_, v);
+    zero1_ = false;
+  }
+  build_chunks();
+}
+
+// Copies moment `which` (2: m, 3: v) of flat elements [offset, offset + n) into a
+// device buffer, each owner broadcasting its part (every rank calls this).
+void Trainer::gather_moment(int which, uint64_t offset, uint64_t n, float* dst) {
+  const float* src = which == 2 ? M_ : V_;
+  if (!zero1_ || world_ == 1) {
+    check_cuda(cudaMemcpyAsync(dst, src + offset, n * 4, cudaMemcpyDeviceToDevice, stream_), "moments");
+    return;
+  }
+  ncclComm_t comm = static_cast<ncclComm_t>(comm_);
+  nccl_check(nccl().GroupStart(), "ncclGroupStart");
+  for (int r = 0; r < world_; ++r) {
+    const uint64_t lo = std::max(offset, bounds_[r]), hi = std::min(offset + n, bounds_[r + 1]);
+    if (lo >= hi) continue;
+    const float* send = r == rank_ ? src + (lo - bounds_[r]) : dst + (lo - offset);
+    nccl_check(nccl().Broadcast(send, dst + (lo - offset), hi - lo, ncclFloat, r, comm, stream_), "ncclBroadcast");
+  }
+  nccl_check(nccl().GroupEnd(), "ncclGroupEnd");
+}
+
+void Trainer::wait_params(int bucket) {
+  if (!gather_pending_) return;
+  const int last = static_cast<int>(gathered_.size()) - 1;
+  check_cuda(cudaStreamWaitEvent(stream_, gathered_[bucket < 0 ? last : bucket], 0), "wait params");
+  if (bucket < 0 || bucket == last) gather_pending_ = false;
+}
+
 void Trainer::load_params(const float* host) {
+  wait_params(-1);
   check_cuda(cudaMemcpyAsync(P_, host, layout_.total * 4, cudaMemcpyHostToDevice, stream_), "load params");
   check_cuda(cudaStreamSynchronize(stream_), "load params");
 }
 
 void Trainer::restore(const float* params, const float* m, const float* v, uint64_t adam_steps) {
+  wait_params(-1);
   const size_t bytes = layout_.total * 4;
   check_cuda(cudaMemcpyAsync(P_, params, bytes, cudaMemcpyHostToDevice, stream_), "restore params");
-  if (m) check_cuda(cudaMemcpyAsync(M_, m, bytes, cudaMemcpyHostToDevice, stream_), "restore moments");
-  else check_cuda(cudaMemsetAsync(M_, 0, bytes, stream_), "restore moments");
-  if (v) check_cuda(cudaMemcpyAsync(V_, v, bytes, cudaMemcpyHostToDevice, stream_), "restore moments");
-  else check_cuda(cudaMemsetAsync(V_, 0, bytes, stream_), "restore moments");
+  // this rank's range of the moments (all of them without sharding)
+  const uint64_t lo = mv_begin();
+  const size_t mv_bytes = (shard_end(rank_) - lo) * 4;
+  if (m) check_cuda(cudaMemcpyAsync(M_, m + lo, mv_bytes, cudaMemcpyHostToDevice, stream_), "restore moments");
+  else check_cuda(cudaMemsetAsync(M_, 0, mv_bytes, stream_), "restore moments");
+  if (v) check_cuda(cudaMemcpyAsync(V_, v + lo, mv_bytes, cudaMemcpyHostToDevice, stream_), "restore moments");
+  else check_cuda(cudaMemsetAsync(V_, 0, mv_bytes, stream_), "restore moments");
   check_cuda(cudaStreamSynchronize(stream_), "restore");
   adam_steps_ = adam_steps;
 }
@@ -191,7 +289,31 @@ void Trainer::read_grads(float* host) { read_tensor(0, layout_.total, host, 1); 
 
 void Trainer::read_tensor(uint64_t offset, uint64_t n, float* host, int which) {
   if (offset + n > layout_.total) throw std::out_of_range("tensor range outside the parameter vector");
-  const float* src = (which == 0 ? P_ : which == 1 ? G_ : which == 2 ? M_ : V_) + offset;
+  if (which == 1 && grads_partial_)
+    throw std::invalid_argument(
+        "the last step reduced each gradient to the rank that owns it (optimizer sharding): run loss_and_grads for "
+        "whole gradients");
+  wait_params(-1);
+  if ((which == 2 || which == 3) && zero1_ && world_ > 1) {
+    // collective: the owners broadcast their parts through a device buffer, in slices
+    const uint64_t slice = 1ull << 26;
+    float* tmp = nullptr;
+    check_cuda(cudaMalloc(&tmp, std::min(n, slice) * 4 + 256), "cudaMalloc");
+    try {
+      for (uint64_t o = 0; o < n; o += slice) {
+        const uint64_t k = std::min(slice, n - o);
+        gather_moment(which, offset + o, k, tmp);
+        check_cuda(cudaMemcpyAsync(host + o, tmp, k * 4, cudaMemcpyDeviceToHost, stream_), "read tensor");
+        check_cuda(cudaStreamSynchronize(stream_), "read tensor");
+      }
+    } catch (...) {
+      cudaFree(tmp);
+      throw;
+    }
+    check_cuda(cudaFree(tmp), "cudaFree");
+    return;
+  }
+  const float* src = which == 0 ? P_ + offset : which == 1 ? G_ + offset : (which == 2 ? M_ : V_) + offset;
   check_cuda(cudaMemcpyAsync(host, src, n * 4, cudaMemcpyDeviceToHost, stream_), "read tensor");
   check_cuda(cudaStreamSynchronize(stream_), "read tensor");
 }
@@ -339,6 +461,44 @@ void Trainer::allreduce_grads_range(uint64_t offset, uint64_t n) {
   nccl_check(nccl().AllReduce(G_ + offset, G_ + offset, n, ncclFloat, ncclAvg, static_cast<ncclComm_t>(comm_),
                            comm_stream_),
              "ncclAllReduce(grads)");
+}
+
+// Averages bucket b's gradients on the communication stream: everywhere, or (a
+// sharded update) only on the ranks owning each part of it.
+void Trainer::reduce_bucket(int b) {
+  const uint64_t beg = buckets_[b].first, end = buckets_[b].second;
+  if (!owner_reduce_) {
+    allreduce_grads_range(beg, end - beg);
+    return;
+  }
+  ncclComm_t comm = static_cast<ncclComm_t>(comm_);
+  nccl_check(nccl().GroupStart(), "ncclGroupStart");
+  for (int r = 0; r < world_; ++r) {
+    const uint64_t lo = std::max(beg, bounds_[r]), hi = std::min(end, bounds_[r + 1]);
+    if (lo < hi)
+      nccl_check(nccl().Reduce(G_ + lo, G_ + lo, hi - lo, ncclFloat, ncclAvg, r, comm, comm_stream_), "ncclReduce");
+  }
+  nccl_check(nccl().GroupEnd(), "ncclGroupEnd");
+}
+
+// After a sharded update: each owner broadcasts its updated parameters, bucket by
+// bucket in forward order, each bucket's completion an event the next forward waits on.
+void Trainer::broadcast_params() {
+  check_cuda(cudaEventRecord(update_done_, stream_), "event");
+  check_cuda(cudaStreamWaitEvent(comm_stream_, update_done_, 0), "wait");
+  ncclComm_t comm = static_cast<ncclComm_t>(comm_);
+  for (size_t b = 0; b < buckets_.size(); ++b) {
+    const uint64_t beg = buckets_[b].first, end = buckets_[b].second;
+    nccl_check(nccl().GroupStart(), "ncclGroupStart");
+    for (int r = 0; r < world_; ++r) {
+      const uint64_t lo = std::max(beg, bounds_[r]), hi = std::min(end, bounds_[r + 1]);
+      if (lo < hi)
+        nccl_check(nccl().Broadcast(P_ + lo, P_ + lo, hi - lo, ncclFloat, r, comm, comm_stream_), "ncclBroadcast");
+    }
+    nccl_check(nccl().GroupEnd(), "ncclGroupEnd");
+    check_cuda(cudaEventRecord(gathered_[b], comm_stream_), "event");
+  }
+  gather_pending_ = true;
 }
 
 }  // namespace mm

@@ -74,6 +74,23 @@ class Trainer {
   // Per-tensor L2 norms of the last step's gradients (f64 accumulation).
   std::vector<float> grad_norms();
 
+  // Optimizer-state sharding (ZeRO stage 1) over the data-parallel ranks. Rank r
+  // keeps the AdamW moments of the flat range [shard_begin(r), shard_end(r)) only;
+  // a step reduces each gradient bucket to the ranks owning it (ncclReduce, in
+  // place of the all-reduce), takes the global norm from the ranks' shares of the
+  // fixed sum-of-squares grid (one all-reduce of the partials, so it is the same
+  // number as without sharding), updates its own range, and broadcasts it to the
+  // others while the next step's forward waits layer by layer. The ranges end on
+  // blocks of that grid. Turning it on keeps this rank's share of the moments;
+  // turning it off gathers them (collective: every rank calls it).
+  void shard_optimizer(bool on);
+  bool optimizer_sharded() const { return zero1_; }
+  uint64_t shard_begin(int r) const { return zero1_ ? bounds_[r] : 0; }
+  uint64_t shard_end(int r) const { return zero1_ ? bounds_[r + 1] : layout_.total; }
+  // The ranges of the flat vector the step reduces and broadcasts as one bucket,
+  // in forward order: the embedding, each block, the final norm (and untied head).
+  const std::vector<std::pair<uint64_t, uint64_t>>& buckets() const { return buckets_; }
+
   // Kernels this object launched since construction (counted by the launchers).
   uint64_t kernel_launches() const { return launches_; }
 
@@ -113,6 +130,12 @@ class Trainer {
 
  private:
   void allreduce_grads_range(uint64_t offset, uint64_t n);
+  void reduce_bucket(int b);           // all-reduce, or reduce to the owners under sharding
+  void broadcast_params();             // owners -> all, bucket by bucket (sharding)
+  void wait_params(int bucket);        // stream_ waits for a bucket's broadcast (-1: all)
+  void gather_moment(int which, uint64_t offset, uint64_t n, float* dst_device);
+  void build_chunks();
+  uint64_t mv_begin() const { return zero1_ ? bounds_[rank_] : 0; }
   void check_device(const char* where);
   int prof_begin();
   void prof_end(int slot, const char* cls, double flops, std::string shape = {});
@@ -128,8 +151,17 @@ class Trainer {
   std::vector<cudaEvent_t> layer_done_;
   cudaEvent_t comm_done_ = nullptr;
 
-  // parameters, gradients and AdamW moments, flat in parameter order
+  // parameters, gradients and AdamW moments, flat in parameter order (moments:
+  // this rank's range only under optimizer sharding)
   float *P_ = nullptr, *G_ = nullptr, *M_ = nullptr, *V_ = nullptr;
+  bool zero1_ = false;
+  bool owner_reduce_ = false;   // this backward reduces to the owners (a sharded update)
+  bool grads_partial_ = false;  // G_ is complete only on this rank's range
+  std::vector<uint64_t> bounds_;                          // world + 1 range ends
+  std::vector<std::pair<uint64_t, uint64_t>> buckets_;  // forward order
+  std::vector<cudaEvent_t> gathered_;                   // per bucket: broadcast done
+  bool gather_pending_ = false;
+  cudaEvent_t update_done_ = nullptr;
   AdamChunk* d_chunks_ = nullptr;
   int n_chunks_ = 0;
   float *d_cos_ = nullptr, *d_sin_ = nullptr;

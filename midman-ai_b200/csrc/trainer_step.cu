@@ -35,11 +35,14 @@ void Trainer::forward(int B, int T, bool train) {
   const float eps = cfg_.norm_eps;
   const AttnShape shape{B, T, H, Hkv, hd, D, KV, KV, D, 1.0f / std::sqrt(static_cast<float>(hd))};
   const int L = static_cast<int>(cfg_.n_layers);
+  // under optimizer sharding, each bucket's parameters may still be arriving from their owner
+  wait_params(0);
   embedding_forward(d_ids_, N, P_ + layout_.embed, D, acts_[0].x, stream_);
   launches_ += 1;
   for (int l = 0; l < L; ++l) {
     Layer& a = acts_[l];
     const BlockOffsets& bo = layout_.blocks[l];
+    wait_params(1 + l);
     float* next_x = (l + 1 < L) ? acts_[l + 1].x : x_final_;
     // h = x + attention(attn_norm(x)) (block.rs:78-79)
     rmsnorm_forward(a.x, P_ + bo.attn_norm, N, D, eps, a.xn1, a.rstd1, stream_);
@@ -64,6 +67,7 @@ void Trainer::forward(int B, int T, bool train) {
     gemm(N, D, F, a.act, F, false, P_ + bo.down, D, true, next_x, D, a.h, D);
     launches_ += 6;  // two RMSNorms, two RoPEs, attention, SwiGLU (GEMMs are counted in gemm())
   }
+  wait_params(L + 1);
   rmsnorm_forward(x_final_, P_ + layout_.final_norm, N, D, eps, xf_, rstdf_, stream_);
   launches_ += 1;
   if (cfg_.tie)  // logits = xf E^T: E [V, D] is already K-major for this product
@@ -133,9 +137,7 @@ void Trainer::backward(int B, int T) {
       // backward runs (a bucket per layer, in reverse parameter order).
       check_cuda(cudaEventRecord(layer_done_[l], stream_), "event");
       check_cuda(cudaStreamWaitEvent(comm_stream_, layer_done_[l], 0), "wait");
-      const uint64_t beg = bo.attn_norm;
-      const uint64_t end = bo.down + static_cast<uint64_t>(F) * D;
-      allreduce_grads_range(beg, end - beg);
+      reduce_bucket(1 + l);
     }
   }
   // the embedding's share, added after the head's (ops_shape.rs:262-272)
@@ -144,8 +146,8 @@ void Trainer::backward(int B, int T) {
   if (world_ > 1) {
     check_cuda(cudaEventRecord(layer_done_[L], stream_), "event");
     check_cuda(cudaStreamWaitEvent(comm_stream_, layer_done_[L], 0), "wait");
-    allreduce_grads_range(layout_.embed, static_cast<uint64_t>(V) * D);
-    allreduce_grads_range(layout_.final_norm, layout_.total - layout_.final_norm);
+    reduce_bucket(0);
+    reduce_bucket(L + 1);
     nccl_ok(nccl().AllReduce(d_loss_, d_loss_, 1, ncclDouble, ncclAvg, static_cast<ncclComm_t>(comm_), comm_stream_),
             "ncclAllReduce(loss)");
     check_cuda(cudaEventRecord(comm_done_, comm_stream_), "event");
@@ -159,7 +161,18 @@ StepOut Trainer::finish_step(float lr, const AdamHyper& h, bool update) {
 }
 
 void Trainer::finish_launch(float lr, const AdamHyper& h, bool update) {
-  sumsq_partials(G_, static_cast<long long>(layout_.total), d_partials_, stream_);
+  const long long total = static_cast<long long>(layout_.total);
+  if (owner_reduce_) {
+    // each rank sums the grid blocks of its own range (reduced there); the others'
+    // blocks are 0, so the summed partials are the grid of the whole gradient
+    sumsq_partials(G_, total, d_partials_, stream_, static_cast<long long>(shard_begin(rank_)),
+                   static_cast<long long>(shard_end(rank_)));
+    nccl_ok(nccl().AllReduce(d_partials_, d_partials_, kNormBlocks, ncclDouble, ncclSum,
+                             static_cast<ncclComm_t>(comm_), stream_),
+            "ncclAllReduce(norm partials)");
+  } else {
+    sumsq_partials(G_, total, d_partials_, stream_);
+  }
   finish_norm(d_partials_, d_loss_, h.clip_norm, d_norm_, stream_);
   launches_ += 2;
   if (update) {
@@ -168,9 +181,10 @@ void Trainer::finish_launch(float lr, const AdamHyper& h, bool update) {
     const float bias1 = static_cast<float>(1.0 - std::pow(static_cast<double>(h.beta1), t));
     const float bias2_sqrt = static_cast<float>(std::sqrt(1.0 - std::pow(static_cast<double>(h.beta2), t)));
     const float step_size = lr / bias1;
-    adamw_step(d_chunks_, n_chunks_, P_, G_, M_, V_, d_norm_, lr, h.beta1, h.beta2, h.eps, h.weight_decay, step_size,
-               bias2_sqrt, stream_);
+    adamw_step(d_chunks_, n_chunks_, P_, G_, M_, V_, static_cast<long long>(mv_begin()), d_norm_, lr, h.beta1,
+               h.beta2, h.eps, h.weight_decay, step_size, bias2_sqrt, stream_);
     launches_ += 1;
+    if (zero1_ && world_ > 1) broadcast_params();
   }
   check_cuda(cudaMemcpyAsync(h_out_, d_loss_, sizeof(double), cudaMemcpyDeviceToHost, stream_), "loss D2H");
   check_cuda(cudaMemcpyAsync(h_out_ + 2, d_norm_, 3 * sizeof(float), cudaMemcpyDeviceToHost, stream_), "norm D2H");
@@ -201,6 +215,8 @@ StepOut Trainer::step_staged(float lr, const AdamHyper& h) {
 void Trainer::launch_step(float lr, const AdamHyper& h) {
   if (!(std::isfinite(lr) && lr >= 0.0f)) throw std::invalid_argument("lr must be finite and not negative");
   const int N = batch_ * seq_;
+  owner_reduce_ = zero1_ && world_ > 1;
+  grads_partial_ = owner_reduce_;
   forward(batch_, seq_, true);
   cross_entropy(logits_, cfg_.vocab, d_tgt_, N, static_cast<int>(cfg_.vocab), 1.0f / static_cast<float>(N), row_loss_,
                 stream_);
@@ -219,6 +235,8 @@ StepOut Trainer::train_step(const int32_t* inputs, const int32_t* targets, float
 
 float Trainer::loss_and_grads(const int32_t* inputs, const int32_t* targets) {
   stage_batch(inputs, targets);
+  owner_reduce_ = false;  // whole gradients on every rank
+  grads_partial_ = false;
   const int N = batch_ * seq_;
   forward(batch_, seq_, true);
   cross_entropy(logits_, cfg_.vocab, d_tgt_, N, static_cast<int>(cfg_.vocab), 1.0f / static_cast<float>(N), row_loss_,
@@ -283,6 +301,8 @@ void Trainer::attention_maps(const int32_t* inputs, int B, int T, float* host_ou
 }
 
 std::vector<float> Trainer::grad_norms() {
+  if (grads_partial_)
+    throw std::invalid_argument("the last step's gradients are sharded over the ranks (optimizer sharding)");
   const size_t n = layout_.tensors.size();
   double* d = nullptr;
   check_cuda(cudaMalloc(&d, n * sizeof(double)), "grad norms buffer");

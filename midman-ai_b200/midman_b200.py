@@ -30,6 +30,7 @@ API_SYMBOLS = [
     "midman_batcher_next", "midman_batcher_destroy", "midman_train_save", "midman_train_restore",
     "midman_state_inspect", "midman_shard_inspect", "midman_batcher_open", "midman_batcher_seek", "midman_train_run",
     "midman_shard_read", "midman_shard_write", "midman_sha256", "midman_train_evaluate",
+    "midman_train_shard_optimizer",
 ]
 STATUS = {0: "OK", 1: "STOPPED", -1: "ARGUMENT", -2: "CONFIG", -3: "SHAPE", -4: "INDEX", -5: "OTHER",
           -6: "DEVICE", -99: "PANIC"}
@@ -110,6 +111,7 @@ def load(path: str | os.PathLike | None = None) -> C.CDLL:
     _sig(lib, "midman_shard_write", i32, u8p, u32, u32, u32, C.POINTER(C.c_uint32), C.c_uint64)
     _sig(lib, "midman_sha256", i32, u8p, C.c_uint64, u8p)
     _sig(lib, "midman_train_evaluate", i32, u32, u8p, u32, C.c_uint64)
+    _sig(lib, "midman_train_shard_optimizer", i32, u32, u32)
     _lib = lib
     return lib
 
@@ -415,6 +417,11 @@ class Trainer:
         st = api(load().midman_train_run(self.h, batcher.h, steps), ok=(0, 1))
         rec = floats().reshape(-1, 3)
         return rec, st, (_json.loads(text()) if st == 0 else None)
+
+    def shard_optimizer(self, enable: bool = True) -> dict:
+        """midman_train_shard_optimizer: ZeRO-1 on or off; returns the sharding description."""
+        api(load().midman_train_shard_optimizer(self.h, 1 if enable else 0))
+        return _json.loads(text())["sharding"]
 
     def evaluate(self, shards, max_batches: int) -> dict:
         """midman_train_evaluate: {loss, batches, tokens} over held-out shard files."""
