@@ -381,34 +381,69 @@ __global__ void __launch_bounds__(THREADS, 1)
 // accumulator of its 128 rows. Per stage a CTA loads 32 KB (16 KB of A, 16 KB
 // of B) for the same MMA work per SM that costs a single CTA 48 KB (A plus a
 // 256-wide B), so the ring is deeper (6 stages) and L2 serves a third less.
-constexpr int PBN = 256;
-constexpr int P_B_BYTES = (PBN / 2) * BK * 4;  // 16 KB
-constexpr int P_STAGE = A_STAGE_BYTES + P_B_BYTES;
-constexpr int P_STAGES = 6;
-constexpr int P_SMEM = P_STAGES * P_STAGE + 1024 + 256 + 4 * 32 * 32 * 4;
+// Pair tile 256 x PN. Only PN = 256 is launched: 256 x 128 tiles were measured at
+// ~400 TF/s against ~650 (each UMMA reads the same A for half the work).
+template <int PN>
+struct PairTile {
+  static constexpr int B_BYTES = (PN / 2) * BK * 4;  // 16 KB (PN 256) or 8 KB
+  static constexpr int STAGE = A_STAGE_BYTES + B_BYTES;
+  static constexpr int STAGES = PN == 256 ? 6 : 8;
+  static constexpr int SMEM = STAGES * STAGE + 1024 + 256 + 4 * 32 * 32 * 4;
+  static constexpr int TILE_FLOATS = 2 * BM * PN;
+};
 
-template <bool A_MN, bool B_MN>
+constexpr int P_TILE_FLOATS_MAX = 2 * BM * 256;  // one 256 x 256 tile
+
+// Work unit u of a pair launch. Tiles [0, full) are whole units; each of the
+// remaining tiles (the last, partial wave) is cut into `splits` parts of its K
+// loop, so that the last wave keeps more pairs busy for a shorter time. A part
+// writes its partial sum to workspace tile `slot`; split_reduce_kernel adds the
+// parts (in order) and the residual into C.
+struct PairUnit {
+  int tile, kb, ke, slot;  // slot < 0: a whole tile, written to C
+};
+
+__device__ __forceinline__ PairUnit pair_unit(int u, int full, int splits, int n_k) {
+  PairUnit w;
+  if (u < full) {
+    w.tile = u;
+    w.kb = 0;
+    w.ke = n_k;
+    w.slot = -1;
+  } else {
+    const int v = u - full, part = v % splits;
+    w.tile = full + v / splits;
+    w.kb = (n_k * part) / splits;
+    w.ke = (n_k * (part + 1)) / splits;
+    w.slot = v;
+  }
+  return w;
+}
+
+template <bool A_MN, bool B_MN, int PN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, float* C,
                      long long ldc, const float* R, long long ldr, int M, int N, int K, int* err, int total_tiles,
-                     int mn3d) {
+                     int mn3d, int full_tiles, int splits, float* ws) {
+  using Cfg = PairTile<PN>;
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
   const int pair = static_cast<int>(blockIdx.x) / 2, npairs = static_cast<int>(gridDim.x) / 2;
   const int tm = (M + 2 * BM - 1) / (2 * BM);
   const int n_k = (K + BK - 1) / BK;
+  const int total_units = full_tiles + (total_tiles - full_tiles) * splits;
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   const uint32_t base = (raw_addr + 1023u) & ~1023u;
   uint8_t* smem = smem_raw + (base - raw_addr);
-  const uint32_t bar_base = base + P_STAGES * P_STAGE;
+  const uint32_t bar_base = base + Cfg::STAGES * Cfg::STAGE;
   auto full_bar = [&](int s) { return bar_base + 8u * s; };
-  auto empty_bar = [&](int s) { return bar_base + 8u * (P_STAGES + s); };
-  auto acc_full = [&](int b) { return bar_base + 8u * (2 * P_STAGES + b); };
-  auto acc_empty = [&](int b) { return bar_base + 8u * (2 * P_STAGES + 2 + b); };
-  const uint32_t tmem_slot = bar_base + 8u * (2 * P_STAGES + 4);
-  uint8_t* tail = smem + P_STAGES * P_STAGE + 8 * (2 * P_STAGES + 4);
+  auto empty_bar = [&](int s) { return bar_base + 8u * (Cfg::STAGES + s); };
+  auto acc_full = [&](int b) { return bar_base + 8u * (2 * Cfg::STAGES + b); };
+  auto acc_empty = [&](int b) { return bar_base + 8u * (2 * Cfg::STAGES + 2 + b); };
+  const uint32_t tmem_slot = bar_base + 8u * (2 * Cfg::STAGES + 4);
+  uint8_t* tail = smem + Cfg::STAGES * Cfg::STAGE + 8 * (2 * Cfg::STAGES + 4);
   uint32_t* tmem_slot_ptr = reinterpret_cast<uint32_t*>(tail);
   int* loads_issued = reinterpret_cast<int*>(tail + 8);
   int* loads_consumed = loads_issued + 1;
@@ -418,7 +453,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
-    for (int s = 0; s < P_STAGES; ++s) {
+    for (int s = 0; s < Cfg::STAGES; ++s) {
       mbar_init(full_bar(s), 1);
       mbar_init(empty_bar(s), 1);
     }
@@ -432,7 +467,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     fence_proxy_async_smem();
   }
   if (warp == 1) {
-    tmem_alloc_pair(tmem_slot, 2 * PBN);
+    tmem_alloc_pair(tmem_slot, 2 * PN);
     tmem_relinquish_pair();
   }
   tc_fence_before();
@@ -445,18 +480,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       // ---------------- TMA producer (both CTAs); completions land on the leader's barriers
       int it = 0;
       bool ok = true;
-      for (int t = pair; t < total_tiles && ok; t += npairs) {
+      for (int u = pair; u < total_units && ok; u += npairs) {
+        const PairUnit w = pair_unit(u, full_tiles, splits, n_k);
+        const int t = w.tile;
         const int my_m0 = (t % tm) * 2 * BM + static_cast<int>(rank) * BM;
-        const int my_n0 = (t / tm) * PBN + static_cast<int>(rank) * (PBN / 2);
-        for (int i = 0; i < n_k; ++i, ++it) {
-          const int s = it % P_STAGES, round = it / P_STAGES;
+        const int my_n0 = (t / tm) * PN + static_cast<int>(rank) * (PN / 2);
+        for (int i = w.kb; i < w.ke; ++i, ++it) {
+          const int s = it % Cfg::STAGES, round = it / Cfg::STAGES;
           if (round > 0 && !mbar_wait(empty_bar(s), (round - 1) & 1, err, kErrWaitEmpty)) {
             ok = false;
             break;
           }
-          if (leader) mbar_arrive_expect_tx(full_bar(s), 2 * P_STAGE);
+          if (leader) mbar_arrive_expect_tx(full_bar(s), 2 * Cfg::STAGE);
           const uint32_t fb = mapa_shared(full_bar(s), 0);
-          const uint32_t sa = base + s * P_STAGE, sb = sa + A_STAGE_BYTES;
+          const uint32_t sa = base + s * Cfg::STAGE, sb = sa + A_STAGE_BYTES;
           const int k0 = i * BK;
           if (!A_MN) {
             tma_load_2d_pair(sa, &tmA, fb, k0, my_m0);
@@ -472,7 +509,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
             tma_load_3d_pair(sb, &tmB, fb, 0, k0, my_n0 / 32);
           } else {
 #pragma unroll
-            for (int j = 0; j < PBN / 64; ++j) tma_load_2d_pair(sb + j * MN_BLOCK_BYTES, &tmB, fb, my_n0 + 32 * j, k0);
+            for (int j = 0; j < PN / 64; ++j) tma_load_2d_pair(sb + j * MN_BLOCK_BYTES, &tmB, fb, my_n0 + 32 * j, k0);
           }
           *loads_issued = it + 1;
         }
@@ -481,30 +518,31 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   } else if (warp == 1) {
     if (lane == 0 && leader) {
       // ---------------- UMMA issuer (leader only), M = 256 across the pair
-      constexpr uint32_t idesc = idesc_tf32(2 * BM, PBN, A_MN, B_MN);
+      constexpr uint32_t idesc = idesc_tf32(2 * BM, PN, A_MN, B_MN);
       int it = 0, j = 0;
       bool ok = true;
-      for (int t = pair; t < total_tiles && ok; t += npairs) {
+      for (int u = pair; u < total_units && ok; u += npairs) {
+        const PairUnit w = pair_unit(u, full_tiles, splits, n_k);
         const int buf = j & 1;
         if (j >= 2 && !mbar_wait(acc_empty(buf), ((j >> 1) - 1) & 1, err, kErrWaitAccum)) break;
         tc_fence_after();
-        const uint32_t acc = tmem_base + buf * PBN;
-        for (int i = 0; i < n_k; ++i, ++it) {
-          const int s = it % P_STAGES, round = it / P_STAGES;
+        const uint32_t acc = tmem_base + buf * PN;
+        for (int i = w.kb; i < w.ke; ++i, ++it) {
+          const int s = it % Cfg::STAGES, round = it / Cfg::STAGES;
           if (!mbar_wait(full_bar(s), round & 1, err, kErrWaitFull)) {
             ok = false;
             break;
           }
           tc_fence_after();
           *loads_consumed = it + 1;
-          const uint32_t sa = base + s * P_STAGE, sb = sa + A_STAGE_BYTES;
+          const uint32_t sa = base + s * Cfg::STAGE, sb = sa + A_STAGE_BYTES;
 #pragma unroll
           for (int k = 0; k < BK / 8; ++k) {
             const uint64_t adesc = A_MN ? smem_desc(sa + k * 1024, MN_BLOCK_BYTES, 512, kLayoutSw128Base32)
                                         : smem_desc(sa + k * 32, 16, 1024, kLayoutSw128);
             const uint64_t bdesc = B_MN ? smem_desc(sb + k * 1024, MN_BLOCK_BYTES, 512, kLayoutSw128Base32)
                                         : smem_desc(sb + k * 32, 16, 1024, kLayoutSw128);
-            umma_tf32_pair(acc, adesc, bdesc, idesc, (i | k) != 0 ? 1u : 0u);
+            umma_tf32_pair(acc, adesc, bdesc, idesc, (i != w.kb || k != 0) ? 1u : 0u);
           }
           umma_commit_pair(empty_bar(s), 0x3);
         }
@@ -515,16 +553,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   } else {
     // ---------------- epilogue (both CTAs): this CTA's 128 rows, all 256 columns
     const int quarter = warp & 3;
-    float4* stage_tile = reinterpret_cast<float4*>(smem + P_STAGES * P_STAGE + 256) + quarter * 256;
+    float4* stage_tile = reinterpret_cast<float4*>(smem + Cfg::STAGES * Cfg::STAGE + 256) + quarter * 256;
     int j = 0;
-    for (int t = pair; t < total_tiles; t += npairs) {
+    for (int u = pair; u < total_units; u += npairs) {
+      const PairUnit w = pair_unit(u, full_tiles, splits, n_k);
+      const int t = w.tile;
       const int buf = j & 1;
       if (!mbar_wait(acc_full(buf), (j >> 1) & 1, err, kErrWaitAccum)) break;
       tc_fence_after();
-      const int my_m0 = (t % tm) * 2 * BM + static_cast<int>(rank) * BM;
-      store_tile<PBN>(tmem_base + buf * PBN + (static_cast<uint32_t>(quarter * 32) << 16), true, stage_tile,
-                      my_m0 + quarter * 32, (t / tm) * PBN, C, ldc, R, ldr, M, N, mapa_shared(acc_empty(buf), 0),
-                      true);
+      const uint32_t acc = tmem_base + buf * PN + (static_cast<uint32_t>(quarter * 32) << 16);
+      if (w.slot < 0) {
+        const int my_m0 = (t % tm) * 2 * BM + static_cast<int>(rank) * BM;
+        store_tile<PN>(acc, true, stage_tile, my_m0 + quarter * 32, (t / tm) * PN, C, ldc, R, ldr, M, N,
+                        mapa_shared(acc_empty(buf), 0), true);
+      } else {  // a K part: the whole 256 x 256 partial tile into its workspace slot
+        store_tile<PN>(acc, true, stage_tile, static_cast<int>(rank) * BM + quarter * 32, 0,
+                        ws + static_cast<long long>(w.slot) * Cfg::TILE_FLOATS, PN, nullptr, 0, 2 * BM, PN,
+                        mapa_shared(acc_empty(buf), 0), true);
+      }
       ++j;
     }
   }
@@ -534,12 +580,52 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   if (leader && threadIdx.x == 0) {
     // after a timed-out wait, let the pair's copies in flight land (bounded)
     for (int i = *loads_consumed; i < *loads_issued; ++i)
-      if (!mbar_wait(full_bar(i % P_STAGES), (i / P_STAGES) & 1, err, kErrWaitDrain, 1000000000ull)) break;
+      if (!mbar_wait(full_bar(i % Cfg::STAGES), (i / Cfg::STAGES) & 1, err, kErrWaitDrain, 1000000000ull)) break;
   }
   cluster_sync();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc_pair(tmem_base, 2 * PBN);
+    tmem_dealloc_pair(tmem_base, 2 * PN);
+  }
+}
+
+// C = sum of a split tile's K parts (in part order) + R. Grid (split tiles,
+// 256 / rows per block): a block covers 256 / (PN / 4) rows of one tile, a thread
+// 4 columns.
+template <int PN>
+__global__ void __launch_bounds__(256) split_reduce_kernel(const float* __restrict__ ws, int splits, int full_tiles,
+                                                           int tm, float* C, long long ldc, const float* R,
+                                                           long long ldr, int M, int N) {
+  constexpr int P_TILE_FLOATS = PairTile<PN>::TILE_FLOATS;
+  constexpr int ROWS = 256 / (PN / 4);  // rows per block
+  const int tl = blockIdx.x, t = full_tiles + tl;
+  const int row = blockIdx.y * ROWS + threadIdx.x / (PN / 4), col = (threadIdx.x % (PN / 4)) * 4;
+  const int gm = (t % tm) * 2 * BM + row, gn = (t / tm) * PN + col;
+  if (gm >= M || gn >= N) return;
+  const float* src = ws + static_cast<long long>(tl) * splits * P_TILE_FLOATS + row * PN + col;
+  float4 v = *reinterpret_cast<const float4*>(src);
+  for (int p = 1; p < splits; ++p) {
+    const float4 q = *reinterpret_cast<const float4*>(src + static_cast<long long>(p) * P_TILE_FLOATS);
+    v.x += q.x;
+    v.y += q.y;
+    v.z += q.z;
+    v.w += q.w;
+  }
+  const float vals[4] = {v.x, v.y, v.z, v.w};
+  float* cp = C + static_cast<long long>(gm) * ldc + gn;
+  const float* rp = R ? R + static_cast<long long>(gm) * ldr + gn : nullptr;
+  if (gn + 3 < N) {
+    float4 o = v;
+    if (rp) {
+      const float4 r = *reinterpret_cast<const float4*>(rp);
+      o.x += r.x;
+      o.y += r.y;
+      o.z += r.z;
+      o.w += r.w;
+    }
+    *reinterpret_cast<float4*>(cp) = o;
+  } else {
+    for (int e = 0; e < 4 && gn + e < N; ++e) cp[e] = vals[e] + (rp ? rp[e] : 0.0f);
   }
 }
 
@@ -654,21 +740,102 @@ void launch_majors(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMa
   else launch<true, true, BN, BATCHED>(ta, tb, C, ldc, R, ldr, M, N, K, batch, bt, err, s, mn3d);
 }
 
-template <bool A_MN, bool B_MN>
-void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, float* C, long long ldc, const float* R, long long ldr,
-                 int M, int N, int K, int* err, cudaStream_t stream, int mn3d) {
-  auto kern = gemm_pair_kernel<A_MN, B_MN>;
+// How a pair launch of `tiles` tiles on `pairs` CTA pairs cuts its last wave: the
+// tiles past the last full wave are split into `splits` K parts when at least
+// two parts of each fit beside one another (at most 4). Each part keeps at least
+// 64 K steps (K 2,048): below that the reduce kernel costs more than the shorter
+// last wave saves.
+constexpr int kMinPartSteps = 64;
+
+struct PairPlan {
+  int full = 0, splits = 1;
+};
+
+PairPlan pair_plan(long long tiles, int pairs, int n_k) {
+  PairPlan p;
+  p.full = static_cast<int>(tiles);
+  const long long tail = tiles % pairs;
+  if (tail == 0) return p;
+  int s = static_cast<int>(pairs / tail);
+  s = s > 4 ? 4 : s;
+  s = s > n_k / kMinPartSteps ? n_k / kMinPartSteps : s;
+  if (s < 2) return p;
+  p.full = static_cast<int>(tiles - tail);
+  p.splits = s;
+  return p;
+}
+
+// Workspace for split tiles: one per device (pairs x 256 KB), its uses ordered
+// across streams by an event recorded after each reduce; the mutex orders the
+// host side of acquire (wait on the last use) and release (record this one).
+struct SplitWorkspace {
+  float* ptr = nullptr;
+  cudaEvent_t last_use = nullptr;
+};
+
+std::mutex& split_mutex() {
+  static std::mutex mu;
+  return mu;
+}
+
+SplitWorkspace* split_workspace(int dev, cudaStream_t stream, size_t floats) {
+  static SplitWorkspace per_device[64];
+  if (dev < 0 || dev >= 64) return nullptr;
+  SplitWorkspace& w = per_device[dev];
+  if (!w.ptr) {
+    void* p = nullptr;
+    if (cudaMalloc(&p, floats * sizeof(float)) != cudaSuccess) return nullptr;
+    if (cudaEventCreateWithFlags(&w.last_use, cudaEventDisableTiming) != cudaSuccess) {
+      cudaFree(p);
+      return nullptr;
+    }
+    w.ptr = static_cast<float*>(p);
+    if (cudaEventRecord(w.last_use, stream) != cudaSuccess) return nullptr;
+  }
+  if (cudaStreamWaitEvent(stream, w.last_use, 0) != cudaSuccess) return nullptr;
+  return &w;
+}
+
+template <bool A_MN, bool B_MN, int PN>
+int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, float* C, long long ldc, const float* R, long long ldr,
+                int M, int N, int K, int* err, cudaStream_t stream, int mn3d) {
+  using Cfg = PairTile<PN>;
+  auto kern = gemm_pair_kernel<A_MN, B_MN, PN>;
   static thread_local int configured_device = -1;
   int dev = 0;
   cudaGetDevice(&dev);
   if (configured_device != dev) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM);
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
     configured_device = dev;
   }
-  const long long tiles = static_cast<long long>((M + 2 * BM - 1) / (2 * BM)) * ((N + PBN - 1) / PBN);
+  const int tm = (M + 2 * BM - 1) / (2 * BM);
+  const long long tiles = static_cast<long long>(tm) * ((N + PN - 1) / PN);
   const int pairs = device_sms() / 2;
-  const int grid = 2 * static_cast<int>(tiles < pairs ? tiles : pairs);
-  kern<<<grid, THREADS, P_SMEM, stream>>>(ta, tb, C, ldc, R, ldr, M, N, K, err, static_cast<int>(tiles), mn3d);
+  const PairPlan plan = pair_plan(tiles, pairs, (K + BK - 1) / BK);
+  const long long units = plan.full + (tiles - plan.full) * plan.splits;
+  const int grid = 2 * static_cast<int>(units < pairs ? units : pairs);
+  if (plan.splits == 1) {
+    kern<<<grid, THREADS, Cfg::SMEM, stream>>>(ta, tb, C, ldc, R, ldr, M, N, K, err, static_cast<int>(tiles), mn3d,
+                                               plan.full, 1, nullptr);
+    return 0;
+  }
+  std::lock_guard<std::mutex> lock(split_mutex());
+  SplitWorkspace* w = split_workspace(dev, stream, static_cast<size_t>(pairs) * P_TILE_FLOATS_MAX);
+  if (!w) return kGemmLaunch;
+  kern<<<grid, THREADS, Cfg::SMEM, stream>>>(ta, tb, C, ldc, R, ldr, M, N, K, err, static_cast<int>(tiles), mn3d,
+                                             plan.full, plan.splits, w->ptr);
+  const dim3 rgrid(static_cast<unsigned>(tiles - plan.full), 2 * BM / (256 / (PN / 4)));
+  split_reduce_kernel<PN><<<rgrid, 256, 0, stream>>>(w->ptr, plan.splits, plan.full, tm, C, ldc, R, ldr, M, N);
+  return cudaEventRecord(w->last_use, stream) == cudaSuccess ? 0 : kGemmLaunch;
+}
+
+template <int PN>
+int launch_pair_majors(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, float* C, long long ldc,
+                       const float* R, long long ldr, int M, int N, int K, int* err, cudaStream_t s, int mn3d) {
+  if (!a_mn && !b_mn) return launch_pair<false, false, PN>(ta, tb, C, ldc, R, ldr, M, N, K, err, s, mn3d);
+  if (!a_mn) return launch_pair<false, true, PN>(ta, tb, C, ldc, R, ldr, M, N, K, err, s, mn3d);
+  if (!b_mn) return launch_pair<true, false, PN>(ta, tb, C, ldc, R, ldr, M, N, K, err, s, mn3d);
+  return launch_pair<true, true, PN>(ta, tb, C, ldc, R, ldr, M, N, K, err, s, mn3d);
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -696,9 +863,14 @@ int gemm_tf32(int M, int N, int K, GemmOperand A, GemmOperand B, float* C, long 
   // with 128 x 256 tiles, or 128 x 128 ones for narrow outputs and for products
   // whose 256-wide tiles would leave half of the SMs idle.
   const long long tiles256 = static_cast<long long>((M + BM - 1) / BM) * ((N + 255) / 256);
-  const long long pair_tiles = static_cast<long long>((M + 2 * BM - 1) / (2 * BM)) * ((N + PBN - 1) / PBN);
-  const bool use_pair = K > 0 && N > 128 && 2 * pair_tiles >= device_sms();
-  const int bn = use_pair ? PBN : (N <= 128 || 2 * tiles256 <= device_sms()) ? 128 : 256;
+  const long long pair_tiles = static_cast<long long>((M + 2 * BM - 1) / (2 * BM)) * ((N + 255) / 256);
+  // pairs also when the tiles fill them only once each is cut into K parts
+  const int n_k = (K + BK - 1) / BK;
+  const int pairs = device_sms() / 2;
+  const PairPlan plan = pair_plan(pair_tiles, pairs, n_k);
+  const long long units = plan.full + (pair_tiles - plan.full) * plan.splits;
+  const bool use_pair = K > 0 && N > 128 && (2 * pair_tiles >= device_sms() || 8 * units >= 3 * device_sms());
+  const int bn = use_pair ? 256 : (N <= 128 || 2 * tiles256 <= device_sms()) ? 128 : 256;
   CUtensorMap ta{}, tb{};
   int mn3d = 0;
   if (K > 0) {
@@ -710,7 +882,7 @@ int gemm_tf32(int M, int N, int K, GemmOperand A, GemmOperand B, float* C, long 
              : A.mn_major ? make_map2d(&ta, A.ptr, M, K, A.ld, 32, BK, true)
                           : make_map2d(&ta, A.ptr, K, M, A.ld, BK, BM, false);
     if (rc) return kGemmTensorMap;
-    const int b_box = use_pair ? PBN / 2 : bn;  // a pair's CTA loads half of B's tile
+    const int b_box = use_pair ? 128 : bn;  // a pair's CTA loads half of B's 256-wide tile
     rc = b3 ? make_map_mn3d(&tb, B.ptr, N, K, B.ld, b_box)
          : B.mn_major ? make_map2d(&tb, B.ptr, N, K, B.ld, 32, BK, true)
                       : make_map2d(&tb, B.ptr, K, N, B.ld, BK, b_box, false);
@@ -718,10 +890,9 @@ int gemm_tf32(int M, int N, int K, GemmOperand A, GemmOperand B, float* C, long 
     mn3d = (a3 ? 1 : 0) | (b3 ? 2 : 0);
   }
   if (use_pair) {
-    if (!A.mn_major && !B.mn_major) launch_pair<false, false>(ta, tb, C, ldc, R, ldr, M, N, K, d_err, stream, mn3d);
-    else if (!A.mn_major) launch_pair<false, true>(ta, tb, C, ldc, R, ldr, M, N, K, d_err, stream, mn3d);
-    else if (!B.mn_major) launch_pair<true, false>(ta, tb, C, ldc, R, ldr, M, N, K, d_err, stream, mn3d);
-    else launch_pair<true, true>(ta, tb, C, ldc, R, ldr, M, N, K, d_err, stream, mn3d);
+    const int rc2 =
+        launch_pair_majors<256>(A.mn_major, B.mn_major, ta, tb, C, ldc, R, ldr, M, N, K, d_err, stream, mn3d);
+    if (rc2) return rc2;
     return cudaGetLastError() == cudaSuccess ? 0 : kGemmLaunch;
   }
   const GemmBatch bt{};

@@ -209,12 +209,13 @@ __global__ void rmsnorm_bwd_kernel(const float* __restrict__ x, const float* __r
   }
 }
 
-// dw[j] = sum over the blocks' partial rows. A block owns 32 columns; warp w
-// sums rows w, w + 8, ... with four interleaved accumulators (coalesced
-// 128-byte row segments), and the eight warp sums are added in warp order, so
-// the result does not depend on timing.
-__global__ void column_sum_kernel(const float* __restrict__ ws, int nblk, int dim, float* __restrict__ dw) {
-  __shared__ float part[8][32];
+// dw[j] = sum over the blocks' partial rows. A block owns 32 columns; each of
+// its 32 warps sums rows w, w + 32, ... (coalesced 128-byte row segments) with
+// four interleaved accumulators and eight loads in flight, and the warp sums
+// are added in warp order, so the result does not depend on timing.
+__global__ void __launch_bounds__(1024) column_sum_kernel(const float* __restrict__ ws, int nblk, int dim,
+                                                          float* __restrict__ dw) {
+  __shared__ float part[32][33];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int j = blockIdx.x * 32 + lane;
   float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;
@@ -222,20 +223,21 @@ __global__ void column_sum_kernel(const float* __restrict__ ws, int nblk, int di
     const float* col = ws + j;
     const long long st = static_cast<long long>(dim);
     int b = warp;
-    for (; b + 24 < nblk; b += 32) {
+#pragma unroll 2
+    for (; b + 96 < nblk; b += 128) {
       a0 += col[b * st];
-      a1 += col[(b + 8) * st];
-      a2 += col[(b + 16) * st];
-      a3 += col[(b + 24) * st];
+      a1 += col[(b + 32) * st];
+      a2 += col[(b + 64) * st];
+      a3 += col[(b + 96) * st];
     }
-    for (; b < nblk; b += 8) a0 += col[b * st];
+    for (; b < nblk; b += 32) a0 += col[b * st];
   }
   part[warp][lane] = (a0 + a1) + (a2 + a3);
   __syncthreads();
   if (warp == 0 && j < dim) {
     float s = 0.0f;
 #pragma unroll
-    for (int w = 0; w < 8; ++w) s += part[w][lane];
+    for (int w = 0; w < 32; ++w) s += part[w][lane];
     dw[j] = s;
   }
 }
@@ -548,7 +550,7 @@ void rmsnorm_backward(const float* x, const float* w, const float* rstd, const f
   else
     throw std::runtime_error("rmsnorm_backward: d_model above 8192 is not supported");
   check_launch("rmsnorm_backward");
-  column_sum_kernel<<<(dim + 31) / 32, 256, 0, s>>>(ws, nblk, dim, dw);
+  column_sum_kernel<<<(dim + 31) / 32, 1024, 0, s>>>(ws, nblk, dim, dw);
   check_launch("rmsnorm_backward(column sum)");
 }
 

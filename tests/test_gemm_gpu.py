@@ -35,10 +35,15 @@ def rel_l2(got, want):
     return ((got.double() - want).norm() / want.norm().clamp_min(1e-300)).item()
 
 
-# The last three run on CTA pairs (256 x 256 tiles): ragged M and N (2-D boxes for
-# MN-major operands whose extent is not a multiple of 32), ragged K.
+# From (4096, 1408, 512) on they run on CTA pairs (256 x 256 tiles): ragged M and N
+# (2-D boxes for MN-major operands whose extent is not a multiple of 32), ragged K.
+# On 148 SMs (74 pairs) the tiles of the last, partial wave are cut into K parts of
+# at least 2,048 (summed by a second kernel): (2200, 2340, 8200) has 90 tiles, 16 of
+# them in 4 parts, with ragged edges and uneven parts; (2048, 1024, 4100) 32 tiles
+# in 2 parts each; (8192, 2048, 4096) 34 of 256 tiles in 2 parts.
 SHAPES = [(128, 256, 32), (256, 512, 512), (300, 344, 200), (64, 8, 12), (1000, 1032, 1000),
-          (4096, 1408, 512), (2200, 2340, 300), (2304, 4096, 64)]
+          (4096, 1408, 512), (2200, 2340, 300), (2304, 4096, 64), (2200, 2340, 8200), (2048, 1024, 4100),
+          (8192, 2048, 4096)]
 MAJORS = [(False, True), (False, False), (True, True), (True, False)]
 
 
@@ -60,14 +65,17 @@ def test_gemm_matches_float64(mm, shape, majors, precision):
     got = c[:, :n]
     assert torch.isfinite(got).all()
     err = rel_l2(got, want)
-    assert err < (TF32_TOL if precision == 0 else X3_TOL), err
+    # the fp32 accumulation in TMEM adds an error that grows like sqrt(K): the
+    # 3xTF32 bound is for K up to ~1,000 and is scaled beyond
+    assert err < (TF32_TOL if precision == 0 else X3_TOL * max(1.0, (k / 1000) ** 0.5)), err
     if ldc > n:  # padding columns are not written
         assert torch.isnan(c[:, n:]).all()
 
 
 @pytest.mark.parametrize("precision", [0, 1])
-def test_gemm_adds_the_residual_in_place(mm, precision):
-    m, n, k = 384, 512, 256
+@pytest.mark.parametrize("shape", [(384, 512, 256), (2048, 1024, 4100), (2200, 2340, 8200)])
+def test_gemm_adds_the_residual_in_place(mm, precision, shape):
+    m, n, k = shape
     gen = torch.Generator(device="cuda").manual_seed(5)
     a = torch.randn(m, k, generator=gen, device="cuda")
     w = torch.randn(k, n, generator=gen, device="cuda")
@@ -77,7 +85,7 @@ def test_gemm_adds_the_residual_in_place(mm, precision):
             r=c, ldr=n, precision=precision)
     mm.device_status()
     want = resid.double() + a.double() @ w.double()
-    assert rel_l2(c, want) < (TF32_TOL if precision == 0 else X3_TOL)
+    assert rel_l2(c, want) < (TF32_TOL if precision == 0 else X3_TOL * max(1.0, (k / 1000) ** 0.5))
 
 
 def test_gemm_rejects_misaligned_leading_dimensions(mm):
