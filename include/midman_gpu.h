@@ -61,6 +61,16 @@ MM_GPU_EXPORT int32_t mm_gpu_device_status(void *stream);
 MM_GPU_EXPORT int32_t mm_gpu_gemm(int32_t m, int32_t n, int32_t k, const float *a, int64_t lda, int32_t a_mn_major,
                     const float *b, int64_t ldb, int32_t b_mn_major, float *c, int64_t ldc,
                     const float *r, int64_t ldr, int32_t precision, void *stream);
+/* TF32 sum of products: C = sum over g < nseg of A_g(m, k[g]) B_g(n, k[g])^T (+R),
+ * all A_g with one majorness and all B_g with one, summed in one accumulator by a
+ * single launch when the shape runs on CTA pairs and nseg <= 3 (otherwise one
+ * launch per term accumulating into C). The backward of a layer whose output
+ * feeds several projections (dX = dQ Wq^T + dK Wk^T + dV Wv^T) is one call. No
+ * counterpart in the reference, which adds the three products through its tape. */
+MM_GPU_EXPORT int32_t mm_gpu_gemm_sum(int32_t m, int32_t n, int32_t nseg, const float *const *a, const int64_t *lda,
+                                      int32_t a_mn_major, const float *const *b, const int64_t *ldb,
+                                      int32_t b_mn_major, const int32_t *k, float *c, int64_t ldc, const float *r,
+                                      int64_t ldr, void *stream);
 
 /* Causal grouped-query attention (crates/midman-nn/src/attention.rs:79-102 forward,
  * and its autograd backward). Token-major operands: q, o, dout, dq are

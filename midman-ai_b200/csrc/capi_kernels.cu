@@ -64,6 +64,22 @@ int32_t mm_gpu_gemm(int32_t m, int32_t n, int32_t k, const float* a, int64_t lda
   });
 }
 
+int32_t mm_gpu_gemm_sum(int32_t m, int32_t n, int32_t nseg, const float* const* a, const int64_t* lda,
+                        int32_t a_mn_major, const float* const* b, const int64_t* ldb, int32_t b_mn_major,
+                        const int32_t* k, float* c, int64_t ldc, const float* r, int64_t ldr, void* stream) {
+  return guarded([&]() -> int32_t {
+    if (nseg < 1 || nseg > 8 || !a || !lda || !b || !ldb || !k)
+      return fail(MM_GPU_ERR_ARGUMENT, "gemm_sum: 1 to 8 segments with their operands and sizes");
+    mm::GemmSegment segs[8];
+    for (int g = 0; g < nseg; ++g)
+      segs[g] = mm::GemmSegment{{a[g], lda[g], a_mn_major != 0}, {b[g], ldb[g], b_mn_major != 0}, k[g]};
+    mm::DeviceContext& ctx = mm::device_context();
+    const int rc = mm::gemm_tf32_sum(m, n, segs, nseg, c, ldc, r, ldr, ctx.d_err, as_stream(stream));
+    if (rc) return fail(rc == mm::kGemmLaunch ? MM_GPU_ERR_DEVICE : MM_GPU_ERR_ARGUMENT, mm::gemm_status_string(rc));
+    return MM_GPU_OK;
+  });
+}
+
 namespace {
 int32_t attention_shape(int32_t B, int32_t T, int32_t H, int32_t Hkv, int32_t hd, int64_t ldq, int64_t ldk,
                         mm::AttnShape* s) {

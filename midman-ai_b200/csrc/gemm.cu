@@ -420,17 +420,29 @@ __device__ __forceinline__ PairUnit pair_unit(int u, int full, int splits, int n
   return w;
 }
 
+// The operands of a pair launch: up to kMaxSegments (A, B) pairs whose products
+// are summed into one accumulator (C = sum_s A_s B_s^T), their K steps one after
+// another. Each segment has its own tensor maps (a segment's ragged last K step
+// reads zeros past its own K) and MN-major box flags (bit 0: A, bit 1: B).
+constexpr int kMaxSegments = 3;
+struct PairOperands {
+  CUtensorMap a[kMaxSegments];
+  CUtensorMap b[kMaxSegments];
+  int seg_end[kMaxSegments];  // K steps of segments 0..s together
+  int mn3d[kMaxSegments];
+  int nseg;
+};
+
 template <bool A_MN, bool B_MN, int PN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
-    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, float* C,
-                     long long ldc, const float* R, long long ldr, int M, int N, int K, int* err, int total_tiles,
-                     int mn3d, int full_tiles, int splits, float* ws) {
+    gemm_pair_kernel(const __grid_constant__ PairOperands ops, float* C, long long ldc, const float* R, long long ldr,
+                     int M, int N, int* err, int total_tiles, int full_tiles, int splits, float* ws) {
   using Cfg = PairTile<PN>;
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
   const int pair = static_cast<int>(blockIdx.x) / 2, npairs = static_cast<int>(gridDim.x) / 2;
   const int tm = (M + 2 * BM - 1) / (2 * BM);
-  const int n_k = (K + BK - 1) / BK;
+  const int n_k = ops.seg_end[ops.nseg - 1];
   const int total_units = full_tiles + (total_tiles - full_tiles) * splits;
 
   extern __shared__ uint8_t smem_raw[];
@@ -451,8 +463,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   if (threadIdx.x == 0) {
-    tma_prefetch_desc(&tmA);
-    tma_prefetch_desc(&tmB);
+    for (int g = 0; g < ops.nseg; ++g) {
+      tma_prefetch_desc(&ops.a[g]);
+      tma_prefetch_desc(&ops.b[g]);
+    }
     for (int s = 0; s < Cfg::STAGES; ++s) {
       mbar_init(full_bar(s), 1);
       mbar_init(empty_bar(s), 1);
@@ -494,22 +508,27 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           if (leader) mbar_arrive_expect_tx(full_bar(s), 2 * Cfg::STAGE);
           const uint32_t fb = mapa_shared(full_bar(s), 0);
           const uint32_t sa = base + s * Cfg::STAGE, sb = sa + A_STAGE_BYTES;
-          const int k0 = i * BK;
+          int g = 0;  // the segment of K step i
+          while (g + 1 < ops.nseg && i >= ops.seg_end[g]) ++g;
+          const int k0 = (i - (g > 0 ? ops.seg_end[g - 1] : 0)) * BK;
+          const CUtensorMap* tmA = &ops.a[g];
+          const CUtensorMap* tmB = &ops.b[g];
+          const int mn3d = ops.mn3d[g];
           if (!A_MN) {
-            tma_load_2d_pair(sa, &tmA, fb, k0, my_m0);
+            tma_load_2d_pair(sa, tmA, fb, k0, my_m0);
           } else if (mn3d & 1) {
-            tma_load_3d_pair(sa, &tmA, fb, 0, k0, my_m0 / 32);
+            tma_load_3d_pair(sa, tmA, fb, 0, k0, my_m0 / 32);
           } else {
 #pragma unroll
-            for (int j = 0; j < BM / 32; ++j) tma_load_2d_pair(sa + j * MN_BLOCK_BYTES, &tmA, fb, my_m0 + 32 * j, k0);
+            for (int j = 0; j < BM / 32; ++j) tma_load_2d_pair(sa + j * MN_BLOCK_BYTES, tmA, fb, my_m0 + 32 * j, k0);
           }
           if (!B_MN) {
-            tma_load_2d_pair(sb, &tmB, fb, k0, my_n0);
+            tma_load_2d_pair(sb, tmB, fb, k0, my_n0);
           } else if (mn3d & 2) {
-            tma_load_3d_pair(sb, &tmB, fb, 0, k0, my_n0 / 32);
+            tma_load_3d_pair(sb, tmB, fb, 0, k0, my_n0 / 32);
           } else {
 #pragma unroll
-            for (int j = 0; j < PN / 64; ++j) tma_load_2d_pair(sb + j * MN_BLOCK_BYTES, &tmB, fb, my_n0 + 32 * j, k0);
+            for (int j = 0; j < PN / 64; ++j) tma_load_2d_pair(sb + j * MN_BLOCK_BYTES, tmB, fb, my_n0 + 32 * j, k0);
           }
           *loads_issued = it + 1;
         }
@@ -635,6 +654,8 @@ namespace {
 
 // ------------------------------------------------------------------ host side
 
+thread_local uint64_t t_launches = 0;  // kernels launched by this thread (gemm_launch_count)
+
 PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;
@@ -728,6 +749,7 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, float* C, long long ld
   const int sms = device_sms();
   const int grid = static_cast<int>(tiles < sms ? tiles : sms);
   kern<<<grid, THREADS, TL::SMEM_BYTES, stream>>>(ta, tb, C, ldc, R, ldr, M, N, K, err, bt, static_cast<int>(tiles), mn3d);
+  ++t_launches;
 }
 
 template <int BN, bool BATCHED>
@@ -797,8 +819,8 @@ SplitWorkspace* split_workspace(int dev, cudaStream_t stream, size_t floats) {
 }
 
 template <bool A_MN, bool B_MN, int PN>
-int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, float* C, long long ldc, const float* R, long long ldr,
-                int M, int N, int K, int* err, cudaStream_t stream, int mn3d) {
+int launch_pair(const PairOperands& ops, float* C, long long ldc, const float* R, long long ldr, int M, int N, int* err,
+                cudaStream_t stream) {
   using Cfg = PairTile<PN>;
   auto kern = gemm_pair_kernel<A_MN, B_MN, PN>;
   static thread_local int configured_device = -1;
@@ -811,36 +833,40 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, float* C, long lon
   const int tm = (M + 2 * BM - 1) / (2 * BM);
   const long long tiles = static_cast<long long>(tm) * ((N + PN - 1) / PN);
   const int pairs = device_sms() / 2;
-  const PairPlan plan = pair_plan(tiles, pairs, (K + BK - 1) / BK);
+  const PairPlan plan = pair_plan(tiles, pairs, ops.seg_end[ops.nseg - 1]);
   const long long units = plan.full + (tiles - plan.full) * plan.splits;
   const int grid = 2 * static_cast<int>(units < pairs ? units : pairs);
   if (plan.splits == 1) {
-    kern<<<grid, THREADS, Cfg::SMEM, stream>>>(ta, tb, C, ldc, R, ldr, M, N, K, err, static_cast<int>(tiles), mn3d,
-                                               plan.full, 1, nullptr);
+    kern<<<grid, THREADS, Cfg::SMEM, stream>>>(ops, C, ldc, R, ldr, M, N, err, static_cast<int>(tiles), plan.full, 1,
+                                               nullptr);
+    ++t_launches;
     return 0;
   }
   std::lock_guard<std::mutex> lock(split_mutex());
   SplitWorkspace* w = split_workspace(dev, stream, static_cast<size_t>(pairs) * P_TILE_FLOATS_MAX);
   if (!w) return kGemmLaunch;
-  kern<<<grid, THREADS, Cfg::SMEM, stream>>>(ta, tb, C, ldc, R, ldr, M, N, K, err, static_cast<int>(tiles), mn3d,
-                                             plan.full, plan.splits, w->ptr);
+  kern<<<grid, THREADS, Cfg::SMEM, stream>>>(ops, C, ldc, R, ldr, M, N, err, static_cast<int>(tiles), plan.full,
+                                             plan.splits, w->ptr);
   const dim3 rgrid(static_cast<unsigned>(tiles - plan.full), 2 * BM / (256 / (PN / 4)));
   split_reduce_kernel<PN><<<rgrid, 256, 0, stream>>>(w->ptr, plan.splits, plan.full, tm, C, ldc, R, ldr, M, N);
+  t_launches += 2;
   return cudaEventRecord(w->last_use, stream) == cudaSuccess ? 0 : kGemmLaunch;
 }
 
 template <int PN>
-int launch_pair_majors(bool a_mn, bool b_mn, const CUtensorMap& ta, const CUtensorMap& tb, float* C, long long ldc,
-                       const float* R, long long ldr, int M, int N, int K, int* err, cudaStream_t s, int mn3d) {
-  if (!a_mn && !b_mn) return launch_pair<false, false, PN>(ta, tb, C, ldc, R, ldr, M, N, K, err, s, mn3d);
-  if (!a_mn) return launch_pair<false, true, PN>(ta, tb, C, ldc, R, ldr, M, N, K, err, s, mn3d);
-  if (!b_mn) return launch_pair<true, false, PN>(ta, tb, C, ldc, R, ldr, M, N, K, err, s, mn3d);
-  return launch_pair<true, true, PN>(ta, tb, C, ldc, R, ldr, M, N, K, err, s, mn3d);
+int launch_pair_majors(bool a_mn, bool b_mn, const PairOperands& ops, float* C, long long ldc, const float* R,
+                       long long ldr, int M, int N, int* err, cudaStream_t s) {
+  if (!a_mn && !b_mn) return launch_pair<false, false, PN>(ops, C, ldc, R, ldr, M, N, err, s);
+  if (!a_mn) return launch_pair<false, true, PN>(ops, C, ldc, R, ldr, M, N, err, s);
+  if (!b_mn) return launch_pair<true, false, PN>(ops, C, ldc, R, ldr, M, N, err, s);
+  return launch_pair<true, true, PN>(ops, C, ldc, R, ldr, M, N, err, s);
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace
+
+uint64_t gemm_launch_count() { return t_launches; }
 
 const char* gemm_status_string(int status) {
   switch (status) {
@@ -853,47 +879,49 @@ const char* gemm_status_string(int status) {
   }
 }
 
-int gemm_tf32(int M, int N, int K, GemmOperand A, GemmOperand B, float* C, long long ldc, const float* R,
-              long long ldr, int* d_err, cudaStream_t stream) {
-  if (M < 0 || N < 0 || K < 0 || !C) return kGemmBadArgument;
-  if (M == 0 || N == 0) return 0;
-  if (K > 0 && (!A.ptr || !B.ptr)) return kGemmBadArgument;
-  if ((ldc & 3) || !aligned16(C) || (R && ((ldr & 3) || !aligned16(R)))) return kGemmMisaligned;
-  // 256 x 256 tiles on CTA pairs when they fill the SMs; otherwise single CTAs
-  // with 128 x 256 tiles, or 128 x 128 ones for narrow outputs and for products
-  // whose 256-wide tiles would leave half of the SMs idle.
-  const long long tiles256 = static_cast<long long>((M + BM - 1) / BM) * ((N + 255) / 256);
+namespace {
+
+// Tensor maps of one operand pair. MN-major operands whose MN extent is a
+// multiple of 32 load a whole stage in one 3-D box (flag bits: 1 A, 2 B);
+// otherwise one 2-D box per 32-wide block (zero fill past MN). b_box: the B
+// rows or columns one CTA loads per stage.
+int make_maps(int M, int N, int K, const GemmOperand& A, const GemmOperand& B, int b_box, CUtensorMap* ta,
+              CUtensorMap* tb, int* mn3d) {
+  if ((A.ld & 3) || (B.ld & 3) || !aligned16(A.ptr) || !aligned16(B.ptr)) return kGemmMisaligned;
+  const bool a3 = A.mn_major && M % 32 == 0, b3 = B.mn_major && N % 32 == 0;
+  int rc = a3 ? make_map_mn3d(ta, A.ptr, M, K, A.ld, BM)
+           : A.mn_major ? make_map2d(ta, A.ptr, M, K, A.ld, 32, BK, true)
+                        : make_map2d(ta, A.ptr, K, M, A.ld, BK, BM, false);
+  if (rc) return kGemmTensorMap;
+  rc = b3 ? make_map_mn3d(tb, B.ptr, N, K, B.ld, b_box)
+       : B.mn_major ? make_map2d(tb, B.ptr, N, K, B.ld, 32, BK, true)
+                    : make_map2d(tb, B.ptr, K, N, B.ld, BK, b_box, false);
+  if (rc) return kGemmTensorMap;
+  *mn3d = (a3 ? 1 : 0) | (b3 ? 2 : 0);
+  return 0;
+}
+
+// 256 x 256 tiles on CTA pairs when they fill the SMs (also once the last
+// wave's tiles are cut into K parts); otherwise single CTAs.
+bool pair_suits(int M, int N, int n_k) {
+  if (n_k <= 0 || N <= 128) return false;
   const long long pair_tiles = static_cast<long long>((M + 2 * BM - 1) / (2 * BM)) * ((N + 255) / 256);
-  // pairs also when the tiles fill them only once each is cut into K parts
-  const int n_k = (K + BK - 1) / BK;
-  const int pairs = device_sms() / 2;
-  const PairPlan plan = pair_plan(pair_tiles, pairs, n_k);
+  const PairPlan plan = pair_plan(pair_tiles, device_sms() / 2, n_k);
   const long long units = plan.full + (pair_tiles - plan.full) * plan.splits;
-  const bool use_pair = K > 0 && N > 128 && (2 * pair_tiles >= device_sms() || 8 * units >= 3 * device_sms());
-  const int bn = use_pair ? 256 : (N <= 128 || 2 * tiles256 <= device_sms()) ? 128 : 256;
+  return 2 * pair_tiles >= device_sms() || 8 * units >= 3 * device_sms();
+}
+
+// One product on single CTAs: 128 x 256 tiles, or 128 x 128 ones for narrow
+// outputs and for products whose 256-wide tiles would leave half of the SMs idle.
+int gemm_single(int M, int N, int K, const GemmOperand& A, const GemmOperand& B, float* C, long long ldc,
+                const float* R, long long ldr, int* d_err, cudaStream_t stream) {
+  const long long tiles256 = static_cast<long long>((M + BM - 1) / BM) * ((N + 255) / 256);
+  const int bn = (N <= 128 || 2 * tiles256 <= device_sms()) ? 128 : 256;
   CUtensorMap ta{}, tb{};
   int mn3d = 0;
   if (K > 0) {
-    if ((A.ld & 3) || (B.ld & 3) || !aligned16(A.ptr) || !aligned16(B.ptr)) return kGemmMisaligned;
-    // MN-major operands whose MN extent is a multiple of 32 load a whole stage in
-    // one 3-D box; otherwise one 2-D box per 32-wide block (zero fill past MN).
-    const bool a3 = A.mn_major && M % 32 == 0, b3 = B.mn_major && N % 32 == 0;
-    int rc = a3 ? make_map_mn3d(&ta, A.ptr, M, K, A.ld, BM)
-             : A.mn_major ? make_map2d(&ta, A.ptr, M, K, A.ld, 32, BK, true)
-                          : make_map2d(&ta, A.ptr, K, M, A.ld, BK, BM, false);
-    if (rc) return kGemmTensorMap;
-    const int b_box = use_pair ? 128 : bn;  // a pair's CTA loads half of B's 256-wide tile
-    rc = b3 ? make_map_mn3d(&tb, B.ptr, N, K, B.ld, b_box)
-         : B.mn_major ? make_map2d(&tb, B.ptr, N, K, B.ld, 32, BK, true)
-                      : make_map2d(&tb, B.ptr, K, N, B.ld, BK, b_box, false);
-    if (rc) return kGemmTensorMap;
-    mn3d = (a3 ? 1 : 0) | (b3 ? 2 : 0);
-  }
-  if (use_pair) {
-    const int rc2 =
-        launch_pair_majors<256>(A.mn_major, B.mn_major, ta, tb, C, ldc, R, ldr, M, N, K, d_err, stream, mn3d);
-    if (rc2) return rc2;
-    return cudaGetLastError() == cudaSuccess ? 0 : kGemmLaunch;
+    const int rc = make_maps(M, N, K, A, B, bn, &ta, &tb, &mn3d);
+    if (rc) return rc;
   }
   const GemmBatch bt{};
   if (bn == 128)
@@ -901,6 +929,66 @@ int gemm_tf32(int M, int N, int K, GemmOperand A, GemmOperand B, float* C, long 
   else
     launch_majors<256, false>(A.mn_major, B.mn_major, ta, tb, C, ldc, R, ldr, M, N, K, 1, bt, d_err, stream, mn3d);
   return cudaGetLastError() == cudaSuccess ? 0 : kGemmLaunch;
+}
+
+}  // namespace
+
+int gemm_tf32_sum(int M, int N, const GemmSegment* segs, int nseg, float* C, long long ldc, const float* R,
+                  long long ldr, int* d_err, cudaStream_t stream) {
+  if (M < 0 || N < 0 || !C || nseg < 1 || !segs) return kGemmBadArgument;
+  for (int g = 0; g < nseg; ++g)
+    if (segs[g].K < 0 || (segs[g].K > 0 && (!segs[g].a.ptr || !segs[g].b.ptr))) return kGemmBadArgument;
+  if (M == 0 || N == 0) return 0;
+  if ((ldc & 3) || !aligned16(C) || (R && ((ldr & 3) || !aligned16(R)))) return kGemmMisaligned;
+  // the segments that contribute, and whether one pair launch can sum them
+  GemmSegment live[kMaxSegments];
+  int n_live = 0, n_k = 0;
+  bool same_majors = true;
+  for (int g = 0; g < nseg; ++g) {
+    if (segs[g].K == 0) continue;
+    if (n_live == kMaxSegments) {
+      same_majors = false;  // more than one launch holds
+      break;
+    }
+    live[n_live] = segs[g];
+    same_majors = same_majors && segs[g].a.mn_major == live[0].a.mn_major && segs[g].b.mn_major == live[0].b.mn_major;
+    n_k += (segs[g].K + BK - 1) / BK;
+    ++n_live;
+  }
+  if (n_live == 0) return gemm_single(M, N, 0, segs[0].a, segs[0].b, C, ldc, R, ldr, d_err, stream);
+  if (same_majors && pair_suits(M, N, n_k)) {
+    PairOperands ops{};
+    int end = 0;
+    for (int g = 0; g < n_live; ++g) {
+      const int rc = make_maps(M, N, live[g].K, live[g].a, live[g].b, 128, &ops.a[g], &ops.b[g], &ops.mn3d[g]);
+      if (rc) return rc;
+      end += (live[g].K + BK - 1) / BK;
+      ops.seg_end[g] = end;
+    }
+    ops.nseg = n_live;
+    const int rc = launch_pair_majors<256>(live[0].a.mn_major, live[0].b.mn_major, ops, C, ldc, R, ldr, M, N, d_err,
+                                           stream);
+    if (rc) return rc;
+    return cudaGetLastError() == cudaSuccess ? 0 : kGemmLaunch;
+  }
+  // one launch per segment, each after the first accumulating into C
+  for (int g = 0; g < nseg; ++g) {
+    if (segs[g].K == 0 && g > 0) continue;
+    const bool first = g == 0;
+    const int rc = pair_suits(M, N, (segs[g].K + BK - 1) / BK)
+                       ? gemm_tf32_sum(M, N, &segs[g], 1, C, ldc, first ? R : C, first ? ldr : ldc, d_err, stream)
+                       : gemm_single(M, N, segs[g].K, segs[g].a, segs[g].b, C, ldc, first ? R : C, first ? ldr : ldc,
+                                     d_err, stream);
+    if (rc) return rc;
+  }
+  return 0;
+}
+
+int gemm_tf32(int M, int N, int K, GemmOperand A, GemmOperand B, float* C, long long ldc, const float* R,
+              long long ldr, int* d_err, cudaStream_t stream) {
+  if (K < 0) return kGemmBadArgument;
+  const GemmSegment seg{A, B, K};
+  return gemm_tf32_sum(M, N, &seg, 1, C, ldc, R, ldr, d_err, stream);
 }
 
 // 4-D operand view (inner, head, row, batch) of a batched GEMM operand.

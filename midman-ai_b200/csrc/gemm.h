@@ -2,6 +2,8 @@
 #pragma once
 #include <cuda_runtime.h>
 
+#include <cstdint>
+
 namespace mm {
 
 // One GEMM operand. K-major: element (i, k) at ptr[i * ld + k]. MN-major:
@@ -52,7 +54,22 @@ struct BatchedOperand {
 int gemm_tf32(int M, int N, int K, GemmOperand A, GemmOperand B, float* C, long long ldc,
               const float* R, long long ldr, int* d_err, cudaStream_t stream);
 
+// One term of a summed product: K columns of A times K columns of B.
+struct GemmSegment {
+  GemmOperand a, b;
+  int K;
+};
+// C[m, n] = sum over the segments of sum_k A_s(m, k) B_s(n, k) (+ R[m, n]; R may
+// equal C). Up to three segments with the same operand majors are summed in one
+// accumulator by a single launch (their K steps one after another) when the
+// shape runs on CTA pairs; otherwise one launch per segment accumulates into C.
+int gemm_tf32_sum(int M, int N, const GemmSegment* segs, int nseg, float* C, long long ldc, const float* R,
+                  long long ldr, int* d_err, cudaStream_t stream);
+
 const char* gemm_status_string(int status);
+
+// Kernels the GEMM functions have launched from the calling thread so far.
+uint64_t gemm_launch_count();
 
 // The batched form; bn (64, 128 or 256) is the output tile width. No residual.
 int gemm_tf32_batched(int batch, int M, int N, int K, const BatchedOperand& A, const BatchedOperand& B, float* C,

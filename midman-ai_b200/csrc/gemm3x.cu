@@ -54,12 +54,10 @@ int gemm_3xtf32(int M, int N, int K, GemmOperand A, GemmOperand B, float* C, lon
   GemmOperand Ah{a_hi, A.ld, A.mn_major}, Al{a_lo, A.ld, A.mn_major};
   GemmOperand Bh{b_hi, B.ld, B.mn_major}, Bl{b_lo, B.ld, B.mn_major};
   // Small terms first, then the large one, so the small ones are not rounded
-  // away against a large partial sum before they are combined.
-  int rc = gemm_tf32(M, N, K, Al, Bh, C, ldc, R, ldr, d_err, stream);
-  if (rc) return rc;
-  rc = gemm_tf32(M, N, K, Ah, Bl, C, ldc, C, ldc, d_err, stream);
-  if (rc) return rc;
-  return gemm_tf32(M, N, K, Ah, Bh, C, ldc, C, ldc, d_err, stream);
+  // away against a large partial sum before they are combined (one accumulator
+  // over the three K ranges when the shape runs on CTA pairs).
+  const GemmSegment terms[3] = {{Al, Bh, K}, {Ah, Bl, K}, {Ah, Bh, K}};
+  return gemm_tf32_sum(M, N, terms, 3, C, ldc, R, ldr, d_err, stream);
 }
 
 }  // namespace mm

@@ -438,17 +438,39 @@ void Trainer::prof_collect() {
 
 void Trainer::gemm(int M, int N, int K, const float* A, long long lda, bool a_mn, const float* B, long long ldb,
                    bool b_mn, float* C, long long ldc, const float* R, long long ldr) {
+  const GemmSegment seg{{A, lda, a_mn}, {B, ldb, b_mn}, K};
+  gemm_sum(M, N, &seg, 1, C, ldc, R, ldr);
+}
+
+// C = sum of the segments' products (+ R): one launch in TF32 when the shape runs
+// on CTA pairs (gemm_tf32_sum); in 3xTF32 one split product per segment.
+void Trainer::gemm_sum(int M, int N, const GemmSegment* segs, int nseg, float* C, long long ldc, const float* R,
+                       long long ldr) {
   const int slot = prof_begin();
   DeviceContext& ctx = device_context();
-  GemmOperand a{A, lda, a_mn}, b{B, ldb, b_mn};
-  const int rc = precision_ == kPrecisionTF32 ? gemm_tf32(M, N, K, a, b, C, ldc, R, ldr, ctx.d_err, stream_)
-                                              : gemm_3xtf32(M, N, K, a, b, C, ldc, R, ldr, ctx.d_err, stream_);
+  const uint64_t before = gemm_launch_count();
+  int rc = 0;
+  if (precision_ == kPrecisionTF32) {
+    rc = gemm_tf32_sum(M, N, segs, nseg, C, ldc, R, ldr, ctx.d_err, stream_);
+  } else {
+    for (int g = 0; g < nseg && rc == 0; ++g)
+      rc = gemm_3xtf32(M, N, segs[g].K, segs[g].a, segs[g].b, C, ldc, g == 0 ? R : C, g == 0 ? ldr : ldc,
+                       ctx.d_err, stream_);
+    launches_ += 2 * nseg;  // the hi/lo splits of A and B
+  }
   if (rc) throw std::runtime_error(std::string("GEMM: ") + gemm_status_string(rc));
-  launches_ += precision_ == kPrecisionTF32 ? 1 : 5;
-  if (slot >= 0)
-    prof_end(slot, precision_ == kPrecisionTF32 ? "gemm_tf32" : "gemm_3xtf32", 2.0 * M * N * K,
-             std::to_string(M) + "x" + std::to_string(N) + "x" + std::to_string(K) + (a_mn ? " M" : " K") +
-                 (b_mn ? "M" : "K"));
+  launches_ += gemm_launch_count() - before;
+  if (slot >= 0) {
+    double flops = 0.0;
+    std::string ks;
+    for (int g = 0; g < nseg; ++g) {
+      flops += 2.0 * M * N * segs[g].K;
+      ks += (g ? "+" : "") + std::to_string(segs[g].K);
+    }
+    prof_end(slot, precision_ == kPrecisionTF32 ? "gemm_tf32" : "gemm_3xtf32", flops,
+             std::to_string(M) + "x" + std::to_string(N) + "x" + ks + (segs[0].a.mn_major ? " M" : " K") +
+                 (segs[0].b.mn_major ? "M" : "K"));
+  }
 }
 
 void Trainer::check_device(const char* where) {

@@ -10,6 +10,7 @@
 #include <string>
 #include <vector>
 
+#include "gemm.h"
 #include "host.h"
 #include "kernels.h"
 
@@ -116,6 +117,8 @@ class Trainer {
   void build_embedding_csr(const int32_t* inputs, int N, int slot);
   void gemm(int M, int N, int K, const float* A, long long lda, bool a_mn, const float* B, long long ldb, bool b_mn,
             float* C, long long ldc, const float* R, long long ldr);
+  void gemm_sum(int M, int N, const GemmSegment* segs, int nseg, float* C, long long ldc, const float* R,
+                long long ldr);
   StepOut finish_step(float lr, const AdamHyper& h, bool update);
 
  public:

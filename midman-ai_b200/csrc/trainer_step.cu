@@ -106,8 +106,11 @@ void Trainer::backward(int B, int T) {
     gemm(N, F, D, dx, D, false, P_ + bo.down, D, false, dact_, F, nullptr, 0);
     gemm(F, D, N, a.act, F, true, dx, D, true, G_ + bo.down, D, nullptr, 0);
     swiglu_backward(a.g, a.u, dact_, static_cast<long long>(N) * F, stream_);  // g <- dg, u <- du
-    gemm(N, D, F, a.g, F, false, P_ + bo.gate, F, false, dxn_, D, nullptr, 0);
-    gemm(N, D, F, a.u, F, false, P_ + bo.up, F, false, dxn_, D, dxn_, D);
+    {  // dxn = dg Wg^T + du Wu^T, one accumulator
+      const GemmSegment segs[2] = {{{a.g, F, false}, {P_ + bo.gate, F, false}, F},
+                                   {{a.u, F, false}, {P_ + bo.up, F, false}, F}};
+      gemm_sum(N, D, segs, 2, dxn_, D, nullptr, 0);
+    }
     gemm(D, F, N, a.xn2, D, true, a.g, F, true, G_ + bo.gate, F, nullptr, 0);
     gemm(D, F, N, a.xn2, D, true, a.u, F, true, G_ + bo.up, F, nullptr, 0);
     rmsnorm_backward(a.h, P_ + bo.mlp_norm, a.rstd2, dxn_, N, D, dh, dx, G_ + bo.mlp_norm, norm_ws_, stream_);
@@ -124,9 +127,12 @@ void Trainer::backward(int B, int T) {
     prof_end(slot, "attention_bwd", 4.0 * B * H * static_cast<double>(T) * (T + 1) * hd);
     rope(dq_, N, T, H, hd, D, d_cos_, d_sin_, true, stream_);
     rope(dk_, N, T, Hkv, hd, KV, d_cos_, d_sin_, true, stream_);
-    gemm(N, D, D, dq_, D, false, P_ + bo.q, D, false, dxn_, D, nullptr, 0);
-    gemm(N, D, KV, dk_, KV, false, P_ + bo.k, KV, false, dxn_, D, dxn_, D);
-    gemm(N, D, KV, dv_, KV, false, P_ + bo.v, KV, false, dxn_, D, dxn_, D);
+    {  // dxn = dq Wq^T + dk Wk^T + dv Wv^T, one accumulator
+      const GemmSegment segs[3] = {{{dq_, D, false}, {P_ + bo.q, D, false}, D},
+                                   {{dk_, KV, false}, {P_ + bo.k, KV, false}, KV},
+                                   {{dv_, KV, false}, {P_ + bo.v, KV, false}, KV}};
+      gemm_sum(N, D, segs, 3, dxn_, D, nullptr, 0);
+    }
     gemm(D, D, N, a.xn1, D, true, dq_, D, true, G_ + bo.q, D, nullptr, 0);
     gemm(D, KV, N, a.xn1, D, true, dk_, KV, true, G_ + bo.k, KV, nullptr, 0);
     gemm(D, KV, N, a.xn1, D, true, dv_, KV, true, G_ + bo.v, KV, nullptr, 0);

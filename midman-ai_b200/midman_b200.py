@@ -15,7 +15,7 @@ LIB_PATH = HERE / "lib" / "libmidman_gpu.so"
 
 # Every symbol the public headers declare, grouped by header.
 GPU_SYMBOLS = [
-    "mm_gpu_last_error", "mm_gpu_device_status", "mm_gpu_gemm", "mm_gpu_attention_forward",
+    "mm_gpu_last_error", "mm_gpu_device_status", "mm_gpu_gemm", "mm_gpu_gemm_sum", "mm_gpu_attention_forward",
     "mm_gpu_attention_backward", "mm_gpu_attention_forward_noalloc",
 ]
 API_SYMBOLS = [
@@ -57,6 +57,8 @@ def load(path: str | os.PathLike | None = None) -> C.CDLL:
     _sig(lib, "mm_gpu_last_error", C.c_char_p)
     _sig(lib, "mm_gpu_device_status", i32, vp)
     _sig(lib, "mm_gpu_gemm", i32, i32, i32, i32, vp, i64, i32, vp, i64, i32, vp, i64, vp, i64, i32, vp)
+    _sig(lib, "mm_gpu_gemm_sum", i32, i32, i32, i32, C.POINTER(vp), C.POINTER(i64), i32, C.POINTER(vp),
+         C.POINTER(i64), i32, C.POINTER(C.c_int32), vp, i64, vp, i64, vp)
     _sig(lib, "mm_gpu_attention_forward", i32, i32, i32, i32, i32, i32, vp, vp, vp, i64, i64, vp, vp, i32, vp)
     _sig(lib, "mm_gpu_attention_backward", i32, i32, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp, i64, i64, vp, vp,
          vp, i32, vp)
@@ -144,6 +146,18 @@ def gemm(a, b, c, *, m, n, k, lda, ldb, ldc, a_mn_major, b_mn_major, r=None, ldr
     return check(load().mm_gpu_gemm(m, n, k, _ptr(a), lda, int(a_mn_major), _ptr(b), ldb,
                                     int(b_mn_major), _ptr(c), ldc, _ptr(r), ldr, precision,
                                     _stream(stream)))
+
+
+def gemm_sum(terms, c, *, m, n, ldc, a_mn_major, b_mn_major, r=None, ldr=0, stream=None):
+    """C = sum of A_g(m,k_g) B_g(n,k_g)^T (+R); terms: [(a, lda, b, ldb, k), ...] (TF32)."""
+    g = len(terms)
+    a = (C.c_void_p * g)(*[_ptr(t[0]) for t in terms])
+    lda = (C.c_int64 * g)(*[t[1] for t in terms])
+    b = (C.c_void_p * g)(*[_ptr(t[2]) for t in terms])
+    ldb = (C.c_int64 * g)(*[t[3] for t in terms])
+    ks = (C.c_int32 * g)(*[t[4] for t in terms])
+    return check(load().mm_gpu_gemm_sum(m, n, g, a, lda, int(a_mn_major), b, ldb, int(b_mn_major), ks, _ptr(c), ldc,
+                                        _ptr(r), ldr, _stream(stream)))
 
 
 def attention_forward(q, k, v, o, lse, *, batch, seq, n_heads, n_kv_heads, head_dim, ldq, ldk, precision=0,

@@ -95,3 +95,37 @@ def test_gemm_rejects_misaligned_leading_dimensions(mm):
     with pytest.raises(mm.MidmanGpuError):
         mm.gemm(a, b, c, m=16, n=16, k=10, lda=10, ldb=12, ldc=16, a_mn_major=False,
                 b_mn_major=False)
+
+
+# Sums of products (mm_gpu_gemm_sum): one accumulator over the terms' K steps when
+# the shape runs on CTA pairs (the backward's dX = dQ Wq^T + dK Wk^T + dV Wv^T),
+# ragged and zero K per term, more terms than one launch takes, narrow shapes
+# that fall back to one launch per term.
+SUM_CASES = [((2048, 2048), (2048, 1024, 1024)), ((2200, 2340), (300, 40, 0)), ((4096, 1408), (200, 1000)),
+             ((300, 344), (64, 100)), ((2048, 1024), (4100, 2000)), ((2304, 2048), (512, 256, 128, 64))]
+
+
+@pytest.mark.parametrize("case", SUM_CASES)
+@pytest.mark.parametrize("majors", MAJORS)
+@pytest.mark.parametrize("residual", [False, True])
+def test_gemm_sum_matches_float64(mm, case, majors, residual):
+    (m, n), ks = case
+    a_mn, b_mn = majors
+    gen = torch.Generator(device="cuda").manual_seed(m + n + sum(ks) + a_mn * 2 + b_mn)
+    terms, want = [], torch.zeros(m, n, dtype=torch.float64, device="cuda")
+    for k in ks:
+        a_store, lda, a = operand(m, max(k, 1), a_mn, gen)
+        b_store, ldb, b = operand(n, max(k, 1), b_mn, gen)
+        terms.append((a_store, lda, b_store, ldb, k))
+        if k:
+            want += a[:, :k].double() @ b[:, :k].double().t()
+    ldc = round4(n)
+    r = torch.randn(m, ldc, generator=gen, device="cuda") if residual else None
+    if residual:
+        want += r[:, :n].double()
+    c = torch.full((m, ldc), float("nan"), device="cuda")
+    mm.gemm_sum(terms, c, m=m, n=n, ldc=ldc, a_mn_major=a_mn, b_mn_major=b_mn, r=r, ldr=ldc if residual else 0)
+    mm.device_status()
+    got = c[:, :n]
+    assert torch.isfinite(got).all()
+    assert rel_l2(got, want) < TF32_TOL
