@@ -48,11 +48,19 @@ void attention_backward_tc(const AttnShape& s, const float* q, const float* k, c
 bool attention_flash_supported(const AttnShape& s);
 void attention_forward_flash(const AttnShape& s, const float* q, const float* k, const float* v, float* o,
                              float* lse, int* d_err, cudaStream_t stream);
+// A second stream for the backward's dQ kernel, with two events of the caller's:
+// the side stream waits for delta, the main stream for the side's kernel.
+struct BwdSide {
+  cudaStream_t stream;
+  cudaEvent_t ready, done;
+};
 // Fused tensor-core backward (flash_bwd.cu): writes delta (B*H*T floats) and
-// dq, dk, dv (dk/dv summed over each key head's group); no score buffers.
+// dq, dk, dv (dk/dv summed over each key head's group); no score buffers. With
+// `side`, the dQ kernel runs beside the dK/dV kernel on side->stream; the work
+// is complete on `stream` when the call's work there is.
 void attention_backward_flash(const AttnShape& s, const float* q, const float* k, const float* v, const float* o,
                               const float* lse, const float* dout, long long lddo, float* dq, float* dk, float* dv,
-                              float* delta, int* d_err, cudaStream_t stream);
+                              float* delta, int* d_err, cudaStream_t stream, const BwdSide* side = nullptr);
 // delta[b, h, t] = sum_d dout[t, h, d] * o[t, h, d]
 void attention_delta(const AttnShape& s, const float* o, const float* dout, long long lddo, float* delta,
                      cudaStream_t stream);

@@ -1084,7 +1084,7 @@ void launch_bwd(const AttnShape& s, const float* q, const float* k, const float*
 template <int HD>
 void launch_bwd_pair(const AttnShape& s, const float* q, const float* k, const float* v, const float* lse,
                      const float* dout, long long lddo, float* dq, float* dk, float* dv, const float* delta,
-                     int* d_err, cudaStream_t stream) {
+                     int* d_err, cudaStream_t stream, const BwdSide* side) {
   using Cfg = PairBwdCfg<HD>;
   const long long rows = static_cast<long long>(s.B) * s.T;
   const int n_pairs = (s.T + 2 * TILE - 1) / (2 * TILE);
@@ -1133,7 +1133,10 @@ void launch_bwd_pair(const AttnShape& s, const float* q, const float* k, const f
     pq.ld_out = s.ldq;
     set_smem(flash_bwd_q_pair_kernel<HD>, Cfg::Q_SMEM);
     const long long grid = 2ll * n_pairs * pq.BHx;
-    flash_bwd_q_pair_kernel<HD><<<static_cast<unsigned>(grid), BTHREADS, Cfg::Q_SMEM, stream>>>(tq, tkk, tvk, tkm, pq);
+    // on the side stream the dQ kernel's blocks fill the SMs the dK/dV kernel's
+    // last wave leaves idle (the two kernels are independent)
+    const cudaStream_t qs = side ? side->stream : stream;
+    flash_bwd_q_pair_kernel<HD><<<static_cast<unsigned>(grid), BTHREADS, Cfg::Q_SMEM, qs>>>(tq, tkk, tvk, tkm, pq);
   }
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess)
@@ -1144,15 +1147,25 @@ void launch_bwd_pair(const AttnShape& s, const float* q, const float* k, const f
 
 void attention_backward_flash(const AttnShape& s, const float* q, const float* k, const float* v, const float* o,
                               const float* lse, const float* dout, long long lddo, float* dq, float* dk, float* dv,
-                              float* delta, int* d_err, cudaStream_t stream) {
+                              float* delta, int* d_err, cudaStream_t stream, const BwdSide* side) {
   if (!attention_flash_supported(s) || lddo % 4 != 0 || !aligned16(q) || !aligned16(k) || !aligned16(v) ||
       !aligned16(dout) || !aligned16(dq) || !aligned16(dk) || !aligned16(dv))
     throw std::runtime_error("flash attention backward: unsupported head_dim, stride or alignment");
   attention_delta(s, o, dout, lddo, delta, stream);
+  if (side && s.hd != 32) {
+    if (cudaEventRecord(side->ready, stream) != cudaSuccess ||
+        cudaStreamWaitEvent(side->stream, side->ready, 0) != cudaSuccess)
+      throw std::runtime_error("flash attention backward: side stream");
+  }
   switch (s.hd) {
     case 32: launch_bwd<32>(s, q, k, v, lse, dout, lddo, dq, dk, dv, delta, d_err, stream); break;
-    case 64: launch_bwd_pair<64>(s, q, k, v, lse, dout, lddo, dq, dk, dv, delta, d_err, stream); break;
-    default: launch_bwd_pair<128>(s, q, k, v, lse, dout, lddo, dq, dk, dv, delta, d_err, stream); break;
+    case 64: launch_bwd_pair<64>(s, q, k, v, lse, dout, lddo, dq, dk, dv, delta, d_err, stream, side); break;
+    default: launch_bwd_pair<128>(s, q, k, v, lse, dout, lddo, dq, dk, dv, delta, d_err, stream, side); break;
+  }
+  if (side && s.hd != 32) {
+    if (cudaEventRecord(side->done, side->stream) != cudaSuccess ||
+        cudaStreamWaitEvent(stream, side->done, 0) != cudaSuccess)
+      throw std::runtime_error("flash attention backward: side stream");
   }
 }
 

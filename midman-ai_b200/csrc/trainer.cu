@@ -150,12 +150,18 @@ Trainer::Trainer(const ModelConfig& cfg, int batch, int seq, int precision, int 
     // TF32: fused tensor-core attention (no score buffers); 3xTF32: FP32 flash kernels
     attn_tc_ = precision == kPrecisionTF32 && attention_flash_supported(shape);
   }
+  if (attn_tc_) {
+    check_cuda(cudaStreamCreateWithFlags(&attn_side_stream_, cudaStreamNonBlocking), "stream");
+    check_cuda(cudaEventCreateWithFlags(&attn_side_ready_, cudaEventDisableTiming), "event");
+    check_cuda(cudaEventCreateWithFlags(&attn_side_done_, cudaEventDisableTiming), "event");
+  }
   check_cuda(cudaDeviceSynchronize(), "trainer setup");
 }
 
 Trainer::~Trainer() {
   if (stream_) cudaStreamSynchronize(stream_);
   if (comm_stream_) cudaStreamSynchronize(comm_stream_);
+  if (attn_side_stream_) cudaStreamSynchronize(attn_side_stream_);
   for (void* p : allocations_) cudaFree(p);
   for (int32_t* p : h_pinned_)
     if (p) cudaFreeHost(p);
@@ -167,6 +173,9 @@ Trainer::~Trainer() {
   if (comm_done_) cudaEventDestroy(comm_done_);
   if (comm_) nccl().CommDestroy(static_cast<ncclComm_t>(comm_));
   if (comm_stream_) cudaStreamDestroy(comm_stream_);
+  if (attn_side_ready_) cudaEventDestroy(attn_side_ready_);
+  if (attn_side_done_) cudaEventDestroy(attn_side_done_);
+  if (attn_side_stream_) cudaStreamDestroy(attn_side_stream_);
   if (stream_) cudaStreamDestroy(stream_);
 }
 

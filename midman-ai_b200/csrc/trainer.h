@@ -194,6 +194,9 @@ class Trainer {
 
   // Attention on the tensor cores (TF32 mode, head_dim 32/64/128): score buffers.
   bool attn_tc_ = false;
+  // the side stream of the attention backward's dQ kernel and its two events
+  cudaStream_t attn_side_stream_ = nullptr;
+  cudaEvent_t attn_side_ready_ = nullptr, attn_side_done_ = nullptr;
 
   bool profiling_ = false;
   std::vector<cudaEvent_t> prof_events_;

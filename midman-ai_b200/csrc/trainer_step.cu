@@ -118,11 +118,13 @@ void Trainer::backward(int B, int T) {
     gemm(N, D, D, dh, D, false, P_ + bo.o, D, false, do_, D, nullptr, 0);
     gemm(D, D, N, a.o, D, true, dh, D, true, G_ + bo.o, D, nullptr, 0);
     int slot = prof_begin();
-    if (attn_tc_)
+    if (attn_tc_) {
+      const BwdSide side{attn_side_stream_, attn_side_ready_, attn_side_done_};
       attention_backward_flash(shape, a.q, a.k, a.v, a.o, a.lse, do_, D, dq_, dk_, dv_, delta_, device_context().d_err,
-                               stream_);
-    else
+                               stream_, &side);
+    } else {
       attention_backward(shape, a.q, a.k, a.v, a.o, a.lse, do_, D, dq_, dk_, dv_, delta_, stream_);
+    }
     // dV, dP, dQ, dK: four causal products (the recomputed scores are not counted)
     prof_end(slot, "attention_bwd", 4.0 * B * H * static_cast<double>(T) * (T + 1) * hd);
     rope(dq_, N, T, H, hd, D, d_cos_, d_sin_, true, stream_);
