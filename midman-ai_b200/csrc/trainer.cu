@@ -150,18 +150,17 @@ Trainer::Trainer(const ModelConfig& cfg, int batch, int seq, int precision, int 
     // TF32: fused tensor-core attention (no score buffers); 3xTF32: FP32 flash kernels
     attn_tc_ = precision == kPrecisionTF32 && attention_flash_supported(shape);
   }
-  if (attn_tc_) {
-    check_cuda(cudaStreamCreateWithFlags(&attn_side_stream_, cudaStreamNonBlocking), "stream");
-    check_cuda(cudaEventCreateWithFlags(&attn_side_ready_, cudaEventDisableTiming), "event");
-    check_cuda(cudaEventCreateWithFlags(&attn_side_done_, cudaEventDisableTiming), "event");
-  }
+  check_cuda(cudaStreamCreateWithFlags(&side_stream_, cudaStreamNonBlocking), "stream");
+  check_cuda(cudaEventCreateWithFlags(&attn_side_ready_, cudaEventDisableTiming), "event");
+  check_cuda(cudaEventCreateWithFlags(&attn_side_done_, cudaEventDisableTiming), "event");
+  for (auto& e : side_ev_) check_cuda(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "event");
   check_cuda(cudaDeviceSynchronize(), "trainer setup");
 }
 
 Trainer::~Trainer() {
   if (stream_) cudaStreamSynchronize(stream_);
   if (comm_stream_) cudaStreamSynchronize(comm_stream_);
-  if (attn_side_stream_) cudaStreamSynchronize(attn_side_stream_);
+  if (side_stream_) cudaStreamSynchronize(side_stream_);
   for (void* p : allocations_) cudaFree(p);
   for (int32_t* p : h_pinned_)
     if (p) cudaFreeHost(p);
@@ -175,7 +174,9 @@ Trainer::~Trainer() {
   if (comm_stream_) cudaStreamDestroy(comm_stream_);
   if (attn_side_ready_) cudaEventDestroy(attn_side_ready_);
   if (attn_side_done_) cudaEventDestroy(attn_side_done_);
-  if (attn_side_stream_) cudaStreamDestroy(attn_side_stream_);
+  for (auto e : side_ev_)
+    if (e) cudaEventDestroy(e);
+  if (side_stream_) cudaStreamDestroy(side_stream_);
   if (stream_) cudaStreamDestroy(stream_);
 }
 
@@ -446,25 +447,26 @@ void Trainer::prof_collect() {
 }
 
 void Trainer::gemm(int M, int N, int K, const float* A, long long lda, bool a_mn, const float* B, long long ldb,
-                   bool b_mn, float* C, long long ldc, const float* R, long long ldr) {
+                   bool b_mn, float* C, long long ldc, const float* R, long long ldr, cudaStream_t st) {
   const GemmSegment seg{{A, lda, a_mn}, {B, ldb, b_mn}, K};
-  gemm_sum(M, N, &seg, 1, C, ldc, R, ldr);
+  gemm_sum(M, N, &seg, 1, C, ldc, R, ldr, st);
 }
 
 // C = sum of the segments' products (+ R): one launch in TF32 when the shape runs
 // on CTA pairs (gemm_tf32_sum); in 3xTF32 one split product per segment.
 void Trainer::gemm_sum(int M, int N, const GemmSegment* segs, int nseg, float* C, long long ldc, const float* R,
-                       long long ldr) {
-  const int slot = prof_begin();
+                       long long ldr, cudaStream_t st) {
+  if (!st) st = stream_;
+  const int slot = st == stream_ ? prof_begin() : -1;
   DeviceContext& ctx = device_context();
   const uint64_t before = gemm_launch_count();
   int rc = 0;
   if (precision_ == kPrecisionTF32) {
-    rc = gemm_tf32_sum(M, N, segs, nseg, C, ldc, R, ldr, ctx.d_err, stream_);
+    rc = gemm_tf32_sum(M, N, segs, nseg, C, ldc, R, ldr, ctx.d_err, st);
   } else {
     for (int g = 0; g < nseg && rc == 0; ++g)
       rc = gemm_3xtf32(M, N, segs[g].K, segs[g].a, segs[g].b, C, ldc, g == 0 ? R : C, g == 0 ? ldr : ldc,
-                       ctx.d_err, stream_);
+                       ctx.d_err, st);
     launches_ += 2 * nseg;  // the hi/lo splits of A and B
   }
   if (rc) throw std::runtime_error(std::string("GEMM: ") + gemm_status_string(rc));

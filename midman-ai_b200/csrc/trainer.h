@@ -115,10 +115,11 @@ class Trainer {
   StepOut finish_collect(bool update);
   void finish_launch(float lr, const AdamHyper& h, bool update);
   void build_embedding_csr(const int32_t* inputs, int N, int slot);
+  // GEMMs on `st` (the trainer's stream when null)
   void gemm(int M, int N, int K, const float* A, long long lda, bool a_mn, const float* B, long long ldb, bool b_mn,
-            float* C, long long ldc, const float* R, long long ldr);
+            float* C, long long ldc, const float* R, long long ldr, cudaStream_t st = nullptr);
   void gemm_sum(int M, int N, const GemmSegment* segs, int nseg, float* C, long long ldc, const float* R,
-                long long ldr);
+                long long ldr, cudaStream_t st = nullptr);
   StepOut finish_step(float lr, const AdamHyper& h, bool update);
 
  public:
@@ -194,9 +195,11 @@ class Trainer {
 
   // Attention on the tensor cores (TF32 mode, head_dim 32/64/128): score buffers.
   bool attn_tc_ = false;
-  // the side stream of the attention backward's dQ kernel and its two events
-  cudaStream_t attn_side_stream_ = nullptr;
+  // The backward's side stream (weight-gradient products, the attention
+  // backward's dQ kernel) and its events.
+  cudaStream_t side_stream_ = nullptr;
   cudaEvent_t attn_side_ready_ = nullptr, attn_side_done_ = nullptr;
+  cudaEvent_t side_ev_[4] = {nullptr, nullptr, nullptr, nullptr};
 
   bool profiling_ = false;
   std::vector<cudaEvent_t> prof_events_;

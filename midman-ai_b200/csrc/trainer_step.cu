@@ -84,15 +84,37 @@ void Trainer::backward(int B, int T) {
   const int hd = static_cast<int>(cfg_.head_dim());
   const AttnShape shape{B, T, H, Hkv, hd, D, KV, KV, D, 1.0f / std::sqrt(static_cast<float>(hd))};
   const int L = static_cast<int>(cfg_.n_layers);
+  // The weight-gradient products are off the path the gradient flows down: they
+  // run on the side stream (ws), each after an event of the main stream that
+  // made its inputs, while the main stream goes on; the main stream waits for
+  // them before it overwrites a buffer they read (the scratch dh, dq, dk, dv, dx)
+  // and before the gradients are used. One stream with profiling on (per-kernel
+  // times) and in 3xTF32 (its split operands share one scratch arena).
+  const bool dual = side_stream_ != nullptr && !profiling_ && precision_ == kPrecisionTF32;
+  cudaStream_t ws = dual ? side_stream_ : stream_;
+  auto to_side = [&] {  // the side stream waits for the main stream's work so far
+    if (!dual) return;
+    check_cuda(cudaEventRecord(side_ev_[0], stream_), "event");
+    check_cuda(cudaStreamWaitEvent(ws, side_ev_[0], 0), "wait");
+  };
+  auto side_mark = [&](int e) {  // an event after the side stream's work so far
+    if (dual) check_cuda(cudaEventRecord(side_ev_[e], ws), "event");
+  };
+  auto main_waits = [&](int e) {
+    if (dual) check_cuda(cudaStreamWaitEvent(stream_, side_ev_[e], 0), "wait");
+  };
   // logits_ holds d loss / d logits. Head products first (the tape starts there):
   if (cfg_.tie) {
     gemm(N, D, V, logits_, V, false, P_ + layout_.embed, D, true, tmp_, D, nullptr, 0);
-    gemm(V, D, N, logits_, V, true, xf_, D, true, G_ + layout_.embed, D, nullptr, 0);
+    to_side();
+    gemm(V, D, N, logits_, V, true, xf_, D, true, G_ + layout_.embed, D, nullptr, 0, ws);
   } else {
     gemm(N, D, V, logits_, V, false, P_ + layout_.lm_head, V, false, tmp_, D, nullptr, 0);
-    gemm(D, V, N, xf_, D, true, logits_, V, true, G_ + layout_.lm_head, V, nullptr, 0);
-    check_cuda(cudaMemsetAsync(G_ + layout_.embed, 0, static_cast<size_t>(V) * D * 4, stream_), "zero dE");
+    to_side();
+    gemm(D, V, N, xf_, D, true, logits_, V, true, G_ + layout_.lm_head, V, nullptr, 0, ws);
+    check_cuda(cudaMemsetAsync(G_ + layout_.embed, 0, static_cast<size_t>(V) * D * 4, ws), "zero dE");
   }
+  side_mark(3);  // the head's share of dE
   const int c = 0;  // dx_[c] carries the gradient down the residual stream
   float* dx = dx_[c];
   float* dh = dx_[1 - c];
@@ -103,23 +125,28 @@ void Trainer::backward(int B, int T) {
     Layer& a = acts_[l];
     const BlockOffsets& bo = layout_.blocks[l];
     // x_next = h + act Wd
+    to_side();  // dx of this layer is ready
+    gemm(F, D, N, a.act, F, true, dx, D, true, G_ + bo.down, D, nullptr, 0, ws);
+    side_mark(1);  // dx read
     gemm(N, F, D, dx, D, false, P_ + bo.down, D, false, dact_, F, nullptr, 0);
-    gemm(F, D, N, a.act, F, true, dx, D, true, G_ + bo.down, D, nullptr, 0);
     swiglu_backward(a.g, a.u, dact_, static_cast<long long>(N) * F, stream_);  // g <- dg, u <- du
+    to_side();
+    gemm(D, F, N, a.xn2, D, true, a.g, F, true, G_ + bo.gate, F, nullptr, 0, ws);
+    gemm(D, F, N, a.xn2, D, true, a.u, F, true, G_ + bo.up, F, nullptr, 0, ws);
     {  // dxn = dg Wg^T + du Wu^T, one accumulator
       const GemmSegment segs[2] = {{{a.g, F, false}, {P_ + bo.gate, F, false}, F},
                                    {{a.u, F, false}, {P_ + bo.up, F, false}, F}};
       gemm_sum(N, D, segs, 2, dxn_, D, nullptr, 0);
     }
-    gemm(D, F, N, a.xn2, D, true, a.g, F, true, G_ + bo.gate, F, nullptr, 0);
-    gemm(D, F, N, a.xn2, D, true, a.u, F, true, G_ + bo.up, F, nullptr, 0);
+    if (l + 1 < L) main_waits(2);  // the layer above's products have read dh, dq, dk, dv
     rmsnorm_backward(a.h, P_ + bo.mlp_norm, a.rstd2, dxn_, N, D, dh, dx, G_ + bo.mlp_norm, norm_ws_, stream_);
     // h = x + o Wo
+    to_side();
+    gemm(D, D, N, a.o, D, true, dh, D, true, G_ + bo.o, D, nullptr, 0, ws);
     gemm(N, D, D, dh, D, false, P_ + bo.o, D, false, do_, D, nullptr, 0);
-    gemm(D, D, N, a.o, D, true, dh, D, true, G_ + bo.o, D, nullptr, 0);
     int slot = prof_begin();
     if (attn_tc_) {
-      const BwdSide side{attn_side_stream_, attn_side_ready_, attn_side_done_};
+      const BwdSide side{side_stream_, attn_side_ready_, attn_side_done_};
       attention_backward_flash(shape, a.q, a.k, a.v, a.o, a.lse, do_, D, dq_, dk_, dv_, delta_, device_context().d_err,
                                stream_, &side);
     } else {
@@ -129,15 +156,18 @@ void Trainer::backward(int B, int T) {
     prof_end(slot, "attention_bwd", 4.0 * B * H * static_cast<double>(T) * (T + 1) * hd);
     rope(dq_, N, T, H, hd, D, d_cos_, d_sin_, true, stream_);
     rope(dk_, N, T, Hkv, hd, KV, d_cos_, d_sin_, true, stream_);
+    to_side();
+    gemm(D, D, N, a.xn1, D, true, dq_, D, true, G_ + bo.q, D, nullptr, 0, ws);
+    gemm(D, KV, N, a.xn1, D, true, dk_, KV, true, G_ + bo.k, KV, nullptr, 0, ws);
+    gemm(D, KV, N, a.xn1, D, true, dv_, KV, true, G_ + bo.v, KV, nullptr, 0, ws);
+    side_mark(2);  // this layer's weight gradients are done
     {  // dxn = dq Wq^T + dk Wk^T + dv Wv^T, one accumulator
       const GemmSegment segs[3] = {{{dq_, D, false}, {P_ + bo.q, D, false}, D},
                                    {{dk_, KV, false}, {P_ + bo.k, KV, false}, KV},
                                    {{dv_, KV, false}, {P_ + bo.v, KV, false}, KV}};
       gemm_sum(N, D, segs, 3, dxn_, D, nullptr, 0);
     }
-    gemm(D, D, N, a.xn1, D, true, dq_, D, true, G_ + bo.q, D, nullptr, 0);
-    gemm(D, KV, N, a.xn1, D, true, dk_, KV, true, G_ + bo.k, KV, nullptr, 0);
-    gemm(D, KV, N, a.xn1, D, true, dv_, KV, true, G_ + bo.v, KV, nullptr, 0);
+    main_waits(1);  // the down projection's product has read dx
     rmsnorm_backward(a.x, P_ + bo.attn_norm, a.rstd1, dxn_, N, D, dx, dh, G_ + bo.attn_norm, norm_ws_, stream_);
     launches_ += 10;  // SwiGLU, two RMSNorm backwards (2 kernels each), attention backward (3), two RoPEs
     if (world_ > 1) {
@@ -145,9 +175,12 @@ void Trainer::backward(int B, int T) {
       // backward runs (a bucket per layer, in reverse parameter order).
       check_cuda(cudaEventRecord(layer_done_[l], stream_), "event");
       check_cuda(cudaStreamWaitEvent(comm_stream_, layer_done_[l], 0), "wait");
+      if (dual) check_cuda(cudaStreamWaitEvent(comm_stream_, side_ev_[2], 0), "wait");
       reduce_bucket(1 + l);
     }
   }
+  main_waits(2);  // every weight gradient of the blocks
+  main_waits(3);  // and the head's share of dE
   // the embedding's share, added after the head's (ops_shape.rs:262-272)
   embedding_backward(d_uniq_, d_off_, d_pos_, n_uniq_, dx, D, G_ + layout_.embed, stream_);
   launches_ += 1;
