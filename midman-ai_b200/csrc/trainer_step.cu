@@ -35,6 +35,22 @@ void Trainer::forward(int B, int T, bool train) {
   const float eps = cfg_.norm_eps;
   const AttnShape shape{B, T, H, Hkv, hd, D, KV, KV, D, 1.0f / std::sqrt(static_cast<float>(hd))};
   const int L = static_cast<int>(cfg_.n_layers);
+  // The k/v projections (and RoPE of k) and the up projection run on the side
+  // stream beside q and gate, which read the same normalized input; the main
+  // stream waits for them before attention and SwiGLU. One stream with
+  // profiling on and in 3xTF32 (its split operands share one scratch arena).
+  const bool dual = side_stream_ != nullptr && !profiling_ && precision_ == kPrecisionTF32;
+  cudaStream_t ws = dual ? side_stream_ : stream_;
+  auto to_side = [&] {
+    if (!dual) return;
+    check_cuda(cudaEventRecord(side_ev_[0], stream_), "event");
+    check_cuda(cudaStreamWaitEvent(ws, side_ev_[0], 0), "wait");
+  };
+  auto from_side = [&] {
+    if (!dual) return;
+    check_cuda(cudaEventRecord(side_ev_[1], ws), "event");
+    check_cuda(cudaStreamWaitEvent(stream_, side_ev_[1], 0), "wait");
+  };
   // under optimizer sharding, each bucket's parameters may still be arriving from their owner
   wait_params(0);
   embedding_forward(d_ids_, N, P_ + layout_.embed, D, acts_[0].x, stream_);
@@ -46,11 +62,13 @@ void Trainer::forward(int B, int T, bool train) {
     float* next_x = (l + 1 < L) ? acts_[l + 1].x : x_final_;
     // h = x + attention(attn_norm(x)) (block.rs:78-79)
     rmsnorm_forward(a.x, P_ + bo.attn_norm, N, D, eps, a.xn1, a.rstd1, stream_);
+    to_side();
+    gemm(N, KV, D, a.xn1, D, false, P_ + bo.k, KV, true, a.k, KV, nullptr, 0, ws);
+    gemm(N, KV, D, a.xn1, D, false, P_ + bo.v, KV, true, a.v, KV, nullptr, 0, ws);
+    rope(a.k, N, T, Hkv, hd, KV, d_cos_, d_sin_, false, ws);
     gemm(N, D, D, a.xn1, D, false, P_ + bo.q, D, true, a.q, D, nullptr, 0);
-    gemm(N, KV, D, a.xn1, D, false, P_ + bo.k, KV, true, a.k, KV, nullptr, 0);
-    gemm(N, KV, D, a.xn1, D, false, P_ + bo.v, KV, true, a.v, KV, nullptr, 0);
     rope(a.q, N, T, H, hd, D, d_cos_, d_sin_, false, stream_);
-    rope(a.k, N, T, Hkv, hd, KV, d_cos_, d_sin_, false, stream_);
+    from_side();
     const double attn_flops = 2.0 * B * H * static_cast<double>(T) * (T + 1) * hd;  // QK^T and PV, causal half
     int slot = prof_begin();
     if (attn_tc_)  // fused: the scores stay on chip
@@ -61,8 +79,10 @@ void Trainer::forward(int B, int T, bool train) {
     gemm(N, D, D, a.o, D, false, P_ + bo.o, D, true, a.h, D, a.x, D);
     // out = h + swiglu(mlp_norm(h)) (mlp.rs:20-24)
     rmsnorm_forward(a.h, P_ + bo.mlp_norm, N, D, eps, a.xn2, a.rstd2, stream_);
+    to_side();
+    gemm(N, F, D, a.xn2, D, false, P_ + bo.up, F, true, a.u, F, nullptr, 0, ws);
     gemm(N, F, D, a.xn2, D, false, P_ + bo.gate, F, true, a.g, F, nullptr, 0);
-    gemm(N, F, D, a.xn2, D, false, P_ + bo.up, F, true, a.u, F, nullptr, 0);
+    from_side();
     swiglu_forward(a.g, a.u, a.act, static_cast<long long>(N) * F, stream_);
     gemm(N, D, F, a.act, F, false, P_ + bo.down, D, true, next_x, D, a.h, D);
     launches_ += 6;  // two RMSNorms, two RoPEs, attention, SwiGLU (GEMMs are counted in gemm())
