@@ -11,9 +11,10 @@ the per-GPU batch is fixed). Rank 0 prints one JSON line.
 
 `value` times K steps on a batch already in HBM (midman_train_step_staged),
 with CUDA events on the library's stream, max over ranks. `e2e` times K steps
-through midman_train_step with host token arrays: the host-to-device copy of
-each step's ids and the read-back of its loss and gradient norm are inside the
-timed region. `--impl reference` times the CPU restatement of the reference's
+of midman_train_run, the library's training loop over the batcher: taking each
+global batch on the host, the host-to-device copy of this rank's ids and the
+read-back of its loss and gradient norm are inside the timed region (the host
+prepares batch s+1 while the GPU runs step s). `--impl reference` times the CPU restatement of the reference's
 f32 path (oracle/) on a bounded sample of the same workload on all host cores.
 """
 from __future__ import annotations
@@ -248,7 +249,7 @@ def run_kernels(args):
     return 0
 
 
-GEMM_TRAFFIC_BYTES = 462e6  # see the roofline entry below
+GEMM_TRAFFIC_BYTES = 538e6  # see the roofline entry below
 
 
 def gemm_shapes(prof, steps, top=10):
@@ -375,16 +376,20 @@ def main():
     desc = trainer.describe()
     trainer.profile(False)
 
-    # ---- e2e: host ids through the public step call, copies inside the timed region
+    # ---- e2e: the training loop of the public API (midman_train_run) over the
+    # batcher: per step the host takes the global batch, checks it and builds the
+    # embedding index in pinned memory, copies this rank's ids to the device and
+    # reads back loss and gradient norm, all inside the timed region
+    batcher.seek(0, 1 + args.warmup)
     barrier()
     t0 = time.perf_counter()
     e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e_start.record(stream)
-    for k in range(args.steps):
-        trainer.step(*batches[1 + args.warmup + k])
+    e_rec, e_status, _ = trainer.run(batcher, args.steps)
     e_end.record(stream)
     e_end.synchronize()
     barrier()
+    assert e_status == 0 and len(e_rec) == args.steps
     e2e_ms = max_over_ranks(max(e_start.elapsed_time(e_end), (time.perf_counter() - t0) * 1e3))
     stop.set()
     sampler.join(timeout=10)
