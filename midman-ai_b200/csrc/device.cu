@@ -65,6 +65,7 @@ std::string device_error_message(int code) {
     case kErrWaitAccum: return "GEMM: epilogue timed out waiting for the accumulator";
     case kErrWaitDrain: return "GEMM: teardown timed out draining TMA copies";
     case kErrBadShape: return "kernel rejected its shape";
+    case kErrWaitUnit: return "GEMM: a role timed out waiting for its next work unit";
     default: return "device error " + std::to_string(code);
   }
 }

@@ -433,10 +433,24 @@ struct PairOperands {
   int nseg;
 };
 
+// Work units reach a pair's roles through a ring of kUnitRing slots in both CTAs'
+// shared memory: the leader's producer takes each next unit and publishes it
+// (unit_full, one arrival; the peer CTA's slot by a remote store and a
+// cluster-scope release arrival), and every other role of the pair (the peer's
+// producer, the UMMA issuer, the eight epilogue warps) reads it and frees the
+// slot (the leader's unit_empty). -1 ends every role's loop. A pair's first
+// unit is its position in the grid; the next ones come from the launch's
+// ticket counter (`sched`: tickets, finished pairs) when one is given, so that
+// pairs whose SMs were busy when the launch started (another stream's kernel,
+// NCCL) take fewer units; otherwise the pair strides by the grid.
+constexpr int kUnitRing = 4;
+constexpr int kUnitConsumers = 1 + 1 + 8;  // peer producer, UMMA issuer, epilogue warps of both CTAs
+
 template <bool A_MN, bool B_MN, int PN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     gemm_pair_kernel(const __grid_constant__ PairOperands ops, float* C, long long ldc, const float* R, long long ldr,
-                     int M, int N, int* err, int total_tiles, int full_tiles, int splits, float* ws) {
+                     int M, int N, int* err, int total_tiles, int full_tiles, int splits, float* ws,
+                     unsigned int* sched) {
   using Cfg = PairTile<PN>;
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
@@ -454,11 +468,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   auto empty_bar = [&](int s) { return bar_base + 8u * (Cfg::STAGES + s); };
   auto acc_full = [&](int b) { return bar_base + 8u * (2 * Cfg::STAGES + b); };
   auto acc_empty = [&](int b) { return bar_base + 8u * (2 * Cfg::STAGES + 2 + b); };
-  const uint32_t tmem_slot = bar_base + 8u * (2 * Cfg::STAGES + 4);
-  uint8_t* tail = smem + Cfg::STAGES * Cfg::STAGE + 8 * (2 * Cfg::STAGES + 4);
+  auto unit_full = [&](int s) { return bar_base + 8u * (2 * Cfg::STAGES + 4 + s); };
+  auto unit_empty = [&](int s) { return bar_base + 8u * (2 * Cfg::STAGES + 4 + kUnitRing + s); };
+  constexpr int kBars = 2 * Cfg::STAGES + 4 + 2 * kUnitRing;
+  const uint32_t tmem_slot = bar_base + 8u * kBars;
+  uint8_t* tail = smem + Cfg::STAGES * Cfg::STAGE + 8 * kBars;
   uint32_t* tmem_slot_ptr = reinterpret_cast<uint32_t*>(tail);
   int* loads_issued = reinterpret_cast<int*>(tail + 8);
   int* loads_consumed = loads_issued + 1;
+  volatile int* unit_ring = reinterpret_cast<volatile int*>(tail + 16);
+  static_assert(8 * kBars + 16 + 4 * kUnitRing <= 256, "barriers and counters fit their 256 bytes");
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -475,6 +494,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       mbar_init(acc_full(b), 1);
       mbar_init(acc_empty(b), 8);  // four epilogue warps in each CTA
     }
+    for (int s = 0; s < kUnitRing; ++s) {
+      mbar_init(unit_full(s), 1);
+      mbar_init(unit_empty(s), kUnitConsumers);
+    }
     *loads_issued = 0;
     *loads_consumed = 0;
     fence_barrier_init();
@@ -489,12 +512,53 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot_ptr;
 
+  // The unit after `cur` for this pair: strided, or the next ticket. A pair's
+  // last (failing) ticket counts it as finished; the last pair to finish resets
+  // the counter for the next launch on the stream.
+  auto next_unit = [&](int cur) -> int {
+    if (!sched) return cur + npairs < total_units ? cur + npairs : -1;
+    const int v = npairs + static_cast<int>(atomicAdd(&sched[0], 1u));
+    if (v < total_units) return v;
+    __threadfence();
+    if (atomicAdd(&sched[1], 1u) == static_cast<unsigned>(npairs - 1)) {
+      __threadfence();
+      atomicExch(&sched[0], 0u);
+      atomicExch(&sched[1], 0u);
+    }
+    return -1;
+  };
+
   if (warp == 0) {
     if (lane == 0) {
       // ---------------- TMA producer (both CTAs); completions land on the leader's barriers
-      int it = 0;
+      int it = 0, ring_i = 0;
       bool ok = true;
-      for (int u = pair; u < total_units && ok; u += npairs) {
+      int u = leader ? pair : -1;
+      for (;;) {
+        const int rs = ring_i % kUnitRing, rr = ring_i / kUnitRing;
+        if (leader) {  // publish this unit (or the end) to the pair
+          if (rr > 0 && !mbar_wait_cluster(unit_empty(rs), (rr - 1) & 1, err, kErrWaitUnit)) {
+            ok = false;
+            break;
+          }
+          unit_ring[rs] = u;
+          st_shared_cluster(mapa_shared(smem_u32(const_cast<int*>(&unit_ring[rs])), 1), u);
+          mbar_arrive(unit_full(rs));
+          mbar_arrive_remote_release(mapa_shared(unit_full(rs), 1));
+        } else {
+          if (!mbar_wait_cluster(unit_full(rs), rr & 1, err, kErrWaitUnit)) {
+            ok = false;
+            break;
+          }
+          u = unit_ring[rs];
+          mbar_arrive_remote_release(mapa_shared(unit_empty(rs), 0));
+        }
+        ++ring_i;
+        if (u >= total_units) {  // never handed out; guards the workspace index
+          atomicCAS(err, 0, kErrWaitUnit);
+          u = -1;
+        }
+        if (u < 0) break;
         const PairUnit w = pair_unit(u, full_tiles, splits, n_k);
         const int t = w.tile;
         const int my_m0 = (t % tm) * 2 * BM + static_cast<int>(rank) * BM;
@@ -532,15 +596,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           }
           *loads_issued = it + 1;
         }
+        if (!ok) break;
+        if (leader) u = next_unit(u);
       }
+      // keep the ticket protocol whole after a timed-out wait: take tickets
+      // until this pair's last one
+      if (leader && sched && u >= 0)
+        while (next_unit(u) >= 0) {
+        }
     }
   } else if (warp == 1) {
     if (lane == 0 && leader) {
       // ---------------- UMMA issuer (leader only), M = 256 across the pair
       constexpr uint32_t idesc = idesc_tf32(2 * BM, PN, A_MN, B_MN);
-      int it = 0, j = 0;
+      int it = 0, j = 0, ring_i = 0;
       bool ok = true;
-      for (int u = pair; u < total_units && ok; u += npairs) {
+      for (;;) {
+        const int rs = ring_i % kUnitRing, rr = ring_i / kUnitRing;
+        if (!mbar_wait(unit_full(rs), rr & 1, err, kErrWaitUnit)) break;
+        const int u = unit_ring[rs];
+        mbar_arrive(unit_empty(rs));
+        ++ring_i;
+        if (u < 0 || u >= total_units) break;
         const PairUnit w = pair_unit(u, full_tiles, splits, n_k);
         const int buf = j & 1;
         if (j >= 2 && !mbar_wait(acc_empty(buf), ((j >> 1) - 1) & 1, err, kErrWaitAccum)) break;
@@ -565,6 +642,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           }
           umma_commit_pair(empty_bar(s), 0x3);
         }
+        if (!ok) break;
         umma_commit_pair(acc_full(buf), 0x3);
         ++j;
       }
@@ -573,8 +651,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     // ---------------- epilogue (both CTAs): this CTA's 128 rows, all 256 columns
     const int quarter = warp & 3;
     float4* stage_tile = reinterpret_cast<float4*>(smem + Cfg::STAGES * Cfg::STAGE + 256) + quarter * 256;
-    int j = 0;
-    for (int u = pair; u < total_units; u += npairs) {
+    int j = 0, ring_i = 0;
+    for (;;) {
+      const int rs = ring_i % kUnitRing, rr = ring_i / kUnitRing;
+      int u = -1;
+      if (lane == 0) {
+        const bool got = leader ? mbar_wait(unit_full(rs), rr & 1, err, kErrWaitUnit)
+                                : mbar_wait_cluster(unit_full(rs), rr & 1, err, kErrWaitUnit);
+        if (got) {
+          u = unit_ring[rs];
+          if (leader)
+            mbar_arrive(unit_empty(rs));
+          else
+            mbar_arrive_remote_release(mapa_shared(unit_empty(rs), 0));
+        }
+      }
+      u = __shfl_sync(0xffffffffu, u, 0);
+      ++ring_i;
+      if (u < 0 || u >= total_units) break;
       const PairUnit w = pair_unit(u, full_tiles, splits, n_k);
       const int t = w.tile;
       const int buf = j & 1;
@@ -818,6 +912,37 @@ SplitWorkspace* split_workspace(int dev, cudaStream_t stream, size_t floats) {
   return &w;
 }
 
+// The ticket counters of pair launches: two zeroed words per (device, stream)
+// (launches on one stream run one after another, and each launch leaves its
+// counter at zero). Streams past the 64th of a device get strided units.
+unsigned int* unit_counter(int dev, cudaStream_t stream) {
+  constexpr int kSlots = 64;
+  struct Table {
+    unsigned int* counters = nullptr;
+    cudaStream_t streams[kSlots];
+    int used = 0;
+  };
+  static std::mutex mu;
+  static Table tables[64];
+  std::lock_guard<std::mutex> lock(mu);
+  if (dev < 0 || dev >= 64) return nullptr;
+  Table& t = tables[dev];
+  if (!t.counters) {
+    void* p = nullptr;
+    if (cudaMalloc(&p, kSlots * 2 * sizeof(unsigned int)) != cudaSuccess) return nullptr;
+    if (cudaMemset(p, 0, kSlots * 2 * sizeof(unsigned int)) != cudaSuccess) {
+      cudaFree(p);
+      return nullptr;
+    }
+    t.counters = static_cast<unsigned int*>(p);
+  }
+  for (int i = 0; i < t.used; ++i)
+    if (t.streams[i] == stream) return t.counters + 2 * i;
+  if (t.used == kSlots) return nullptr;
+  t.streams[t.used] = stream;
+  return t.counters + 2 * t.used++;
+}
+
 template <bool A_MN, bool B_MN, int PN>
 int launch_pair(const PairOperands& ops, float* C, long long ldc, const float* R, long long ldr, int M, int N, int* err,
                 cudaStream_t stream) {
@@ -836,9 +961,10 @@ int launch_pair(const PairOperands& ops, float* C, long long ldc, const float* R
   const PairPlan plan = pair_plan(tiles, pairs, ops.seg_end[ops.nseg - 1]);
   const long long units = plan.full + (tiles - plan.full) * plan.splits;
   const int grid = 2 * static_cast<int>(units < pairs ? units : pairs);
+  unsigned int* sched = units > pairs ? unit_counter(dev, stream) : nullptr;  // one wave needs no tickets
   if (plan.splits == 1) {
     kern<<<grid, THREADS, Cfg::SMEM, stream>>>(ops, C, ldc, R, ldr, M, N, err, static_cast<int>(tiles), plan.full, 1,
-                                               nullptr);
+                                               nullptr, sched);
     ++t_launches;
     return 0;
   }
@@ -846,7 +972,7 @@ int launch_pair(const PairOperands& ops, float* C, long long ldc, const float* R
   SplitWorkspace* w = split_workspace(dev, stream, static_cast<size_t>(pairs) * P_TILE_FLOATS_MAX);
   if (!w) return kGemmLaunch;
   kern<<<grid, THREADS, Cfg::SMEM, stream>>>(ops, C, ldc, R, ldr, M, N, err, static_cast<int>(tiles), plan.full,
-                                             plan.splits, w->ptr);
+                                             plan.splits, w->ptr, sched);
   const dim3 rgrid(static_cast<unsigned>(tiles - plan.full), 2 * BM / (256 / (PN / 4)));
   split_reduce_kernel<PN><<<rgrid, 256, 0, stream>>>(w->ptr, plan.splits, plan.full, tm, C, ldc, R, ldr, M, N);
   t_launches += 2;

@@ -19,6 +19,7 @@ enum DeviceError : int {
   kErrWaitAccum = 3,    // the epilogue gave up waiting for the accumulator
   kErrWaitDrain = 4,    // teardown gave up waiting for copies in flight
   kErrBadShape = 5,
+  kErrWaitUnit = 6,     // a GEMM role gave up waiting for its next work unit
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -101,6 +102,39 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
 // tcgen05.fence::after_thread_sync after the wait on the other.
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+// Hands a value to the peer CTA: a store to its shared memory, then an arrival
+// on its barrier with cluster-scope release; the peer waits with
+// mbar_wait_cluster (cluster-scope acquire) before it reads the value.
+__device__ __forceinline__ void st_shared_cluster(uint32_t cluster_addr, int v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_remote_release(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// mbar_wait with cluster-scope acquire (same bound and error report).
+__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, int* err, int code,
+                                                  uint64_t timeout_ns = 4000000000ull) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t start = global_timer_ns();
+  for (uint32_t i = 1; i < (1u << 30); ++i) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if ((i & 255u) == 0u && global_timer_ns() - start > timeout_ns) break;
+  }
+  if (err) atomicCAS(err, 0, code);
+  return false;
 }
 
 // ---------------------------------------------------------------- TMA
