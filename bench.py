@@ -283,8 +283,9 @@ def main():
     ap.add_argument("--precision", default="tf32", choices=["tf32", "3xtf32"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--optimizer", default="replicated", choices=["replicated", "sharded"],
-                    help="sharded: ZeRO-1, each rank keeps and updates 1/N of the AdamW state (N > 1)")
+    ap.add_argument("--optimizer", default="auto", choices=["auto", "replicated", "sharded"],
+                    help="sharded: ZeRO-1, each rank keeps and updates 1/N of the AdamW state; auto: sharded "
+                         "for N > 1 (measured 2-3%% faster at N = 2 and 8)")
     args = ap.parse_args()
 
     if args.config in ("linear", "attention", "attention-large"):
@@ -329,6 +330,8 @@ def main():
                            beta1=0.9, beta2=0.95)
     trainer = mm.Trainer(mm.config_array(*cfg), hyper, seed=0, batch=B, seq=T, precision=precision, world=world,
                          rank=rank, nccl_id=nccl_id)
+    if args.optimizer == "auto":
+        args.optimizer = "sharded" if world > 1 else "replicated"
     if args.optimizer == "sharded":
         trainer.shard_optimizer(True)
     stream = torch.cuda.ExternalStream(trainer.stream())
