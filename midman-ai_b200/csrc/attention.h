@@ -30,19 +30,14 @@ void attention_backward(const AttnShape& s, const float* q, const float* k, cons
 void attention_probs(const AttnShape& s, const float* q, const float* k, const float* lse, float* probs,
                      cudaStream_t stream);
 
-// The tensor-core path (attention_tc.cu), for head_dim 32, 64 or 128 in TF32:
-// S and dP scratch buffers hold B*H*T*attention_scores_ld(T) floats each;
-// `tmp` (backward, grouped-query only) B*T*H*hd floats.
+// The tensor-core forward through a score buffer (attention_tc.cu), for head_dim
+// 32, 64 or 128 in TF32: S holds B*H*T*attention_scores_ld(T) floats. It serves
+// the allocation-free entry point, with the pipeline-timeout flag given by the
+// caller (no library state).
 bool attention_tc_supported(const AttnShape& s);
 long long attention_scores_ld(int T);
 void attention_forward_tc(const AttnShape& s, const float* q, const float* k, const float* v, float* o, float* lse,
-                          float* S, cudaStream_t stream);
-// The same with the pipeline-timeout flag given by the caller (no library state).
-void attention_forward_tc(const AttnShape& s, const float* q, const float* k, const float* v, float* o, float* lse,
                           float* S, int* d_err, cudaStream_t stream);
-void attention_backward_tc(const AttnShape& s, const float* q, const float* k, const float* v, const float* o,
-                           const float* lse, const float* dout, long long lddo, float* dq, float* dk, float* dv,
-                           float* delta, float* S, float* dP, float* tmp, cudaStream_t stream);
 // Fused tensor-core forward (flash_tc.cu): scores stay on chip, no scratch.
 // head_dim 32, 64 or 128; row strides multiples of 4; 16-byte aligned pointers.
 bool attention_flash_supported(const AttnShape& s);
