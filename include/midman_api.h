@@ -220,6 +220,10 @@ MIDMAN_EXPORT int32_t midman_train_run(uint32_t handle, uint32_t batcher, uint32
  * "world","rank","ranges":[[begin,end]...],"buckets":[[begin,end]...]}}; the
  * same object appears in midman_train_describe. */
 MIDMAN_EXPORT int32_t midman_train_shard_optimizer(uint32_t handle, uint32_t enable);
+/* The plan optimizer sharding follows for a config and world size, without a GPU:
+ * {"params","norm_block","norm_blocks","ranges":[[begin,end] per rank],
+ * "buckets":[[begin,end]...]} (the ranges a trainer of that world reports). */
+MIDMAN_EXPORT int32_t midman_shard_plan(const double *config, uint32_t world);
 /* Trainer::evaluate (trainer.rs:209-262) over held-out shard files (paths
  * separated by '\n'), windows of the run's seq: batches of the run's global batch
  * (or all the sequences, if fewer), row k of the `rows` taken is sequence

@@ -774,6 +774,42 @@ int32_t midman_train_save(uint32_t handle, const uint8_t* path, uint32_t path_le
   });
 }
 
+int32_t midman_shard_plan(const double* config, uint32_t world) {
+  return run([&] {
+    const ModelConfig c = config_from(read_f64s(config, "config"));
+    const std::string bad = validate_config(c);
+    if (!bad.empty()) throw ConfigError(bad);
+    if (world < 1 || world > 4096) throw ArgumentError("world must be between 1 and 4096");
+    const ParamLayout L = param_layout(c);
+    const uint64_t block = static_cast<uint64_t>(norm_block_elems(static_cast<long long>(L.total)));
+    const std::vector<uint64_t> bounds = shard_bounds(L.total, static_cast<int>(world), block, kNormBlocks);
+    JsonWriter w;
+    w.begin_object();
+    w.key("params").integer(L.total);
+    w.key("norm_block").integer(block);
+    w.key("norm_blocks").integer(kNormBlocks);
+    w.key("ranges").begin_array();
+    for (uint32_t r = 0; r < world; ++r) {
+      w.begin_array();
+      w.integer(bounds[r]);
+      w.integer(bounds[r + 1]);
+      w.end_array();
+    }
+    w.end_array();
+    w.key("buckets").begin_array();
+    for (const auto& b : gradient_buckets(c, L)) {
+      w.begin_array();
+      w.integer(b.first);
+      w.integer(b.second);
+      w.end_array();
+    }
+    w.end_array();
+    w.end_object();
+    set_text(w.finish());
+    return MIDMAN_OK;
+  });
+}
+
 int32_t midman_train_shard_optimizer(uint32_t handle, uint32_t enable) {
   return run([&] {
     Train& t = train_ref(handle);

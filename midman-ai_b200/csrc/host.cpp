@@ -76,6 +76,21 @@ ModelConfig preset_config(int i) {
   return c;
 }
 
+std::vector<std::pair<uint64_t, uint64_t>> gradient_buckets(const ModelConfig& c, const ParamLayout& L) {
+  std::vector<std::pair<uint64_t, uint64_t>> b;
+  b.push_back({L.embed, L.embed + c.vocab * c.d_model});
+  for (const BlockOffsets& bo : L.blocks) b.push_back({bo.attn_norm, bo.down + c.d_ff * c.d_model});
+  b.push_back({L.final_norm, L.total});
+  return b;
+}
+
+std::vector<uint64_t> shard_bounds(uint64_t total, int world, uint64_t block, int blocks) {
+  std::vector<uint64_t> bounds(world + 1, total);
+  for (int r = 0; r < world; ++r)
+    bounds[r] = std::min<uint64_t>(total, block * ((static_cast<uint64_t>(blocks) * r) / world));
+  return bounds;
+}
+
 ParamLayout param_layout(const ModelConfig& c) {
   ParamLayout L;
   uint64_t off = 0;

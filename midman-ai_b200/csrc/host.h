@@ -50,6 +50,14 @@ struct ParamLayout {
 };
 ParamLayout param_layout(const ModelConfig& c);
 
+// The flat ranges a data-parallel step exchanges as one bucket, in forward order:
+// the embedding, each block, the final norm (and an untied head).
+std::vector<std::pair<uint64_t, uint64_t>> gradient_buckets(const ModelConfig& c, const ParamLayout& L);
+// Optimizer sharding: rank r owns [bounds[r], bounds[r + 1]) of the flat vector.
+// The bounds are multiples of `block` elements (the gradient norm's fixed grid
+// block), about total / world apart.
+std::vector<uint64_t> shard_bounds(uint64_t total, int world, uint64_t block, int blocks);
+
 // crates/midman-foundation/src/rng.rs:16-119 (xoshiro256** seeded by SplitMix64,
 // Box-Muller normals with a cached second value).
 class HostRng {

@@ -58,11 +58,7 @@ Trainer::Trainer(const ModelConfig& cfg, int batch, int seq, int precision, int 
     for (auto& e : gathered_) check_cuda(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "event");
     check_cuda(cudaEventCreateWithFlags(&update_done_, cudaEventDisableTiming), "event");
   }
-  // gradient buckets in forward order: embedding, blocks, final norm (+ untied head)
-  buckets_.push_back({layout_.embed, layout_.embed + cfg.vocab * cfg.d_model});
-  for (const BlockOffsets& bo : layout_.blocks)
-    buckets_.push_back({bo.attn_norm, bo.down + cfg.d_ff * cfg.d_model});
-  buckets_.push_back({layout_.final_norm, layout_.total});
+  buckets_ = gradient_buckets(cfg, layout_);
 
   auto alloc = [&](size_t bytes) {
     void* p = nullptr;
@@ -222,10 +218,8 @@ void Trainer::shard_optimizer(bool on) {
   };
   if (on) {
     // ranges end on blocks of the fixed norm grid, so each block's partial is one rank's
-    const uint64_t per = static_cast<uint64_t>(norm_block_elems(static_cast<long long>(total)));
-    bounds_.assign(world_ + 1, total);
-    for (int r = 0; r < world_; ++r)
-      bounds_[r] = std::min<uint64_t>(total, per * ((static_cast<uint64_t>(kNormBlocks) * r) / world_));
+    bounds_ = shard_bounds(total, world_, static_cast<uint64_t>(norm_block_elems(static_cast<long long>(total))),
+                           kNormBlocks);
     const uint64_t lo = bounds_[rank_], n = bounds_[rank_ + 1] - lo;
     float* m = falloc(n);
     float* v = falloc(n);

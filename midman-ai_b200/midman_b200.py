@@ -30,7 +30,7 @@ API_SYMBOLS = [
     "midman_batcher_next", "midman_batcher_destroy", "midman_train_save", "midman_train_restore",
     "midman_state_inspect", "midman_shard_inspect", "midman_batcher_open", "midman_batcher_seek", "midman_train_run",
     "midman_shard_read", "midman_shard_write", "midman_sha256", "midman_train_evaluate",
-    "midman_train_shard_optimizer",
+    "midman_train_shard_optimizer", "midman_shard_plan",
 ]
 STATUS = {0: "OK", 1: "STOPPED", -1: "ARGUMENT", -2: "CONFIG", -3: "SHAPE", -4: "INDEX", -5: "OTHER",
           -6: "DEVICE", -99: "PANIC"}
@@ -114,6 +114,7 @@ def load(path: str | os.PathLike | None = None) -> C.CDLL:
     _sig(lib, "midman_sha256", i32, u8p, C.c_uint64, u8p)
     _sig(lib, "midman_train_evaluate", i32, u32, u8p, u32, C.c_uint64)
     _sig(lib, "midman_train_shard_optimizer", i32, u32, u32)
+    _sig(lib, "midman_shard_plan", i32, dp, u32)
     _lib = lib
     return lib
 
@@ -268,6 +269,13 @@ def sha256(data: bytes) -> bytes:
     out = (C.c_uint8 * 32)()
     api(load().midman_sha256(buf, len(data), out))
     return bytes(out)
+
+
+def shard_plan(cfg, world: int) -> dict:
+    """midman_shard_plan: optimizer-sharding ranges and gradient buckets (no GPU)."""
+    c = _np.ascontiguousarray(cfg, _np.float64)
+    api(load().midman_shard_plan(_dp(c), world))
+    return _json.loads(text())
 
 
 def state_inspect(path) -> dict:
