@@ -54,10 +54,11 @@ Trainer::Trainer(const ModelConfig& cfg, int batch, int seq, int precision, int 
     layer_done_.resize(cfg.n_layers + 1);
     for (auto& e : layer_done_) check_cuda(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "event");
     check_cuda(cudaEventCreateWithFlags(&comm_done_, cudaEventDisableTiming), "event");
-    gathered_.resize(cfg.n_layers + 2);
-    for (auto& e : gathered_) check_cuda(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "event");
-    check_cuda(cudaEventCreateWithFlags(&update_done_, cudaEventDisableTiming), "event");
   }
+  // per bucket: its parameters are final (updated, or broadcast by their owner)
+  gathered_.resize(cfg.n_layers + 2);
+  for (auto& e : gathered_) check_cuda(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "event");
+  check_cuda(cudaEventCreateWithFlags(&update_done_, cudaEventDisableTiming), "event");
   buckets_ = gradient_buckets(cfg, layout_);
 
   auto alloc = [&](size_t bytes) {
@@ -195,6 +196,13 @@ void Trainer::build_chunks() {
                         t.shape.size() >= 2 ? 1 : 0});
   }
   n_chunks_ = static_cast<int>(chunks.size());
+  // the chunks of each bucket (buckets are unions of whole tensors; chunks come in order)
+  bucket_chunks_.assign(buckets_.size(), {0, 0});
+  for (size_t b = 0, c = 0; b < buckets_.size(); ++b) {
+    bucket_chunks_[b].first = static_cast<int>(c);
+    while (c < chunks.size() && static_cast<uint64_t>(chunks[c].offset) < buckets_[b].second) ++c;
+    bucket_chunks_[b].second = static_cast<int>(c);
+  }
   if (n_chunks_)
     check_cuda(cudaMemcpy(d_chunks_, chunks.data(), chunks.size() * sizeof(AdamChunk), cudaMemcpyHostToDevice),
                "chunks");

@@ -168,6 +168,7 @@ class Trainer {
   cudaEvent_t update_done_ = nullptr;
   AdamChunk* d_chunks_ = nullptr;
   int n_chunks_ = 0;
+  std::vector<std::pair<int, int>> bucket_chunks_;  // [first, end) chunk of each bucket (unsharded)
   float *d_cos_ = nullptr, *d_sin_ = nullptr;
 
   // token ids and the embedding-gradient CSR

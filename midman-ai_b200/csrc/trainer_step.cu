@@ -242,10 +242,26 @@ void Trainer::finish_launch(float lr, const AdamHyper& h, bool update) {
     const float bias1 = static_cast<float>(1.0 - std::pow(static_cast<double>(h.beta1), t));
     const float bias2_sqrt = static_cast<float>(std::sqrt(1.0 - std::pow(static_cast<double>(h.beta2), t)));
     const float step_size = lr / bias1;
-    adamw_step(d_chunks_, n_chunks_, P_, G_, M_, V_, static_cast<long long>(mv_begin()), d_norm_, lr, h.beta1,
-               h.beta2, h.eps, h.weight_decay, step_size, bias2_sqrt, stream_);
-    launches_ += 1;
-    if (zero1_ && world_ > 1) broadcast_params();
+    if (!zero1_ && side_stream_ && !profiling_) {
+      // Bucket by bucket on the side stream, each bucket's event the next
+      // forward's wait (wait_params): the HBM-bound update of the later buckets
+      // runs beside the tensor-bound forward of the first layers.
+      check_cuda(cudaEventRecord(update_done_, stream_), "event");
+      check_cuda(cudaStreamWaitEvent(side_stream_, update_done_, 0), "wait");
+      for (size_t b = 0; b < bucket_chunks_.size(); ++b) {
+        const int c0 = bucket_chunks_[b].first, n = bucket_chunks_[b].second - c0;
+        adamw_step(d_chunks_ + c0, n, P_, G_, M_, V_, 0, d_norm_, lr, h.beta1, h.beta2, h.eps, h.weight_decay,
+                   step_size, bias2_sqrt, side_stream_);
+        check_cuda(cudaEventRecord(gathered_[b], side_stream_), "event");
+        launches_ += n > 0 ? 1 : 0;
+      }
+      gather_pending_ = true;
+    } else {
+      adamw_step(d_chunks_, n_chunks_, P_, G_, M_, V_, static_cast<long long>(mv_begin()), d_norm_, lr, h.beta1,
+                 h.beta2, h.eps, h.weight_decay, step_size, bias2_sqrt, stream_);
+      launches_ += 1;
+      if (zero1_ && world_ > 1) broadcast_params();
+    }
   }
   check_cuda(cudaMemcpyAsync(h_out_, d_loss_, sizeof(double), cudaMemcpyDeviceToHost, stream_), "loss D2H");
   check_cuda(cudaMemcpyAsync(h_out_ + 2, d_norm_, 3 * sizeof(float), cudaMemcpyDeviceToHost, stream_), "norm D2H");
