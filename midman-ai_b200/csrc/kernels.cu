@@ -265,20 +265,21 @@ __global__ void rope_kernel(float* x, int rows, int T, int heads, int half, long
 }
 
 // Four consecutive i per thread (half % 4 == 0, 16-byte aligned rows and tables).
-__global__ void rope4_kernel(float* x, int rows, int T, int heads, int half, long long ld,
-                             const float* __restrict__ cos_t, const float* __restrict__ sin_t, float sign) {
+// One block per row (token): thread j of the row's heads * half / 4 handles
+// four pairs (x[i], x[i + half]) of one head; the row's position picks the table row.
+__global__ void rope4_kernel(float* x, int T, int heads, int half, long long ld, const float* __restrict__ cos_t,
+                             const float* __restrict__ sin_t, float sign) {
   const int q4 = half / 4;
-  const long long total = static_cast<long long>(rows) * heads * q4;
-  for (long long idx = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; idx < total;
-       idx += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const int i = static_cast<int>(idx % q4) * 4;
-    const long long rh = idx / q4;
-    const int h = static_cast<int>(rh % heads);
-    const long long r = rh / heads;
-    const int t = static_cast<int>(r % T);
-    float* v = x + r * ld + static_cast<long long>(h) * 2 * half;
-    const float4 c = *reinterpret_cast<const float4*>(cos_t + static_cast<long long>(t) * half + i);
-    const float4 sn = *reinterpret_cast<const float4*>(sin_t + static_cast<long long>(t) * half + i);
+  const long long r = blockIdx.x;
+  const int t = static_cast<int>(r % T);
+  const float* ct = cos_t + static_cast<long long>(t) * half;
+  const float* st = sin_t + static_cast<long long>(t) * half;
+  float* row = x + r * ld;
+  for (int j = threadIdx.x; j < heads * q4; j += blockDim.x) {
+    const int h = j / q4, i = (j - h * q4) * 4;
+    float* v = row + static_cast<long long>(h) * 2 * half;
+    const float4 c = *reinterpret_cast<const float4*>(ct + i);
+    const float4 sn = *reinterpret_cast<const float4*>(st + i);
     const float4 a = *reinterpret_cast<const float4*>(v + i), b = *reinterpret_cast<const float4*>(v + i + half);
     const float s0 = sign * sn.x, s1 = sign * sn.y, s2 = sign * sn.z, s3 = sign * sn.w;
     *reinterpret_cast<float4*>(v + i) =
@@ -559,12 +560,14 @@ void rope(float* x, int rows, int T, int heads, int hd, long long ld, const floa
   const long long total = static_cast<long long>(rows) * heads * (hd / 2);
   if (total <= 0) return;
   const bool vec = (hd / 2) % 4 == 0 && ld % 4 == 0 && aligned16(x) && aligned16(cos_t) && aligned16(sin_t);
-  if (vec)
-    rope4_kernel<<<grid_for(total / 4, 2), kThreads, 0, s>>>(x, rows, T, heads, hd / 2, ld, cos_t, sin_t,
-                                                           backward ? -1.0f : 1.0f);
-  else
+  if (vec) {
+    const int per_row = heads * (hd / 8);  // float4 pairs per row
+    const int threads = per_row >= 1024 ? 1024 : (per_row + 31) / 32 * 32;
+    rope4_kernel<<<rows, threads, 0, s>>>(x, T, heads, hd / 2, ld, cos_t, sin_t, backward ? -1.0f : 1.0f);
+  } else {
     rope_kernel<<<grid_for(total, 1), kThreads, 0, s>>>(x, rows, T, heads, hd / 2, ld, cos_t, sin_t,
                                                          backward ? -1.0f : 1.0f);
+  }
   check_launch("rope");
 }
 
