@@ -259,6 +259,14 @@ def gemm_shapes(prof, steps, top=10):
             for k, v in rows if v["ms"] > 0]
 
 
+def workload_config(args, cfg, B, T, world):
+    """The `config` of both arms' JSON lines (the reference arm times the same workload)."""
+    optimizer = args.optimizer if args.optimizer != "auto" else ("sharded" if world > 1 else "replicated")
+    return {"workload": args.config, "preset": list(cfg), "batch_per_gpu": B, "global_batch": B * world,
+            "seq_len": T, "parallelism": f"dp{world}", "optimizer": optimizer,
+            "l2": "no flush: the step's working set (weights, moments, activations) is far above the 126 MB L2"}
+
+
 def run_reference(args, cfg, B, T, world, rank):
     if rank != 0:
         return 0
@@ -267,7 +275,7 @@ def run_reference(args, cfg, B, T, world, rank):
     line = {"impl": "reference", "metric": "train tokens/s (fwd+bwd+AdamW)", "value": value, "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": args.config, "preset": list(cfg), "global_batch": B * world, "seq_len": T},
+            "config": workload_config(args, cfg, B, T, world),
             "cpu_baseline": cb,
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -416,10 +424,7 @@ def main():
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "tf32" if precision == 0 else "3xtf32",
             "data": "synthetic uniform token ids (Rng(0).below(vocab)), seeded init",
-            "config": {"workload": args.config, "preset": list(cfg), "batch_per_gpu": B, "global_batch": B * world,
-                       "seq_len": T, "parallelism": f"dp{world}", "optimizer": args.optimizer,
-                       "l2": "no flush: the step's working set (weights, moments, activations) is far above the "
-                             "126 MB L2"},
+            "config": workload_config(args, cfg, B, T, world),
             "loss_first_last": [float(rec[0, 0]), float(rec[-1, 0])],
             "roofline": {"bound": "tensor", "kernel": gk, "achieved": achieved, "peak": tf32, "unit": "TFLOP/s",
                          "frac": (achieved / tf32) if achieved else None,
