@@ -512,12 +512,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot_ptr;
 
-  // The unit after `cur` for this pair: strided, or the next ticket. A pair's
-  // last (failing) ticket counts it as finished; the last pair to finish resets
-  // the counter for the next launch on the stream.
-  auto next_unit = [&](int cur) -> int {
-    if (!sched) return cur + npairs < total_units ? cur + npairs : -1;
-    const int v = npairs + static_cast<int>(atomicAdd(&sched[0], 1u));
+  // Tickets: the leader takes the ticket of its next unit one unit ahead (the
+  // atomic's latency hides behind the current unit's loads). A ticket past the
+  // last unit ends the pair and counts it as finished; the last pair to finish
+  // resets the counter for the next launch on the stream.
+  auto take_ticket = [&]() -> unsigned { return atomicAdd(&sched[0], 1u); };
+  auto unit_of_ticket = [&](unsigned ticket) -> int {
+    const int v = npairs + static_cast<int>(ticket);
     if (v < total_units) return v;
     __threadfence();
     if (atomicAdd(&sched[1], 1u) == static_cast<unsigned>(npairs - 1)) {
@@ -534,6 +535,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       int it = 0, ring_i = 0;
       bool ok = true;
       int u = leader ? pair : -1;
+      unsigned ticket = (leader && sched) ? take_ticket() : 0u;  // the unit after u
       for (;;) {
         const int rs = ring_i % kUnitRing, rr = ring_i / kUnitRing;
         if (leader) {  // publish this unit (or the end) to the pair
@@ -597,13 +599,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           *loads_issued = it + 1;
         }
         if (!ok) break;
-        if (leader) u = next_unit(u);
+        if (leader) {
+          if (!sched) {
+            u = u + npairs < total_units ? u + npairs : -1;
+          } else {
+            u = unit_of_ticket(ticket);
+            if (u >= 0) ticket = take_ticket();
+          }
+        }
       }
       // keep the ticket protocol whole after a timed-out wait: take tickets
       // until this pair's last one
-      if (leader && sched && u >= 0)
-        while (next_unit(u) >= 0) {
-        }
+      if (leader && sched && u >= 0) {
+        while ((u = unit_of_ticket(ticket)) >= 0) ticket = take_ticket();
+      }
     }
   } else if (warp == 1) {
     if (lane == 0 && leader) {
