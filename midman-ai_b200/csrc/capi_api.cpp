@@ -1169,13 +1169,15 @@ int32_t midman_train_run(uint32_t handle, uint32_t batcher, uint32_t steps) {
       tr.prepare_batch(in.data() + r * rows, tg.data() + r * rows, B, T, slot);
     };
     auto put_back = [&](int slot) { b.seek(before[slot].first, before[slot].second); };
-    try {
-      take(0);
-    } catch (...) {
-      put_back(0);
-      throw;
+    if (steps > 0) {
+      try {
+        take(0);
+      } catch (...) {
+        put_back(0);
+        throw;
+      }
+      tr.upload_prepared(0, B, T, true);
     }
-    tr.upload_prepared(0, B, T, true);
     for (uint32_t s = 0; s < steps; ++s) {
       const int cur = s & 1, nxt = cur ^ 1;
       const float lr = schedule_lr(t.hyper.max_lr, t.hyper.min_lr, t.hyper.warmup, t.hyper.total, t.step);

@@ -122,6 +122,18 @@ def test_a_run_resumes_from_its_state_file_and_batcher_place(mm, tmp_path):
         h.close()
 
 
+def test_zero_steps_take_no_batch(mm, tmp_path):
+    paths = shards(tmp_path, [300], seed=6)
+    t = trainer(mm)
+    b = mm.Batcher(shards=paths, seq=T, batch=B, seed=1)
+    rec, status, place = t.run(b, 0)
+    assert status == 0 and rec.shape == (0, 3) and (place["epoch"], place["position"]) == (0, 0)
+    fresh = mm.Batcher(shards=paths, seq=T, batch=B, seed=1)
+    assert np.array_equal(b.next()[0], fresh.next()[0])
+    for h in (t, b, fresh):
+        h.close()
+
+
 def test_the_batcher_must_fit_the_run(mm, tmp_path):
     paths = shards(tmp_path, [300], seed=3)
     t = trainer(mm)
