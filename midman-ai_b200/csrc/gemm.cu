@@ -457,6 +457,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   const int pair = static_cast<int>(blockIdx.x) / 2, npairs = static_cast<int>(gridDim.x) / 2;
   const int tm = (M + 2 * BM - 1) / (2 * BM);
   const int n_k = ops.seg_end[ops.nseg - 1];
+  // The segments' bounds, tensor maps and box flags in registers, read once:
+  // segment g covers K steps [seg_end[g-1], seg_end[g]); bounds past nseg are
+  // n_k, so steps never select a segment that does not exist.
+  static_assert(kMaxSegments == 3, "the selects below assume three segments");
+  const int seg_end0 = ops.nseg > 1 ? ops.seg_end[0] : n_k;
+  const int seg_end1 = ops.nseg > 2 ? ops.seg_end[1] : n_k;
+  const CUtensorMap* map_a0 = &ops.a[0];
+  const CUtensorMap* map_a1 = &ops.a[1];
+  const CUtensorMap* map_a2 = &ops.a[2];
+  const CUtensorMap* map_b0 = &ops.b[0];
+  const CUtensorMap* map_b1 = &ops.b[1];
+  const CUtensorMap* map_b2 = &ops.b[2];
+  const int mn3d0 = ops.mn3d[0], mn3d1 = ops.mn3d[1], mn3d2 = ops.mn3d[2];
   const int total_units = full_tiles + (total_tiles - full_tiles) * splits;
 
   extern __shared__ uint8_t smem_raw[];
@@ -574,12 +587,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           if (leader) mbar_arrive_expect_tx(full_bar(s), 2 * Cfg::STAGE);
           const uint32_t fb = mapa_shared(full_bar(s), 0);
           const uint32_t sa = base + s * Cfg::STAGE, sb = sa + A_STAGE_BYTES;
-          int g = 0;  // the segment of K step i
-          while (g + 1 < ops.nseg && i >= ops.seg_end[g]) ++g;
-          const int k0 = (i - (g > 0 ? ops.seg_end[g - 1] : 0)) * BK;
-          const CUtensorMap* tmA = &ops.a[g];
-          const CUtensorMap* tmB = &ops.b[g];
-          const int mn3d = ops.mn3d[g];
+          // the segment of K step i, from registers (selects, no parameter loads)
+          const int g = (i >= seg_end0 ? 1 : 0) + (i >= seg_end1 ? 1 : 0);
+          const int k0 = (i - (g == 0 ? 0 : g == 1 ? seg_end0 : seg_end1)) * BK;
+          const CUtensorMap* tmA = g == 0 ? map_a0 : g == 1 ? map_a1 : map_a2;
+          const CUtensorMap* tmB = g == 0 ? map_b0 : g == 1 ? map_b1 : map_b2;
+          const int mn3d = g == 0 ? mn3d0 : g == 1 ? mn3d1 : mn3d2;
           if (!A_MN) {
             tma_load_2d_pair(sa, tmA, fb, k0, my_m0);
           } else if (mn3d & 1) {
