@@ -470,6 +470,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   const CUtensorMap* map_b1 = &ops.b[1];
   const CUtensorMap* map_b2 = &ops.b[2];
   const int mn3d0 = ops.mn3d[0], mn3d1 = ops.mn3d[1], mn3d2 = ops.mn3d[2];
+  const bool single = ops.nseg == 1;
   const int total_units = full_tiles + (total_tiles - full_tiles) * splits;
 
   extern __shared__ uint8_t smem_raw[];
@@ -587,27 +588,33 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           if (leader) mbar_arrive_expect_tx(full_bar(s), 2 * Cfg::STAGE);
           const uint32_t fb = mapa_shared(full_bar(s), 0);
           const uint32_t sa = base + s * Cfg::STAGE, sb = sa + A_STAGE_BYTES;
-          // the segment of K step i, from registers (selects, no parameter loads)
-          const int g = (i >= seg_end0 ? 1 : 0) + (i >= seg_end1 ? 1 : 0);
-          const int k0 = (i - (g == 0 ? 0 : g == 1 ? seg_end0 : seg_end1)) * BK;
-          const CUtensorMap* tmA = g == 0 ? map_a0 : g == 1 ? map_a1 : map_a2;
-          const CUtensorMap* tmB = g == 0 ? map_b0 : g == 1 ? map_b1 : map_b2;
-          const int mn3d = g == 0 ? mn3d0 : g == 1 ? mn3d1 : mn3d2;
-          if (!A_MN) {
-            tma_load_2d_pair(sa, tmA, fb, k0, my_m0);
-          } else if (mn3d & 1) {
-            tma_load_3d_pair(sa, tmA, fb, 0, k0, my_m0 / 32);
-          } else {
+          // One (A, B) pair: the tensor maps are addressed in the kernel's parameter
+          // space directly. Several: the segment of K step i from registers.
+          auto issue = [&](const CUtensorMap* tmA, const CUtensorMap* tmB, int mn3d, int k0) {
+            if (!A_MN) {
+              tma_load_2d_pair(sa, tmA, fb, k0, my_m0);
+            } else if (mn3d & 1) {
+              tma_load_3d_pair(sa, tmA, fb, 0, k0, my_m0 / 32);
+            } else {
 #pragma unroll
-            for (int j = 0; j < BM / 32; ++j) tma_load_2d_pair(sa + j * MN_BLOCK_BYTES, tmA, fb, my_m0 + 32 * j, k0);
-          }
-          if (!B_MN) {
-            tma_load_2d_pair(sb, tmB, fb, k0, my_n0);
-          } else if (mn3d & 2) {
-            tma_load_3d_pair(sb, tmB, fb, 0, k0, my_n0 / 32);
-          } else {
+              for (int j = 0; j < BM / 32; ++j) tma_load_2d_pair(sa + j * MN_BLOCK_BYTES, tmA, fb, my_m0 + 32 * j, k0);
+            }
+            if (!B_MN) {
+              tma_load_2d_pair(sb, tmB, fb, k0, my_n0);
+            } else if (mn3d & 2) {
+              tma_load_3d_pair(sb, tmB, fb, 0, k0, my_n0 / 32);
+            } else {
 #pragma unroll
-            for (int j = 0; j < PN / 64; ++j) tma_load_2d_pair(sb + j * MN_BLOCK_BYTES, tmB, fb, my_n0 + 32 * j, k0);
+              for (int j = 0; j < PN / 64; ++j)
+                tma_load_2d_pair(sb + j * MN_BLOCK_BYTES, tmB, fb, my_n0 + 32 * j, k0);
+            }
+          };
+          if (single) {
+            issue(&ops.a[0], &ops.b[0], mn3d0, i * BK);
+          } else {
+            const int g = (i >= seg_end0 ? 1 : 0) + (i >= seg_end1 ? 1 : 0);
+            issue(g == 0 ? map_a0 : g == 1 ? map_a1 : map_a2, g == 0 ? map_b0 : g == 1 ? map_b1 : map_b2,
+                  g == 0 ? mn3d0 : g == 1 ? mn3d1 : mn3d2, (i - (g == 0 ? 0 : g == 1 ? seg_end0 : seg_end1)) * BK);
           }
           *loads_issued = it + 1;
         }
