@@ -1,11 +1,13 @@
 """Checks that every known answer in reference_pins.json appears in the reference file it cites.
 
-Run in a checkout that has the reference tree (default /root/reference):
+Run where the reference tree is checked out (its directory as the argument, or in
+MIDMAN_REFERENCE_DIR):
     python tests/golden/check_provenance.py [REFERENCE_DIR]
 Numbers are compared by their digits (underscores removed, hex lower-cased), so a value
 pinned from `0x99ec_5f36_cb75_f2b4` or `0.602_082_3` is found.
 """
 import json
+import os
 import re
 import sys
 from pathlib import Path
@@ -64,4 +66,5 @@ def main(ref_dir):
 
 
 if __name__ == "__main__":
-    sys.exit(main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference"))
+    default = os.environ.get("MIDMAN_REFERENCE_DIR", "/root/reference")
+    sys.exit(main(sys.argv[1] if len(sys.argv) > 1 else default))
