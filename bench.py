@@ -249,7 +249,7 @@ def run_kernels(args):
     return 0
 
 
-GEMM_TRAFFIC_BYTES = 538e6  # see the roofline entry below
+GEMM_TRAFFIC_BYTES = 547e6  # see the roofline entry below
 
 
 def gemm_shapes(prof, steps, top=10):

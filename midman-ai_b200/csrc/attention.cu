@@ -12,7 +12,6 @@
 #include <cuda_runtime.h>
 
 #include <cmath>
-#include <cstdint>
 #include <stdexcept>
 #include <string>
 
@@ -163,16 +162,7 @@ __global__ void attn_delta_kernel(AttnShape s, const float* __restrict__ o, cons
   const float* orow = o + tok * s.ldo + static_cast<long long>(h) * s.hd;
   const float* drow = dout + tok * lddo + static_cast<long long>(h) * s.hd;
   float acc = 0.0f;
-  const bool vec = (s.hd & 3) == 0 && ((s.ldo | lddo) & 3) == 0 &&
-                   ((reinterpret_cast<uintptr_t>(o) | reinterpret_cast<uintptr_t>(dout)) & 15) == 0;
-  if (vec) {
-    for (int d = 4 * lane; d < s.hd; d += 128) {  // 128-bit loads: a warp reads 512 bytes of each row at once
-      const float4 a = *reinterpret_cast<const float4*>(orow + d), g = *reinterpret_cast<const float4*>(drow + d);
-      acc += ((a.x * g.x + a.y * g.y) + a.z * g.z) + a.w * g.w;
-    }
-  } else {
-    for (int d = lane; d < s.hd; d += 32) acc += orow[d] * drow[d];
-  }
+  for (int d = lane; d < s.hd; d += 32) acc += orow[d] * drow[d];
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
   if (lane == 0) delta[warp] = acc;
