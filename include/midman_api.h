@@ -139,6 +139,10 @@ MIDMAN_EXPORT int32_t midman_train_loss_and_grads(uint32_t handle, const int32_t
  * moments of tensor `index` in MidManModel::parameters order, or of the whole
  * flat vector when index == 0xFFFFFFFF. Numeric result: the values. */
 MIDMAN_EXPORT int32_t midman_train_read(uint32_t handle, uint32_t which, uint32_t index);
+/* midman_train_read with which = 0 (parameter values) and 1 (gradients): one
+ * tensor D2H for parity checks, or the whole vector with index 0xFFFFFFFF. */
+MIDMAN_EXPORT int32_t midman_train_params(uint32_t handle, uint32_t index);
+MIDMAN_EXPORT int32_t midman_train_grads(uint32_t handle, uint32_t index);
 /* Replaces every parameter (`len` must equal the parameter count). */
 MIDMAN_EXPORT int32_t midman_train_load(uint32_t handle, const float *values, uint64_t len);
 /* Text result: {"params":..,"steps":..,"kernel_launches":..,"tensors":[{"name":..,"shape":[..],"offset":..}]} */

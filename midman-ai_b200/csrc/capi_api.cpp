@@ -658,6 +658,10 @@ int32_t midman_train_read(uint32_t handle, uint32_t which, uint32_t index) {
   });
 }
 
+int32_t midman_train_params(uint32_t handle, uint32_t index) { return midman_train_read(handle, 0, index); }
+
+int32_t midman_train_grads(uint32_t handle, uint32_t index) { return midman_train_read(handle, 1, index); }
+
 int32_t midman_train_load(uint32_t handle, const float* values, uint64_t len) {
   return run([&] {
     Train& t = train_ref(handle);

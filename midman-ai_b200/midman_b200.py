@@ -30,7 +30,7 @@ API_SYMBOLS = [
     "midman_batcher_next", "midman_batcher_destroy", "midman_train_save", "midman_train_restore",
     "midman_state_inspect", "midman_shard_inspect", "midman_batcher_open", "midman_batcher_seek", "midman_train_run",
     "midman_shard_read", "midman_shard_write", "midman_sha256", "midman_train_evaluate",
-    "midman_train_shard_optimizer", "midman_shard_plan",
+    "midman_train_shard_optimizer", "midman_shard_plan", "midman_train_params", "midman_train_grads",
 ]
 STATUS = {0: "OK", 1: "STOPPED", -1: "ARGUMENT", -2: "CONFIG", -3: "SHAPE", -4: "INDEX", -5: "OTHER",
           -6: "DEVICE", -99: "PANIC"}
@@ -115,6 +115,8 @@ def load(path: str | os.PathLike | None = None) -> C.CDLL:
     _sig(lib, "midman_train_evaluate", i32, u32, u8p, u32, C.c_uint64)
     _sig(lib, "midman_train_shard_optimizer", i32, u32, u32)
     _sig(lib, "midman_shard_plan", i32, dp, u32)
+    _sig(lib, "midman_train_params", i32, u32, u32)
+    _sig(lib, "midman_train_grads", i32, u32, u32)
     _lib = lib
     return lib
 

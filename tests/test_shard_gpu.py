@@ -202,3 +202,18 @@ def test_evaluation_refuses_what_does_not_fit(mm, tmp_path):
             t.evaluate(*args)
         assert e.value.status == -1 and mention in e.value.message, (args, e.value.message)
     t.close()
+
+
+def test_params_and_grads_entry_points_read_one_tensor(mm, tmp_path):
+    # midman_train_params / midman_train_grads: midman_train_read with which = 0 / 1
+    t = trainer(mm)
+    x = (np.arange(B * T) % 64).astype(np.int32)
+    t.loss_and_grads(x, x[::-1].copy())
+    lib = mm.load()
+    for i in (0, 3):
+        assert lib.midman_train_params(t.h, i) == 0
+        assert np.array_equal(mm.floats(), t.read(0, i))
+        assert lib.midman_train_grads(t.h, i) == 0
+        assert np.array_equal(mm.floats(), t.read(1, i))
+    assert lib.midman_train_grads(t.h, 10**6) == -4  # MIDMAN_ERR_INDEX
+    t.close()
