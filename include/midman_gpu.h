@@ -61,6 +61,20 @@ MM_GPU_EXPORT int32_t mm_gpu_device_status(void *stream);
 MM_GPU_EXPORT int32_t mm_gpu_gemm(int32_t m, int32_t n, int32_t k, const float *a, int64_t lda, int32_t a_mn_major,
                     const float *b, int64_t ldb, int32_t b_mn_major, float *c, int64_t ldc,
                     const float *r, int64_t ldr, int32_t precision, void *stream);
+/* Global-norm clip and one AdamW step over n_tensors tensors stored one after
+ * another in the device arrays p, g, m, v (crates/midman-optim/src/clip.rs:29-59,
+ * adamw.rs:141-217): the gradient norm in f64 over a fixed grid (deterministic),
+ * gradients scaled by max_norm / (norm + 1e-6) when the norm exceeds max_norm,
+ * decoupled decay for the tensors with decay[i] != 0 (the reference decays rank
+ * >= 2 tensors), bias corrections in f64 for `step` (1 for the first update).
+ * When the norm is not finite nothing changes. norm_out (host, 3 floats):
+ * [norm, clip factor, 1 if the update was applied]. Every tensor but the last
+ * must hold a multiple of 4 values. Synchronizes the stream. */
+MM_GPU_EXPORT int32_t mm_gpu_clip_adamw(int32_t n_tensors, const int64_t *numel, const int32_t *decay, float *p,
+                                        const float *g, float *m, float *v, double max_norm, double lr, double beta1,
+                                        double beta2, double eps, double weight_decay, uint64_t step,
+                                        float *norm_out, void *stream);
+
 /* TF32 sum of products: C = sum over g < nseg of A_g(m, k[g]) B_g(n, k[g])^T (+R),
  * all A_g with one majorness and all B_g with one, summed in one accumulator by a
  * single launch when the shape runs on CTA pairs and nseg <= 3 (otherwise one

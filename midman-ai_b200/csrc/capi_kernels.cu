@@ -12,6 +12,7 @@
 #include "attention.h"
 #include "device.h"
 #include "gemm.h"
+#include "kernels.h"
 
 namespace {
 thread_local std::string g_last_error;
@@ -60,6 +61,55 @@ int32_t mm_gpu_gemm(int32_t m, int32_t n, int32_t k, const float* a, int64_t lda
                        ? mm::gemm_tf32(m, n, k, A, B, c, ldc, r, ldr, ctx.d_err, as_stream(stream))
                        : mm::gemm_3xtf32(m, n, k, A, B, c, ldc, r, ldr, ctx.d_err, as_stream(stream));
     if (rc) return fail(rc == mm::kGemmLaunch ? MM_GPU_ERR_DEVICE : MM_GPU_ERR_ARGUMENT, mm::gemm_status_string(rc));
+    return MM_GPU_OK;
+  });
+}
+
+int32_t mm_gpu_clip_adamw(int32_t n_tensors, const int64_t* numel, const int32_t* decay, float* p, const float* g,
+                          float* m, float* v, double max_norm, double lr, double beta1, double beta2, double eps,
+                          double weight_decay, uint64_t step, float* norm_out, void* stream) {
+  return guarded([&]() -> int32_t {
+    if (n_tensors < 0 || (n_tensors > 0 && (!numel || !decay || !p || !g || !m || !v)) || !norm_out)
+      return fail(MM_GPU_ERR_ARGUMENT, "clip_adamw: null pointer or negative tensor count");
+    if (step == 0) return fail(MM_GPU_ERR_ARGUMENT, "clip_adamw: step counts from 1");
+    if (!(std::isfinite(lr) && lr >= 0.0) || !(std::isfinite(max_norm) && max_norm > 0.0))
+      return fail(MM_GPU_ERR_ARGUMENT, "clip_adamw: lr and max_norm must be finite (max_norm positive)");
+    // chunks of at most 16,384 elements inside one tensor, decay for the flagged ones
+    std::vector<mm::AdamChunk> chunks;
+    long long total = 0;
+    for (int32_t i = 0; i < n_tensors; ++i) {
+      if (numel[i] < 0) return fail(MM_GPU_ERR_ARGUMENT, "clip_adamw: negative tensor size");
+      for (long long o = 0; o < numel[i]; o += 16384)
+        chunks.push_back({total + o, static_cast<int>(numel[i] - o < 16384 ? numel[i] - o : 16384), decay[i] ? 1 : 0});
+      total += numel[i];
+    }
+    // tensors start on 16-byte boundaries (the update reads four floats at a time)
+    for (const mm::AdamChunk& c : chunks)
+      if (c.offset % 4)
+        return fail(MM_GPU_ERR_ARGUMENT, "clip_adamw: every tensor but the last must hold a multiple of 4 values");
+    const cudaStream_t st = as_stream(stream);
+    const size_t chunk_bytes = chunks.size() * sizeof(mm::AdamChunk);
+    const size_t part_bytes = mm::kNormBlocks * sizeof(double);
+    uint8_t* ws = static_cast<uint8_t*>(mm::device_scratch(part_bytes + 256 + chunk_bytes, st));
+    double* partials = reinterpret_cast<double*>(ws);
+    float* d_norm = reinterpret_cast<float*>(ws + part_bytes);
+    mm::AdamChunk* d_chunks = reinterpret_cast<mm::AdamChunk*>(ws + part_bytes + 256);
+    if (!chunks.empty())
+      mm::check_cuda(cudaMemcpyAsync(d_chunks, chunks.data(), chunk_bytes, cudaMemcpyHostToDevice, st), "chunks");
+    // clip.rs:29-59 (f64 sum of squares, scale by max/(norm+1e-6) above max) and
+    // adamw.rs:141-217 (bias corrections in f64 for this step; nothing changes
+    // when the norm is not finite)
+    mm::sumsq_partials(g, total, partials, st);
+    mm::finish_norm(partials, nullptr, static_cast<float>(max_norm), d_norm, st);
+    const double t = static_cast<double>(step);
+    const float bias1 = static_cast<float>(1.0 - std::pow(beta1, t));
+    const float bias2_sqrt = static_cast<float>(std::sqrt(1.0 - std::pow(beta2, t)));
+    const float flr = static_cast<float>(lr);
+    mm::adamw_step(d_chunks, static_cast<int>(chunks.size()), p, g, m, v, 0, d_norm, flr, static_cast<float>(beta1),
+                   static_cast<float>(beta2), static_cast<float>(eps), static_cast<float>(weight_decay), flr / bias1,
+                   bias2_sqrt, st);
+    mm::check_cuda(cudaMemcpyAsync(norm_out, d_norm, 3 * sizeof(float), cudaMemcpyDeviceToHost, st), "norm");
+    mm::check_cuda(cudaStreamSynchronize(st), "clip_adamw");
     return MM_GPU_OK;
   });
 }

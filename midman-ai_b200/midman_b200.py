@@ -15,7 +15,7 @@ LIB_PATH = HERE / "lib" / "libmidman_gpu.so"
 
 # Every symbol the public headers declare, grouped by header.
 GPU_SYMBOLS = [
-    "mm_gpu_last_error", "mm_gpu_device_status", "mm_gpu_gemm", "mm_gpu_gemm_sum", "mm_gpu_attention_forward",
+    "mm_gpu_last_error", "mm_gpu_device_status", "mm_gpu_gemm", "mm_gpu_gemm_sum", "mm_gpu_clip_adamw", "mm_gpu_attention_forward",
     "mm_gpu_attention_backward", "mm_gpu_attention_forward_noalloc",
 ]
 API_SYMBOLS = [
@@ -59,6 +59,8 @@ def load(path: str | os.PathLike | None = None) -> C.CDLL:
     _sig(lib, "mm_gpu_gemm", i32, i32, i32, i32, vp, i64, i32, vp, i64, i32, vp, i64, vp, i64, i32, vp)
     _sig(lib, "mm_gpu_gemm_sum", i32, i32, i32, i32, C.POINTER(vp), C.POINTER(i64), i32, C.POINTER(vp),
          C.POINTER(i64), i32, C.POINTER(C.c_int32), vp, i64, vp, i64, vp)
+    _sig(lib, "mm_gpu_clip_adamw", i32, i32, C.POINTER(i64), C.POINTER(C.c_int32), vp, vp, vp, vp, C.c_double,
+         C.c_double, C.c_double, C.c_double, C.c_double, C.c_double, C.c_uint64, f32p, vp)
     _sig(lib, "mm_gpu_attention_forward", i32, i32, i32, i32, i32, i32, vp, vp, vp, i64, i64, vp, vp, i32, vp)
     _sig(lib, "mm_gpu_attention_backward", i32, i32, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp, i64, i64, vp, vp,
          vp, i32, vp)
@@ -161,6 +163,17 @@ def gemm_sum(terms, c, *, m, n, ldc, a_mn_major, b_mn_major, r=None, ldr=0, stre
     ks = (C.c_int32 * g)(*[t[4] for t in terms])
     return check(load().mm_gpu_gemm_sum(m, n, g, a, lda, int(a_mn_major), b, ldb, int(b_mn_major), ks, _ptr(c), ldc,
                                         _ptr(r), ldr, _stream(stream)))
+
+
+def clip_adamw(p, g, m, v, numel, decay, *, max_norm, lr, beta1, beta2, eps, weight_decay, step, stream=None):
+    """mm_gpu_clip_adamw on torch CUDA tensors (flat, tensors one after another): [norm, factor, applied]."""
+    n = len(numel)
+    sizes = (C.c_int64 * max(n, 1))(*numel)
+    flags = (C.c_int32 * max(n, 1))(*[1 if d else 0 for d in decay])
+    out = (C.c_float * 3)()
+    check(load().mm_gpu_clip_adamw(n, sizes, flags, _ptr(p), _ptr(g), _ptr(m), _ptr(v), max_norm, lr, beta1, beta2,
+                                   eps, weight_decay, step, out, _stream(stream)))
+    return list(out)
 
 
 def attention_forward(q, k, v, o, lse, *, batch, seq, n_heads, n_kv_heads, head_dim, ldq, ldk, precision=0,
