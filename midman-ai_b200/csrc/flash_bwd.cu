@@ -638,8 +638,13 @@ __device__ __forceinline__ void pair_teardown(bool leader, const PairBars<STAGES
 }
 
 // ---------------- dK, dV (pair of 128-key tiles)
+// Two UMMA issuers in the leader: warp 1 issues each step's S^T and dP^T, warp
+// 10 its dV and dK products, so the many small UMMAs of a step are issued from
+// two threads.
+constexpr int KV_PAIR_THREADS = BTHREADS + 32;
+
 template <int HD>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(BTHREADS, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KV_PAIR_THREADS, 1)
     flash_bwd_kv_pair_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmQk,
                              const __grid_constant__ CUtensorMap tmDOk, const __grid_constant__ CUtensorMap tmQm,
                              const __grid_constant__ CUtensorMap tmDOm, BwdParams p) {
@@ -715,18 +720,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(BTHREADS, 1)
     }
   } else if (warp == 1) {
     if (lane == 0 && leader) {
-      // ---------------- UMMA issuer (leader only), M = 256 keys across the pair
+      // ---------------- UMMA issuer A (leader only), M = 256 keys across the pair:
+      // S^T and dP^T of every step
       constexpr uint32_t idesc_s = idesc_tf32(2 * TILE, PBLK_KV, false, false);
-      constexpr uint32_t idesc_g = idesc_tf32(2 * TILE, HD, false, true);
       const uint64_t dk0 = kmajor_desc(sK, TILE, 0);
       bool ok = mbar_wait(bars.tile_full(), 0, p.err, kErrWaitFull);
       if (ok) tl->tile_pending = 0;
       ok = ok && mbar_wait(bars.opnd_ready(), 0, p.err, kErrWaitAccum);
-      auto issue_s = [&](int t) -> bool {
+      for (int t = 0; ok && t < n_steps; ++t) {
         const int s = t % STAGES, bb = t & 1, u = t >> 1;
-        if (!mbar_wait(bars.full(s), (t / STAGES) & 1, p.err, kErrWaitFull)) return false;
+        if (!mbar_wait(bars.full(s), (t / STAGES) & 1, p.err, kErrWaitFull)) break;
         tl->consumed = t + 1;
-        if (u > 0 && !mbar_wait(bars.s_free(bb), (u - 1) & 1, p.err, kErrWaitAccum)) return false;
+        if (u > 0 && !mbar_wait(bars.s_free(bb), (u - 1) & 1, p.err, kErrWaitAccum)) break;
         tc_fence_after();
         const uint32_t st = stage(s);
         const uint64_t dq0 = kmajor_desc(st, PBLK_KV / 2, 0), ddo0 = kmajor_desc(st + Cfg::KV_HALF_K, PBLK_KV / 2, 0);
@@ -734,20 +739,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(BTHREADS, 1)
         for (int kk = 0; kk < HD / 8; ++kk)  // S^T = K Q^T
           umma_tf32_pair(tmem + s_col_of(bb, PBLK_KV), desc_add(dk0, kchunk_off(TILE, kk)),
                          desc_add(dq0, kchunk_off(PBLK_KV / 2, kk)), idesc_s, kk > 0 ? 1u : 0u);
-        if (u > 0 && !mbar_wait(bars.dp_free(bb), (u - 1) & 1, p.err, kErrWaitAccum)) return false;
+        if (u > 0 && !mbar_wait(bars.dp_free(bb), (u - 1) & 1, p.err, kErrWaitAccum)) break;
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < HD / 8; ++kk)  // dP^T = V dO^T, V in TMEM
           umma_tf32_ts_pair(tmem + dp_col_of(bb, PBLK_KV), tmem + Cfg::KV_OPND + kk * 8,
                             desc_add(ddo0, kchunk_off(PBLK_KV / 2, kk)), idesc_s, kk > 0 ? 1u : 0u);
         umma_commit_pair(bars.s_full(bb), 0x3);
-        return true;
-      };
-      if (ok) ok = issue_s(0);
-      for (int t = 0; ok && t < n_steps; ++t) {
-        if (t + 1 < n_steps && !issue_s(t + 1)) break;
+      }
+    }
+  } else if (warp == 10) {
+    if (lane == 0 && leader) {
+      // ---------------- UMMA issuer B (leader only): dV += P dO, dK += dS Q of every
+      // step once its softmax is done (which implies its S^T and dP^T completed)
+      constexpr uint32_t idesc_g = idesc_tf32(2 * TILE, HD, false, true);
+      for (int t = 0; t < n_steps; ++t) {
         const int s = t % STAGES, bb = t & 1;
         if (!mbar_wait(bars.p_full(bb), (t >> 1) & 1, p.err, kErrWaitAccum)) break;
+        if (!mbar_wait(bars.full(s), (t / STAGES) & 1, p.err, kErrWaitFull)) break;
         tc_fence_after();
         const uint32_t st = stage(s);
         const uint64_t ddom0 = mnmajor_desc_rows(st + 2 * Cfg::KV_HALF_K + Cfg::KV_HALF_M, PBLK_KV, 0);
@@ -1117,7 +1126,7 @@ void launch_bwd_pair(const AttnShape& s, const float* q, const float* k, const f
     set_smem(flash_bwd_kv_pair_kernel<HD>, Cfg::KV_SMEM);
     const long long grid = 2ll * n_pairs * pk.BHx;
     flash_bwd_kv_pair_kernel<HD>
-        <<<static_cast<unsigned>(grid), BTHREADS, Cfg::KV_SMEM, stream>>>(tk, tqk, tdok, tqm, tdom, pk);
+        <<<static_cast<unsigned>(grid), KV_PAIR_THREADS, Cfg::KV_SMEM, stream>>>(tk, tqk, tdok, tqm, tdom, pk);
   }
   {  // dQ
     CUtensorMap tq, tkk, tvk, tkm;
