@@ -640,11 +640,11 @@ __device__ __forceinline__ void pair_teardown(bool leader, const PairBars<STAGES
 // ---------------- dK, dV (pair of 128-key tiles)
 // Two UMMA issuers in the leader: warp 1 issues each step's S^T and dP^T, warp
 // 10 its dV and dK products, so the many small UMMAs of a step are issued from
-// two threads.
-constexpr int KV_PAIR_THREADS = BTHREADS + 32;
+// two threads (one issuer was the limit).
+constexpr int PAIR_BWD_THREADS = BTHREADS + 32;
 
 template <int HD>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KV_PAIR_THREADS, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PAIR_BWD_THREADS, 1)
     flash_bwd_kv_pair_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmQk,
                              const __grid_constant__ CUtensorMap tmDOk, const __grid_constant__ CUtensorMap tmQm,
                              const __grid_constant__ CUtensorMap tmDOm, BwdParams p) {
@@ -834,8 +834,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(KV_PAIR_THREADS, 1)
 }
 
 // ---------------- dQ (pair of 128-query tiles)
+// Two UMMA issuers in the leader as in the dK/dV kernel: warp 1 issues S and dP,
+// warp 10 the dQ products.
 template <int HD>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(BTHREADS, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PAIR_BWD_THREADS, 1)
     flash_bwd_q_pair_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKk,
                             const __grid_constant__ CUtensorMap tmVk, const __grid_constant__ CUtensorMap tmKm,
                             BwdParams p) {
@@ -906,19 +908,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(BTHREADS, 1)
     }
   } else if (warp == 1) {
     if (lane == 0 && leader) {
-      // ---------------- UMMA issuer (leader only), M = 256 queries across the pair
+      // ---------------- UMMA issuer A (leader only), M = 256 queries across the pair:
+      // S and dP of every key block
       constexpr uint32_t idesc_s = idesc_tf32(2 * TILE, PBLK_Q, false, false);
-      constexpr uint32_t idesc_g = idesc_tf32(2 * TILE, HD, false, true);
       const uint64_t dqt0 = kmajor_desc(sQ, TILE, 0);
       bool ok = mbar_wait(bars.tile_full(), 0, p.err, kErrWaitFull);
       if (ok) tl->tile_pending = 0;
       ok = ok && mbar_wait(bars.opnd_ready(), 0, p.err, kErrWaitAccum);
-      auto issue_s = [&](int j) -> bool {
+      for (int j = 0; ok && j < n_kv; ++j) {
         const int s = j % STAGES, bb = j & 1, u = j >> 1;
-        if (!mbar_wait(bars.full(s), (j / STAGES) & 1, p.err, kErrWaitFull)) return false;
+        if (!mbar_wait(bars.full(s), (j / STAGES) & 1, p.err, kErrWaitFull)) break;
         tl->consumed = j + 1;
-        // the S part was last read by the softmax of block j - 2, whose p_full
-        // this thread has already waited for; the dP part by dQ(j - 2)
+        // the S part was last read by the softmax of block j - 2 (its p_full), the
+        // dP part by dQ(j - 2) (dp_free)
+        if (u > 0 && !mbar_wait(bars.p_full(bb), (u - 1) & 1, p.err, kErrWaitAccum)) break;
         tc_fence_after();
         const uint32_t st = stage(s);
         const uint64_t dkk0 = kmajor_desc(st, PBLK_Q / 2, 0), dvk0 = kmajor_desc(st + Cfg::Q_HALF_K, PBLK_Q / 2, 0);
@@ -926,20 +929,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(BTHREADS, 1)
         for (int kk = 0; kk < HD / 8; ++kk)  // S = Q K^T
           umma_tf32_pair(tmem + s_col_of(bb, PBLK_Q), desc_add(dqt0, kchunk_off(TILE, kk)),
                          desc_add(dkk0, kchunk_off(PBLK_Q / 2, kk)), idesc_s, kk > 0 ? 1u : 0u);
-        if (u > 0 && !mbar_wait(bars.dp_free(bb), (u - 1) & 1, p.err, kErrWaitAccum)) return false;
+        if (u > 0 && !mbar_wait(bars.dp_free(bb), (u - 1) & 1, p.err, kErrWaitAccum)) break;
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < HD / 8; ++kk)  // dP = dO V^T, dO in TMEM
           umma_tf32_ts_pair(tmem + dp_col_of(bb, PBLK_Q), tmem + Cfg::Q_OPND + kk * 8,
                             desc_add(dvk0, kchunk_off(PBLK_Q / 2, kk)), idesc_s, kk > 0 ? 1u : 0u);
         umma_commit_pair(bars.s_full(bb), 0x3);
-        return true;
-      };
-      if (ok) ok = issue_s(0);
-      for (int j = 0; ok && j < n_kv; ++j) {
-        if (j + 1 < n_kv && !issue_s(j + 1)) break;
+      }
+    }
+  } else if (warp == 10) {
+    if (lane == 0 && leader) {
+      // ---------------- UMMA issuer B (leader only): dQ += dS K of every key block
+      // once its softmax is done (which implies its S and dP completed)
+      constexpr uint32_t idesc_g = idesc_tf32(2 * TILE, HD, false, true);
+      for (int j = 0; j < n_kv; ++j) {
         const int s = j % STAGES, bb = j & 1;
         if (!mbar_wait(bars.p_full(bb), (j >> 1) & 1, p.err, kErrWaitAccum)) break;
+        if (!mbar_wait(bars.full(s), (j / STAGES) & 1, p.err, kErrWaitFull)) break;
         tc_fence_after();
         const uint32_t st = stage(s);
         const uint64_t dkm0 = mnmajor_desc_rows(st + 2 * Cfg::Q_HALF_K, PBLK_Q, 0);
@@ -1126,7 +1133,7 @@ void launch_bwd_pair(const AttnShape& s, const float* q, const float* k, const f
     set_smem(flash_bwd_kv_pair_kernel<HD>, Cfg::KV_SMEM);
     const long long grid = 2ll * n_pairs * pk.BHx;
     flash_bwd_kv_pair_kernel<HD>
-        <<<static_cast<unsigned>(grid), KV_PAIR_THREADS, Cfg::KV_SMEM, stream>>>(tk, tqk, tdok, tqm, tdom, pk);
+        <<<static_cast<unsigned>(grid), PAIR_BWD_THREADS, Cfg::KV_SMEM, stream>>>(tk, tqk, tdok, tqm, tdom, pk);
   }
   {  // dQ
     CUtensorMap tq, tkk, tvk, tkm;
@@ -1145,7 +1152,8 @@ void launch_bwd_pair(const AttnShape& s, const float* q, const float* k, const f
     // on the side stream the dQ kernel's blocks fill the SMs the dK/dV kernel's
     // last wave leaves idle (the two kernels are independent)
     const cudaStream_t qs = side ? side->stream : stream;
-    flash_bwd_q_pair_kernel<HD><<<static_cast<unsigned>(grid), BTHREADS, Cfg::Q_SMEM, qs>>>(tq, tkk, tvk, tkm, pq);
+    flash_bwd_q_pair_kernel<HD><<<static_cast<unsigned>(grid), PAIR_BWD_THREADS, Cfg::Q_SMEM, qs>>>(tq, tkk, tvk, tkm,
+                                                                                               pq);
   }
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess)
