@@ -601,7 +601,9 @@ struct PairBars {
   __device__ uint32_t dp_free(int bb) const { return base + 8u * (7 + 2 * STAGES + bb); }
   __device__ uint32_t opnd_ready() const { return base + 8u * (9 + 2 * STAGES); }
   __device__ uint32_t acc_done() const { return base + 8u * (10 + 2 * STAGES); }
-  __device__ uint32_t slot() const { return base + 8u * (11 + 2 * STAGES); }
+  // the dP (dP^T) product of buffer bb complete (S-full covers the S product)
+  __device__ uint32_t dp_full(int bb) const { return base + 8u * (11 + 2 * STAGES + bb); }
+  __device__ uint32_t slot() const { return base + 8u * (13 + 2 * STAGES); }
   __device__ void init() const {
     mbar_init(tile_full(), 1);
     for (int s = 0; s < STAGES; ++s) {
@@ -610,6 +612,7 @@ struct PairBars {
     }
     for (int bb = 0; bb < 2; ++bb) {
       mbar_init(s_full(bb), 1);
+      mbar_init(dp_full(bb), 1);
       mbar_init(p_full(bb), 8);  // one warpgroup of each CTA
       mbar_init(s_free(bb), 1);
       mbar_init(dp_free(bb), 1);
@@ -638,10 +641,10 @@ __device__ __forceinline__ void pair_teardown(bool leader, const PairBars<STAGES
 }
 
 // ---------------- dK, dV (pair of 128-key tiles)
-// Two UMMA issuers in the leader: warp 1 issues each step's S^T and dP^T, warp
-// 10 its dV and dK products, so the many small UMMAs of a step are issued from
-// two threads (one issuer was the limit).
-constexpr int PAIR_BWD_THREADS = BTHREADS + 32;
+// Three UMMA issuers in the leader: warp 1 issues each step's S^T, warp 11 its
+// dP^T and warp 10 its dV and dK products, so the many small UMMAs of a step are
+// issued from three threads (one issuer was the limit).
+constexpr int PAIR_BWD_THREADS = BTHREADS + 64;
 
 template <int HD>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PAIR_BWD_THREADS, 1)
@@ -721,31 +724,41 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PAIR_BWD_THREADS, 1)
   } else if (warp == 1) {
     if (lane == 0 && leader) {
       // ---------------- UMMA issuer A (leader only), M = 256 keys across the pair:
-      // S^T and dP^T of every step
+      // S^T of every step
       constexpr uint32_t idesc_s = idesc_tf32(2 * TILE, PBLK_KV, false, false);
       const uint64_t dk0 = kmajor_desc(sK, TILE, 0);
-      bool ok = mbar_wait(bars.tile_full(), 0, p.err, kErrWaitFull);
+      const bool ok = mbar_wait(bars.tile_full(), 0, p.err, kErrWaitFull);
       if (ok) tl->tile_pending = 0;
-      ok = ok && mbar_wait(bars.opnd_ready(), 0, p.err, kErrWaitAccum);
       for (int t = 0; ok && t < n_steps; ++t) {
         const int s = t % STAGES, bb = t & 1, u = t >> 1;
         if (!mbar_wait(bars.full(s), (t / STAGES) & 1, p.err, kErrWaitFull)) break;
         tl->consumed = t + 1;
         if (u > 0 && !mbar_wait(bars.s_free(bb), (u - 1) & 1, p.err, kErrWaitAccum)) break;
         tc_fence_after();
-        const uint32_t st = stage(s);
-        const uint64_t dq0 = kmajor_desc(st, PBLK_KV / 2, 0), ddo0 = kmajor_desc(st + Cfg::KV_HALF_K, PBLK_KV / 2, 0);
+        const uint64_t dq0 = kmajor_desc(stage(s), PBLK_KV / 2, 0);
 #pragma unroll
         for (int kk = 0; kk < HD / 8; ++kk)  // S^T = K Q^T
           umma_tf32_pair(tmem + s_col_of(bb, PBLK_KV), desc_add(dk0, kchunk_off(TILE, kk)),
                          desc_add(dq0, kchunk_off(PBLK_KV / 2, kk)), idesc_s, kk > 0 ? 1u : 0u);
+        umma_commit_pair(bars.s_full(bb), 0x3);
+      }
+    }
+  } else if (warp == 11) {
+    if (lane == 0 && leader) {
+      // ---------------- UMMA issuer C (leader only): dP^T = V dO^T of every step, V in TMEM
+      constexpr uint32_t idesc_s = idesc_tf32(2 * TILE, PBLK_KV, false, false);
+      const bool ok = mbar_wait(bars.opnd_ready(), 0, p.err, kErrWaitAccum);
+      for (int t = 0; ok && t < n_steps; ++t) {
+        const int s = t % STAGES, bb = t & 1, u = t >> 1;
+        if (!mbar_wait(bars.full(s), (t / STAGES) & 1, p.err, kErrWaitFull)) break;
         if (u > 0 && !mbar_wait(bars.dp_free(bb), (u - 1) & 1, p.err, kErrWaitAccum)) break;
         tc_fence_after();
+        const uint64_t ddo0 = kmajor_desc(stage(s) + Cfg::KV_HALF_K, PBLK_KV / 2, 0);
 #pragma unroll
-        for (int kk = 0; kk < HD / 8; ++kk)  // dP^T = V dO^T, V in TMEM
+        for (int kk = 0; kk < HD / 8; ++kk)
           umma_tf32_ts_pair(tmem + dp_col_of(bb, PBLK_KV), tmem + Cfg::KV_OPND + kk * 8,
                             desc_add(ddo0, kchunk_off(PBLK_KV / 2, kk)), idesc_s, kk > 0 ? 1u : 0u);
-        umma_commit_pair(bars.s_full(bb), 0x3);
+        umma_commit_pair(bars.dp_full(bb), 0x3);
       }
     }
   } else if (warp == 10) {
@@ -798,7 +811,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PAIR_BWD_THREADS, 1)
       float l2[32], dl[32];
       load32(p.lse + lrow + qs, p.T - qs, kLog2e, l2);
       load32(p.delta + lrow + qs, p.T - qs, 1.0f, dl);
-      if (!mbar_wait(bars.s_full(grp), (t >> 1) & 1, p.err, kErrWaitAccum)) {
+      if (!mbar_wait(bars.s_full(grp), (t >> 1) & 1, p.err, kErrWaitAccum) ||
+          !mbar_wait(bars.dp_full(grp), (t >> 1) & 1, p.err, kErrWaitAccum)) {
         ok = false;
         break;
       }
@@ -834,8 +848,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PAIR_BWD_THREADS, 1)
 }
 
 // ---------------- dQ (pair of 128-query tiles)
-// Two UMMA issuers in the leader as in the dK/dV kernel: warp 1 issues S and dP,
-// warp 10 the dQ products.
+// Three UMMA issuers in the leader as in the dK/dV kernel: warp 1 issues S,
+// warp 11 dP and warp 10 the dQ products.
 template <int HD>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PAIR_BWD_THREADS, 1)
     flash_bwd_q_pair_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmKk,
@@ -909,33 +923,43 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PAIR_BWD_THREADS, 1)
   } else if (warp == 1) {
     if (lane == 0 && leader) {
       // ---------------- UMMA issuer A (leader only), M = 256 queries across the pair:
-      // S and dP of every key block
+      // S of every key block
       constexpr uint32_t idesc_s = idesc_tf32(2 * TILE, PBLK_Q, false, false);
       const uint64_t dqt0 = kmajor_desc(sQ, TILE, 0);
-      bool ok = mbar_wait(bars.tile_full(), 0, p.err, kErrWaitFull);
+      const bool ok = mbar_wait(bars.tile_full(), 0, p.err, kErrWaitFull);
       if (ok) tl->tile_pending = 0;
-      ok = ok && mbar_wait(bars.opnd_ready(), 0, p.err, kErrWaitAccum);
       for (int j = 0; ok && j < n_kv; ++j) {
         const int s = j % STAGES, bb = j & 1, u = j >> 1;
         if (!mbar_wait(bars.full(s), (j / STAGES) & 1, p.err, kErrWaitFull)) break;
         tl->consumed = j + 1;
-        // the S part was last read by the softmax of block j - 2 (its p_full), the
-        // dP part by dQ(j - 2) (dp_free)
+        // the S part was last read by the softmax of block j - 2 (its p_full)
         if (u > 0 && !mbar_wait(bars.p_full(bb), (u - 1) & 1, p.err, kErrWaitAccum)) break;
         tc_fence_after();
-        const uint32_t st = stage(s);
-        const uint64_t dkk0 = kmajor_desc(st, PBLK_Q / 2, 0), dvk0 = kmajor_desc(st + Cfg::Q_HALF_K, PBLK_Q / 2, 0);
+        const uint64_t dkk0 = kmajor_desc(stage(s), PBLK_Q / 2, 0);
 #pragma unroll
         for (int kk = 0; kk < HD / 8; ++kk)  // S = Q K^T
           umma_tf32_pair(tmem + s_col_of(bb, PBLK_Q), desc_add(dqt0, kchunk_off(TILE, kk)),
                          desc_add(dkk0, kchunk_off(PBLK_Q / 2, kk)), idesc_s, kk > 0 ? 1u : 0u);
+        umma_commit_pair(bars.s_full(bb), 0x3);
+      }
+    }
+  } else if (warp == 11) {
+    if (lane == 0 && leader) {
+      // ---------------- UMMA issuer C (leader only): dP = dO V^T of every key block,
+      // dO in TMEM; the dP part was last read by dQ(j - 2) (dp_free)
+      constexpr uint32_t idesc_s = idesc_tf32(2 * TILE, PBLK_Q, false, false);
+      const bool ok = mbar_wait(bars.opnd_ready(), 0, p.err, kErrWaitAccum);
+      for (int j = 0; ok && j < n_kv; ++j) {
+        const int s = j % STAGES, bb = j & 1, u = j >> 1;
+        if (!mbar_wait(bars.full(s), (j / STAGES) & 1, p.err, kErrWaitFull)) break;
         if (u > 0 && !mbar_wait(bars.dp_free(bb), (u - 1) & 1, p.err, kErrWaitAccum)) break;
         tc_fence_after();
+        const uint64_t dvk0 = kmajor_desc(stage(s) + Cfg::Q_HALF_K, PBLK_Q / 2, 0);
 #pragma unroll
-        for (int kk = 0; kk < HD / 8; ++kk)  // dP = dO V^T, dO in TMEM
+        for (int kk = 0; kk < HD / 8; ++kk)
           umma_tf32_ts_pair(tmem + dp_col_of(bb, PBLK_Q), tmem + Cfg::Q_OPND + kk * 8,
                             desc_add(dvk0, kchunk_off(PBLK_Q / 2, kk)), idesc_s, kk > 0 ? 1u : 0u);
-        umma_commit_pair(bars.s_full(bb), 0x3);
+        umma_commit_pair(bars.dp_full(bb), 0x3);
       }
     }
   } else if (warp == 10) {
@@ -979,7 +1003,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PAIR_BWD_THREADS, 1)
     const uint32_t p_full_lead = mapa_shared(bars.p_full(grp), 0);
     bool ok = true;
     for (int j = grp; j < n_kv; j += 2) {
-      if (!mbar_wait(bars.s_full(grp), (j >> 1) & 1, p.err, kErrWaitAccum)) {
+      if (!mbar_wait(bars.s_full(grp), (j >> 1) & 1, p.err, kErrWaitAccum) ||
+          !mbar_wait(bars.dp_full(grp), (j >> 1) & 1, p.err, kErrWaitAccum)) {
         ok = false;
         break;
       }
