@@ -350,6 +350,9 @@ __global__ void __launch_bounds__(FTHREADS, 1)
 // O += P_j V_j (N = hd, P_j read from each CTA's own TMEM). Barriers the
 // UMMA issuer waits on live in the leader; the commits that release stages,
 // S buffers and O reach both CTAs.
+// Two UMMA issuers in the leader: warp 1 issues the S products, warp 10 the PV
+// products, so a PV is queued as soon as its P is ready.
+constexpr int FPAIR_THREADS = FTHREADS + 32;
 constexpr int PQ = 128;   // query rows per CTA (a pair: 256)
 constexpr int PKV = 128;  // keys per block = N of the S product
 
@@ -369,7 +372,7 @@ struct PairCfg {
 };
 
 template <int HD>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(FTHREADS, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(FPAIR_THREADS, 1)
     flash_fwd_pair_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                           const __grid_constant__ CUtensorMap tmV, FlashParams p) {
   using Cfg = PairCfg<HD>;
@@ -467,16 +470,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(FTHREADS, 1)
     }
   } else if (warp == 1) {
     if (lane == 0 && leader) {
-      // ---------------- UMMA issuer (leader only), M = 256 across the pair
+      // ---------------- UMMA issuer A (leader only), M = 256 across the pair: S = Q K^T
       constexpr uint32_t idesc_s = idesc_tf32(2 * PQ, PKV, false, false);
-      constexpr uint32_t idesc_o = idesc_tf32(2 * PQ, HD, false, true);
       const uint64_t dq0 = smem_desc(sQ, 16, 1024, kLayoutSw128);
-      bool ok = mbar_wait(q_full, 0, p.err, kErrWaitFull);
+      const bool ok = mbar_wait(q_full, 0, p.err, kErrWaitFull);
       if (ok) *q_pending = 0;
-      auto issue_s = [&](int j) -> bool {
+      for (int j = 0; ok && j < n_kv; ++j) {
         const int s = j % STAGES, bb = j & 1, u = j >> 1;
-        if (!mbar_wait(k_full(s), (j / STAGES) & 1, p.err, kErrWaitFull)) return false;
-        if (u > 0 && !mbar_wait(s_free(bb), (u - 1) & 1, p.err, kErrWaitAccum)) return false;
+        if (!mbar_wait(k_full(s), (j / STAGES) & 1, p.err, kErrWaitFull)) break;
+        if (u > 0 && !mbar_wait(s_free(bb), (u - 1) & 1, p.err, kErrWaitAccum)) break;
         tc_fence_after();
         const uint64_t dk0 = smem_desc(sK(s), 16, 1024, kLayoutSw128);
 #pragma unroll
@@ -486,11 +488,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(FTHREADS, 1)
                          desc_add(dk0, (kk / 4) * ((PKV / 2) * 128) + off), idesc_s, kk > 0 ? 1u : 0u);
         }
         umma_commit_pair(s_full(bb), 0x3);
-        return true;
-      };
-      if (ok) ok = issue_s(0);
-      for (int j = 0; ok && j < n_kv; ++j) {
-        if (j + 1 < n_kv && !issue_s(j + 1)) break;
+      }
+    }
+  } else if (warp == FTHREADS / 32) {
+    if (lane == 0 && leader) {
+      // ---------------- UMMA issuer B (leader only): O += P V once the block's softmax is done
+      constexpr uint32_t idesc_o = idesc_tf32(2 * PQ, HD, false, true);
+      for (int j = 0; j < n_kv; ++j) {
         const int s = j % STAGES, bb = j & 1;
         if (!mbar_wait(p_full(bb), (j >> 1) & 1, p.err, kErrWaitAccum)) break;
         if (!mbar_wait(v_full(s), (j / STAGES) & 1, p.err, kErrWaitFull)) break;
@@ -714,7 +718,7 @@ void launch_flash_pair(const AttnShape& s, const float* q, const float* k, const
   p.lse = lse;
   p.err = d_err;
   const long long grid = 2ll * p.n_qt * p.BH;
-  flash_fwd_pair_kernel<HD><<<static_cast<unsigned>(grid), FTHREADS, Cfg::SMEM, stream>>>(tq, tk, tv, p);
+  flash_fwd_pair_kernel<HD><<<static_cast<unsigned>(grid), FPAIR_THREADS, Cfg::SMEM, stream>>>(tq, tk, tv, p);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) throw std::runtime_error(std::string("flash attention launch: ") + cudaGetErrorString(e));
 }
