@@ -1023,6 +1023,10 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 uint64_t gemm_launch_count() { return t_launches; }
 
+int sm_count() { return device_sms(); }
+
+unsigned int* pair_ticket_counter(int dev, cudaStream_t stream) { return unit_counter(dev, stream); }
+
 const char* gemm_status_string(int status) {
   switch (status) {
     case 0: return "ok";

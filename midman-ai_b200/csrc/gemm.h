@@ -71,6 +71,14 @@ const char* gemm_status_string(int status);
 // Kernels the GEMM functions have launched from the calling thread so far.
 uint64_t gemm_launch_count();
 
+// Streaming multiprocessors of the current device.
+int sm_count();
+
+// Two ticket words for persistent CTA-pair kernels launched on `stream` of
+// device `dev`, shared by every such launch on the stream: each launch leaves
+// them at zero. Null when the device's table of streams is full.
+unsigned int* pair_ticket_counter(int dev, cudaStream_t stream);
+
 // The batched form; bn (64, 128 or 256) is the output tile width. No residual.
 int gemm_tf32_batched(int batch, int M, int N, int K, const BatchedOperand& A, const BatchedOperand& B, float* C,
                       long long ldc, const GemmBatch& bt, int bn, int* d_err, cudaStream_t stream);
