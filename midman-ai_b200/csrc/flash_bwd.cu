@@ -173,6 +173,84 @@ __device__ __forceinline__ void tmem_to_row(uint32_t taddr, float* dst, bool val
   }
 }
 
+// Loads 32-column chunks c0, c0 + 2, ... of rows row_first .. row_first + 31 of
+// src (`ld` apart; rows at or past n_rows read as 0) into this warp's 32 TMEM
+// lanes through the warp's 32 x 16 staging tile `wst`, so that each load
+// instruction reads eight whole 64-byte row segments.
+template <int HD>
+__device__ __forceinline__ void rows_to_tmem(const float* src, long long ld, int row_first, int n_rows,
+                                             uint32_t taddr, float4* wst, int c0) {
+  const int lane = threadIdx.x % 32, sub = lane & 3, rsub = lane >> 2;
+#pragma unroll 1
+  for (int c = c0; c < HD / 32; c += 2) {
+    uint32_t r[32];
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      float4 v[4];
+#pragma unroll
+      for (int it = 0; it < 4; ++it) {
+        const int rr = it * 8 + rsub;
+        v[it] = row_first + rr < n_rows
+                    ? *reinterpret_cast<const float4*>(src + static_cast<long long>(row_first + rr) * ld + c * 32 +
+                                                       half * 16 + sub * 4)
+                    : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int it = 0; it < 4; ++it) {
+        const int rr = it * 8 + rsub;
+        wst[rr * 4 + (sub ^ (rr & 3))] = v[it];
+      }
+      __syncwarp();
+#pragma unroll
+      for (int gr = 0; gr < 4; ++gr) {
+        const float4 w = wst[lane * 4 + (gr ^ (lane & 3))];
+        const int i = half * 16 + gr * 4;
+        r[i] = __float_as_uint(w.x);
+        r[i + 1] = __float_as_uint(w.y);
+        r[i + 2] = __float_as_uint(w.z);
+        r[i + 3] = __float_as_uint(w.w);
+      }
+      __syncwarp();
+    }
+    tmem_st_32x32b_x32(taddr + c * 32, r);
+  }
+}
+
+// Writes 32-column chunks c0, c0 + step, ... of this warp's 32 TMEM lanes to
+// rows row_first .. row_first + 31 of dst (`ld` apart; rows at or past n_rows
+// are skipped) through the warp's 32 x 16 staging tile `wst` (4-float granules
+// XOR-swizzled by row), so that each store instruction writes eight whole
+// 64-byte row segments.
+template <int HD>
+__device__ __forceinline__ void tmem_to_rows(uint32_t taddr, float* dst, long long ld, int row_first, int n_rows,
+                                             float4* wst, int c0 = 0, int step = 1) {
+  const int lane = threadIdx.x % 32, sub = lane & 3, rsub = lane >> 2;
+#pragma unroll 1
+  for (int c = c0; c < HD / 32; c += step) {
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(taddr + c * 32, r);
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+#pragma unroll
+      for (int gr = 0; gr < 4; ++gr) {
+        const int i = half * 16 + gr * 4;
+        wst[lane * 4 + (gr ^ (lane & 3))] = make_float4(__uint_as_float(r[i]), __uint_as_float(r[i + 1]),
+                                                        __uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
+      }
+      __syncwarp();
+#pragma unroll
+      for (int it = 0; it < 4; ++it) {
+        const int rr = it * 8 + rsub;
+        const float4 v = wst[rr * 4 + (sub ^ (rr & 3))];
+        if (row_first + rr < n_rows)
+          *reinterpret_cast<float4*>(dst + static_cast<long long>(row_first + rr) * ld + c * 32 + half * 16 + sub * 4) =
+              v;
+      }
+      __syncwarp();
+    }
+  }
+}
+
 // out[i] = src[i] * mul for the first n_valid of 32 consecutive floats, 0 past them.
 __device__ __forceinline__ void load32(const float* src, int n_valid, float mul, float (&out)[32]) {
   if (n_valid >= 32 && (reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
@@ -572,8 +650,10 @@ struct PairBwdCfg {
   static constexpr int Q_FIT = (210 * 1024 - TILE_BYTES) / Q_STAGE;
   static constexpr int KV_STAGES = KV_FIT > 4 ? 4 : KV_FIT;
   static constexpr int Q_STAGES = Q_FIT > 4 ? 4 : Q_FIT;
-  static constexpr int KV_SMEM = TILE_BYTES + KV_STAGES * KV_STAGE + 1024 + 256;
-  static constexpr int Q_SMEM = TILE_BYTES + Q_STAGES * Q_STAGE + 1024 + 256;
+  // after the barriers: a 32 x 16 output staging tile per softmax warp
+  static constexpr int STAGE_OUT = 8 * 2048;
+  static constexpr int KV_SMEM = TILE_BYTES + KV_STAGES * KV_STAGE + 1024 + 256 + STAGE_OUT;
+  static constexpr int Q_SMEM = TILE_BYTES + Q_STAGES * Q_STAGE + 1024 + 256 + STAGE_OUT;
   // TMEM: S (or P) and dP (or dS) buffers, two of each, then the TMEM operand
   // (V or dO) and the accumulators
   static constexpr uint32_t KV_OPND = 4 * PBLK_KV, KV_DV = KV_OPND + HD, KV_DK = KV_DV + HD;
@@ -795,10 +875,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PAIR_BWD_THREADS, 1)
     const int quarter = warp & 3;
     const int row = quarter * 32 + lane;
     const int key = my_k0 + row;
-    const bool key_ok = key < p.T;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-    row_to_tmem<HD>(p.tm_src + static_cast<long long>(row0 + key) * p.ld_in + static_cast<long long>(hk) * HD,
-                    key_ok, tmem + lane_base + Cfg::KV_OPND, grp);
+    float4* wst = reinterpret_cast<float4*>(smem_raw + (bars.base - raw_addr) + 256) + (warp - 2) * 128;
+    rows_to_tmem<HD>(p.tm_src + static_cast<long long>(row0) * p.ld_in + static_cast<long long>(hk) * HD, p.ld_in,
+                     my_k0 + quarter * 32, p.T, tmem + lane_base + Cfg::KV_OPND, wst, grp);
     tc_fence_before();
     __syncwarp();
     if (lane == 0) mbar_arrive_remote(mapa_shared(bars.opnd_ready(), 0));
@@ -835,13 +915,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PAIR_BWD_THREADS, 1)
     }
     if (ok && mbar_wait(bars.acc_done(), 0, p.err, kErrWaitAccum)) {
       tc_fence_after();
-      const long long r = row0 + key;
       if (grp == 0)
-        tmem_to_row<HD>(tmem + lane_base + Cfg::KV_DV, p.out2 + r * p.ld_out2 + static_cast<long long>(hk) * HD,
-                        key_ok, 1.0f);
+        tmem_to_rows<HD>(tmem + lane_base + Cfg::KV_DV,
+                         p.out2 + static_cast<long long>(row0) * p.ld_out2 + static_cast<long long>(hk) * HD, p.ld_out2,
+                         my_k0 + quarter * 32, p.T, wst);
       else
-        tmem_to_row<HD>(tmem + lane_base + Cfg::KV_DK, p.out + r * p.ld_out + static_cast<long long>(hk) * HD,
-                        key_ok, 1.0f);
+        tmem_to_rows<HD>(tmem + lane_base + Cfg::KV_DK,
+                         p.out + static_cast<long long>(row0) * p.ld_out + static_cast<long long>(hk) * HD, p.ld_out,
+                         my_k0 + quarter * 32, p.T, wst);
     }
   }
   pair_teardown<STAGES>(leader, bars, tl, p.err, warp, tmem);
@@ -992,8 +1073,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PAIR_BWD_THREADS, 1)
     const int q = my_q0 + row;
     const bool q_ok = q < p.T;
     const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
-    row_to_tmem<HD>(p.tm_src + static_cast<long long>(row0 + q) * p.ld_in + static_cast<long long>(h) * HD, q_ok,
-                    tmem + lane_base + Cfg::Q_OPND, grp);
+    float4* wst = reinterpret_cast<float4*>(smem_raw + (bars.base - raw_addr) + 256) + (warp - 2) * 128;
+    rows_to_tmem<HD>(p.tm_src + static_cast<long long>(row0) * p.ld_in + static_cast<long long>(h) * HD, p.ld_in,
+                     my_q0 + quarter * 32, p.T, tmem + lane_base + Cfg::Q_OPND, wst, grp);
     const long long li = static_cast<long long>(bh) * p.T + q;
     const float lse2 = q_ok ? p.lse[li] * kLog2e : 0.0f;
     const float dlt = q_ok ? p.delta[li] : 0.0f;
@@ -1029,9 +1111,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PAIR_BWD_THREADS, 1)
     }
     if (ok && mbar_wait(bars.acc_done(), 0, p.err, kErrWaitAccum)) {
       tc_fence_after();
-      tmem_to_row<HD>(tmem + lane_base + Cfg::Q_DQ,
-                      p.out + static_cast<long long>(row0 + q) * p.ld_out + static_cast<long long>(h) * HD, q_ok,
-                      1.0f, grp, 2);
+      tmem_to_rows<HD>(tmem + lane_base + Cfg::Q_DQ,
+                       p.out + static_cast<long long>(row0) * p.ld_out + static_cast<long long>(h) * HD, p.ld_out,
+                       my_q0 + quarter * 32, p.T, wst, grp, 2);
     }
   }
   pair_teardown<STAGES>(leader, bars, tl, p.err, warp, tmem);

@@ -368,7 +368,8 @@ struct PairCfg {
   static constexpr int STAGE_BYTES = K_BYTES + V_BYTES;
   static constexpr int FIT = (200 * 1024 - Q_BYTES) / STAGE_BYTES;
   static constexpr int STAGES = FIT > 4 ? 4 : FIT;
-  static constexpr int SMEM = Q_BYTES + STAGES * STAGE_BYTES + 1024 + 512 + 2048 /*group exchange*/;
+  static constexpr int STAGE_OUT = 8 * 2048;  // a 32 x 16 output staging tile per softmax warp
+  static constexpr int SMEM = Q_BYTES + STAGES * STAGE_BYTES + 1024 + 512 + 2048 /*group exchange*/ + STAGE_OUT;
   static constexpr uint32_t O_COL = 2 * PKV;  // two S/P buffers, then O of each warpgroup
   static constexpr uint32_t TMEM_COLS = 512;
   static_assert(O_COL + 2 * HD <= TMEM_COLS, "TMEM budget");
@@ -466,6 +467,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(FPAIR_THREADS, 1)
   FwdTail* tl = reinterpret_cast<FwdTail*>(smem + (bars.tail() - base));
   volatile int* ring = tl->ring;
   float* xch = reinterpret_cast<float*>(smem + Cfg::Q_BYTES + STAGES * Cfg::STAGE_BYTES + 512);
+  float4* stage_out = reinterpret_cast<float4*>(smem + Cfg::Q_BYTES + STAGES * Cfg::STAGE_BYTES + 512 + 2048);
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
@@ -756,22 +758,41 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(FPAIR_THREADS, 1)
         const float l = (a0 > 0.0f ? l0 * a0 : 0.0f) + (a1 > 0.0f ? l1 * a1 : 0.0f);
         const float inv = 1.0f / l;
         const float w0 = a0 * inv, w1 = a1 * inv;
-        float* orow = p.o + static_cast<long long>(x.b * p.T + q) * p.ldo + static_cast<long long>(x.h) * HD;
+        // Rows leave through this warp's staging tile, 16 columns at a time
+        // (4-float granules XOR-swizzled by row), so that each store
+        // instruction writes eight whole 64-byte row segments.
+        float4* wst = stage_out + (warp - 2) * 128;
+        const int sub = lane & 3, rsub = lane >> 2;
+        float* obase = p.o + static_cast<long long>(x.b * p.T) * p.ldo + static_cast<long long>(x.h) * HD;
 #pragma unroll 1
         for (int c = grp; c < HD / 32; c += 2) {
           uint32_t o0[32], o1[32];
           tmem_ld_32x32b_x32(tmem + lane_base + Cfg::O_COL + c * 32, o0);
           tmem_ld_32x32b_x32(tmem + lane_base + Cfg::O_COL + HD + c * 32, o1);
-          if (q < p.T) {
 #pragma unroll
-            for (int i = 0; i < 32; i += 4) {
+          for (int half = 0; half < 2; ++half) {
+#pragma unroll
+            for (int gr = 0; gr < 4; ++gr) {
               float v[4];
 #pragma unroll
-              for (int e = 0; e < 4; ++e)
-                v[e] = (a0 > 0.0f ? __uint_as_float(o0[i + e]) * w0 : 0.0f) +
-                       (a1 > 0.0f ? __uint_as_float(o1[i + e]) * w1 : 0.0f);
-              *reinterpret_cast<float4*>(orow + c * 32 + i) = make_float4(v[0], v[1], v[2], v[3]);
+              for (int e = 0; e < 4; ++e) {
+                const int i = half * 16 + gr * 4 + e;
+                v[e] = (a0 > 0.0f ? __uint_as_float(o0[i]) * w0 : 0.0f) +
+                       (a1 > 0.0f ? __uint_as_float(o1[i]) * w1 : 0.0f);
+              }
+              wst[lane * 4 + (gr ^ (lane & 3))] = make_float4(v[0], v[1], v[2], v[3]);
             }
+            __syncwarp();
+#pragma unroll
+            for (int it = 0; it < 4; ++it) {
+              const int rr = it * 8 + rsub;
+              const float4 v = wst[rr * 4 + (sub ^ (rr & 3))];
+              const int qr = my_q0 + quarter * 32 + rr;
+              if (qr < p.T)
+                *reinterpret_cast<float4*>(obase + static_cast<long long>(qr) * p.ldo + c * 32 + half * 16 + sub * 4) =
+                    v;
+            }
+            __syncwarp();
           }
         }
         if (grp == 0 && q < p.T)
