@@ -130,63 +130,70 @@ __global__ void rmsnorm_fwd_kernel(const float* __restrict__ x, const float* __r
 // Each block owns a contiguous range of rows; per row it writes dx and keeps the
 // row's contribution to dw in registers (G float4 column groups per thread).
 template <int G>
-__global__ void rmsnorm_bwd_kernel(const float* __restrict__ x, const float* __restrict__ w,
-                                   const float* __restrict__ rstd, const float* __restrict__ dy, int rows, int dim,
-                                   int rows_per_block, float* dx, const float* dres, float* __restrict__ ws) {
+__global__ void __launch_bounds__(kThreads, G <= 2 ? 4 : 1)
+    rmsnorm_bwd_kernel(const float* __restrict__ x, const float* __restrict__ w, const float* __restrict__ rstd,
+                       const float* __restrict__ dy, int rows, int dim, int rows_per_block, float* dx,
+                       const float* dres, float* __restrict__ ws) {
   __shared__ float red[32];
   const int r0 = blockIdx.x * rows_per_block;
   const int r1 = min(rows, r0 + rows_per_block);
   const int nv = dim / 4;
   const float4* w4 = reinterpret_cast<const float4*>(w);
   float4 acc[G];
-  float4 wv[G];
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
-    acc[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int g = 0; g < G; ++g) acc[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+  // the weights are read per row from L1 (registers go to the prefetched rows)
+  auto wv = [&](int g) {
     const int j = threadIdx.x + g * blockDim.x;
-    wv[g] = j < nv ? w4[j] : make_float4(0.f, 0.f, 0.f, 0.f);
-  }
+    return j < nv ? __ldg(w4 + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+  };
   const float inv_dim = 1.0f / static_cast<float>(dim);
-  // x and dy of row r + 1 are loaded while row r is reduced and written
-  float4 xv[G], gv[G], xn[G], gn[G];
-  auto load_row = [&](int r, float4 (&xa)[G], float4 (&ga)[G]) {
+  // x, dy, the residual gradient and 1/rms of row r + 1 are loaded while row r
+  // is reduced and written (rows differ, so dx may alias dy or dres)
+  float4 xv[G], gv[G], dv[G], xn[G], gn[G], dn[G];
+  float iv = 0.0f, in_ = 0.0f;
+  auto load_row = [&](int r, float4 (&xa)[G], float4 (&ga)[G], float4 (&da)[G], float& ia) {
     const float4* xr = reinterpret_cast<const float4*>(x + static_cast<long long>(r) * dim);
     const float4* gr = reinterpret_cast<const float4*>(dy + static_cast<long long>(r) * dim);
+    const float4* dr = dres ? reinterpret_cast<const float4*>(dres + static_cast<long long>(r) * dim) : nullptr;
 #pragma unroll
     for (int g = 0; g < G; ++g) {
       const int j = threadIdx.x + g * blockDim.x;
       xa[g] = j < nv ? xr[j] : make_float4(0.f, 0.f, 0.f, 0.f);
       ga[g] = j < nv ? gr[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+      da[g] = (dr && j < nv) ? dr[j] : make_float4(0.f, 0.f, 0.f, 0.f);
     }
+    ia = rstd[r];
   };
-  if (r0 < r1) load_row(r0, xv, gv);
+  if (r0 < r1) load_row(r0, xv, gv, dv, iv);
   for (int r = r0; r < r1; ++r) {
-    if (r + 1 < r1) load_row(r + 1, xn, gn);
+    if (r + 1 < r1) load_row(r + 1, xn, gn, dn, in_);
     float dot = 0.0f;
 #pragma unroll
     for (int g = 0; g < G; ++g) {
       const int j = threadIdx.x + g * blockDim.x;
-      if (j < nv)
-        dot += (gv[g].x * wv[g].x) * xv[g].x + (gv[g].y * wv[g].y) * xv[g].y + (gv[g].z * wv[g].z) * xv[g].z +
-               (gv[g].w * wv[g].w) * xv[g].w;
+      if (j < nv) {
+        const float4 wg = wv(g);
+        dot += (gv[g].x * wg.x) * xv[g].x + (gv[g].y * wg.y) * xv[g].y + (gv[g].z * wg.z) * xv[g].z +
+               (gv[g].w * wg.w) * xv[g].w;
+      }
     }
     dot = block_sum(dot, red);
-    const float inv = rstd[r];
+    const float inv = iv;
     // d/dx of x*inv*w through inv = (mean(x^2)+eps)^-1/2: the powf closure gives
     // -0.5*t^-1.5 = -0.5*inv^3, the mean's 1/len, and x*x contributes twice.
     const float dsum = (dot * (-0.5f * inv * inv * inv)) * inv_dim;
     float4* dxr = reinterpret_cast<float4*>(dx + static_cast<long long>(r) * dim);
-    const float4* dr = dres ? reinterpret_cast<const float4*>(dres + static_cast<long long>(r) * dim) : nullptr;
 #pragma unroll
     for (int g = 0; g < G; ++g) {
       const int j = threadIdx.x + g * blockDim.x;
       if (j < nv) {
         const float4 b = make_float4(dsum * xv[g].x, dsum * xv[g].y, dsum * xv[g].z, dsum * xv[g].w);
-        float4 o = make_float4(((gv[g].x * wv[g].x) * inv + b.x) + b.x, ((gv[g].y * wv[g].y) * inv + b.y) + b.y,
-                               ((gv[g].z * wv[g].z) * inv + b.z) + b.z, ((gv[g].w * wv[g].w) * inv + b.w) + b.w);
-        if (dr) {
-          const float4 d = dr[j];
-          o.x += d.x; o.y += d.y; o.z += d.z; o.w += d.w;
+        const float4 wg = wv(g);
+        float4 o = make_float4(((gv[g].x * wg.x) * inv + b.x) + b.x, ((gv[g].y * wg.y) * inv + b.y) + b.y,
+                               ((gv[g].z * wg.z) * inv + b.z) + b.z, ((gv[g].w * wg.w) * inv + b.w) + b.w);
+        if (dres) {
+          o.x += dv[g].x; o.y += dv[g].y; o.z += dv[g].z; o.w += dv[g].w;
         }
         dxr[j] = o;
         acc[g].x += gv[g].x * (xv[g].x * inv);
@@ -199,7 +206,9 @@ __global__ void rmsnorm_bwd_kernel(const float* __restrict__ x, const float* __r
     for (int g = 0; g < G; ++g) {
       xv[g] = xn[g];
       gv[g] = gn[g];
+      dv[g] = dn[g];
     }
+    iv = in_;
   }
   float4* out = reinterpret_cast<float4*>(ws + static_cast<long long>(blockIdx.x) * dim);
 #pragma unroll
