@@ -4,13 +4,16 @@
  * The reference (MidManStudio/midman-ai) runs these computations as Rust
  * functions over host slices; each entry point below names the reference
  * function it replaces (path:line inside the reference project). A Rust FFI
- * crate, or ctypes, binds these directly; INTEGRATION.md shows both.
+ * crate (`extern "C"` declarations) or ctypes binds these directly.
  *
  * Conventions
  *   - All pointers are device pointers unless a parameter says "host".
  *   - f32 everywhere; token ids are int32.
  *   - `stream` is a cudaStream_t passed as void* (NULL = the legacy default
- *     stream). Every call is asynchronous on that stream.
+ *     stream). Every call is asynchronous on that stream. The GEMM and the
+ *     attention forward take their work from two ticket words kept per
+ *     (device, stream), so calls on one stream must not be made from two host
+ *     threads at once.
  *   - Return value: 0 on success, a negative MM_GPU_ERR_* code otherwise, with a
  *     message from mm_gpu_last_error(). Kernels that wait on hardware pipelines
  *     record timeouts in a device flag read by mm_gpu_device_status().
