@@ -663,9 +663,9 @@ struct PairBwdCfg {
   static_assert(KV_STAGES >= 2 && Q_STAGES >= 2, "two stages");
 };
 
-// Barriers of a pair kernel. Those the UMMA issuer waits on are used in the
-// leader only; stage-empty, S-full and accumulator-done ones receive commits
-// multicast to both CTAs.
+// Barriers of a pair kernel. Those the UMMA issuers wait on are used in the
+// leader only; stage-empty, S-full, dP-full and accumulator-done ones receive
+// commits multicast to both CTAs.
 template <int STAGES>
 struct PairBars {
   uint32_t base;
