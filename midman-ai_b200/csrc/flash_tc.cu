@@ -1,6 +1,6 @@
 // Fused causal attention forward on the tensor cores (TF32, tcgen05 + TMEM).
 //
-// One CTA per (128-query tile, batch, head). Per block of 64 keys:
+// Per block of keys:
 //   S_j = Q K_j^T         tcgen05.mma, A = Q (smem), B = K_j (smem), D in TMEM
 //   P_j = exp(S_j - m)    softmax warps: tcgen05.ld of their own row, online
 //                         max/sum, tcgen05.st of P_j over S_j in TMEM
@@ -12,13 +12,16 @@
 // 1/sqrt(hd), -1e9 above the diagonal, softmax over keys, P V), with grouped
 // key/value heads read in place rather than expanded by copy.
 //
-// Warp roles (192 threads):
+// Two forms. head_dim 64 and 128: persistent CTA pairs over 256-query tiles
+// (flash_fwd_pair_kernel, below). head_dim 32: one CTA per (128-query tile,
+// batch, head) with 64-key blocks (flash_fwd_kernel), 320 threads:
 //   warp 0      TMA producer (one lane): Q once, then a ring of K/V stages
 //   warp 1      TMEM allocator + UMMA issuer (one lane)
-//   warps 2..5  softmax, O rescaling and the epilogue; warp w owns TMEM lanes
-//               32 (w % 4) .. +31, i.e. query rows of that quarter
+//   warps 2..9  two softmax warpgroups taking alternate key blocks, each with its
+//               own running max/sum and O accumulator (merged at the end); warp
+//               w owns TMEM lanes 32 (w % 4) .. +31, the query rows of that quarter
 // TMEM columns: three S/P buffers of 64 at 0, 64, 128 (S_{j+1} is computed
-// while the softmax works on S_j), O at 192 .. 192 + hd.
+// while the softmax works on S_j), then the two O accumulators.
 #include <cuda.h>
 #include <cuda_runtime.h>
 
