@@ -156,11 +156,8 @@ void attention_fwd(const Config& c, size_t B, size_t T, LayerSaved& L, Vec& cont
     std::vector<float> kt(hd * T), s(T * T, 0.0f);
     for (size_t j = 0; j < T; ++j)
       for (size_t p = 0; p < hd; ++p) kt[p * T + j] = k[j * hd + p];
-    for (size_t i = 0; i < T; ++i)
-      for (size_t p = 0; p < hd; ++p) {
-        const float a = q[i * hd + p];
-        for (size_t j = 0; j < T; ++j) s[i * T + j] += a * kt[p * T + j];
-      }
+    // s[i][j] += q[i][p] * kt[p][j], p ascending
+    gemm_strided_serial(q, hd, 1, kt.data(), T, s.data(), T, T, hd, T);
     float* y = L.probs.data() + bh * T * T;
     for (size_t i = 0; i < T; ++i) {
       float* row = s.data() + i * T;
@@ -177,11 +174,8 @@ void attention_fwd(const Config& c, size_t B, size_t T, LayerSaved& L, Vec& cont
       for (size_t j = 0; j < T; ++j) y[i * T + j] *= inv;
     }
     float* ctx = context.data() + bh * T * hd;
-    for (size_t i = 0; i < T; ++i)
-      for (size_t j = 0; j < T; ++j) {
-        const float pij = y[i * T + j];
-        for (size_t p = 0; p < hd; ++p) ctx[i * hd + p] += pij * v[j * hd + p];
-      }
+    // ctx[i][p] += y[i][j] * v[j][p], j ascending
+    gemm_strided_serial(y, T, 1, v, hd, ctx, hd, T, T, hd);
   }
 }
 
@@ -205,19 +199,15 @@ void attention_bwd(const Config& c, size_t B, size_t T, const LayerSaved& L, con
     const float* g = dctx.data() + bh * T * hd;
     std::vector<float> dp(T * T, 0.0f), ds(T * T, 0.0f);
     // dprobs = gemm_nt(g, v): dot-product form over hd
-    for (size_t i = 0; i < T; ++i)
-      for (size_t j = 0; j < T; ++j) {
-        float acc = 0.0f;
-        for (size_t p = 0; p < hd; ++p) acc += g[i * hd + p] * v[j * hd + p];
-        dp[i * T + j] = acc;
-      }
+    // (as gemm_nn of g and a transposed copy of v: p ascending from zero per element)
+    std::vector<float> vt(hd * T);
+    for (size_t j = 0; j < T; ++j)
+      for (size_t p = 0; p < hd; ++p) vt[p * T + j] = v[j * hd + p];
+    gemm_strided_serial(g, hd, 1, vt.data(), T, dp.data(), T, T, hd, T);
     // dv_expanded = gemm_tn(probs, g)
     float* dve = dv_e.data() + bh * T * hd;
-    for (size_t j = 0; j < T; ++j)
-      for (size_t i = 0; i < T; ++i) {
-        const float pij = y[i * T + j];
-        for (size_t p = 0; p < hd; ++p) dve[j * hd + p] += pij * g[i * hd + p];
-      }
+    // dve[j][p] += y[i][j] * g[i][p], i ascending
+    gemm_strided_serial(y, 1, T, g, hd, dve, hd, T, T, hd);
     // softmax backward, then the scale
     for (size_t i = 0; i < T; ++i) {
       float dot = 0.0f;
@@ -226,19 +216,12 @@ void attention_bwd(const Config& c, size_t B, size_t T, const LayerSaved& L, con
     }
     // dq = gemm_nt(ds, k^T) = ds k (dot-product form over j)
     float* dqo = dq.data() + bh * T * hd;
-    for (size_t i = 0; i < T; ++i)
-      for (size_t p = 0; p < hd; ++p) {
-        float acc = 0.0f;
-        for (size_t j = 0; j < T; ++j) acc += ds[i * T + j] * k[j * hd + p];
-        dqo[i * hd + p] = acc;
-      }
+    // dq[i][p] = sum of ds[i][j] * k[j][p], j ascending from zero
+    gemm_strided_serial(ds.data(), T, 1, k, hd, dqo, hd, T, T, hd);
     // dk^T = gemm_tn(q, ds): dkt[p][j] = sum_i q[i][p] ds[i][j]; transposed back
     float* dke = dk_e.data() + bh * T * hd;
-    for (size_t p = 0; p < hd; ++p)
-      for (size_t i = 0; i < T; ++i) {
-        const float qip = q[i * hd + p];
-        for (size_t j = 0; j < T; ++j) dke[j * hd + p] += qip * ds[i * T + j];
-      }
+    // dke[j][p] += ds[i][j] * q[i][p], i ascending
+    gemm_strided_serial(ds.data(), 1, T, q, hd, dke, hd, T, T, hd);
   }
   dk.assign(B * Hkv * T * hd, 0.0f);
   dv.assign(B * Hkv * T * hd, 0.0f);
@@ -334,8 +317,9 @@ int model_loss(Model& m, const int32_t* inputs, const int32_t* targets, int batc
   const float* head;
   if (c.tie) {
     head_t.resize(D * V);
-    for (size_t v = 0; v < V; ++v)
-      for (size_t d = 0; d < D; ++d) head_t[d * V + v] = P[m.embed + v * D + d];
+#pragma omp parallel for schedule(static)
+    for (long long d = 0; d < static_cast<long long>(D); ++d)
+      for (size_t v = 0; v < V; ++v) head_t[d * V + v] = P[m.embed + v * D + d];
     head = head_t.data();
   } else {
     head = P + m.lm_head;
@@ -378,7 +362,8 @@ int model_loss(Model& m, const int32_t* inputs, const int32_t* targets, int batc
   if (c.tie) {
     Vec dhead_t(D * V, 0.0f);
     gemm_tn(xf.data(), g.data(), dhead_t.data(), N, D, V);
-    for (size_t v = 0; v < V; ++v)
+#pragma omp parallel for schedule(static)
+    for (long long v = 0; v < static_cast<long long>(V); ++v)
       for (size_t d = 0; d < D; ++d) grads[m.embed + v * D + d] = dhead_t[d * V + v];
   } else {
     gemm_tn(xf.data(), g.data(), grads + m.lm_head, N, D, V);

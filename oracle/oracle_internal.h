@@ -79,6 +79,10 @@ void gemm_nn(const float* a, const float* b, float* c, size_t m, size_t k, size_
 void gemm_nt(const float* a, const float* b, float* c, size_t m, size_t k, size_t n);
 // C[m,n] += A[k,m]^T * B[k,n]
 void gemm_tn(const float* a, const float* b, float* c, size_t k, size_t m, size_t n);
+// One thread: C(i, j) += sum_p A(i, p) * B[p][j] with A(i, p) = a[i * rs + p * cs],
+// B row stride ldb, C row stride ldc; the same per-element order as gemm_nn.
+void gemm_strided_serial(const float* a, size_t rs, size_t cs, const float* b, size_t ldb, float* c, size_t ldc,
+                         size_t m, size_t k, size_t n);
 
 void set_threads(int n);
 
