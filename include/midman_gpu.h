@@ -38,6 +38,7 @@ extern "C" {
 #define MM_GPU_OK 0
 #define MM_GPU_ERR_ARGUMENT -1
 #define MM_GPU_ERR_SHAPE -3
+#define MM_GPU_ERR_INDEX -4
 #define MM_GPU_ERR_DEVICE -6
 
 /* Arithmetic of the tensor-core products. */
@@ -107,6 +108,84 @@ MM_GPU_EXPORT int32_t mm_gpu_attention_backward(int32_t batch, int32_t seq, int3
                                                 int64_t ldk, float *dq, float *dk, float *dv, int32_t precision,
                                                 void *stream);
 
+/* ---- The layers around the products (crates/midman-nn, crates/midman-tensor).
+ * Token-major activations [rows = batch * seq, features], contiguous unless a
+ * row stride is given. Ids and targets outside [0, vocab) are never used to
+ * address memory: the host-side checks return MM_GPU_ERR_INDEX, the device-side
+ * ones write a zero row (embedding) or a NaN row loss (cross-entropy) and set
+ * the device error flag that mm_gpu_device_status reports. */
+
+/* RMSNorm forward (crates/midman-nn/src/norm.rs:21-39): y = x * rstd * w per
+ * row, rstd[r] = 1 / sqrt(mean(x[r]^2) + eps) saved for the backward.
+ * dim a multiple of 4 up to 8192; x, w, y 16-byte aligned. */
+MM_GPU_EXPORT int32_t mm_gpu_rmsnorm_forward(int32_t rows, int32_t dim, const float *x, const float *w, float eps,
+                                             float *y, float *rstd, void *stream);
+/* RMSNorm backward (the autograd of norm.rs:21-39's six primitives): dx = dres +
+ * d(rmsnorm)/dx . dy (dres may be NULL or equal to dx), dw = sum over rows of
+ * dy * x * rstd (overwritten), summed in a fixed order (deterministic). */
+MM_GPU_EXPORT int32_t mm_gpu_rmsnorm_backward(int32_t rows, int32_t dim, const float *x, const float *w,
+                                              const float *rstd, const float *dy, const float *dres, float *dx,
+                                              float *dw, void *stream);
+/* Rotary embedding in place (crates/midman-nn/src/rope.rs:20-33): x is
+ * [rows, heads, head_dim] with row stride ld, rows = batch * seq, row r at
+ * position r % seq; each head's halves (x1, x2) become (x1 c - x2 s, x2 c + x1 s)
+ * with c, s the rows of the [seq, head_dim / 2] tables (midman_rope_table,
+ * rope.rs:54-132). backward != 0 applies the gradient (the rotation by -angle). */
+MM_GPU_EXPORT int32_t mm_gpu_rope(int32_t rows, int32_t seq, int32_t heads, int32_t head_dim, float *x, int64_t ld,
+                                  const float *cos_t, const float *sin_t, int32_t backward, void *stream);
+/* SwiGLU (crates/midman-nn/src/mlp.rs:20-24, silu ops_elementwise.rs:355-364):
+ * act = silu(gate) * up over n values. The backward works in place:
+ * gate <- dact * up * silu'(gate), up <- dact * silu(gate). */
+MM_GPU_EXPORT int32_t mm_gpu_swiglu_forward(int64_t n, const float *gate, const float *up, float *act, void *stream);
+MM_GPU_EXPORT int32_t mm_gpu_swiglu_backward(int64_t n, float *gate, float *up, const float *dact, void *stream);
+/* Embedding gather (crates/midman-tensor/src/ops_shape.rs:230-255): out[r] =
+ * table[ids[r]] with ids on the device; table [vocab, dim], dim a multiple of 4. */
+MM_GPU_EXPORT int32_t mm_gpu_embedding_forward(int32_t rows, const int32_t *ids, int32_t vocab, int32_t dim,
+                                               const float *table, float *out, void *stream);
+/* Embedding scatter-add (ops_shape.rs:262-272): dtable[ids[r]] += dx[r], each
+ * table row adding its rows in ascending row order (bit-identical run to run).
+ * ids_host is HOST memory: the index that orders the additions is built on the
+ * host and copied to the device. Ids outside [0, vocab): MM_GPU_ERR_INDEX,
+ * nothing queued. */
+MM_GPU_EXPORT int32_t mm_gpu_embedding_backward(int32_t rows, const int32_t *ids_host, int32_t vocab, int32_t dim,
+                                                const float *dx, float *dtable, void *stream);
+/* Softmax cross-entropy, forward and backward in one pass (crates/midman-tensor/
+ * src/ops_reduce.rs:236-276): logits [rows, vocab] (row stride ld) are replaced
+ * by grad_scale * (softmax - onehot(target)); row_loss[r] = max + ln(sum exp) -
+ * logit[target]; mean_loss (device, may be NULL) receives the mean of row_loss
+ * summed in f64 in a fixed order (the reference sums the loss in f64).
+ * grad_scale is d(loss)/d(mean), divided by rows (1 / rows for the mean loss). */
+MM_GPU_EXPORT int32_t mm_gpu_cross_entropy(int32_t rows, int32_t vocab, float *logits, int64_t ld,
+                                           const int32_t *targets, float grad_scale, float *row_loss,
+                                           double *mean_loss, void *stream);
+
+/* Failure-path self-test of the bounded waits (no counterpart in the
+ * reference): launches one thread that waits on a barrier nothing completes,
+ * through the same bounded wait the GEMM and attention pipelines use, limited
+ * to timeout_us (1 us .. 10 s). The wait runs out, the kernel records its code
+ * in the device error flag and returns, so mm_gpu_device_status reports
+ * MM_GPU_ERR_DEVICE ("a bounded wait ran out") and the context stays usable. */
+MM_GPU_EXPORT int32_t mm_gpu_wait_selftest(int32_t timeout_us, void *stream);
+
+/* ---- Data-parallel gradient exchange (the step crates/midman-training/src/
+ * trainer.rs:162-207 would take between backward and clip with more than one
+ * process; the reference is single-process and has no counterpart).
+ * One communicator per process and GPU, made from the 128-byte NCCL unique id
+ * that rank 0 produced (midman_nccl_unique_id) and shared out of band; create it
+ * with the rank's GPU current. */
+MM_GPU_EXPORT int32_t mm_gpu_comm_create(const uint8_t *nccl_id, int32_t world, int32_t rank, void **comm_out);
+MM_GPU_EXPORT int32_t mm_gpu_comm_destroy(void *comm);
+/* In-place all-reduce of one gradient bucket (n floats) across the ranks:
+ * the sum, or the mean when average != 0 (equal shards: the gradient of the
+ * mean loss over the global batch). Asynchronous on `stream`. */
+MM_GPU_EXPORT int32_t mm_gpu_allreduce_bucket(void *comm, float *data, int64_t n, int32_t average, void *stream);
+/* Waits for `stream` while polling the communicator for asynchronous NCCL
+ * errors. If a peer failed, or the stream has not finished after timeout_ms,
+ * the communicator is aborted (its collectives in flight end) and the call
+ * returns MM_GPU_ERR_DEVICE; an aborted communicator refuses further use and
+ * only mm_gpu_comm_destroy remains. */
+MM_GPU_EXPORT int32_t mm_gpu_comm_wait(void *comm, void *stream, int32_t timeout_ms);
+
 /* Allocation-free variant of mm_gpu_attention_forward with precision
  * MM_GPU_TF32 (the tensor-core path; head_dim 32, 64 or 128). No counterpart in
  * the reference, which has no device memory to manage.
@@ -121,6 +200,10 @@ MM_GPU_EXPORT int32_t mm_gpu_attention_backward(int32_t batch, int32_t seq, int3
  * holds until the process exits.
  *   - The first call on a device looks up that array's device address (once
  *     per device, with the device current); make it before any stream capture.
+ *     The address is kept for the life of the process: do not call this entry
+ *     point after a cudaDeviceReset of that device.
+ *   - head_dim 32, 64 or 128; ldq and ldk multiples of 4; q, k, v and o 16-byte
+ *     aligned (checked before anything is queued).
  *   - All calls share the array: calls whose kernels overlap on the GPU (on
  *     different streams, or from several threads) race on it. Serialize them.
  *   - device_status: device pointer to one int32 that the caller zeroes; the

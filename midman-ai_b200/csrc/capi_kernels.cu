@@ -37,6 +37,8 @@ int32_t guarded(F&& body) {
 cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
 }  // namespace
 
+void mm::set_last_error(const std::string& msg) { g_last_error = msg; }
+
 extern "C" {
 
 const char* mm_gpu_last_error(void) { return g_last_error.c_str(); }
@@ -206,7 +208,9 @@ static __device__ __align__(256) float g_static_scores[kStaticScoreFloats];
 
 // Device address of g_static_scores per device. In host code the array's name
 // is only a host-side stand-in, so the address is looked up once per device
-// with that device current.
+// with that device current and kept for the life of the process: a
+// cudaDeviceReset (which destroys the context holding the array) leaves the
+// cached address stale, so the entry point must not be used after one.
 std::mutex g_static_mu;
 std::vector<float*> g_static_ptr;
 
@@ -234,8 +238,17 @@ extern "C" int32_t mm_gpu_attention_forward_noalloc(int32_t batch, int32_t seq, 
     if (int32_t rc = attention_shape(batch, seq, n_heads, n_kv_heads, head_dim, ldq, ldk, &s)) return rc;
     if (!q || !k || !v || !o || !lse || !device_status)
       return fail(MM_GPU_ERR_ARGUMENT, "attention (no-alloc): null pointer");
-    if (!mm::attention_tc_supported(s))
+    if (head_dim != 32 && head_dim != 64 && head_dim != 128)
       return fail(MM_GPU_ERR_SHAPE, "attention (no-alloc): head_dim must be 32, 64 or 128");
+    if (ldq % 4 || ldk % 4)
+      return fail(MM_GPU_ERR_SHAPE, "attention (no-alloc): row strides ldq and ldk must be multiples of 4");
+    // checked before anything is queued, so a refused call leaves o and lse alone
+    for (const void* p : {static_cast<const void*>(q), static_cast<const void*>(k), static_cast<const void*>(v),
+                          static_cast<const void*>(o)})
+      if (reinterpret_cast<uintptr_t>(p) & 15u)
+        return fail(MM_GPU_ERR_ARGUMENT, "attention (no-alloc): q, k, v and o must be 16-byte aligned");
+    if (!mm::attention_tc_supported(s))
+      return fail(MM_GPU_ERR_SHAPE, "attention (no-alloc): shape not supported by the tensor-core path");
     const size_t need = static_cast<size_t>(batch) * n_heads * seq * mm::attention_scores_ld(seq);
     if (need > kStaticScoreFloats)
       return fail(MM_GPU_ERR_SHAPE, "attention (no-alloc): batch * n_heads * seq * round4(seq) = " +

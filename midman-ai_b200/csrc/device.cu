@@ -57,6 +57,26 @@ int take_device_error(cudaStream_t stream) {
   return code;
 }
 
+namespace {
+// One thread waits on a shared-memory barrier that nothing completes, through
+// the same bounded wait the GEMM and attention pipelines use: after timeout_ns
+// it records kErrWaitSelfTest in the error flag and the kernel returns. No copy
+// or tensor-memory allocation is outstanding when it gives up.
+__global__ void bounded_wait_selftest_kernel(int* err, unsigned long long timeout_ns) {
+  __shared__ __align__(8) unsigned long long bar;
+  const uint32_t a = smem_u32(&bar);
+  mbar_init(a, 1);
+  fence_barrier_init();
+  mbar_wait(a, 0, err, kErrWaitSelfTest, timeout_ns);
+}
+}  // namespace
+
+void bounded_wait_selftest(unsigned long long timeout_ns, cudaStream_t stream) {
+  DeviceContext& c = device_context();
+  bounded_wait_selftest_kernel<<<1, 1, 0, stream>>>(c.d_err, timeout_ns);
+  check_cuda(cudaGetLastError(), "bounded wait self-test");
+}
+
 std::string device_error_message(int code) {
   switch (code) {
     case kErrNone: return "no device error";
@@ -66,6 +86,8 @@ std::string device_error_message(int code) {
     case kErrWaitDrain: return "GEMM: teardown timed out draining TMA copies";
     case kErrBadShape: return "kernel rejected its shape";
     case kErrWaitUnit: return "GEMM: a role timed out waiting for its next work unit";
+    case kErrIndex: return "a token id or target class is outside [0, vocab)";
+    case kErrWaitSelfTest: return "self-test: a bounded wait ran out and the kernel returned";
     default: return "device error " + std::to_string(code);
   }
 }

@@ -29,6 +29,14 @@ int take_device_error(cudaStream_t stream);
 
 std::string device_error_message(int code);
 
+// Launches one thread that waits on a barrier nothing completes, bounded by
+// timeout_ns: it records kErrWaitSelfTest in the error flag and returns.
+void bounded_wait_selftest(unsigned long long timeout_ns, cudaStream_t stream);
+
+// Message of the last failing kernel-level C ABI call on this thread
+// (mm_gpu_last_error); the entry points of every capi_*.cu file set it.
+void set_last_error(const std::string& msg);
+
 // Throws std::runtime_error with the CUDA error text if `e` is not cudaSuccess.
 void check_cuda(cudaError_t e, const char* what);
 

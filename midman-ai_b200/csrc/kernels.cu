@@ -68,11 +68,19 @@ void check_launch(const char* what) {
 }
 
 // ---------------------------------------------------------------- embedding
-__global__ void embedding_fwd_kernel(const int32_t* __restrict__ ids, const float* __restrict__ table, int dim,
-                                     float* __restrict__ out) {
+// An id outside [0, vocab) reads nothing: its row is zero and the error flag
+// gets kErrIndex (the reference refuses such ids, ops_shape.rs:238-244).
+__global__ void embedding_fwd_kernel(const int32_t* __restrict__ ids, const float* __restrict__ table, int vocab,
+                                     int dim, float* __restrict__ out, int* err) {
   const int r = blockIdx.x;
-  const float4* src = reinterpret_cast<const float4*>(table + static_cast<long long>(ids[r]) * dim);
+  const int id = ids[r];
   float4* dst = reinterpret_cast<float4*>(out + static_cast<long long>(r) * dim);
+  if (id < 0 || id >= vocab) {
+    for (int j = threadIdx.x; j < dim / 4; j += blockDim.x) dst[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (threadIdx.x == 0 && err) atomicCAS(err, 0, 7 /* kErrIndex */);
+    return;
+  }
+  const float4* src = reinterpret_cast<const float4*>(table + static_cast<long long>(id) * dim);
   for (int j = threadIdx.x; j < dim / 4; j += blockDim.x) dst[j] = src[j];
 }
 
@@ -366,12 +374,17 @@ __device__ __forceinline__ MaxSum combine(MaxSum a, MaxSum b) {
   return {m, a.s * expf(a.m - m) + b.s * expf(b.m - m)};
 }
 
+// A target outside [0, vocab) reads no logit: the row's loss is NaN, its
+// gradient row is the softmax alone, and the error flag gets kErrIndex.
 __global__ void cross_entropy_kernel(float* logits, long long ld, const int32_t* __restrict__ targets, int vocab,
-                                     float grad_scale, float* __restrict__ row_loss) {
+                                     float grad_scale, float* __restrict__ row_loss, int* err) {
   __shared__ float sm[32], ss[32];
   __shared__ float row_max, row_sum;
   const long long r = blockIdx.x;
   float* z = logits + r * ld;
+  const int t_raw = targets[r];
+  const bool t_ok = t_raw >= 0 && t_raw < vocab;
+  if (!t_ok && threadIdx.x == 0 && err) atomicCAS(err, 0, 7 /* kErrIndex */);
   MaxSum acc{-INFINITY, 0.0f};
   const bool vec = (vocab & 3) == 0 && (ld & 3) == 0 && (reinterpret_cast<uintptr_t>(logits) & 15u) == 0;
   if (vec) {  // four logits per step: one max update, then four exponentials against it
@@ -418,13 +431,12 @@ __global__ void cross_entropy_kernel(float* logits, long long ld, const int32_t*
     if (lane == 0) {
       row_max = a.m;
       row_sum = a.s;
-      const int t = targets[r];
-      row_loss[r] = a.m + logf(a.s) - z[t];  // ops_reduce.rs:256-258
+      row_loss[r] = t_ok ? a.m + logf(a.s) - z[t_raw] : NAN;  // ops_reduce.rs:256-258
     }
   }
   __syncthreads();
   const float mx = row_max, sum = row_sum;
-  const int t = targets[r];
+  const int t = t_ok ? t_raw : -1;
   if (vec) {
     float4* z4 = reinterpret_cast<float4*>(z);
     for (int j = threadIdx.x; j < vocab / 4; j += blockDim.x) {
@@ -511,9 +523,10 @@ __global__ void scale_kernel(float* x, float f, long long n) {
 
 }  // namespace
 
-void embedding_forward(const int32_t* ids, int rows, const float* table, int dim, float* out, cudaStream_t s) {
+void embedding_forward(const int32_t* ids, int rows, const float* table, int vocab, int dim, float* out, int* err,
+                       cudaStream_t s) {
   if (rows <= 0) return;
-  embedding_fwd_kernel<<<rows, 128, 0, s>>>(ids, table, dim, out);
+  embedding_fwd_kernel<<<rows, 128, 0, s>>>(ids, table, vocab, dim, out, err);
   check_launch("embedding_forward");
 }
 
@@ -603,10 +616,10 @@ void swiglu_backward(float* g, float* u, const float* dact, long long n, cudaStr
 }
 
 void cross_entropy(float* logits, long long ld, const int32_t* targets, int rows, int vocab, float grad_scale,
-                   float* row_loss, cudaStream_t s) {
+                   float* row_loss, int* err, cudaStream_t s) {
   if (rows <= 0) return;
   const int threads = vocab >= 8192 ? 1024 : 256;
-  cross_entropy_kernel<<<rows, threads, 0, s>>>(logits, ld, targets, vocab, grad_scale, row_loss);
+  cross_entropy_kernel<<<rows, threads, 0, s>>>(logits, ld, targets, vocab, grad_scale, row_loss, err);
   check_launch("cross_entropy");
 }
 

@@ -8,8 +8,10 @@
 namespace mm {
 
 // ---- embedding (crates/midman-tensor/src/ops_shape.rs:230-275)
-// out[r] = table[ids[r]]
-void embedding_forward(const int32_t* ids, int rows, const float* table, int dim, float* out, cudaStream_t s);
+// out[r] = table[ids[r]]; an id outside [0, vocab) gives a zero row and sets *err
+// (when err is not null) to kErrIndex.
+void embedding_forward(const int32_t* ids, int rows, const float* table, int vocab, int dim, float* out, int* err,
+                       cudaStream_t s);
 // Deterministic scatter-add in the reference's order: for every distinct id u,
 // dtable[ids_u] += dx[p] for its positions p in ascending order (CSR on the host).
 void embedding_backward(const int32_t* uniq, const int32_t* offsets, const int32_t* positions, int n_uniq,
@@ -38,8 +40,9 @@ void swiglu_backward(float* g, float* u, const float* dact, long long n, cudaStr
 
 // ---- softmax cross-entropy (crates/midman-tensor/src/ops_reduce.rs:236-276)
 // In place: logits <- d(mean loss)/d logits (scale = 1/total_rows); row_loss[r] = max + ln(sum) - z_t.
+// A target outside [0, vocab) gives a NaN row loss and sets *err (when not null) to kErrIndex.
 void cross_entropy(float* logits, long long ld, const int32_t* targets, int rows, int vocab, float grad_scale,
-                   float* row_loss, cudaStream_t s);
+                   float* row_loss, int* err, cudaStream_t s);
 // loss_out[0] = sum(row_loss) / rows accumulated in f64 in a fixed order.
 void mean_loss(const float* row_loss, int rows, double* loss_out, cudaStream_t s);
 // Top-1 prediction per row (first index of the maximum, as lab.rs:300-302).

@@ -17,6 +17,8 @@ struct NcclApi {
   ncclResult_t (*GroupStart)();
   ncclResult_t (*GroupEnd)();
   const char* (*GetErrorString)(ncclResult_t);
+  ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*);
+  ncclResult_t (*CommAbort)(ncclComm_t);
 };
 
 // Throws std::runtime_error when NCCL cannot be loaded.

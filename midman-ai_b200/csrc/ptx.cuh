@@ -20,6 +20,8 @@ enum DeviceError : int {
   kErrWaitDrain = 4,    // teardown gave up waiting for copies in flight
   kErrBadShape = 5,
   kErrWaitUnit = 6,     // a GEMM role gave up waiting for its next work unit
+  kErrIndex = 7,        // a token id or target class outside [0, vocab); the row was not read
+  kErrWaitSelfTest = 8, // the bounded-wait self-test's wait ran out (as it is meant to)
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

@@ -5,9 +5,12 @@
 #include "nccl_api.h"
 
 #include <algorithm>
+#include <chrono>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <stdexcept>
+#include <thread>
 
 #include "attention.h"
 #include "device.h"
@@ -45,6 +48,8 @@ Trainer::Trainer(const ModelConfig& cfg, int batch, int seq, int precision, int 
   check_cuda(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "stream");
   if (world_ > 1) {
     if (!nccl_unique_id) throw std::invalid_argument("data parallelism needs an NCCL unique id");
+    if (const char* t = std::getenv("MIDMAN_EXCHANGE_TIMEOUT_MS"))
+      if (std::atoll(t) > 0) exchange_timeout_ms_ = std::atoll(t);
     ncclUniqueId id;
     std::memcpy(&id, nccl_unique_id, sizeof(id));
     ncclComm_t comm;
@@ -486,7 +491,38 @@ void Trainer::gemm_sum(int M, int N, const GemmSegment* segs, int nseg, float* C
   }
 }
 
+// With more than one rank, the wait for the step also watches the exchange: a
+// peer that failed shows up as an asynchronous NCCL error, a peer that left as
+// collectives that never finish. Either way the communicator is aborted (its
+// kernels in flight end) after the error or the deadline, and the step fails
+// with the reason; the trainer refuses further data-parallel work.
+void Trainer::wait_exchange(const char* where) {
+  if (world_ <= 1) return;
+  if (!comm_) throw std::runtime_error(std::string(where) + ": the data-parallel exchange was aborted earlier");
+  const auto deadline = std::chrono::steady_clock::now() + std::chrono::milliseconds(exchange_timeout_ms_);
+  for (;;) {
+    const cudaError_t q = cudaStreamQuery(stream_);
+    if (q == cudaSuccess) return;
+    if (q != cudaErrorNotReady) check_cuda(q, where);
+    ncclResult_t async = ncclSuccess;
+    const ncclResult_t r = nccl().CommGetAsyncError(static_cast<ncclComm_t>(comm_), &async);
+    const bool failed = r != ncclSuccess || (async != ncclSuccess && async != ncclInProgress);
+    if (failed || std::chrono::steady_clock::now() >= deadline) {
+      nccl().CommAbort(static_cast<ncclComm_t>(comm_));
+      comm_ = nullptr;
+      throw std::runtime_error(std::string(where) + ": " +
+                               (failed ? std::string("NCCL reported an asynchronous error: ") +
+                                             nccl().GetErrorString(r != ncclSuccess ? r : async)
+                                       : "the data-parallel exchange did not finish within " +
+                                             std::to_string(exchange_timeout_ms_) + " ms") +
+                               "; communicator aborted");
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(100));
+  }
+}
+
 void Trainer::check_device(const char* where) {
+  wait_exchange(where);
   const int code = take_device_error(stream_);
   if (code) throw std::runtime_error(std::string(where) + ": " + device_error_message(code));
 }

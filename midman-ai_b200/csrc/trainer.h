@@ -141,6 +141,7 @@ class Trainer {
   void build_chunks();
   uint64_t mv_begin() const { return zero1_ ? bounds_[rank_] : 0; }
   void check_device(const char* where);
+  void wait_exchange(const char* where);
   int prof_begin();
   void prof_end(int slot, const char* cls, double flops, std::string shape = {});
   void prof_collect();
@@ -151,7 +152,10 @@ class Trainer {
   uint64_t adam_steps_ = 0;
   uint64_t launches_ = 0;
   cudaStream_t stream_ = nullptr, comm_stream_ = nullptr;
-  void* comm_ = nullptr;  // ncclComm_t
+  void* comm_ = nullptr;  // ncclComm_t; null after an abort
+  // how long a step may wait for the exchange before the communicator is
+  // aborted (MIDMAN_EXCHANGE_TIMEOUT_MS, default 10 minutes)
+  long long exchange_timeout_ms_ = 600000;
   std::vector<cudaEvent_t> layer_done_;
   cudaEvent_t comm_done_ = nullptr;
 

@@ -53,7 +53,8 @@ void Trainer::forward(int B, int T, bool train) {
   };
   // under optimizer sharding, each bucket's parameters may still be arriving from their owner
   wait_params(0);
-  embedding_forward(d_ids_, N, P_ + layout_.embed, D, acts_[0].x, stream_);
+  embedding_forward(d_ids_, N, P_ + layout_.embed, static_cast<int>(cfg_.vocab), D, acts_[0].x,
+                    device_context().d_err, stream_);
   launches_ += 1;
   for (int l = 0; l < L; ++l) {
     Layer& a = acts_[l];
@@ -296,7 +297,7 @@ void Trainer::launch_step(float lr, const AdamHyper& h) {
   grads_partial_ = owner_reduce_;
   forward(batch_, seq_, true);
   cross_entropy(logits_, cfg_.vocab, d_tgt_, N, static_cast<int>(cfg_.vocab), 1.0f / static_cast<float>(N), row_loss_,
-                stream_);
+                device_context().d_err, stream_);
   mean_loss(row_loss_, N, d_loss_, stream_);
   launches_ += 2;
   backward(batch_, seq_);
@@ -317,7 +318,7 @@ float Trainer::loss_and_grads(const int32_t* inputs, const int32_t* targets) {
   const int N = batch_ * seq_;
   forward(batch_, seq_, true);
   cross_entropy(logits_, cfg_.vocab, d_tgt_, N, static_cast<int>(cfg_.vocab), 1.0f / static_cast<float>(N), row_loss_,
-                stream_);
+                device_context().d_err, stream_);
   mean_loss(row_loss_, N, d_loss_, stream_);
   backward(batch_, seq_);
   AdamHyper h;
@@ -334,7 +335,7 @@ float Trainer::eval(const int32_t* inputs, const int32_t* targets, int B, int T,
     check_cuda(cudaMemcpyAsync(predictions, d_pred_, N * 4, cudaMemcpyDeviceToHost, stream_), "predictions");
   }
   cross_entropy(logits_, cfg_.vocab, d_tgt_, N, static_cast<int>(cfg_.vocab), 1.0f / static_cast<float>(N), row_loss_,
-                stream_);
+                device_context().d_err, stream_);
   mean_loss(row_loss_, N, d_loss_, stream_);
   check_cuda(cudaMemcpyAsync(h_out_, d_loss_, sizeof(double), cudaMemcpyDeviceToHost, stream_), "loss D2H");
   check_device("eval");

@@ -16,7 +16,10 @@ LIB_PATH = HERE / "lib" / "libmidman_gpu.so"
 # Every symbol the public headers declare, grouped by header.
 GPU_SYMBOLS = [
     "mm_gpu_last_error", "mm_gpu_device_status", "mm_gpu_gemm", "mm_gpu_gemm_sum", "mm_gpu_clip_adamw", "mm_gpu_attention_forward",
-    "mm_gpu_attention_backward", "mm_gpu_attention_forward_noalloc",
+    "mm_gpu_attention_backward", "mm_gpu_attention_forward_noalloc", "mm_gpu_rmsnorm_forward",
+    "mm_gpu_rmsnorm_backward", "mm_gpu_rope", "mm_gpu_swiglu_forward", "mm_gpu_swiglu_backward",
+    "mm_gpu_embedding_forward", "mm_gpu_embedding_backward", "mm_gpu_cross_entropy", "mm_gpu_comm_create",
+    "mm_gpu_comm_destroy", "mm_gpu_allreduce_bucket", "mm_gpu_comm_wait", "mm_gpu_wait_selftest",
 ]
 API_SYMBOLS = [
     "midman_abi_version", "midman_alloc", "midman_free", "midman_text_ptr", "midman_text_len",
@@ -67,6 +70,19 @@ def load(path: str | os.PathLike | None = None) -> C.CDLL:
     _sig(lib, "mm_gpu_attention_forward_noalloc", i32, i32, i32, i32, i32, i32, vp, vp, vp, i64, i64, vp, vp, vp,
          vp)
     u32, u8p, dp, i32p = C.c_uint32, C.POINTER(C.c_uint8), C.POINTER(C.c_double), C.POINTER(C.c_int32)
+    _sig(lib, "mm_gpu_rmsnorm_forward", i32, i32, i32, vp, vp, C.c_float, vp, vp, vp)
+    _sig(lib, "mm_gpu_rmsnorm_backward", i32, i32, i32, vp, vp, vp, vp, vp, vp, vp, vp)
+    _sig(lib, "mm_gpu_rope", i32, i32, i32, i32, i32, vp, i64, vp, vp, i32, vp)
+    _sig(lib, "mm_gpu_swiglu_forward", i32, i64, vp, vp, vp, vp)
+    _sig(lib, "mm_gpu_swiglu_backward", i32, i64, vp, vp, vp, vp)
+    _sig(lib, "mm_gpu_embedding_forward", i32, i32, vp, i32, i32, vp, vp, vp)
+    _sig(lib, "mm_gpu_embedding_backward", i32, i32, i32p, i32, i32, vp, vp, vp)
+    _sig(lib, "mm_gpu_cross_entropy", i32, i32, i32, vp, i64, vp, C.c_float, vp, vp, vp)
+    _sig(lib, "mm_gpu_comm_create", i32, u8p, i32, i32, C.POINTER(vp))
+    _sig(lib, "mm_gpu_comm_destroy", i32, vp)
+    _sig(lib, "mm_gpu_allreduce_bucket", i32, vp, vp, i64, i32, vp)
+    _sig(lib, "mm_gpu_comm_wait", i32, vp, vp, i32)
+    _sig(lib, "mm_gpu_wait_selftest", i32, i32, vp)
     _sig(lib, "midman_abi_version", u32)
     _sig(lib, "midman_alloc", u8p, u32)
     _sig(lib, "midman_free", None, u8p, u32)
@@ -124,13 +140,14 @@ def load(path: str | os.PathLike | None = None) -> C.CDLL:
 
 
 class MidmanGpuError(RuntimeError):
-    pass
+    def __init__(self, status, message):
+        super().__init__(f"status {status}: {message}")
+        self.status = status
 
 
 def check(rc: int) -> int:
     if rc < 0:
-        msg = load().mm_gpu_last_error().decode(errors="replace")
-        raise MidmanGpuError(f"status {rc}: {msg}")
+        raise MidmanGpuError(rc, load().mm_gpu_last_error().decode(errors="replace"))
     return rc
 
 
@@ -195,6 +212,72 @@ def attention_forward_noalloc(q, k, v, o, lse, status, *, batch, seq, n_heads, n
     return check(load().mm_gpu_attention_forward_noalloc(batch, seq, n_heads, n_kv_heads, head_dim, _ptr(q), _ptr(k),
                                                          _ptr(v), ldq, ldk, _ptr(o), _ptr(lse), _ptr(status),
                                                          _stream(stream)))
+
+
+def rmsnorm_forward(x, w, y, rstd, *, rows, dim, eps=1e-5, stream=None):
+    return check(load().mm_gpu_rmsnorm_forward(rows, dim, _ptr(x), _ptr(w), eps, _ptr(y), _ptr(rstd),
+                                               _stream(stream)))
+
+
+def rmsnorm_backward(x, w, rstd, dy, dx, dw, *, rows, dim, dres=None, stream=None):
+    return check(load().mm_gpu_rmsnorm_backward(rows, dim, _ptr(x), _ptr(w), _ptr(rstd), _ptr(dy), _ptr(dres),
+                                                _ptr(dx), _ptr(dw), _stream(stream)))
+
+
+def rope(x, cos_t, sin_t, *, rows, seq, heads, head_dim, ld, backward=False, stream=None):
+    return check(load().mm_gpu_rope(rows, seq, heads, head_dim, _ptr(x), ld, _ptr(cos_t), _ptr(sin_t),
+                                    int(bool(backward)), _stream(stream)))
+
+
+def swiglu_forward(gate, up, act, *, n, stream=None):
+    return check(load().mm_gpu_swiglu_forward(n, _ptr(gate), _ptr(up), _ptr(act), _stream(stream)))
+
+
+def swiglu_backward(gate, up, dact, *, n, stream=None):
+    return check(load().mm_gpu_swiglu_backward(n, _ptr(gate), _ptr(up), _ptr(dact), _stream(stream)))
+
+
+def embedding_forward(ids, table, out, *, rows, vocab, dim, stream=None):
+    return check(load().mm_gpu_embedding_forward(rows, _ptr(ids), vocab, dim, _ptr(table), _ptr(out),
+                                                 _stream(stream)))
+
+
+def embedding_backward(ids_host, dx, dtable, *, vocab, dim, stream=None):
+    """ids_host: a numpy int32 array (host memory)."""
+    ids = _np.ascontiguousarray(ids_host, _np.int32)
+    return check(load().mm_gpu_embedding_backward(ids.size, _ip(ids), vocab, dim, _ptr(dx), _ptr(dtable),
+                                                  _stream(stream)))
+
+
+def cross_entropy(logits, targets, row_loss, *, rows, vocab, ld, grad_scale, mean_loss=None, stream=None):
+    return check(load().mm_gpu_cross_entropy(rows, vocab, _ptr(logits), ld, _ptr(targets), grad_scale,
+                                             _ptr(row_loss), _ptr(mean_loss), _stream(stream)))
+
+
+class Comm:
+    """mm_gpu_comm_*: one data-parallel communicator of this process's GPU."""
+
+    def __init__(self, nccl_id: bytes, world: int, rank: int):
+        idb = (C.c_uint8 * 128).from_buffer_copy(nccl_id)
+        out = C.c_void_p()
+        check(load().mm_gpu_comm_create(C.cast(idb, C.POINTER(C.c_uint8)), world, rank, C.byref(out)))
+        self.h = out.value
+
+    def allreduce(self, t, n=None, average=True, stream=None):
+        return check(load().mm_gpu_allreduce_bucket(self.h, _ptr(t), t.numel() if n is None else n,
+                                                    int(bool(average)), _stream(stream)))
+
+    def wait(self, stream=None, timeout_ms=10_000):
+        return check(load().mm_gpu_comm_wait(self.h, _stream(stream), timeout_ms))
+
+    def close(self):
+        if self.h:
+            check(load().mm_gpu_comm_destroy(self.h))
+            self.h = None
+
+
+def wait_selftest(timeout_us, stream=None):
+    return check(load().mm_gpu_wait_selftest(timeout_us, _stream(stream)))
 
 
 def device_status(stream=None):

@@ -262,6 +262,23 @@ void or_gemm_nn(const float* a, const float* b, float* c, size_t m, size_t k, si
 void or_gemm_nt(const float* a, const float* b, float* c, size_t m, size_t k, size_t n) { gemm_nt(a, b, c, m, k, n); }
 void or_gemm_tn(const float* a, const float* b, float* c, size_t k, size_t m, size_t n) { gemm_tn(a, b, c, k, m, n); }
 void or_softmax_rows(const float* x, float* y, size_t rows, size_t cols) { softmax_rows(x, y, rows, cols); }
+void or_rms_norm(const float* x, const float* w, size_t rows, size_t d, float eps, float* y, float* rstd) {
+  rms_norm_layer(x, w, rows, d, eps, y, rstd);
+}
+void or_rms_norm_bwd(const float* x, const float* w, const float* gy, size_t rows, size_t d, float eps, float* dx,
+                     float* dw) {
+  rms_norm_layer_bwd(x, w, gy, rows, d, eps, dx, dw);
+}
+void or_rope(float* x, size_t bh, size_t t, size_t hd, const float* cos_t, const float* sin_t, int backward) {
+  rope_layer(x, bh, t, hd, cos_t, sin_t, backward != 0);
+}
+void or_swiglu(const float* g, const float* u, size_t n, float* act, const float* dact, float* dg, float* du) {
+  swiglu_layer(g, u, n, act, dact, dg, du);
+}
+void or_embedding(const int32_t* ids, size_t rows, const float* table, size_t d, float* out, const float* dx,
+                  float* dtable) {
+  embedding_layer(ids, rows, table, d, out, dx, dtable);
+}
 float or_cross_entropy(const float* logits, const int32_t* targets, size_t n, size_t v, float* grad) {
   return cross_entropy(logits, targets, n, v, grad);
 }

@@ -471,6 +471,57 @@ void softmax_rows(const float* x, float* y, size_t rows, size_t cols) {
 }
 
 // ops_reduce.rs:236-276: mean loss (f64 total) and, if grad != null, d loss / d logits.
+// Known-answer entry points of single layers, for the kernel-level tests.
+// rms_norm (norm.rs:21-39); rstd_out[r] = the row's t^-0.5.
+void rms_norm_layer(const float* x, const float* w, size_t rows, size_t d, float eps, float* y, float* rstd_out) {
+  NormSaved s;
+  rms_norm_fwd(x, w, rows, d, eps, y, s);
+  if (rstd_out) std::memcpy(rstd_out, s.inv.data(), rows * sizeof(float));
+}
+
+// Backward of rms_norm (the six primitives' closures): dx, dw overwritten.
+void rms_norm_layer_bwd(const float* x, const float* w, const float* gy, size_t rows, size_t d, float eps, float* dx,
+                        float* dw) {
+  NormSaved s;
+  Vec y(rows * d);
+  rms_norm_fwd(x, w, rows, d, eps, y.data(), s);
+  std::memset(dx, 0, rows * d * sizeof(float));
+  std::memset(dw, 0, d * sizeof(float));
+  rms_norm_bwd(x, w, s, gy, rows, d, dx, dw);
+}
+
+// apply_rope (rope.rs:20-33) or its gradient, in place on [B, heads, T, hd].
+void rope_layer(float* x, size_t BH, size_t T, size_t hd, const float* cos_t, const float* sin_t, bool backward) {
+  if (backward)
+    rope_bwd(x, BH, T, hd, cos_t, sin_t);
+  else
+    rope_fwd(x, BH, T, hd, cos_t, sin_t);
+}
+
+// swiglu (mlp.rs:20-24): act = silu(g) * u; with dact, the gradients dg, du.
+void swiglu_layer(const float* g, const float* u, size_t n, float* act, const float* dact, float* dg, float* du) {
+  for (size_t i = 0; i < n; ++i) {
+    const float gs = g[i] * sigmoid(g[i]);
+    if (act) act[i] = gs * u[i];
+    if (dact) {
+      const float dgs = dact[i] * u[i];
+      du[i] = dact[i] * gs;
+      const float sg = sigmoid(g[i]);
+      dg[i] = dgs * (sg * (1.0f + g[i] * (1.0f - sg)));
+    }
+  }
+}
+
+// embedding gather (ops_shape.rs:230-255) and scatter-add (:262-272, rows in order).
+void embedding_layer(const int32_t* ids, size_t rows, const float* table, size_t d, float* out, const float* dx,
+                     float* dtable) {
+  for (size_t r = 0; r < rows; ++r) {
+    if (out) std::memcpy(out + r * d, table + static_cast<size_t>(ids[r]) * d, d * sizeof(float));
+    if (dx)
+      for (size_t j = 0; j < d; ++j) dtable[static_cast<size_t>(ids[r]) * d + j] += dx[r * d + j];
+  }
+}
+
 float cross_entropy(const float* logits, const int32_t* targets, size_t n, size_t v, float* grad) {
   double total = 0.0;
   const float scale = 1.0f / static_cast<float>(n);

@@ -83,6 +83,11 @@ def lib() -> C.CDLL:
     sig("or_cross_entropy", f32, P(f32), P(C.c_int32), sz, sz, P(f32))
     sig("or_causal_attention", i32, P(f64), P(f32), P(f32), P(f32), i32, i32, P(f32), P(f32))
     sig("or_adamw_update", i32, P(f32), P(f32), P(f32), P(f32), sz, i32, u64, f32, f32, f32, f32, f32)
+    sig("or_rms_norm", None, P(f32), P(f32), sz, sz, f32, P(f32), P(f32))
+    sig("or_rms_norm_bwd", None, P(f32), P(f32), P(f32), sz, sz, f32, P(f32), P(f32))
+    sig("or_rope", None, P(f32), sz, sz, sz, P(f32), P(f32), i32)
+    sig("or_swiglu", None, P(f32), P(f32), sz, P(f32), P(f32), P(f32), P(f32))
+    sig("or_embedding", None, P(C.c_int32), sz, P(f32), sz, P(f32), P(f32), P(f32))
     _lib = L
     return L
 
@@ -214,11 +219,15 @@ class Model:
         assert a.size == self.n
         lib().or_model_set_params(self.h, _p(a, C.c_float))
 
-    def loss(self, inputs, targets, batch, seq, grads: bool = False):
+    def loss(self, inputs, targets, batch, seq, grads: bool = False, out=None):
+        """(loss, gradients) or loss; `out` (float32, n values) receives the gradients when given."""
         i = np.ascontiguousarray(inputs, np.int32)
         t = np.ascontiguousarray(targets, np.int32)
         loss = np.zeros(1, np.float32)
-        g = np.zeros(self.n, np.float32) if grads else None
+        g = None
+        if grads:
+            g = out if out is not None else np.zeros(self.n, np.float32)
+            assert g.dtype == np.float32 and g.size == self.n and g.flags.c_contiguous
         rc = lib().or_model_loss(self.h, _p(i, C.c_int32), _p(t, C.c_int32), batch, seq, _p(loss, C.c_float),
                                  _p(g, C.c_float) if grads else None)
         if rc:
@@ -300,6 +309,71 @@ def causal_attention(q, k, v, n_heads, n_kv_heads):
     if rc:
         raise ValueError("bad attention config")
     return out, probs
+
+
+def rms_norm(x, w, eps=1e-5):
+    """norm.rs:21-39 on rows of x [rows, d]: (y, rstd per row)."""
+    x, w = _f32(x), _f32(w)
+    rows, d = x.shape
+    y = np.zeros_like(x)
+    rstd = np.zeros(rows, np.float32)
+    lib().or_rms_norm(_p(x, C.c_float), _p(w, C.c_float), rows, d, eps, _p(y, C.c_float), _p(rstd, C.c_float))
+    return y, rstd
+
+
+def rms_norm_backward(x, w, dy, eps=1e-5):
+    """The reference autograd of rms_norm: (dx, dw)."""
+    x, w, dy = _f32(x), _f32(w), _f32(dy)
+    rows, d = x.shape
+    dx = np.zeros_like(x)
+    dw = np.zeros(d, np.float32)
+    lib().or_rms_norm_bwd(_p(x, C.c_float), _p(w, C.c_float), _p(dy, C.c_float), rows, d, eps, _p(dx, C.c_float),
+                          _p(dw, C.c_float))
+    return dx, dw
+
+
+def rope(x, cos_t, sin_t, backward=False):
+    """apply_rope (rope.rs:20-33) or its gradient on x [B, heads, T, hd]; returns a new array."""
+    y = np.array(x, np.float32, copy=True, order="C")
+    B, Hh, T, hd = y.shape
+    c, s = _f32(cos_t), _f32(sin_t)
+    lib().or_rope(_p(y, C.c_float), B * Hh, T, hd, _p(c, C.c_float), _p(s, C.c_float), int(bool(backward)))
+    return y
+
+
+def swiglu(g, u, dact=None):
+    """mlp.rs:20-24: act = silu(g) * u, or with dact the gradients (dg, du)."""
+    g, u = _f32(g), _f32(u)
+    n = g.size
+    if dact is None:
+        act = np.zeros_like(g)
+        lib().or_swiglu(_p(g, C.c_float), _p(u, C.c_float), n, _p(act, C.c_float), None, None, None)
+        return act
+    dact = _f32(dact)
+    dg, du = np.zeros_like(g), np.zeros_like(u)
+    lib().or_swiglu(_p(g, C.c_float), _p(u, C.c_float), n, None, _p(dact, C.c_float), _p(dg, C.c_float),
+                    _p(du, C.c_float))
+    return dg, du
+
+
+def embedding(ids, table):
+    """ops_shape.rs:230-255: table[ids]."""
+    ids = np.ascontiguousarray(ids, np.int32)
+    table = _f32(table)
+    out = np.zeros((ids.size, table.shape[1]), np.float32)
+    lib().or_embedding(_p(ids, C.c_int32), ids.size, _p(table, C.c_float), table.shape[1], _p(out, C.c_float), None,
+                       None)
+    return out
+
+
+def embedding_backward(ids, dx, dtable):
+    """ops_shape.rs:262-272: dtable[ids[r]] += dx[r] in row order, in place on dtable."""
+    ids = np.ascontiguousarray(ids, np.int32)
+    dx = _f32(dx)
+    assert dtable.dtype == np.float32 and dtable.flags.c_contiguous
+    lib().or_embedding(_p(ids, C.c_int32), ids.size, None, dtable.shape[1], None, _p(dx, C.c_float),
+                       _p(dtable, C.c_float))
+    return dtable
 
 
 def adamw_update(x, g, m, v, decay, step, lr, beta1, beta2, eps, wd):

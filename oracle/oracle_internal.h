@@ -91,6 +91,13 @@ void causal_attention(const Config& c, const float* q, const float* k, const flo
                       float* out, float* probs);
 void softmax_rows(const float* x, float* y, size_t rows, size_t cols);
 float cross_entropy(const float* logits, const int32_t* targets, size_t n, size_t v, float* grad);
+void rms_norm_layer(const float* x, const float* w, size_t rows, size_t d, float eps, float* y, float* rstd_out);
+void rms_norm_layer_bwd(const float* x, const float* w, const float* gy, size_t rows, size_t d, float eps, float* dx,
+                        float* dw);
+void rope_layer(float* x, size_t BH, size_t T, size_t hd, const float* cos_t, const float* sin_t, bool backward);
+void swiglu_layer(const float* g, const float* u, size_t n, float* act, const float* dact, float* dg, float* du);
+void embedding_layer(const int32_t* ids, size_t rows, const float* table, size_t d, float* out, const float* dx,
+                     float* dtable);
 
 // One AdamW update over a flat array (adamw.rs:192-215); decay: the parameter has rank >= 2.
 void adamw_update(float* x, const float* g, float* m, float* v, size_t n, bool decay, uint64_t step, float lr,

@@ -66,5 +66,5 @@ def main(ref_dir):
 
 
 if __name__ == "__main__":
-    default = os.environ.get("MIDMAN_REFERENCE_DIR", "/root/reference")
+    default = os.environ.get("MIDMAN_REFERENCE_DIR", str(Path(__file__).resolve().parents[3] / "reference"))
     sys.exit(main(sys.argv[1] if len(sys.argv) > 1 else default))

@@ -20,6 +20,8 @@ CASES = [  # (B, T, H, Hkv, hd)
     (1, 64, 2, 1, 16),
     (1, 2048, 4, 2, 128),
     (3, 77, 6, 3, 64),
+    (8, 1024, 16, 16, 64),  # configs[2]: B 8, 16 heads of 64, T 1024
+    (4, 2048, 16, 8, 128),  # the attention of configs[4]'s layers: 512 query tiles over the persistent pairs
 ]
 
 

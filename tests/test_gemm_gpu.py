@@ -129,3 +129,35 @@ def test_gemm_sum_matches_float64(mm, case, majors, residual):
     got = c[:, :n]
     assert torch.isfinite(got).all()
     assert rel_l2(got, want) < TF32_TOL
+
+
+# the isolated Linear op fwd+bwd, X [4096 x K], W [K x N], dY [4096 x N], N(0,1) from a
+# seed, checked against the reference's CPU matmul (the oracle's gemm_nn / gemm_nt / gemm_tn, which
+# keep kernels.rs:87-109's per-element order): Y = X W, dX = dY W^T, dW = X^T dY.
+LINEAR_SHAPES = [(512, 512), (512, 1408), (1024, 4096), (2048, 5632)]
+
+
+@pytest.mark.parametrize("precision", [0, 1])
+@pytest.mark.parametrize("kn", LINEAR_SHAPES)
+def test_linear_config_products_match_the_reference_matmul(mm, kn, precision):
+    import numpy as np
+    import oracle as orc
+    K, N = kn
+    M = 4096
+    rs = np.random.default_rng(K * 10_000 + N)
+    x = rs.standard_normal((M, K), dtype=np.float32)
+    w = rs.standard_normal((K, N), dtype=np.float32)
+    dy = rs.standard_normal((M, N), dtype=np.float32)
+    want = {"y": orc.gemm_nn(x, w), "dx": orc.gemm_nt(dy, w), "dw": orc.gemm_tn(x, dy)}
+    xg, wg, dyg = (torch.from_numpy(a).cuda() for a in (x, w, dy))
+    y, dx, dw = torch.empty(M, N, device="cuda"), torch.empty(M, K, device="cuda"), torch.empty(K, N, device="cuda")
+    mm.gemm(xg, wg, y, m=M, n=N, k=K, lda=K, ldb=N, ldc=N, a_mn_major=False, b_mn_major=True, precision=precision)
+    mm.gemm(dyg, wg, dx, m=M, n=K, k=N, lda=N, ldb=N, ldc=K, a_mn_major=False, b_mn_major=False,
+            precision=precision)
+    mm.gemm(xg, dyg, dw, m=K, n=N, k=M, lda=K, ldb=N, ldc=N, a_mn_major=True, b_mn_major=True, precision=precision)
+    mm.device_status()
+    for name, got, k in (("y", y, K), ("dx", dx, N), ("dw", dw, M)):
+        ref = torch.from_numpy(want[name]).cuda().double()
+        err = rel_l2(got, ref)
+        # the reference's own f32 sums carry an error growing like sqrt(K) as well
+        assert err < (TF32_TOL if precision == 0 else X3_TOL * max(1.0, (k / 1000) ** 0.5)), (name, err)

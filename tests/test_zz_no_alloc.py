@@ -29,7 +29,9 @@ def inputs(B, T, H, Hkv, hd, seed):
 
 def test_noalloc_matches_allocating_entry_point(mm):
     status = torch.zeros(1, dtype=torch.int32, device="cuda")
-    for n, (B, T, H, Hkv, hd) in enumerate([(2, 300, 4, 1, 32), (3, 77, 6, 3, 64)]):
+    # head_dim 32, 64 and 128 (the O = PV product's two tile widths); the last case is
+    # smaller than the first, so the shared array still holds older scores
+    for n, (B, T, H, Hkv, hd) in enumerate([(1, 512, 8, 2, 128), (2, 300, 4, 1, 32), (3, 77, 6, 3, 64)]):
         q, k, v = inputs(B, T, H, Hkv, hd, seed=17 + n)
         kw = dict(batch=B, seq=T, n_heads=H, n_kv_heads=Hkv, head_dim=hd, ldq=H * hd, ldk=Hkv * hd)
         o_ref, lse_ref = torch.empty(B, T, H, hd, device="cuda"), torch.empty(B, H, T, device="cuda")
@@ -57,3 +59,53 @@ def test_noalloc_refuses_sizes_past_its_scratch(mm):
     q, k, v = inputs(1, 64, H, Hkv, 16, seed=4)
     with pytest.raises(mm.MidmanGpuError, match="head_dim must be 32, 64 or 128"):
         mm.attention_forward_noalloc(q, k, v, o, lse, status, **dict(kw, seq=64))
+    # row strides that TMA cannot address, and a misaligned output: refused before anything runs
+    q, k, v = inputs(1, 64, 2, 2, 64, seed=5)
+    o, lse = torch.full((1, 64, 2, 64), 7.0, device="cuda"), torch.full((1, 2, 64), 7.0, device="cuda")
+    kw = dict(batch=1, seq=64, n_heads=2, n_kv_heads=2, head_dim=64, ldq=128, ldk=128)
+    with pytest.raises(mm.MidmanGpuError, match="multiples of 4"):
+        mm.attention_forward_noalloc(q, k, v, o, lse, status, **dict(kw, ldq=130))
+    o_flat = torch.full((64 * 128 + 1,), 7.0, device="cuda")
+    with pytest.raises(mm.MidmanGpuError, match="16-byte aligned"):
+        mm.attention_forward_noalloc(q, k, v, o_flat[1:], lse, status, **kw)
+    torch.cuda.synchronize()
+    assert (lse == 7.0).all() and (o_flat == 7.0).all()
+
+
+FRESH = r"""
+import sys, torch
+sys.path.insert(0, sys.argv[1])
+import midman_b200 as mm
+torch.cuda.init()
+B, T, H, Hkv, hd = 2, 256, 4, 2, 64
+g = torch.Generator(device="cuda").manual_seed(1)
+q = torch.randn(B, T, H, hd, device="cuda", generator=g)
+k = torch.randn(B, T, Hkv, hd, device="cuda", generator=g)
+v = torch.randn(B, T, Hkv, hd, device="cuda", generator=g)
+o, lse = torch.empty_like(q), torch.empty(B, H, T, device="cuda")
+status = torch.zeros(1, dtype=torch.int32, device="cuda")
+kw = dict(batch=B, seq=T, n_heads=H, n_kv_heads=Hkv, head_dim=hd, ldq=H * hd, ldk=Hkv * hd)
+mm.attention_forward_noalloc(q, k, v, o, lse, status, **kw)  # first call: loads the kernels
+torch.cuda.synchronize()
+free0 = torch.cuda.mem_get_info()[0]
+for _ in range(3):
+    mm.attention_forward_noalloc(q, k, v, o, lse, status, **kw)
+torch.cuda.synchronize()
+free1 = torch.cuda.mem_get_info()[0]
+assert status.item() == 0 and torch.isfinite(o).all()
+print("FREE", free0, free1)
+"""
+
+
+def test_noalloc_in_a_fresh_process_takes_no_device_memory(mm, tmp_path):
+    """Called first thing in a new process, repeated calls leave the device's free memory unchanged."""
+    import subprocess
+    import sys
+    from pathlib import Path
+    script = tmp_path / "fresh.py"
+    script.write_text(FRESH)
+    pkg = Path(mm.__file__).resolve().parent
+    r = subprocess.run([sys.executable, str(script), str(pkg)], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    free0, free1 = (int(x) for x in r.stdout.split("FREE")[1].split())
+    assert free0 == free1, (free0, free1)
