@@ -1,8 +1,10 @@
-// 3xTF32 ("exact") mode of the GEMM: each operand is split into a TF32-exact
-// high part and the remainder, x = hi + lo with hi = x with its low 13 mantissa
-// bits cleared, and the product is formed as hi*hi + hi*lo + lo*hi on the TF32
-// tensor cores (the lo*lo term is below f32 resolution). This is the split of
-// Ootomo & Yokota (2022); it recovers close to f32 accuracy at 3x the MMA work.
+// 3xTF32 ("exact") mode of the GEMM: each operand is split into two TF32
+// numbers, x ~ hi + lo with hi = x rounded to TF32 (nearest) and lo = (x - hi)
+// rounded to TF32 as well, and the product is formed as hi*hi + hi*lo + lo*hi
+// on the TF32 tensor cores (lo*lo is below f32 resolution). This is the split
+// of Ootomo & Yokota (2022); rounding both parts to nearest (rather than
+// truncating hi and letting the tensor core truncate lo) leaves
+// |x - hi - lo| <= 2^-22 |x|, close to f32's own 2^-24, at 3x the MMA work.
 #include <cuda_runtime.h>
 
 #include "device.h"
@@ -12,15 +14,23 @@ namespace mm {
 
 namespace {
 
+// Round to the nearest TF32 value (ties away from zero); the result's low 13
+// mantissa bits are zero, so the tensor core reads it unchanged.
+__device__ __forceinline__ float to_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
 __global__ void split_tf32_kernel(const float* __restrict__ x, float* __restrict__ hi,
                                   float* __restrict__ lo, long long n) {
   long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
   const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
   for (; i < n; i += stride) {
     const float v = x[i];
-    const float h = __uint_as_float(__float_as_uint(v) & 0xFFFFE000u);
+    const float h = to_tf32(v);
     hi[i] = h;
-    lo[i] = v - h;  // exact in f32
+    lo[i] = to_tf32(v - h);  // v - h is exact in f32; its TF32 rounding drops < 2^-11 of it
   }
 }
 
@@ -39,6 +49,10 @@ void split(const float* x, float* hi, float* lo, long long n, cudaStream_t s) {
 
 long long round4(long long n) { return (n + 3) & ~3ll; }
 
+// K per tensor-memory accumulation in 3xTF32 (a multiple of 4, so that every
+// chunk's first element stays 16-byte aligned for the tensor maps).
+constexpr int kChunkK = 256;
+
 }  // namespace
 
 int gemm_3xtf32(int M, int N, int K, GemmOperand A, GemmOperand B, float* C, long long ldc,
@@ -51,13 +65,28 @@ int gemm_3xtf32(int M, int N, int K, GemmOperand A, GemmOperand B, float* C, lon
   float *a_hi = ws, *a_lo = ws + pa, *b_hi = ws + 2 * pa, *b_lo = ws + 2 * pa + pb;
   split(A.ptr, a_hi, a_lo, na, stream);
   split(B.ptr, b_hi, b_lo, nb, stream);
-  GemmOperand Ah{a_hi, A.ld, A.mn_major}, Al{a_lo, A.ld, A.mn_major};
-  GemmOperand Bh{b_hi, B.ld, B.mn_major}, Bl{b_lo, B.ld, B.mn_major};
-  // Small terms first, then the large one, so the small ones are not rounded
-  // away against a large partial sum before they are combined (one accumulator
-  // over the three K ranges when the shape runs on CTA pairs).
-  const GemmSegment terms[3] = {{Al, Bh, K}, {Ah, Bl, K}, {Ah, Bh, K}};
-  return gemm_tf32_sum(M, N, terms, 3, C, ldc, R, ldr, d_err, stream);
+  // The tensor core's f32 accumulation loses a little on every step, in the
+  // same direction, so its error grows linearly with K (measured against
+  // float64: 4.8e-6 relative at K = 2048, 1.9e-5 at K = 8192, where f32 on the
+  // CUDA cores stays at 0.8-1.6e-6). K is therefore taken in chunks of
+  // kChunkK: each launch accumulates one chunk from zero in tensor memory and
+  // its epilogue adds the result to the sum so far (R = C) in f32 on the CUDA
+  // cores, with round-to-nearest.
+  int rc = 0;
+  for (int k0 = 0; k0 < K && rc == 0; k0 += kChunkK) {
+    const int kc = K - k0 < kChunkK ? K - k0 : kChunkK;
+    auto at = [&](const float* base, const GemmOperand& op) {  // the operand from K index k0 on
+      return op.mn_major ? base + static_cast<long long>(k0) * op.ld : base + k0;
+    };
+    GemmOperand Ah{at(a_hi, A), A.ld, A.mn_major}, Al{at(a_lo, A), A.ld, A.mn_major};
+    GemmOperand Bh{at(b_hi, B), B.ld, B.mn_major}, Bl{at(b_lo, B), B.ld, B.mn_major};
+    // Small terms first, then the large one, so the small ones are not rounded
+    // away against a large partial sum before they are combined (one
+    // accumulator over the three K ranges when the shape runs on CTA pairs).
+    const GemmSegment terms[3] = {{Al, Bh, kc}, {Ah, Bl, kc}, {Ah, Bh, kc}};
+    rc = gemm_tf32_sum(M, N, terms, 3, C, ldc, k0 == 0 ? R : C, k0 == 0 ? ldr : ldc, d_err, stream);
+  }
+  return rc;
 }
 
 }  // namespace mm
