@@ -15,7 +15,9 @@ of midman_train_run, the library's training loop over the batcher: taking each
 global batch on the host, the host-to-device copy of this rank's ids and the
 read-back of its loss and gradient norm are inside the timed region (the host
 prepares batch s+1 while the GPU runs step s). `--impl reference` times the CPU restatement of the reference's
-f32 path (oracle/) on a bounded sample of the same workload on all host cores.
+f32 path (oracle/) on one host thread, as the reference runs (its step time at the workload's size extrapolated
+in FLOPs from a bounded sample, and labelled so). A one-GPU run of the default workload also measures
+BASELINE.json's other configs (tiny, mid, Linear, attention block) under the `configs` key.
 """
 from __future__ import annotations
 
@@ -125,128 +127,285 @@ def measured_peaks():
     return json.loads(p.read_text()) if p.exists() else {}
 
 
-def cpu_baseline(cfg, seq_full, steps=1, warmup=0, threads=None):
-    """The oracle (CPU restatement of the reference f32 step) on a bounded sample of the workload: full
-    steps (forward, backward, clip, AdamW) of the same model on 1 x S tokens, S = min(64, seq) for models
-    above 100M parameters, else min(256, seq). Returns the median tokens/s over `steps` steps."""
+def executed_flops_per_token(cfg, seq):
+    """FLOPs per token the reference's CPU path executes: 6 x (matmul params incl. the head) plus the
+    full T x T score and value products (the reference computes the masked half too,
+    attention.rs:79-85), forward and backward."""
+    v, d, l, h, kv_h, ff, _ = cfg
+    kv = kv_h * (d // h)
+    matmul = l * (2 * d * d + 2 * d * kv + 3 * d * ff) + d * v
+    return 6 * matmul + l * 3 * 2 * 2 * seq * d
+
+
+def cpu_baseline(cfg, batch, seq, steps=1, threads=1):
+    """The oracle (C++ restatement of the reference's f32 training step, AVX register-tile products with
+    separate multiply and add like the reference's `--features avx` kernels) on `threads` host threads
+    (1 = the reference, which is single-threaded).
+
+    Models up to 10M parameters: full steps (forward, loss, backward, clip, AdamW) of the workload itself.
+    Larger models: forward + backward of a sample of 1 x 64 tokens, and clip + AdamW over every parameter,
+    timed apart; the step time at the workload's batch x seq is extrapolated linearly in the executed FLOPs
+    of forward + backward, plus the measured optimizer time."""
     sys.path.insert(0, str(ROOT / "oracle"))
     import oracle as orc
-    threads = threads or os.cpu_count() or 1
-    orc.set_threads(threads)
+    nproc = os.cpu_count() or 1
+    orc.set_threads(nproc)  # the seeded init may use every core; it is not timed
     c = orc.config_array(*cfg)
-    big = orc.param_breakdown(c)["total"] > 100_000_000
-    sample_seq = min(64 if big else 256, seq_full)
+    n_params = orc.param_breakdown(c)["total"]
     rng = orc.Rng(0)
     model = orc.Model(c, rng=rng)
-    ids = np.array([rng.below(cfg[0]) for _ in range(sample_seq + 1)], np.int32)
     opt = orc.AdamW(model, 0.9, 0.95, 1e-8, 0.1)
-    times = []
-    for k in range(warmup + steps):
-        t0 = time.perf_counter()
-        orc.train_update(model, opt, ids[:-1], ids[1:], 1, sample_seq, 1.0, 3e-4)
-        if k >= warmup:
+    orc.set_threads(threads)
+    out = {"unit": "tokens/s", "cores": threads, "nproc": nproc, "kind": "port", "params": n_params}
+    if n_params <= 10_000_000:
+        n = batch * seq
+        ids = np.array([rng.below(cfg[0]) for _ in range(n + 1)], np.int32)
+        times = []
+        for _ in range(steps + 1):  # the first step warms the caches and the allocator
+            t0 = time.perf_counter()
+            orc.train_update(model, opt, ids[:-1], ids[1:], batch, seq, 1.0, 3e-4)
             times.append(time.perf_counter() - t0)
-    dt = statistics.median(times)
-    return {"value": sample_seq / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
-            "sample": f"{len(times)} full step(s) (fwd+bwd+clip+AdamW) of the same model on 1 x {sample_seq} "
-                      f"tokens, median {dt:.2f} s on {threads} threads; the C++ restatement of the reference CPU "
-                      f"path (oracle/), not the Rust binary (no cargo on this image); shorter sequences than the "
-                      f"workload's {seq_full} make the CPU's attention share smaller, so this favours the CPU"}
+        dt = statistics.median(times[1:])
+        out.update(value=n / dt, extrapolated=False,
+                   sample=f"{steps} full step(s) (fwd+bwd+clip+AdamW) of the workload ({batch} x {seq} tokens) after "
+                          f"one warm-up step, median {dt:.3f} s on {threads} of {nproc} host threads; the C++ "
+                          f"restatement of the reference CPU path (oracle/), not the Rust binary (no cargo here)")
+        return out
+    s_tok = min(64, seq)
+    ids = np.array([rng.below(cfg[0]) for _ in range(s_tok + 1)], np.int32)
+    g = np.zeros(n_params, np.float32)
+    fb = []
+    for k in range(steps + 1):  # the first pass warms the caches and maps the buffers
+        t0 = time.perf_counter()
+        model.loss(ids[:-1], ids[1:], 1, s_tok, grads=True, out=g)
+        if k:
+            fb.append(time.perf_counter() - t0)
+    t0 = time.perf_counter()
+    orc.clip_global_norm(g, 1.0)
+    opt.step(g, 3e-4)
+    t_opt = time.perf_counter() - t0
+    t_fb = statistics.median(fb)
+    scale = batch * seq * executed_flops_per_token(cfg, seq) / (s_tok * executed_flops_per_token(cfg, s_tok))
+    step = t_fb * scale + t_opt
+    out.update(value=batch * seq / step, extrapolated=True, step_s=step, sample_fwd_bwd_s=t_fb, optimizer_s=t_opt,
+               sample=f"EXTRAPOLATED: forward+backward of 1 x {s_tok} tokens of the same model ({n_params:,} "
+                      f"parameters) took {t_fb:.2f} s (median of {steps} after one warm-up pass) and clip+AdamW "
+                      f"over all parameters {t_opt:.2f} s, on {threads} of {nproc} host threads; the "
+                      f"forward+backward time is scaled by executed FLOPs ({scale:.0f}x, full T x T attention as "
+                      f"the reference computes it) to {batch} x {seq} tokens and the optimizer time added: "
+                      f"{step:.0f} s per step. The C++ restatement of the reference CPU path (oracle/), not the "
+                      f"Rust binary (no cargo here)")
+    return out
 
 
 LINEAR_SHAPES = [(512, 512), (512, 1408), (1024, 4096), (2048, 5632)]  # configs[1]: (K, N), M = 4096 tokens
 
 
+def _timed(torch, mm, fn, steps, warmup):
+    """Mean ms of fn() over `steps` calls after `warmup` (>= 3) untimed ones: CUDA events on the current stream,
+    on which every launch of fn is queued."""
+    for _ in range(max(3, warmup)):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        fn()
+    e.record()
+    e.synchronize()
+    mm.device_status()
+    return s.elapsed_time(e) / steps
+
+
+def linear_config(torch, mm, precision, steps, warmup, tf32):
+    """the isolated Linear op fwd+bwd (Y = XW, dX = dY W^T, dW = X^T dY, M = 4096 tokens) per
+    (K, N), through the kernel-level C ABI (mm_gpu_gemm)."""
+    g = torch.Generator(device="cuda").manual_seed(0)
+    M = 4096
+    out = []
+    for K, N in LINEAR_SHAPES:
+        x = torch.randn(M, K, device="cuda", generator=g)
+        w = torch.randn(K, N, device="cuda", generator=g)
+        dy = torch.randn(M, N, device="cuda", generator=g)
+        y, dx, dw = (torch.empty(M, N, device="cuda"), torch.empty(M, K, device="cuda"),
+                     torch.empty(K, N, device="cuda"))
+
+        def fwd():  # Y = X W
+            mm.gemm(x, w, y, m=M, n=N, k=K, lda=K, ldb=N, ldc=N, a_mn_major=False, b_mn_major=True,
+                    precision=precision)
+
+        def bwd_x():  # dX = dY W^T
+            mm.gemm(dy, w, dx, m=M, n=K, k=N, lda=N, ldb=N, ldc=K, a_mn_major=False, b_mn_major=False,
+                    precision=precision)
+
+        def bwd_w():  # dW = X^T dY
+            mm.gemm(x, dy, dw, m=K, n=N, k=M, lda=K, ldb=N, ldc=N, a_mn_major=True, b_mn_major=True,
+                    precision=precision)
+
+        def step():
+            fwd()
+            bwd_x()
+            bwd_w()
+        flops = 3 * 2 * M * K * N
+        ms = _timed(torch, mm, step, steps, warmup)
+        parts = {name: round(flops / 3 / (_timed(torch, mm, fn, steps, warmup) * 1e-3) / 1e12, 1)
+                 for name, fn in (("Y=XW", fwd), ("dX=dYW^T", bwd_x), ("dW=X^TdY", bwd_w))}
+        tfl = flops / (ms * 1e-3) / 1e12
+        out.append({"M": M, "K": K, "N": N, "ms": round(ms, 4), "tflops": round(tfl, 1),
+                    "frac_of_cublas_tf32": round(tfl / tf32, 3), "parts": parts})
+        del x, w, dy, y, dx, dw
+    return {"metric": "Linear fwd+bwd TFLOP/s", "value": statistics.mean(r["tflops"] for r in out),
+            "unit": "TFLOP/s", "shapes": out}
+
+
+def attention_block_config(torch, mm, precision, steps, warmup, tf32, large=False):
+    """causal attention B 8, H 16, hd 64, T 1024 (RoPE theta 10000 on Q and K, scale 1/8) forward
+    and backward, with the RMSNorm (eps 1e-5) and the SwiGLU MLP (d_model 1024, hidden 2816) forward and
+    backward on the same 8,192 tokens, each part through the kernel-level C ABI. With large=True the
+    attention alone at configs[4]'s layer shape (B 4, H 16 / 8 key-value heads, hd 128, T 2048)."""
+    import oracle as orc
+    B, H, Hkv, hd, T = (4, 16, 8, 128, 2048) if large else (8, 16, 16, 64, 1024)
+    D, KV, F, N = H * hd, Hkv * hd, 2816, B * T
+    g = torch.Generator(device="cuda").manual_seed(0)
+    q = torch.randn(N, D, device="cuda", generator=g)
+    k = torch.randn(N, KV, device="cuda", generator=g)
+    v = torch.randn(N, KV, device="cuda", generator=g)
+    do = torch.randn(N, D, device="cuda", generator=g)
+    o, lse = torch.empty_like(q), torch.empty(B, H, T, device="cuda")
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    cos_np, sin_np = orc.rope_table(hd, T, 10000.0)
+    cos_t, sin_t = torch.from_numpy(cos_np).cuda(), torch.from_numpy(sin_np).cuda()
+    kw = dict(batch=B, seq=T, n_heads=H, n_kv_heads=Hkv, head_dim=hd, ldq=D, ldk=KV, precision=precision)
+
+    def attention():
+        mm.rope(q, cos_t, sin_t, rows=N, seq=T, heads=H, head_dim=hd, ld=D)
+        mm.rope(k, cos_t, sin_t, rows=N, seq=T, heads=Hkv, head_dim=hd, ld=KV)
+        mm.attention_forward(q, k, v, o, lse, **kw)
+        mm.attention_backward(q, k, v, o, lse, do, dq, dk, dv, **kw)
+        mm.rope(dq, cos_t, sin_t, rows=N, seq=T, heads=H, head_dim=hd, ld=D, backward=True)
+        mm.rope(dk, cos_t, sin_t, rows=N, seq=T, heads=Hkv, head_dim=hd, ld=KV, backward=True)
+        # q and k rotate back so that every timed pass sees the same inputs
+        mm.rope(q, cos_t, sin_t, rows=N, seq=T, heads=H, head_dim=hd, ld=D, backward=True)
+        mm.rope(k, cos_t, sin_t, rows=N, seq=T, heads=Hkv, head_dim=hd, ld=KV, backward=True)
+
+    attn_flops = 6 * 2 * B * H * (T * T // 2) * hd  # six causal T x T x hd products, no recompute
+    res = {"shape": {"B": B, "H": H, "Hkv": Hkv, "hd": hd, "T": T}}
+    ms_attn = _timed(torch, mm, attention, steps, warmup)
+    res["attention"] = {"ms": round(ms_attn, 4), "tflops": round(attn_flops / (ms_attn * 1e-3) / 1e12, 1),
+                        "frac_of_cublas_tf32": round(attn_flops / (ms_attn * 1e-3) / 1e12 / tf32, 3),
+                        "includes": "RoPE of q and k forward, backward and undo (6 HBM passes)"}
+    if large:
+        return res
+    x = torch.randn(N, D, device="cuda", generator=g)
+    wn = 1 + 0.1 * torch.randn(D, device="cuda", generator=g)
+    wg = 0.03 * torch.randn(D, F, device="cuda", generator=g)
+    wu = 0.03 * torch.randn(D, F, device="cuda", generator=g)
+    wd = 0.02 * torch.randn(F, D, device="cuda", generator=g)
+    dout = torch.randn(N, D, device="cuda", generator=g)
+    y, rstd = torch.empty(N, D, device="cuda"), torch.empty(N, device="cuda")
+    gate, up, act = (torch.empty(N, F, device="cuda") for _ in range(3))
+    out, dact, dy, dx = (torch.empty(N, D, device="cuda"), torch.empty(N, F, device="cuda"),
+                         torch.empty(N, D, device="cuda"), torch.empty(N, D, device="cuda"))
+    dwn, dwg, dwu, dwd = (torch.empty(D, device="cuda"), torch.empty(D, F, device="cuda"),
+                          torch.empty(D, F, device="cuda"), torch.empty(F, D, device="cuda"))
+
+    def norm_fwd():
+        mm.rmsnorm_forward(x, wn, y, rstd, rows=N, dim=D, eps=1e-5)
+
+    def mlp():
+        mm.gemm(y, wg, gate, m=N, n=F, k=D, lda=D, ldb=F, ldc=F, a_mn_major=False, b_mn_major=True,
+                precision=precision)
+        mm.gemm(y, wu, up, m=N, n=F, k=D, lda=D, ldb=F, ldc=F, a_mn_major=False, b_mn_major=True,
+                precision=precision)
+        mm.swiglu_forward(gate, up, act, n=N * F)
+        mm.gemm(act, wd, out, m=N, n=D, k=F, lda=F, ldb=D, ldc=D, a_mn_major=False, b_mn_major=True,
+                precision=precision)
+        # backward: dact = dout Wd^T, dWd = act^T dout, SwiGLU in place, dy = dG Wg^T + dU Wu^T, dW = y^T dG|dU
+        mm.gemm(dout, wd, dact, m=N, n=F, k=D, lda=D, ldb=D, ldc=F, a_mn_major=False, b_mn_major=False,
+                precision=precision)
+        mm.gemm(act, dout, dwd, m=F, n=D, k=N, lda=F, ldb=D, ldc=D, a_mn_major=True, b_mn_major=True,
+                precision=precision)
+        mm.swiglu_backward(gate, up, dact, n=N * F)
+        if precision == 0:
+            mm.gemm_sum([(gate, F, wg, F, F), (up, F, wu, F, F)], dy, m=N, n=D, ldc=D, a_mn_major=False,
+                        b_mn_major=False)
+        else:
+            mm.gemm(gate, wg, dy, m=N, n=D, k=F, lda=F, ldb=F, ldc=D, a_mn_major=False, b_mn_major=False,
+                    precision=precision)
+            mm.gemm(up, wu, dy, m=N, n=D, k=F, lda=F, ldb=F, ldc=D, a_mn_major=False, b_mn_major=False,
+                    r=dy, ldr=D, precision=precision)
+        mm.gemm(y, gate, dwg, m=D, n=F, k=N, lda=D, ldb=F, ldc=F, a_mn_major=True, b_mn_major=True,
+                precision=precision)
+        mm.gemm(y, up, dwu, m=D, n=F, k=N, lda=D, ldb=F, ldc=F, a_mn_major=True, b_mn_major=True,
+                precision=precision)
+
+    def norm_bwd():
+        mm.rmsnorm_backward(x, wn, rstd, dy, dx, dwn, rows=N, dim=D)
+
+    norm_fwd()
+    ms_nf = _timed(torch, mm, norm_fwd, steps, warmup)
+    ms_mlp = _timed(torch, mm, mlp, steps, warmup)
+    ms_nb = _timed(torch, mm, norm_bwd, steps, warmup)
+    mlp_flops = 9 * 2 * N * D * F  # three products forward, six backward
+    res["swiglu_mlp"] = {"ms": round(ms_mlp, 4), "tflops": round(mlp_flops / (ms_mlp * 1e-3) / 1e12, 1),
+                         "frac_of_cublas_tf32": round(mlp_flops / (ms_mlp * 1e-3) / 1e12 / tf32, 3),
+                         "includes": "SwiGLU forward and backward (HBM) between the nine products"}
+    res["rmsnorm"] = {"forward_ms": round(ms_nf, 4), "backward_ms": round(ms_nb, 4),
+                      "forward_gbs": round(2 * N * D * 4 / (ms_nf * 1e-3) / 1e9, 1),
+                      "backward_gbs": round(3 * N * D * 4 / (ms_nb * 1e-3) / 1e9, 1),
+                      "bytes": "forward reads x, writes y (8 B/element); backward reads x and dy, writes dx "
+                               "(12 B/element)"}
+    res["block_ms"] = round(ms_attn + ms_nf + ms_mlp + ms_nb, 4)
+    return res
+
+
 def run_kernels(args):
-    """configs[1] (isolated Linear fwd+bwd: Y = XW, dX = dY W^T, dW = X^T dY, M = 4096) or configs[2] (causal
-    attention B8 H16 hd64 T1024 fwd+bwd) through the kernel-level C ABI, timed with CUDA events."""
+    """`--config linear|attention|attention-large`: one JSON line for configs[1] or configs[2] alone."""
     import torch
     import midman_b200 as mm
     mm.load()
     torch.cuda.set_device(0)
+    sys.path.insert(0, str(ROOT / "oracle"))
     precision = 0 if args.precision == "tf32" else 1
-    g = torch.Generator(device="cuda").manual_seed(0)
-    results = []
-    if args.config == "linear":
-        M = 4096
-        for K, N in LINEAR_SHAPES:
-            x = torch.randn(M, K, device="cuda", generator=g)
-            w = torch.randn(K, N, device="cuda", generator=g)
-            dy = torch.randn(M, N, device="cuda", generator=g)
-            y, dx, dw = torch.empty(M, N, device="cuda"), torch.empty(M, K, device="cuda"), torch.empty(K, N,
-                                                                                                        device="cuda")
-
-            def fwd(x=x, w=w, y=y, K=K, N=N):  # Y = X W (bind this shape's tensors)
-                mm.gemm(x, w, y, m=M, n=N, k=K, lda=K, ldb=N, ldc=N, a_mn_major=False, b_mn_major=True,
-                        precision=precision)
-
-            def bwd_x(dy=dy, w=w, dx=dx, K=K, N=N):  # dX = dY W^T
-                mm.gemm(dy, w, dx, m=M, n=K, k=N, lda=N, ldb=N, ldc=K, a_mn_major=False, b_mn_major=False,
-                        precision=precision)
-
-            def bwd_w(x=x, dy=dy, dw=dw, K=K, N=N):  # dW = X^T dY
-                mm.gemm(x, dy, dw, m=K, n=N, k=M, lda=K, ldb=N, ldc=N, a_mn_major=True, b_mn_major=True,
-                        precision=precision)
-
-            def step(parts=(fwd, bwd_x, bwd_w)):
-                for p in parts:
-                    p()
-            flops = 3 * 2 * M * K * N
-            results.append(({"K": K, "N": N, "M": M}, flops, step,
-                            {"Y=XW": (fwd, flops / 3), "dX=dYW^T": (bwd_x, flops / 3),
-                             "dW=X^TdY": (bwd_w, flops / 3)}))
-    else:
-        # configs[2] (B8 H16 hd64 T1024), or with attention-large the attention of configs[4]'s layers
-        B, H, Hkv, hd, T = (8, 16, 16, 64, 1024) if args.config == "attention" else (4, 16, 8, 128, 2048)
-        q = torch.randn(B, T, H, hd, device="cuda", generator=g)
-        k = torch.randn(B, T, Hkv, hd, device="cuda", generator=g)
-        v = torch.randn(B, T, Hkv, hd, device="cuda", generator=g)
-        do = torch.randn(B, T, H, hd, device="cuda", generator=g)
-        o, lse = torch.empty_like(q), torch.empty(B, H, T, device="cuda")
-        dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
-        kw = dict(batch=B, seq=T, n_heads=H, n_kv_heads=Hkv, head_dim=hd, ldq=H * hd, ldk=Hkv * hd,
-                  precision=precision)
-
-        def fwd():
-            mm.attention_forward(q, k, v, o, lse, **kw)
-
-        def bwd():
-            mm.attention_backward(q, k, v, o, lse, do, dq, dk, dv, **kw)
-
-        def step():
-            fwd()
-            bwd()
-        flops = 6 * 2 * B * H * (T * T // 2) * hd  # six causal T x T x hd products, no recompute
-        results.append(({"B": B, "H": H, "Hkv": Hkv, "hd": hd, "T": T}, flops, step,
-                        {"forward": (fwd, flops / 3), "backward": (bwd, flops * 2 / 3)}))
     tf32 = tf32_peak_tflops(torch)
-    def timed(fn):
-        for _ in range(max(3, args.warmup)):
-            fn()
-        torch.cuda.synchronize()
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record()
-        for _ in range(args.steps):
-            fn()
-        e.record()
-        e.synchronize()
-        mm.device_status()
-        return s.elapsed_time(e) / args.steps
-
-    out = []
-    for shape, flops, step, parts in results:
-        ms = timed(step)
-        row = {**shape, "ms": ms, "tflops": flops / (ms * 1e-3) / 1e12, "frac_of_cublas_tf32": flops / (ms * 1e-3)
-               / 1e12 / tf32}
-        if parts:  # TFLOP/s of each part alone
-            row["parts"] = {name: round(f / (timed(fn) * 1e-3) / 1e12, 1) for name, (fn, f) in parts.items()}
-        out.append(row)
-    line = {"metric": "fwd+bwd TFLOP/s" if args.config == "linear" else "attention fwd+bwd TFLOP/s",
-            "value": statistics.mean(r["tflops"] for r in out), "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps,
-            "warmup": args.warmup, "higher_is_better": True, "dtype": args.precision, "data": "synthetic N(0,1)",
-            "config": {"workload": args.config, "shapes": out}, "tf32_peak_cublas": tf32}
+    if args.config == "linear":
+        res = linear_config(torch, mm, precision, args.steps, args.warmup, tf32)
+        line = {"metric": res["metric"], "value": res["value"], "unit": "TFLOP/s",
+                "config": {"workload": "linear", "shapes": res["shapes"]}}
+    else:
+        res = attention_block_config(torch, mm, precision, args.steps, args.warmup, tf32,
+                                     large=args.config == "attention-large")
+        line = {"metric": "attention fwd+bwd TFLOP/s", "value": res["attention"]["tflops"], "unit": "TFLOP/s",
+                "config": {"workload": args.config, **res}}
+    line.update({"n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+                 "dtype": args.precision, "data": "synthetic N(0,1)", "tf32_peak_cublas": tf32})
     print(json.dumps(line), flush=True)
     return 0
+
+
+def trainer_tokens_per_s(torch, mm, cfg, B, T, precision, steps, warmup):
+    """tokens/s of K staged training steps of a config on one GPU (CUDA events on the library's stream)."""
+    batcher = mm.Batcher(vocab=cfg[0], seq=T, batch=B, seed=0, synthetic_tokens=(B + 1) * T * 2 + 1, token_seed=0)
+    i, t, _, _ = batcher.next()
+    batcher.close()
+    hyper = mm.hyper_array(max_lr=3e-4, min_lr=3e-4, warmup=0, total=10**9, weight_decay=0.1, clip_norm=1.0,
+                           beta1=0.9, beta2=0.95)
+    tr = mm.Trainer(mm.config_array(*cfg), hyper, seed=0, batch=B, seq=T, precision=precision)
+    try:
+        stream = torch.cuda.ExternalStream(tr.stream())
+        tr.stage(i, t)
+        tr.step_staged(max(3, warmup))
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        rec, status = tr.step_staged(steps)
+        e.record(stream)
+        e.synchronize()
+        ms = s.elapsed_time(e) / steps
+    finally:
+        tr.close()
+    return {"value": B * T / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms, "steps": steps,
+            "batch": B, "seq_len": T, "loss_first_last": [float(rec[0, 0]), float(rec[-1, 0])]}
 
 
 GEMM_TRAFFIC_BYTES = 547e6  # see the roofline entry below
@@ -270,7 +429,7 @@ def workload_config(args, cfg, B, T, world):
 def run_reference(args, cfg, B, T, world, rank):
     if rank != 0:
         return 0
-    cb = cpu_baseline(cfg, T, steps=max(1, min(args.steps, 3)), warmup=min(args.warmup, 1))
+    cb = cpu_baseline(cfg, B, T, steps=max(1, min(args.steps, 2)))
     value = cb["value"]
     line = {"impl": "reference", "metric": "train tokens/s (fwd+bwd+AdamW)", "value": value, "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
@@ -291,6 +450,9 @@ def main():
     ap.add_argument("--precision", default="tf32", choices=["tf32", "3xtf32"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="skip the other BASELINE configs (tiny, mid, Linear, attention block) that a one-GPU run "
+                         "of the default workload adds under the `configs` key")
     ap.add_argument("--optimizer", default="auto", choices=["auto", "replicated", "sharded"],
                     help="sharded: ZeRO-1, each rank keeps and updates 1/N of the AdamW state; auto: sharded "
                          "for N > 1 (measured 2-3%% faster at N = 2 and 8)")
@@ -452,10 +614,41 @@ def main():
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:
+        if world == 1 and not args.no_configs and args.config == "large":
+            line["configs"] = other_configs(args, torch, mm, precision, with_cpu=not args.no_cpu_baseline)
         if world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline(cfg, T, steps=1, warmup=0)
+            line["cpu_baseline"] = cpu_baseline(cfg, B, T, steps=1)
         print(json.dumps(line), flush=True)
     return 0
+
+
+PUBLISHED_TINY = ("reference tiny preset, batch 8 x seq 256, --features avx, one CPU thread: ~2,000-2,300 tokens/s "
+                  "(README.md:109), 1,282 tokens/s on a 2.1 GHz Xeon (docs/midman-training.md:100)")
+
+
+def other_configs(args, torch, mm, precision, with_cpu=True):
+    """BASELINE.json's other configs on this GPU: configs[0] tiny and configs[3] mid (training steps,
+    tokens/s, with the CPU baseline of the same workload), configs[1] (Linear fwd+bwd) and configs[2]
+    (attention block fwd+bwd) through the kernel-level C ABI."""
+    sys.path.insert(0, str(ROOT / "oracle"))
+    tf32 = tf32_peak_tflops(torch)
+    out = {}
+    for name, idx, steps in (("tiny", 0, 20), ("mid", 3, 10)):
+        cfg, B, T = CONFIGS[name]
+        r = trainer_tokens_per_s(torch, mm, cfg, B, T, precision, steps, max(3, args.warmup))
+        fpt = flops_per_token(cfg, T)
+        r.update(config=f"configs[{idx}]", preset=list(cfg), step_tflops=r["value"] * fpt / 1e12,
+                 step_frac_of_cublas_tf32=r["value"] * fpt / 1e12 / tf32)
+        if with_cpu:
+            r["cpu_baseline"] = cpu_baseline(cfg, B, T, steps=2 if name == "tiny" else 1)
+        if name == "tiny":
+            r["published_reference"] = PUBLISHED_TINY
+        out[name] = r
+    out["linear"] = {"config": "configs[1]", **linear_config(torch, mm, precision, 10, 3, tf32)}
+    out["attention_block"] = {"config": "configs[2]", **attention_block_config(torch, mm, precision, 10, 3, tf32)}
+    out["tf32_peak_cublas"] = tf32
+    torch.cuda.empty_cache()
+    return out
 
 
 if __name__ == "__main__":
