@@ -644,6 +644,14 @@ def other_configs(args, torch, mm, precision, with_cpu=True):
         if name == "tiny":
             r["published_reference"] = PUBLISHED_TINY
         out[name] = r
+    if precision == 0:
+        # the same large-preset step in the exact mode (3xTF32 products, FP32 attention), a few steps
+        cfg, B, T = CONFIGS["large"]
+        r = trainer_tokens_per_s(torch, mm, cfg, B, T, 1, 4, 3)
+        fpt = flops_per_token(cfg, T)
+        r.update(config="configs[4] in 3xTF32", step_tflops=r["value"] * fpt / 1e12,
+                 step_frac_of_cublas_tf32=r["value"] * fpt / 1e12 / tf32)
+        out["large_3xtf32"] = r
     out["linear"] = {"config": "configs[1]", **linear_config(torch, mm, precision, 10, 3, tf32)}
     out["attention_block"] = {"config": "configs[2]", **attention_block_config(torch, mm, precision, 10, 3, tf32)}
     out["tf32_peak_cublas"] = tf32
