@@ -21,6 +21,11 @@ GPU_SYMBOLS = [
     "mm_gpu_embedding_forward", "mm_gpu_embedding_backward", "mm_gpu_cross_entropy", "mm_gpu_comm_create",
     "mm_gpu_comm_destroy", "mm_gpu_allreduce_bucket", "mm_gpu_comm_wait", "mm_gpu_wait_selftest",
 ]
+TENSOR_SYMBOLS = [
+    "mm_tape_create", "mm_tape_destroy", "mm_tensor_new", "mm_tensor_shape", "mm_tensor_read", "mm_tensor_grad",
+    "mm_tensor_free", "mm_tape_backward", "mm_op_matmul", "mm_op_add", "mm_op_mul", "mm_op_embedding",
+    "mm_op_rms_norm", "mm_op_rope", "mm_op_causal_attention", "mm_op_swiglu", "mm_op_cross_entropy",
+]
 API_SYMBOLS = [
     "midman_abi_version", "midman_alloc", "midman_free", "midman_text_ptr", "midman_text_len",
     "midman_floats_ptr", "midman_floats_len", "midman_error_ptr", "midman_error_len", "midman_describe",
@@ -83,6 +88,24 @@ def load(path: str | os.PathLike | None = None) -> C.CDLL:
     _sig(lib, "mm_gpu_allreduce_bucket", i32, vp, vp, i64, i32, vp)
     _sig(lib, "mm_gpu_comm_wait", i32, vp, vp, i32)
     _sig(lib, "mm_gpu_wait_selftest", i32, i32, vp)
+    u64, i64p = C.c_uint64, C.POINTER(C.c_int64)
+    _sig(lib, "mm_tape_create", u32, i32)
+    _sig(lib, "mm_tape_destroy", i32, u32)
+    _sig(lib, "mm_tensor_new", u64, u32, i64p, i32, f32p, i32)
+    _sig(lib, "mm_tensor_shape", i32, u32, u64, i64p, i32p)
+    _sig(lib, "mm_tensor_read", i32, u32, u64, f32p, i64)
+    _sig(lib, "mm_tensor_grad", i32, u32, u64, f32p, i64)
+    _sig(lib, "mm_tensor_free", i32, u32, u64)
+    _sig(lib, "mm_tape_backward", i32, u32, u64)
+    _sig(lib, "mm_op_matmul", u64, u32, u64, u64, i32)
+    _sig(lib, "mm_op_add", u64, u32, u64, u64)
+    _sig(lib, "mm_op_mul", u64, u32, u64, u64)
+    _sig(lib, "mm_op_embedding", u64, u32, u64, i32p, i64)
+    _sig(lib, "mm_op_rms_norm", u64, u32, u64, u64, C.c_float)
+    _sig(lib, "mm_op_rope", u64, u32, u64, i32, i32, C.c_float)
+    _sig(lib, "mm_op_causal_attention", u64, u32, u64, u64, u64, i32, i32, i32, i32)
+    _sig(lib, "mm_op_swiglu", u64, u32, u64, u64)
+    _sig(lib, "mm_op_cross_entropy", u64, u32, u64, i32p, i64)
     _sig(lib, "midman_abi_version", u32)
     _sig(lib, "midman_alloc", u8p, u32)
     _sig(lib, "midman_free", None, u8p, u32)
@@ -274,6 +297,84 @@ class Comm:
         if self.h:
             check(load().mm_gpu_comm_destroy(self.h))
             self.h = None
+
+
+class Tape:
+    """mm_tape_* / mm_tensor_* / mm_op_*: device tensors with a recording autograd tape on the current GPU.
+    Tensors are integer handles; values and gradients cross to the host as float32 numpy arrays."""
+
+    def __init__(self, precision: int = 0):
+        self.h = load().mm_tape_create(precision)
+        if self.h == 0:
+            raise MidmanGpuError(-1, load().mm_gpu_last_error().decode(errors="replace"))
+
+    def _t(self, handle):
+        if handle == 0:
+            raise MidmanGpuError(-1, load().mm_gpu_last_error().decode(errors="replace"))
+        return handle
+
+    def tensor(self, values=None, shape=None, requires_grad=False):
+        if values is not None:
+            values = _np.ascontiguousarray(values, _np.float32)
+            shape = values.shape if shape is None else shape
+        sh = (C.c_int64 * len(shape))(*shape)
+        vp = values.ctypes.data_as(C.POINTER(C.c_float)) if values is not None else None
+        return self._t(load().mm_tensor_new(self.h, sh, len(shape), vp, int(bool(requires_grad))))
+
+    def shape(self, t):
+        sh, rank = (C.c_int64 * 4)(), C.c_int32()
+        check(load().mm_tensor_shape(self.h, t, sh, C.byref(rank)))
+        return tuple(sh[i] for i in range(rank.value))
+
+    def read(self, t):
+        out = _np.zeros(self.shape(t), _np.float32)
+        check(load().mm_tensor_read(self.h, t, out.ctypes.data_as(C.POINTER(C.c_float)), out.size))
+        return out
+
+    def grad(self, t):
+        out = _np.zeros(self.shape(t), _np.float32)
+        check(load().mm_tensor_grad(self.h, t, out.ctypes.data_as(C.POINTER(C.c_float)), out.size))
+        return out
+
+    def free(self, t):
+        check(load().mm_tensor_free(self.h, t))
+
+    def backward(self, loss):
+        check(load().mm_tape_backward(self.h, loss))
+
+    def matmul(self, a, b, b_transposed=False):
+        return self._t(load().mm_op_matmul(self.h, a, b, int(bool(b_transposed))))
+
+    def add(self, a, b):
+        return self._t(load().mm_op_add(self.h, a, b))
+
+    def mul(self, a, b):
+        return self._t(load().mm_op_mul(self.h, a, b))
+
+    def embedding(self, table, ids):
+        ids = _np.ascontiguousarray(ids, _np.int32)
+        return self._t(load().mm_op_embedding(self.h, table, _ip(ids), ids.size))
+
+    def rms_norm(self, x, w, eps=1e-5):
+        return self._t(load().mm_op_rms_norm(self.h, x, w, eps))
+
+    def rope(self, x, seq, heads, theta=10000.0):
+        return self._t(load().mm_op_rope(self.h, x, seq, heads, theta))
+
+    def causal_attention(self, q, k, v, batch, seq, n_heads, n_kv_heads):
+        return self._t(load().mm_op_causal_attention(self.h, q, k, v, batch, seq, n_heads, n_kv_heads))
+
+    def swiglu(self, gate, up):
+        return self._t(load().mm_op_swiglu(self.h, gate, up))
+
+    def cross_entropy(self, logits, targets):
+        t = _np.ascontiguousarray(targets, _np.int32)
+        return self._t(load().mm_op_cross_entropy(self.h, logits, _ip(t), t.size))
+
+    def close(self):
+        if self.h:
+            check(load().mm_tape_destroy(self.h))
+            self.h = 0
 
 
 def wait_selftest(timeout_us, stream=None):

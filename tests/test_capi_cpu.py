@@ -17,7 +17,8 @@ PINS = json.loads((ROOT / "tests" / "golden" / "reference_pins.json").read_text(
 def declared_symbols():
     out = []
     for h in (ROOT / "include").glob("*.h"):
-        for m in re.finditer(r"(?:MIDMAN_EXPORT|MM_GPU_EXPORT)[^;]*?\b((?:midman|mm_gpu)_\w+)\s*\(", h.read_text(),
+        for m in re.finditer(r"(?:MIDMAN_EXPORT|MM_GPU_EXPORT)[^;]*?\b((?:midman|mm_gpu|mm_tape|mm_tensor|mm_op)_\w+)\s*\(",
+                             h.read_text(),
                              re.S):
             out.append(m.group(1))
     return sorted(set(out))
@@ -29,7 +30,7 @@ def test_every_declared_symbol_is_exported(mm):
     lib = mm.load()
     for s in syms:
         assert hasattr(lib, s), s
-    assert set(syms) == set(mm.GPU_SYMBOLS + mm.API_SYMBOLS)
+    assert set(syms) == set(mm.GPU_SYMBOLS + mm.API_SYMBOLS + mm.TENSOR_SYMBOLS)
 
 
 def test_abi_version_and_alloc(mm):
