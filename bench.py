@@ -372,6 +372,10 @@ def run_kernels(args):
         res = linear_config(torch, mm, precision, args.steps, args.warmup, tf32)
         line = {"metric": res["metric"], "value": res["value"], "unit": "TFLOP/s",
                 "config": {"workload": "linear", "shapes": res["shapes"]}}
+    elif args.config == "gemm-step":
+        res = gemm_step_config(torch, mm, args.steps, args.warmup, tf32)
+        line = {"metric": res["metric"], "value": res["value"], "unit": "TFLOP/s",
+                "config": {"workload": "gemm-step", **{k: v for k, v in res.items() if k not in ("metric", "value")}}}
     else:
         res = attention_block_config(torch, mm, precision, args.steps, args.warmup, tf32,
                                      large=args.config == "attention-large")
@@ -381,6 +385,60 @@ def run_kernels(args):
                  "dtype": args.precision, "data": "synthetic N(0,1)", "tf32_peak_cublas": tf32})
     print(json.dumps(line), flush=True)
     return 0
+
+
+# The TF32 products of one large-preset step (configs[4], 4 x 2048 tokens): (M, N, K-list, A MN-major,
+# B MN-major, launches per step). Summed K lists are one launch (dX of the projections that share an input).
+LARGE_STEP_GEMMS = [
+    (8192, 2048, [2048], False, True, 40),         # q, o projections
+    (8192, 1024, [2048], False, True, 40),         # k, v projections
+    (8192, 5632, [2048], False, True, 40),         # gate, up
+    (8192, 2048, [5632], False, True, 20),         # down
+    (8192, 32000, [2048], False, False, 1),        # logits = x E^T
+    (8192, 2048, [32000], False, True, 1),         # dX of the head
+    (32000, 2048, [8192], True, True, 1),          # dE of the head
+    (5632, 2048, [8192], True, True, 20),          # dW down
+    (8192, 5632, [2048], False, False, 20),        # d act = dx Wd^T
+    (2048, 5632, [8192], True, True, 40),          # dW gate, up
+    (8192, 2048, [5632, 5632], False, False, 20),  # dX = dG Wg^T + dU Wu^T
+    (2048, 2048, [8192], True, True, 40),          # dW o, q
+    (8192, 2048, [2048], False, False, 20),        # d o = dh Wo^T
+    (2048, 1024, [8192], True, True, 40),          # dW k, v
+    (8192, 2048, [2048, 1024, 1024], False, False, 20),  # dX = dQ Wq^T + dK Wk^T + dV Wv^T
+]
+
+
+def gemm_step_config(torch, mm, steps, warmup, tf32):
+    """Each distinct TF32 product of the large step once, standalone (operands < 2 GB on the device): TFLOP/s per
+    shape and the step's mix. Small enough for an ncu capture of the products' DRAM traffic."""
+    g = torch.Generator(device="cuda").manual_seed(0)
+    out, total_ms, total_flops = [], 0.0, 0.0
+    for M, N, ks, a_mn, b_mn, per_step in LARGE_STEP_GEMMS:
+        terms = []
+        for K in ks:
+            a = torch.randn(*((K, M) if a_mn else (M, K)), device="cuda", generator=g)
+            b = torch.randn(*((K, N) if b_mn else (N, K)), device="cuda", generator=g)
+            terms.append((a, a.shape[1], b, b.shape[1], K))
+        c = torch.empty(M, N, device="cuda")
+        if len(terms) == 1:
+            a, lda, b, ldb, K = terms[0]
+
+            def fn():
+                mm.gemm(a, b, c, m=M, n=N, k=K, lda=lda, ldb=ldb, ldc=N, a_mn_major=a_mn, b_mn_major=b_mn)
+        else:
+            def fn():
+                mm.gemm_sum(terms, c, m=M, n=N, ldc=N, a_mn_major=a_mn, b_mn_major=b_mn)
+        ms = _timed(torch, mm, fn, steps, warmup)
+        flops = 2.0 * M * N * sum(ks)
+        out.append({"shape": f"{M}x{N}x{'+'.join(map(str, ks))} {'M' if a_mn else 'K'}{'M' if b_mn else 'K'}",
+                    "per_step": per_step, "ms": round(ms, 4), "tflops": round(flops / (ms * 1e-3) / 1e12, 1),
+                    "algorithmic_bytes": int(4 * (M * sum(ks) + N * sum(ks) + M * N))})
+        total_ms += per_step * ms
+        total_flops += per_step * flops
+        del terms, c
+    return {"metric": "TF32 GEMM TFLOP/s over the large step's products", "value": total_flops / (total_ms * 1e-3) / 1e12,
+            "unit": "TFLOP/s", "frac_of_cublas_tf32": total_flops / (total_ms * 1e-3) / 1e12 / tf32, "shapes": out,
+            "step_gemm_ms_serialized": total_ms}
 
 
 def trainer_tokens_per_s(torch, mm, cfg, B, T, precision, steps, warmup):
@@ -408,7 +466,12 @@ def trainer_tokens_per_s(torch, mm, cfg, B, T, precision, steps, warmup):
             "batch": B, "seq_len": T, "loss_first_last": [float(rec[0, 0]), float(rec[-1, 0])]}
 
 
-GEMM_TRAFFIC_BYTES = 547e6  # see the roofline entry below
+# DRAM read + write bytes per TF32 GEMM launch of the large step, the step's mix of products (weights: launches
+# per step): measured by ncu (dram__bytes_read.sum + dram__bytes_write.sum) on each product of LARGE_STEP_GEMMS
+# run alone (`--config gemm-step`), summarized in profiles/gemm_tf32_large_step_shapes.md. Algorithmic (each
+# operand read once, C written once): 233.9e6 bytes per launch.
+GEMM_TRAFFIC_BYTES = 334.4e6
+GEMM_ALGORITHMIC_BYTES = 233.9e6
 
 
 def gemm_shapes(prof, steps, top=10):
@@ -446,7 +509,8 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=8)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--config", default="large", choices=sorted(CONFIGS) + ["linear", "attention", "attention-large"])
+    ap.add_argument("--config", default="large",
+                    choices=sorted(CONFIGS) + ["linear", "attention", "attention-large", "gemm-step"])
     ap.add_argument("--precision", default="tf32", choices=["tf32", "3xtf32"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -458,7 +522,7 @@ def main():
                          "for N > 1 (measured 2-3%% faster at N = 2 and 8)")
     args = ap.parse_args()
 
-    if args.config in ("linear", "attention", "attention-large"):
+    if args.config in ("linear", "attention", "attention-large", "gemm-step"):
         return run_kernels(args) if args.impl == "ours" else 0
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -595,8 +659,11 @@ def main():
                          # DRAM read+write bytes per GEMM launch, averaged over one step's 423 GEMM launches
                          # of this command under ncu (one-pass launch list; measured, not computed here)
                          "traffic": GEMM_TRAFFIC_BYTES if args.config == "large" and precision == 0 else None,
-                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, large preset step, "
-                                           "mean over the step's GEMM launches",
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of each product of the "
+                                           "large step run alone (--config gemm-step), weighted by launches per "
+                                           "step (profiles/gemm_tf32_large_step_shapes.md)",
+                         "algorithmic_bytes": GEMM_ALGORITHMIC_BYTES if args.config == "large" and precision == 0
+                         else None,
                          "kernel_launches": g["launches"],
                          "step_tflops": fpt * B * T * args.steps / (ms * 1e-3) / 1e12 / world,
                          "step_frac": fpt * B * T * args.steps / (ms * 1e-3) / 1e12 / world / tf32,

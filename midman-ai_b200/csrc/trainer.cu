@@ -517,7 +517,7 @@ void Trainer::wait_exchange(const char* where) {
                                              std::to_string(exchange_timeout_ms_) + " ms") +
                                "; communicator aborted");
     }
-    std::this_thread::sleep_for(std::chrono::microseconds(100));
+    std::this_thread::sleep_for(std::chrono::microseconds(20));
   }
 }
 
