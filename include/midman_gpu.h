@@ -95,9 +95,12 @@ MM_GPU_EXPORT int32_t mm_gpu_gemm_sum(int32_t m, int32_t n, int32_t nseg, const 
  * [batch * seq, n_heads * head_dim] with row stride ldq (= ldo = lddo = lddq);
  * k, v, dk, dv are [batch * seq, n_kv_heads * head_dim] with row stride ldk.
  * lse and delta are [batch, n_heads, seq]. precision MM_GPU_TF32 runs the score
- * and value products on the tensor cores (head_dim 32, 64 or 128; other sizes
- * fall back to the FP32 path), MM_GPU_3XTF32 the FP32 flash kernels. The
- * library keeps the score scratch (2 * batch * n_heads * seq * seq floats). */
+ * and value products on the tensor cores in the fused flash kernels;
+ * MM_GPU_3XTF32 runs them on the tensor cores as three TF32 terms of hi/lo
+ * operand pairs through score buffers, with the contractions over seq summed
+ * in f32 every 256 values (about 4 * batch * n_heads * seq * seq floats of
+ * library scratch). Both need head_dim 32, 64 or 128, row strides multiples of
+ * 4 and 16-byte aligned operands; other shapes run the FP32 flash kernels. */
 MM_GPU_EXPORT int32_t mm_gpu_attention_forward(int32_t batch, int32_t seq, int32_t n_heads, int32_t n_kv_heads,
                                                int32_t head_dim, const float *q, const float *k, const float *v,
                                                int64_t ldq, int64_t ldk, float *o, float *lse, int32_t precision,

@@ -64,6 +64,22 @@ __global__ void softmax_rows_kernel(float* __restrict__ S, long long ldS, int T,
   if (lane == 0) lse[r] = m + logf(s);
 }
 
+// One warp per score row of dP: dS = P * (dP - delta) * scale for j <= i, zeros
+// for i < j < row_end (the softmax backward, ops_reduce.rs:131-142, then the
+// score scale; P is the softmax's output in the same layout).
+__global__ void softmax_grad_rows_kernel(const float* __restrict__ P, float* __restrict__ D, long long ldS, int T,
+                                         long long rows, const float* __restrict__ delta, float scale) {
+  const long long r = (blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x) / 32;
+  const int lane = threadIdx.x & 31;
+  if (r >= rows) return;
+  const int i = static_cast<int>(r % T);
+  const float* prow = P + r * ldS;
+  float* drow = D + r * ldS;
+  const int n = i + 1, end = row_end(i, T);
+  const float dl = delta[r];
+  for (int j = lane; j < end; j += 32) drow[j] = j < n ? (prow[j] * (drow[j] - dl)) * scale : 0.0f;
+}
+
 int blocks_for(long long threads) {
   long long b = (threads + 255) / 256;
   return static_cast<int>(b < 1 ? 1 : b);
@@ -84,7 +100,220 @@ BatchedOperand scores_view(const float* p, bool mn, const AttnShape& s, long lon
 
 int tile_for(int hd) { return hd <= 64 ? 64 : 128; }
 
+// ---------------------------------------------------------------- 3xTF32 products
+// A TF32 number pair (hi, lo) per operand element, and a product formed as
+// lo*hi + hi*lo + hi*hi, each term one launch of the batched GEMM accumulating
+// into C through its residual (the first launch writes C unless `accumulate`).
+// A contraction longer than kChunk is taken kChunk values at a time, each chunk
+// accumulated from zero in tensor memory and added to C by the epilogue in f32,
+// so the tensor core's accumulation error does not grow with the length.
+constexpr int kChunk = 256;
+
+struct Pair3 {
+  BatchedOperand hi, lo;
+};
+
+// The view restricted to K values [k0, k0 + kc).
+BatchedOperand k_slice(BatchedOperand o, int k0, int kc) {
+  if (!o.mn_major) {  // K contiguous
+    o.ptr += k0;
+    o.inner = kc;
+  } else {  // K along the rows
+    o.ptr += static_cast<long long>(k0) * o.row_stride;
+    o.rows = kc;
+  }
+  return o;
+}
+
+void product3(int batch, int M, int N, int K, const Pair3& A, const Pair3& B, float* C, long long ldc, GemmBatch bt,
+              int bn, bool accumulate, int* d_err, cudaStream_t stream, const char* what) {
+  bool first = !accumulate;
+  const int k_base = bt.k_off;
+  for (int k0 = 0; k0 < K; k0 += kChunk) {
+    const int kc = K - k0 < kChunk ? K - k0 : kChunk;
+    bt.k_off = k_base + k0;
+    const BatchedOperand terms[3][2] = {{k_slice(A.lo, k0, kc), k_slice(B.hi, k0, kc)},
+                                        {k_slice(A.hi, k0, kc), k_slice(B.lo, k0, kc)},
+                                        {k_slice(A.hi, k0, kc), k_slice(B.hi, k0, kc)}};
+    for (const auto& t : terms) {
+      check_gemm(gemm_tf32_batched(batch, M, N, kc, t[0], t[1], C, ldc, bt, bn, d_err, stream, first ? nullptr : C),
+                 what);
+      first = false;
+    }
+  }
+}
+
+// Head g of every key/value group of a token-major [B, T, H, hd] operand, as a
+// batch over (b, kv head): z = b * Hkv + hk reads head hk * G + g.
+BatchedOperand group_head_view(const float* p, bool mn, const AttnShape& s, long long ld, int g) {
+  const int G = s.H / s.Hkv;
+  return BatchedOperand{p + static_cast<long long>(g) * s.hd, mn, s.hd, s.Hkv, s.T, s.B,
+                        static_cast<long long>(G) * s.hd, ld, static_cast<long long>(s.T) * ld, s.Hkv, 1};
+}
+
+// The same for the [B*H, T, ldS] score matrices, read with the keys as M
+// (MN-major: A(key, query) = P[query][key]).
+BatchedOperand group_scores_view(const float* p, const AttnShape& s, long long ldS, int g) {
+  const int G = s.H / s.Hkv;
+  const long long mat = static_cast<long long>(s.T) * ldS;
+  return BatchedOperand{p + g * mat, true, s.T, s.Hkv, s.T, s.B, G * mat, ldS, static_cast<long long>(s.H) * mat,
+                        s.Hkv, 1};
+}
+
+struct Ws3 {
+  float *S, *D, *Xh, *Xl, *qh, *ql, *kh, *kl, *vh, *vl, *gh, *gl, *lse, *delta;
+};
+
+long long rows_footprint(const AttnShape& s, long long ld, int heads) {
+  return (static_cast<long long>(s.B) * s.T - 1) * ld + static_cast<long long>(heads) * s.hd;
+}
+
+long long r4(long long n) { return (n + 63) & ~63ll; }
+
+// Sizes (floats) of the pieces of the workspace, in carve's order.
+struct Ws3Sizes {
+  long long mat, nq, nk, nv, ng, nr;
+  long long total() const { return 4 * mat + 2 * (nq + nk + nv + ng) + 2 * nr; }
+};
+
+Ws3Sizes ws3_sizes(const AttnShape& s, long long ld_dout) {
+  return Ws3Sizes{r4(static_cast<long long>(s.B) * s.H * s.T * attention_scores_ld(s.T)),
+                  r4(rows_footprint(s, s.ldq, s.H)),
+                  r4(rows_footprint(s, s.ldk, s.Hkv)),
+                  r4(rows_footprint(s, s.ldv, s.Hkv)),
+                  r4(rows_footprint(s, ld_dout, s.H)),
+                  r4(static_cast<long long>(s.B) * s.H * s.T)};
+}
+
+Ws3 carve(const AttnShape& s, float* ws, long long ld_dout) {
+  const Ws3Sizes z = ws3_sizes(s, ld_dout);
+  const long long mat = z.mat, nq = z.nq, nk = z.nk, nv = z.nv, ng = z.ng, nr = z.nr;
+  Ws3 w;
+  float* p = ws;
+  auto take = [&](long long n) { float* q = p; p += n; return q; };
+  w.S = take(mat);
+  w.D = take(mat);
+  w.Xh = take(mat);
+  w.Xl = take(mat);
+  w.qh = take(nq);
+  w.ql = take(nq);
+  w.kh = take(nk);
+  w.kl = take(nk);
+  w.vh = take(nv);
+  w.vl = take(nv);
+  w.gh = take(ng);
+  w.gl = take(ng);
+  w.lse = take(nr);
+  w.delta = take(nr);
+  return w;
+}
+
+// S = Q K^T (three terms; K = head_dim needs no chunks), tiles above the diagonal skipped.
+void scores3(const AttnShape& s, const Ws3& w, int* d_err, cudaStream_t st) {
+  const int G = s.H / s.Hkv, BH = s.B * s.H;
+  const long long ldS = attention_scores_ld(s.T);
+  GemmBatch bs;
+  bs.c_zdiv = BH;
+  bs.c_sh = static_cast<long long>(s.T) * ldS;
+  bs.causal = kCausalSkipUpper;
+  product3(BH, s.T, s.T, s.hd, {heads_view(w.qh, false, s, s.ldq, s.H, 1), heads_view(w.ql, false, s, s.ldq, s.H, 1)},
+           {heads_view(w.kh, false, s, s.ldk, s.Hkv, G), heads_view(w.kl, false, s, s.ldk, s.Hkv, G)}, w.S, ldS, bs,
+           256, false, d_err, st, "attention (3xTF32) S = QK^T");
+}
+
+void softmax_into(const AttnShape& s, float* S, float* lse, cudaStream_t st) {
+  const long long rows = static_cast<long long>(s.B) * s.H * s.T;
+  softmax_rows_kernel<<<blocks_for(rows * 32), 256, 0, st>>>(S, attention_scores_ld(s.T), s.T, rows, s.scale, lse);
+  check("attention softmax");
+}
+
+void split_scores(const AttnShape& s, const float* X, const Ws3& w, cudaStream_t st) {
+  split_tf32(X, w.Xh, w.Xl, static_cast<long long>(s.B) * s.H * s.T * attention_scores_ld(s.T), st);
+}
+
 }  // namespace
+
+long long attention_3x_ws_floats(const AttnShape& s, long long ld_dout) { return ws3_sizes(s, ld_dout).total(); }
+
+void attention_forward_3x(const AttnShape& s, const float* q, const float* k, const float* v, float* o, float* lse,
+                          float* ws, int* d_err, cudaStream_t st) {
+  const Ws3 w = carve(s, ws, s.ldo);
+  const int G = s.H / s.Hkv, BH = s.B * s.H;
+  const long long ldS = attention_scores_ld(s.T);
+  split_tf32(q, w.qh, w.ql, rows_footprint(s, s.ldq, s.H), st);
+  split_tf32(k, w.kh, w.kl, rows_footprint(s, s.ldk, s.Hkv), st);
+  split_tf32(v, w.vh, w.vl, rows_footprint(s, s.ldv, s.Hkv), st);
+  scores3(s, w, d_err, st);
+  softmax_into(s, w.S, lse, st);
+  split_scores(s, w.S, w, st);
+  // O = P V, K = keys in chunks, each row block's K loop ending at its diagonal
+  GemmBatch bo;
+  bo.c_zdiv = s.H;
+  bo.c_sb = static_cast<long long>(s.T) * s.ldo;
+  bo.c_sh = s.hd;
+  bo.causal = kCausalKBelow;
+  product3(BH, s.T, s.hd, s.T, {scores_view(w.Xh, false, s, ldS), scores_view(w.Xl, false, s, ldS)},
+           {heads_view(w.vh, true, s, s.ldv, s.Hkv, G), heads_view(w.vl, true, s, s.ldv, s.Hkv, G)}, o, s.ldo, bo,
+           tile_for(s.hd), false, d_err, st, "attention (3xTF32) O = PV");
+}
+
+void attention_backward_3x(const AttnShape& s, const float* q, const float* k, const float* v, const float* o,
+                           const float* dout, long long lddo, float* dq, float* dk, float* dv, float* ws, int* d_err,
+                           cudaStream_t st) {
+  const Ws3 w = carve(s, ws, lddo);
+  const int G = s.H / s.Hkv, BH = s.B * s.H, BHkv = s.B * s.Hkv;
+  const long long ldS = attention_scores_ld(s.T);
+  split_tf32(q, w.qh, w.ql, rows_footprint(s, s.ldq, s.H), st);
+  split_tf32(k, w.kh, w.kl, rows_footprint(s, s.ldk, s.Hkv), st);
+  split_tf32(v, w.vh, w.vl, rows_footprint(s, s.ldv, s.Hkv), st);
+  split_tf32(dout, w.gh, w.gl, rows_footprint(s, lddo, s.H), st);
+  // P again (the same arithmetic as the forward, so the same values)
+  scores3(s, w, d_err, st);
+  softmax_into(s, w.S, w.lse, st);
+  // dP = dO V^T into D
+  {
+    GemmBatch bd;
+    bd.c_zdiv = BH;
+    bd.c_sh = static_cast<long long>(s.T) * ldS;
+    bd.causal = kCausalSkipUpper;
+    product3(BH, s.T, s.T, s.hd, {heads_view(w.gh, false, s, lddo, s.H, 1), heads_view(w.gl, false, s, lddo, s.H, 1)},
+             {heads_view(w.vh, false, s, s.ldv, s.Hkv, G), heads_view(w.vl, false, s, s.ldv, s.Hkv, G)}, w.D, ldS, bd,
+             256, false, d_err, st, "attention (3xTF32) dP = dO V^T");
+  }
+  attention_delta(s, o, dout, lddo, w.delta, st);
+  // dV = P^T dO, summed over each key/value head's group; K = queries in chunks,
+  // each key row block's K loop starting at its first key
+  split_scores(s, w.S, w, st);
+  GemmBatch bk;
+  bk.c_zdiv = s.Hkv;
+  bk.c_sb = static_cast<long long>(s.T) * s.ldv;
+  bk.c_sh = s.hd;
+  bk.causal = kCausalKAbove;
+  for (int g = 0; g < G; ++g)
+    product3(BHkv, s.T, s.hd, s.T, {group_scores_view(w.Xh, s, ldS, g), group_scores_view(w.Xl, s, ldS, g)},
+             {group_head_view(w.gh, true, s, lddo, g), group_head_view(w.gl, true, s, lddo, g)}, dv, s.ldv, bk,
+             tile_for(s.hd), g > 0, d_err, st, "attention (3xTF32) dV = P^T dO");
+  // dS = P (dP - delta) * scale, in D
+  const long long rows = static_cast<long long>(BH) * s.T;
+  softmax_grad_rows_kernel<<<blocks_for(rows * 32), 256, 0, st>>>(w.S, w.D, ldS, s.T, rows, w.delta, s.scale);
+  check("attention softmax backward");
+  split_scores(s, w.D, w, st);
+  // dK = dS^T Q, summed over the group
+  bk.c_sb = static_cast<long long>(s.T) * s.ldk;
+  for (int g = 0; g < G; ++g)
+    product3(BHkv, s.T, s.hd, s.T, {group_scores_view(w.Xh, s, ldS, g), group_scores_view(w.Xl, s, ldS, g)},
+             {group_head_view(w.qh, true, s, s.ldq, g), group_head_view(w.ql, true, s, s.ldq, g)}, dk, s.ldk, bk,
+             tile_for(s.hd), g > 0, d_err, st, "attention (3xTF32) dK = dS^T Q");
+  // dQ = dS K, K = keys in chunks ending at each row block's diagonal
+  GemmBatch bq;
+  bq.c_zdiv = s.H;
+  bq.c_sb = static_cast<long long>(s.T) * s.ldq;
+  bq.c_sh = s.hd;
+  bq.causal = kCausalKBelow;
+  product3(BH, s.T, s.hd, s.T, {scores_view(w.Xh, false, s, ldS), scores_view(w.Xl, false, s, ldS)},
+           {heads_view(w.kh, true, s, s.ldk, s.Hkv, G), heads_view(w.kl, true, s, s.ldk, s.Hkv, G)}, dq, s.ldq, bq,
+           tile_for(s.hd), false, d_err, st, "attention (3xTF32) dQ = dS K");
+}
 
 long long attention_scores_ld(int T) { return (T + 3) & ~3ll; }
 

@@ -154,6 +154,10 @@ int32_t mm_gpu_attention_forward(int32_t batch, int32_t seq, int32_t n_heads, in
     cudaStream_t st = as_stream(stream);
     if (precision == MM_GPU_TF32 && mm::attention_flash_supported(s)) {
       mm::attention_forward_flash(s, q, k, v, o, lse, mm::device_context().d_err, st);
+    } else if (precision == MM_GPU_3XTF32 && mm::attention_tc_supported(s)) {
+      float* ws = static_cast<float*>(mm::device_scratch(
+          static_cast<size_t>(mm::attention_3x_ws_floats(s, s.ldo)) * sizeof(float), st));
+      mm::attention_forward_3x(s, q, k, v, o, lse, ws, mm::device_context().d_err, st);
     } else {
       mm::attention_forward(s, q, k, v, o, lse, st);
     }
@@ -175,6 +179,10 @@ int32_t mm_gpu_attention_backward(int32_t batch, int32_t seq, int32_t n_heads, i
     if (precision == MM_GPU_TF32 && mm::attention_flash_supported(s)) {
       float* delta = static_cast<float*>(mm::device_scratch(rows * sizeof(float), st));
       mm::attention_backward_flash(s, q, k, v, o, lse, dout, ldq, dq, dk, dv, delta, mm::device_context().d_err, st);
+    } else if (precision == MM_GPU_3XTF32 && mm::attention_tc_supported(s)) {
+      float* ws = static_cast<float*>(mm::device_scratch(
+          static_cast<size_t>(mm::attention_3x_ws_floats(s, ldq)) * sizeof(float), st));
+      mm::attention_backward_3x(s, q, k, v, o, dout, ldq, dq, dk, dv, ws, mm::device_context().d_err, st);
     } else {
       float* delta = static_cast<float*>(mm::device_scratch(rows * sizeof(float), st));
       mm::attention_backward(s, q, k, v, o, lse, dout, ldq, dq, dk, dv, delta, st);

@@ -93,11 +93,12 @@ __device__ __forceinline__ TileInfo tile_info(int t, int M, int N, int K, const 
   ti.n0 = (r / tm) * BN;
   ti.skip = BATCHED && bt.causal == kCausalSkipUpper && ti.n0 > ti.m0 + BM - 1;  // above the diagonal
   int kt_begin = 0, k_end = K;
-  if (BATCHED && bt.causal == kCausalKBelow) k_end = min(K, ti.m0 + BM);
-  if (BATCHED && bt.causal == kCausalKAbove) kt_begin = ti.m0 / BK;
+  if (BATCHED && bt.causal == kCausalKBelow) k_end = min(K, ti.m0 + BM - bt.k_off);
+  if (BATCHED && bt.causal == kCausalKAbove) kt_begin = max(0, ti.m0 - bt.k_off) / BK;
   const int kt_end = (k_end + BK - 1) / BK;
   ti.kt_begin = kt_begin;
   ti.n_k = kt_end > kt_begin ? kt_end - kt_begin : 0;
+  if (BATCHED && bt.skip_empty && ti.n_k == 0) ti.skip = true;  // C += 0: nothing to write
   return ti;
 }
 
@@ -352,9 +353,14 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (!mbar_wait(acc_full(buf), (j >> 1) & 1, err, kErrWaitAccum)) break;
       tc_fence_after();
       float* Ct = C;
-      if (BATCHED) Ct += (ti.z / bt.c_zdiv) * bt.c_sb + ((ti.z % bt.c_zdiv) / bt.c_zgroup) * bt.c_sh;
+      const float* Rt = R;
+      if (BATCHED) {
+        const long long zoff = (ti.z / bt.c_zdiv) * bt.c_sb + ((ti.z % bt.c_zdiv) / bt.c_zgroup) * bt.c_sh;
+        Ct += zoff;
+        if (R) Rt += zoff;  // R has C's layout
+      }
       store_tile<BN>(tmem_base + buf * BN + (static_cast<uint32_t>(quarter * 32) << 16), ti.n_k > 0, stage_tile,
-                     ti.m0 + quarter * 32, ti.n0, Ct, ldc, R, ldr, M, N, acc_empty(buf), false);
+                     ti.m0 + quarter * 32, ti.n0, Ct, ldc, Rt, ldr, M, N, acc_empty(buf), false);
       ++j;
     }
   }
@@ -1181,7 +1187,7 @@ static int make_map4d(CUtensorMap* map, const BatchedOperand& o, int box_inner, 
 }
 
 int gemm_tf32_batched(int batch, int M, int N, int K, const BatchedOperand& A, const BatchedOperand& B, float* C,
-                      long long ldc, const GemmBatch& bt_in, int bn, int* d_err, cudaStream_t stream) {
+                      long long ldc, const GemmBatch& bt_in, int bn, int* d_err, cudaStream_t stream, const float* R) {
   GemmBatch bt = bt_in;  // operand z -> (batch, head) maps come from the operands
   bt.a_zdiv = A.zdiv;
   bt.a_zgroup = A.zgroup;
@@ -1192,19 +1198,21 @@ int gemm_tf32_batched(int batch, int M, int N, int K, const BatchedOperand& A, c
   if (bn != 64 && bn != 128 && bn != 256) return kGemmBadArgument;
   if ((ldc & 3) || !aligned16(C) || !aligned16(A.ptr) || !aligned16(B.ptr)) return kGemmMisaligned;
   if ((bt.c_sb & 3) || (bt.c_sh & 3) || bt.a_zdiv <= 0 || bt.b_zdiv <= 0 || bt.c_zdiv <= 0 || bt.a_zgroup <= 0 ||
-      bt.b_zgroup <= 0 || bt.c_zgroup <= 0)
+      bt.b_zgroup <= 0 || bt.c_zgroup <= 0 || bt.k_off < 0 || (bt.k_off % BK))
     return kGemmBadArgument;
+  if (R && !aligned16(R)) return kGemmMisaligned;
+  bt.skip_empty = R == C ? 1 : 0;
   CUtensorMap ta{}, tb{};
   int rc = A.mn_major ? make_map4d(&ta, A, 32, BK) : make_map4d(&ta, A, BK, BM);
   if (rc) return kGemmTensorMap;
   rc = B.mn_major ? make_map4d(&tb, B, 32, BK) : make_map4d(&tb, B, BK, bn);
   if (rc) return kGemmTensorMap;
   if (bn == 64)
-    launch_majors<64, true>(A.mn_major, B.mn_major, ta, tb, C, ldc, nullptr, 0, M, N, K, batch, bt, d_err, stream);
+    launch_majors<64, true>(A.mn_major, B.mn_major, ta, tb, C, ldc, R, ldc, M, N, K, batch, bt, d_err, stream);
   else if (bn == 128)
-    launch_majors<128, true>(A.mn_major, B.mn_major, ta, tb, C, ldc, nullptr, 0, M, N, K, batch, bt, d_err, stream);
+    launch_majors<128, true>(A.mn_major, B.mn_major, ta, tb, C, ldc, R, ldc, M, N, K, batch, bt, d_err, stream);
   else
-    launch_majors<256, true>(A.mn_major, B.mn_major, ta, tb, C, ldc, nullptr, 0, M, N, K, batch, bt, d_err, stream);
+    launch_majors<256, true>(A.mn_major, B.mn_major, ta, tb, C, ldc, R, ldc, M, N, K, batch, bt, d_err, stream);
   return cudaGetLastError() == cudaSuccess ? 0 : kGemmLaunch;
 }
 

@@ -37,6 +37,11 @@ struct GemmBatch {
   long long c_sb = 0, c_sh = 0;
   int c_zdiv = 1, c_zgroup = 1;
   int causal = kCausalNone;
+  // The K index of the operands' first column (a multiple of 32): a product over
+  // one chunk of a longer K range applies the causal K bounds at their place in
+  // the whole range (keys up to m0 + 127 - k_off, queries from m0 - k_off).
+  int k_off = 0;
+  int skip_empty = 0;  // set when R is C: tiles with an empty K range are left alone
 };
 // 4-D view of an operand, extents and strides in elements: `inner` contiguous
 // (K for a K-major operand, M or N for an MN-major one), `rows` the other
@@ -79,13 +84,18 @@ int sm_count();
 // them at zero. Null when the device's table of streams is full.
 unsigned int* pair_ticket_counter(int dev, cudaStream_t stream);
 
-// The batched form; bn (64, 128 or 256) is the output tile width. No residual.
+// The batched form; bn (64, 128 or 256) is the output tile width. R (may be C)
+// has C's layout and batch offsets and is added to each output element; an
+// output tile whose causal K range is empty gets R alone (or zeros without R).
 int gemm_tf32_batched(int batch, int M, int N, int K, const BatchedOperand& A, const BatchedOperand& B, float* C,
-                      long long ldc, const GemmBatch& bt, int bn, int* d_err, cudaStream_t stream);
+                      long long ldc, const GemmBatch& bt, int bn, int* d_err, cudaStream_t stream,
+                      const float* R = nullptr);
 
 }  // namespace mm
 
 namespace mm {
+// hi = x rounded to TF32 (nearest), lo = (x - hi) rounded to TF32, for n values.
+void split_tf32(const float* x, float* hi, float* lo, long long n, cudaStream_t stream);
 // Same contract as gemm_tf32, computed as hi*hi + hi*lo + lo*hi (3xTF32).
 // Uses the device scratch arena for the split operands.
 int gemm_3xtf32(int M, int N, int K, GemmOperand A, GemmOperand B, float* C, long long ldc,

@@ -39,13 +39,17 @@ long long footprint(long long rows, long long cols, long long ld) {
   return rows == 0 || cols == 0 ? 0 : (rows - 1) * ld + cols;
 }
 
-void split(const float* x, float* hi, float* lo, long long n, cudaStream_t s) {
+}  // namespace
+
+void split_tf32(const float* x, float* hi, float* lo, long long n, cudaStream_t s) {
   if (n <= 0) return;
   const int threads = 256;
   long long blocks = (n + threads - 1) / threads;
   if (blocks > 148 * 32) blocks = 148 * 32;
   split_tf32_kernel<<<static_cast<int>(blocks), threads, 0, s>>>(x, hi, lo, n);
 }
+
+namespace {
 
 long long round4(long long n) { return (n + 3) & ~3ll; }
 
@@ -63,8 +67,8 @@ int gemm_3xtf32(int M, int N, int K, GemmOperand A, GemmOperand B, float* C, lon
   const long long pa = round4(na), pb = round4(nb);
   float* ws = static_cast<float*>(device_scratch(static_cast<size_t>(2 * pa + 2 * pb) * sizeof(float), stream));
   float *a_hi = ws, *a_lo = ws + pa, *b_hi = ws + 2 * pa, *b_lo = ws + 2 * pa + pb;
-  split(A.ptr, a_hi, a_lo, na, stream);
-  split(B.ptr, b_hi, b_lo, nb, stream);
+  split_tf32(A.ptr, a_hi, a_lo, na, stream);
+  split_tf32(B.ptr, b_hi, b_lo, nb, stream);
   // The tensor core's f32 accumulation loses a little on every step, in the
   // same direction, so its error grows linearly with K (measured against
   // float64: 4.8e-6 relative at K = 2048, 1.9e-5 at K = 8192, where f32 on the

@@ -149,8 +149,12 @@ Trainer::Trainer(const ModelConfig& cfg, int batch, int seq, int precision, int 
     const AttnShape shape{batch, seq, static_cast<int>(H), static_cast<int>(cfg.n_kv_heads), hd,
                           static_cast<long long>(D), static_cast<long long>(KV), static_cast<long long>(KV),
                           static_cast<long long>(D), 1.0f};
-    // TF32: fused tensor-core attention (no score buffers); 3xTF32: FP32 flash kernels
+    // TF32: fused tensor-core attention (no score buffers); 3xTF32: the tensor-core
+    // form with hi/lo operands through score buffers when head_dim is 32, 64 or
+    // 128, else the FP32 flash kernels
     attn_tc_ = precision == kPrecisionTF32 && attention_flash_supported(shape);
+    attn_3x_ = precision == kPrecision3xTF32 && attention_tc_supported(shape);
+    if (attn_3x_) attn3_ws_ = falloc(attention_3x_ws_floats(shape, static_cast<long long>(D)));
   }
   check_cuda(cudaStreamCreateWithFlags(&side_stream_, cudaStreamNonBlocking), "stream");
   check_cuda(cudaEventCreateWithFlags(&attn_side_ready_, cudaEventDisableTiming), "event");

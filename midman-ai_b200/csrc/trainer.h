@@ -200,6 +200,8 @@ class Trainer {
 
   // Attention on the tensor cores (TF32 mode, head_dim 32/64/128): score buffers.
   bool attn_tc_ = false;
+  bool attn_3x_ = false;       // 3xTF32 attention on the tensor cores (score buffers in attn3_ws_)
+  float* attn3_ws_ = nullptr;
   // The backward's side stream (weight-gradient products, the attention
   // backward's dQ kernel) and its events.
   cudaStream_t side_stream_ = nullptr;

@@ -74,6 +74,8 @@ void Trainer::forward(int B, int T, bool train) {
     int slot = prof_begin();
     if (attn_tc_)  // fused: the scores stay on chip
       attention_forward_flash(shape, a.q, a.k, a.v, a.o, a.lse, device_context().d_err, stream_);
+    else if (attn_3x_)
+      attention_forward_3x(shape, a.q, a.k, a.v, a.o, a.lse, attn3_ws_, device_context().d_err, stream_);
     else
       attention_forward(shape, a.q, a.k, a.v, a.o, a.lse, stream_);
     prof_end(slot, "attention_fwd", attn_flops);
@@ -170,6 +172,9 @@ void Trainer::backward(int B, int T) {
       const BwdSide side{side_stream_, attn_side_ready_, attn_side_done_};
       attention_backward_flash(shape, a.q, a.k, a.v, a.o, a.lse, do_, D, dq_, dk_, dv_, delta_, device_context().d_err,
                                stream_, &side);
+    } else if (attn_3x_) {
+      attention_backward_3x(shape, a.q, a.k, a.v, a.o, do_, D, dq_, dk_, dv_, attn3_ws_, device_context().d_err,
+                            stream_);
     } else {
       attention_backward(shape, a.q, a.k, a.v, a.o, a.lse, do_, D, dq_, dk_, dv_, delta_, stream_);
     }
