@@ -570,22 +570,34 @@ uint64_t mm_op_causal_attention(uint32_t tape, uint64_t q_h, uint64_t k_h, uint6
                       1.0f / std::sqrt(static_cast<float>(hd))};
     Buf o = tp.alloc(static_cast<size_t>(q->numel())), lse = tp.alloc(static_cast<size_t>(batch) * n_heads * seq);
     const bool flash = tp.precision == MM_GPU_TF32 && attention_flash_supported(s);
-    if (flash)
+    const bool tc3 = tp.precision == MM_GPU_3XTF32 && attention_tc_supported(s);  // 3xTF32 on the tensor cores
+    if (flash) {
       attention_forward_flash(s, q->data->ptr, k->data->ptr, v->data->ptr, o->ptr, lse->ptr, device_context().d_err,
                               tp.stream);
-    else
+    } else if (tc3) {
+      Buf ws = tp.alloc(static_cast<size_t>(attention_3x_ws_floats(s, s.ldo)));  // freed in stream order
+      attention_forward_3x(s, q->data->ptr, k->data->ptr, v->data->ptr, o->ptr, lse->ptr, ws->ptr,
+                           device_context().d_err, tp.stream);
+    } else {
       attention_forward(s, q->data->ptr, k->data->ptr, v->data->ptr, o->ptr, lse->ptr, tp.stream);
+    }
     Tape* tpp = &tp;
-    return tp.make(q->shape, o, {q, k, v}, [tpp, q, k, v, o, lse, s, flash](const float* dout, const GradOf& grad_of) {
+    return tp.make(q->shape, o, {q, k, v}, [tpp, q, k, v, o, lse, s, flash, tc3](const float* dout,
+                                                                               const GradOf& grad_of) {
       Buf dq = tpp->alloc(static_cast<size_t>(q->numel())), dk = tpp->alloc(static_cast<size_t>(k->numel())),
           dv = tpp->alloc(static_cast<size_t>(v->numel()));
       Buf delta = tpp->alloc(static_cast<size_t>(s.B) * s.H * s.T);
-      if (flash)
+      if (flash) {
         attention_backward_flash(s, q->data->ptr, k->data->ptr, v->data->ptr, o->ptr, lse->ptr, dout, s.ldo, dq->ptr,
                                  dk->ptr, dv->ptr, delta->ptr, device_context().d_err, tpp->stream);
-      else
+      } else if (tc3) {
+        Buf ws = tpp->alloc(static_cast<size_t>(attention_3x_ws_floats(s, s.ldo)));
+        attention_backward_3x(s, q->data->ptr, k->data->ptr, v->data->ptr, o->ptr, dout, s.ldo, dq->ptr, dk->ptr,
+                              dv->ptr, ws->ptr, device_context().d_err, tpp->stream);
+      } else {
         attention_backward(s, q->data->ptr, k->data->ptr, v->data->ptr, o->ptr, lse->ptr, dout, s.ldo, dq->ptr,
                            dk->ptr, dv->ptr, delta->ptr, tpp->stream);
+      }
       const Buf parts[3] = {dq, dk, dv};
       for (size_t i = 0; i < 3; ++i)
         if (float* d = grad_of(i)) tpp->add_into(d, parts[i]->ptr, static_cast<long long>(parts[i]->n));
