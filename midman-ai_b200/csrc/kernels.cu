@@ -437,12 +437,17 @@ __global__ void cross_entropy_kernel(float* logits, long long ld, const int32_t*
   __syncthreads();
   const float mx = row_max, sum = row_sum;
   const int t = t_ok ? t_raw : -1;
+  // softmax * grad_scale as one multiply per logit: exp(v - max) * (grad_scale / sum).
+  // The reference divides each exponential by the sum and then scales
+  // (ops_reduce.rs:266-270); the product differs from that by at most an ulp or
+  // two, and a division per logit made this pass instruction-bound.
+  const float coef = grad_scale / sum;
   if (vec) {
     float4* z4 = reinterpret_cast<float4*>(z);
     for (int j = threadIdx.x; j < vocab / 4; j += blockDim.x) {
       const float4 v = z4[j];
-      float4 d = make_float4(expf(v.x - mx) / sum * grad_scale, expf(v.y - mx) / sum * grad_scale,
-                             expf(v.z - mx) / sum * grad_scale, expf(v.w - mx) / sum * grad_scale);
+      float4 d = make_float4(expf(v.x - mx) * coef, expf(v.y - mx) * coef, expf(v.z - mx) * coef,
+                             expf(v.w - mx) * coef);
       if ((t >> 2) == j) {
         if ((t & 3) == 0) d.x -= grad_scale;
         if ((t & 3) == 1) d.y -= grad_scale;
@@ -453,7 +458,7 @@ __global__ void cross_entropy_kernel(float* logits, long long ld, const int32_t*
     }
   } else {
     for (int j = threadIdx.x; j < vocab; j += blockDim.x) {
-      float d = expf(z[j] - mx) / sum * grad_scale;  // ops_reduce.rs:266-270
+      float d = expf(z[j] - mx) * coef;
       if (j == t) d -= grad_scale;
       z[j] = d;
     }
