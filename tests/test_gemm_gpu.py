@@ -40,10 +40,12 @@ def rel_l2(got, want):
 # On 148 SMs (74 pairs) the tiles of the last, partial wave are cut into K parts of
 # at least 2,048 (summed by a second kernel): (2200, 2340, 8200) has 90 tiles, 16 of
 # them in 4 parts, with ragged edges and uneven parts; (2048, 1024, 4100) 32 tiles
-# in 2 parts each; (8192, 2048, 4096) 34 of 256 tiles in 2 parts.
+# in 2 parts each; (8192, 2048, 4096) 34 of 256 tiles in 2 parts. (2048, 2048, 8192)
+# and (8192, 5632, 2048) are training-step shapes whose last wave stays whole (64 of
+# 74 pairs busy; 38 tiles of K 2,048); (256, 512, 32768) runs on single CTAs.
 SHAPES = [(128, 256, 32), (256, 512, 512), (300, 344, 200), (64, 8, 12), (1000, 1032, 1000),
           (4096, 1408, 512), (2200, 2340, 300), (2304, 4096, 64), (2200, 2340, 8200), (2048, 1024, 4100),
-          (8192, 2048, 4096)]
+          (8192, 2048, 4096), (2048, 2048, 8192), (8192, 5632, 2048), (256, 512, 32768)]
 MAJORS = [(False, True), (False, False), (True, True), (True, False)]
 
 
@@ -73,7 +75,7 @@ def test_gemm_matches_float64(mm, shape, majors, precision):
 
 
 @pytest.mark.parametrize("precision", [0, 1])
-@pytest.mark.parametrize("shape", [(384, 512, 256), (2048, 1024, 4100), (2200, 2340, 8200)])
+@pytest.mark.parametrize("shape", [(384, 512, 256), (2048, 1024, 4100), (2200, 2340, 8200), (8192, 2048, 2048)])
 def test_gemm_adds_the_residual_in_place(mm, precision, shape):
     m, n, k = shape
     gen = torch.Generator(device="cuda").manual_seed(5)
