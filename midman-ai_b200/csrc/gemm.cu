@@ -799,6 +799,291 @@ __global__ void __launch_bounds__(256) split_reduce_kernel(const float* __restri
   }
 }
 
+// ------------------------------------------------------------------ 3xTF32 on CTA pairs
+// The exact mode's product, C = sum_k A(m, k) B(n, k) with A = Ah + Al and
+// B = Bh + Bl (the hi/lo TF32 copies split_tf32 makes): 256 x 256 tiles on CTA
+// pairs as in gemm_pair_kernel, but each stage holds this CTA's 128 rows of all
+// four of Ah, Al, Bh, Bl for one K step of 32, and the leader issues Al Bh,
+// Ah Bl, Ah Bh (the small terms first) for it. The tensor core's f32
+// accumulation loses a little, in the same direction, on every UMMA, so its
+// error grows with the number of UMMAs summed into one accumulator: every
+// X3_CHUNK K steps (24 UMMAs) start a fresh TMEM accumulator, and the epilogue
+// warps add each one into a running sum held in registers (f32, round to
+// nearest). The two accumulators alternate, so a chunk's add overlaps the next
+// chunk's UMMAs. Eight epilogue warps: warp w reads TMEM lanes 32 (w % 4).. and
+// accumulator columns 128 ((w - 2) / 4).., a running sum of 128 floats per
+// thread. Units (whole tiles, then the last wave's K parts) and the workspace of
+// the parts are those of the TF32 pair kernel; units go to pairs by a fixed
+// stride (the exact mode runs on one stream). Registers: each of the SM's four
+// 16K-register quarters holds up to three of the ten warps, which caps a
+// thread at 168 registers; the sum (128) leaves room for 16-column TMEM loads.
+constexpr int X3_THREADS = 320;
+constexpr int X3_STAGES = 3;
+constexpr int X3_TILE = BM * BK * 4;  // 16 KB: this CTA's rows of one of Ah, Al, Bh, Bl
+constexpr int X3_STAGE = 4 * X3_TILE;
+constexpr int X3_CHUNK = 2;  // K steps per TMEM accumulation
+constexpr int X3_SMEM = X3_STAGES * X3_STAGE + 1024 + 256 + 8 * 32 * 32 * 4;
+static_assert(X3_SMEM <= 232448, "3xTF32 pair kernel shared memory");
+
+struct X3Operands {
+  CUtensorMap ah[kMaxSegments], al[kMaxSegments], bh[kMaxSegments], bl[kMaxSegments];
+  int seg_end[kMaxSegments];  // K steps of segments 0..s together
+  int mn3d[kMaxSegments];
+  int nseg;
+};
+
+// A warp's running sum (its 32 rows, lane = row, and 128 columns from n0)
+// through the warp's staging tile to C (+ R): 8 lanes per 32-column row
+// segment, so every R load and C store instruction covers whole 128-byte
+// segments (the layout of store_tile).
+__device__ __forceinline__ void store_sum(const float (&sum)[128], float4* stage_tile, int wrow0, int n0, float* Ct,
+                                          long long ldc, const float* R, long long ldr, int M, int N) {
+  const int lane = threadIdx.x % 32, sub = lane & 7, rsub = lane >> 3;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+#pragma unroll
+    for (int g = 0; g < 8; ++g)
+      stage_tile[lane * 8 + (g ^ (lane & 7))] =
+          make_float4(sum[c * 32 + 4 * g], sum[c * 32 + 4 * g + 1], sum[c * 32 + 4 * g + 2], sum[c * 32 + 4 * g + 3]);
+    __syncwarp();
+    const int col = n0 + c * 32 + 4 * sub;
+#pragma unroll 4
+    for (int it = 0; it < 8; ++it) {
+      const int rr = it * 4 + rsub, row = wrow0 + rr;
+      float4 v = stage_tile[rr * 8 + (sub ^ (rr & 7))];
+      if (row < M && col < N) {
+        float* cp = Ct + static_cast<long long>(row) * ldc + col;
+        const float* rp = R ? R + static_cast<long long>(row) * ldr + col : nullptr;
+        if (col + 3 < N) {
+          if (rp) {
+            const float4 r = *reinterpret_cast<const float4*>(rp);
+            v.x += r.x;
+            v.y += r.y;
+            v.z += r.z;
+            v.w += r.w;
+          }
+          *reinterpret_cast<float4*>(cp) = v;
+        } else {
+          const float vv[4] = {v.x, v.y, v.z, v.w};
+          for (int e = 0; e < 4 && col + e < N; ++e) cp[e] = vv[e] + (rp ? rp[e] : 0.0f);
+        }
+      }
+    }
+    __syncwarp();  // before the next slice overwrites the staging tile
+  }
+}
+
+template <bool A_MN, bool B_MN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(X3_THREADS, 1)
+    gemm3x_pair_kernel(const __grid_constant__ X3Operands ops, float* C, long long ldc, const float* R, long long ldr,
+                       int M, int N, int* err, int total_tiles, int full_tiles, int splits, float* ws) {
+  constexpr int PN = 256;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = static_cast<int>(blockIdx.x) / 2, npairs = static_cast<int>(gridDim.x) / 2;
+  const int tm = (M + 2 * BM - 1) / (2 * BM), tn = (N + PN - 1) / PN;
+  const int n_k = ops.seg_end[ops.nseg - 1];
+  const int total_units = full_tiles + (total_tiles - full_tiles) * splits;
+  static_assert(kMaxSegments == 3, "the selects below assume three segments");
+  const int seg_end0 = ops.nseg > 1 ? ops.seg_end[0] : n_k;
+  const int seg_end1 = ops.nseg > 2 ? ops.seg_end[1] : n_k;
+
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (base - raw_addr);
+  const uint32_t bar_base = base + X3_STAGES * X3_STAGE;
+  auto full_bar = [&](int s) { return bar_base + 8u * s; };
+  auto empty_bar = [&](int s) { return bar_base + 8u * (X3_STAGES + s); };
+  auto acc_full = [&](int b) { return bar_base + 8u * (2 * X3_STAGES + b); };
+  auto acc_empty = [&](int b) { return bar_base + 8u * (2 * X3_STAGES + 2 + b); };
+  constexpr int kBars = 2 * X3_STAGES + 4;
+  const uint32_t tmem_slot = bar_base + 8u * kBars;
+  uint8_t* tail = smem + X3_STAGES * X3_STAGE + 8 * kBars;
+  uint32_t* tmem_slot_ptr = reinterpret_cast<uint32_t*>(tail);
+  int* loads_issued = reinterpret_cast<int*>(tail + 8);
+  int* loads_consumed = loads_issued + 1;
+  static_assert(8 * kBars + 16 <= 256, "barriers and counters fit their 256 bytes");
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (threadIdx.x == 0) {
+    for (int g = 0; g < ops.nseg; ++g) {
+      tma_prefetch_desc(&ops.ah[g]);
+      tma_prefetch_desc(&ops.al[g]);
+      tma_prefetch_desc(&ops.bh[g]);
+      tma_prefetch_desc(&ops.bl[g]);
+    }
+    for (int s = 0; s < X3_STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(acc_full(b), 1);
+      mbar_init(acc_empty(b), 16);  // eight epilogue warps in each CTA
+    }
+    *loads_issued = 0;
+    *loads_consumed = 0;
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, 2 * PN);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot_ptr;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer (both CTAs); completions land on the leader's barriers
+      int it = 0;
+      bool ok = true;
+      for (int u = pair; u < total_units && ok; u += npairs) {
+        const PairUnit w = pair_unit(u, full_tiles, splits, n_k);
+        int mt, nt;
+        pair_tile_mn(w.tile, tm, tn, mt, nt);
+        const int my_m0 = mt * 2 * BM + static_cast<int>(rank) * BM;
+        const int my_n0 = nt * PN + static_cast<int>(rank) * (PN / 2);
+        for (int i = w.kb; i < w.ke; ++i, ++it) {
+          const int s = it % X3_STAGES, round = it / X3_STAGES;
+          if (round > 0 && !mbar_wait(empty_bar(s), (round - 1) & 1, err, kErrWaitEmpty)) {
+            ok = false;
+            break;
+          }
+          if (leader) mbar_arrive_expect_tx(full_bar(s), 2 * X3_STAGE);
+          const uint32_t fb = mapa_shared(full_bar(s), 0);
+          const uint32_t sa = base + s * X3_STAGE;
+          const int g = (i >= seg_end0 ? 1 : 0) + (i >= seg_end1 ? 1 : 0);
+          const int k0 = (i - (g == 0 ? 0 : g == 1 ? seg_end0 : seg_end1)) * BK;
+          const int mn3d = g == 0 ? ops.mn3d[0] : g == 1 ? ops.mn3d[1] : ops.mn3d[2];
+          // this CTA's 128 rows (M or N) of one operand copy at K step k0
+          auto load = [&](uint32_t dst, const CUtensorMap* map, bool mn, bool box3d, int mn0) {
+            if (!mn) {
+              tma_load_2d_pair(dst, map, fb, k0, mn0);
+            } else if (box3d) {
+              tma_load_3d_pair(dst, map, fb, 0, k0, mn0 / 32);
+            } else {
+#pragma unroll
+              for (int j = 0; j < BM / 32; ++j) tma_load_2d_pair(dst + j * MN_BLOCK_BYTES, map, fb, mn0 + 32 * j, k0);
+            }
+          };
+          load(sa, &ops.ah[g], A_MN, mn3d & 1, my_m0);
+          load(sa + X3_TILE, &ops.al[g], A_MN, mn3d & 1, my_m0);
+          load(sa + 2 * X3_TILE, &ops.bh[g], B_MN, mn3d & 2, my_n0);
+          load(sa + 3 * X3_TILE, &ops.bl[g], B_MN, mn3d & 2, my_n0);
+          *loads_issued = it + 1;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ---------------- UMMA issuer (leader only), M = 256 across the pair
+      constexpr uint32_t idesc = idesc_tf32(2 * BM, PN, A_MN, B_MN);
+      int it = 0, j = 0;
+      bool ok = true;
+      for (int u = pair; u < total_units && ok; u += npairs) {
+        const PairUnit w = pair_unit(u, full_tiles, splits, n_k);
+        for (int cb = w.kb; cb < w.ke && ok; cb += X3_CHUNK) {
+          const int ce = min(w.ke, cb + X3_CHUNK);
+          const int buf = j & 1;
+          if (j >= 2 && !mbar_wait(acc_empty(buf), ((j >> 1) - 1) & 1, err, kErrWaitAccum)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t acc = tmem_base + buf * PN;
+          for (int i = cb; i < ce; ++i, ++it) {
+            const int s = it % X3_STAGES, round = it / X3_STAGES;
+            if (!mbar_wait(full_bar(s), round & 1, err, kErrWaitFull)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            *loads_consumed = it + 1;
+            const uint32_t sa = base + s * X3_STAGE;
+            // the (A, B) copies of the three terms, small ones first: Al Bh, Ah Bl, Ah Bh
+#pragma unroll
+            for (int term = 0; term < 3; ++term) {
+#pragma unroll
+              for (int k = 0; k < BK / 8; ++k) {
+                const uint32_t at = sa + (term == 0 ? X3_TILE : 0);
+                const uint32_t bt = sa + (term == 1 ? 3 * X3_TILE : 2 * X3_TILE);
+                const uint64_t adesc = A_MN ? smem_desc(at + k * 1024, MN_BLOCK_BYTES, 512, kLayoutSw128Base32)
+                                            : smem_desc(at + k * 32, 16, 1024, kLayoutSw128);
+                const uint64_t bdesc = B_MN ? smem_desc(bt + k * 1024, MN_BLOCK_BYTES, 512, kLayoutSw128Base32)
+                                            : smem_desc(bt + k * 32, 16, 1024, kLayoutSw128);
+                umma_tf32_pair(acc, adesc, bdesc, idesc, (i != cb || term != 0 || k != 0) ? 1u : 0u);
+              }
+            }
+            umma_commit_pair(empty_bar(s), 0x3);
+          }
+          if (!ok) break;
+          umma_commit_pair(acc_full(buf), 0x3);
+          ++j;
+        }
+      }
+    }
+  } else {
+    // ---------------- epilogue (both CTAs): 32 rows x 128 columns of the tile per warp
+    const int quarter = warp & 3, half = (warp - 2) >> 2;
+    float4* stage_tile = reinterpret_cast<float4*>(smem + X3_STAGES * X3_STAGE + 256) + (warp - 2) * 256;
+    const int srow = static_cast<int>(rank) * BM + quarter * 32;  // this warp's rows of the tile
+    int j = 0;
+    bool ok = true;
+    for (int u = pair; u < total_units && ok; u += npairs) {
+      const PairUnit w = pair_unit(u, full_tiles, splits, n_k);
+      float sum[128];
+#pragma unroll
+      for (int e = 0; e < 128; ++e) sum[e] = 0.0f;
+      for (int cb = w.kb; cb < w.ke; cb += X3_CHUNK) {
+        const int buf = j & 1;
+        if (!mbar_wait(acc_full(buf), (j >> 1) & 1, err, kErrWaitAccum)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t acc = tmem_base + buf * PN + (static_cast<uint32_t>(quarter * 32) << 16) + half * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          uint32_t r[16];
+          tmem_ld_32x32b_x16(acc + c * 16, r);
+#pragma unroll
+          for (int e = 0; e < 16; ++e) sum[c * 16 + e] += __uint_as_float(r[e]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_remote(mapa_shared(acc_empty(buf), 0));
+        ++j;
+      }
+      if (!ok) break;
+      if (w.slot < 0) {
+        int mt, nt;
+        pair_tile_mn(w.tile, tm, tn, mt, nt);
+        store_sum(sum, stage_tile, mt * 2 * BM + srow, nt * PN + half * 128, C, ldc, R, ldr, M, N);
+      } else {  // a K part: its partial sums into the part's workspace tile
+        store_sum(sum, stage_tile, srow, half * 128, ws + static_cast<long long>(w.slot) * PairTile<PN>::TILE_FLOATS,
+                  PN, nullptr, 0, 2 * BM, PN);
+      }
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync();  // both CTAs are done with their TMEM and with each other's barriers
+  if (leader && threadIdx.x == 0) {
+    // after a timed-out wait, let the pair's copies in flight land (bounded)
+    for (int i = *loads_consumed; i < *loads_issued; ++i)
+      if (!mbar_wait(full_bar(i % X3_STAGES), (i / X3_STAGES) & 1, err, kErrWaitDrain, 1000000000ull)) break;
+  }
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, 2 * PN);
+  }
+}
+
 }  // namespace
 
 namespace {
@@ -806,6 +1091,15 @@ namespace {
 // ------------------------------------------------------------------ host side
 
 thread_local uint64_t t_launches = 0;  // kernels launched by this thread (gemm_launch_count)
+thread_local cudaError_t t_launch_error = cudaSuccess;  // the last failed launch's error
+
+// 0, or kGemmLaunch with the launch's CUDA error kept for gemm_status_string.
+int launch_status() {
+  const cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) return 0;
+  t_launch_error = e;
+  return kGemmLaunch;
+}
 
 PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -1045,6 +1339,40 @@ int launch_pair_majors(bool a_mn, bool b_mn, const PairOperands& ops, float* C, 
   return launch_pair<true, true, PN>(ops, C, ldc, R, ldr, M, N, err, s);
 }
 
+template <bool A_MN, bool B_MN>
+int launch_pair3x(const X3Operands& ops, float* C, long long ldc, const float* R, long long ldr, int M, int N,
+                  int* err, cudaStream_t stream) {
+  auto kern = gemm3x_pair_kernel<A_MN, B_MN>;
+  static thread_local int configured_device = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_device != dev) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, X3_SMEM);
+    configured_device = dev;
+  }
+  const int tm = (M + 2 * BM - 1) / (2 * BM);
+  const long long tiles = static_cast<long long>(tm) * ((N + 255) / 256);
+  const int pairs = device_sms() / 2;
+  const PairPlan plan = pair_plan(tiles, pairs, ops.seg_end[ops.nseg - 1]);
+  const long long units = plan.full + (tiles - plan.full) * plan.splits;
+  const int grid = 2 * static_cast<int>(units < pairs ? units : pairs);
+  if (plan.splits == 1) {
+    kern<<<grid, X3_THREADS, X3_SMEM, stream>>>(ops, C, ldc, R, ldr, M, N, err, static_cast<int>(tiles), plan.full, 1,
+                                                nullptr);
+    ++t_launches;
+    return 0;
+  }
+  std::lock_guard<std::mutex> lock(split_mutex());
+  SplitWorkspace* w = split_workspace(dev, stream, static_cast<size_t>(pairs) * P_TILE_FLOATS_MAX);
+  if (!w) return kGemmLaunch;
+  kern<<<grid, X3_THREADS, X3_SMEM, stream>>>(ops, C, ldc, R, ldr, M, N, err, static_cast<int>(tiles), plan.full,
+                                              plan.splits, w->ptr);
+  const dim3 rgrid(static_cast<unsigned>(tiles - plan.full), 2 * BM / (256 / (256 / 4)));
+  split_reduce_kernel<256><<<rgrid, 256, 0, stream>>>(w->ptr, plan.splits, plan.full, tm, C, ldc, R, ldr, M, N);
+  t_launches += 2;
+  return cudaEventRecord(w->last_use, stream) == cudaSuccess ? 0 : kGemmLaunch;
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace
@@ -1061,7 +1389,11 @@ const char* gemm_status_string(int status) {
     case kGemmBadArgument: return "bad GEMM argument (null pointer, negative size or unsupported tile)";
     case kGemmMisaligned: return "GEMM operand not 16-byte aligned or leading dimension not a multiple of 4";
     case kGemmTensorMap: return "cuTensorMapEncodeTiled is unavailable or rejected an operand";
-    case kGemmLaunch: return "GEMM kernel launch failed";
+    case kGemmLaunch: {
+      static thread_local char text[160];
+      std::snprintf(text, sizeof text, "GEMM kernel launch failed (%s)", cudaGetErrorString(t_launch_error));
+      return text;
+    }
     default: return "unknown GEMM status";
   }
 }
@@ -1115,7 +1447,7 @@ int gemm_single(int M, int N, int K, const GemmOperand& A, const GemmOperand& B,
     launch_majors<128, false>(A.mn_major, B.mn_major, ta, tb, C, ldc, R, ldr, M, N, K, 1, bt, d_err, stream, mn3d);
   else
     launch_majors<256, false>(A.mn_major, B.mn_major, ta, tb, C, ldc, R, ldr, M, N, K, 1, bt, d_err, stream, mn3d);
-  return cudaGetLastError() == cudaSuccess ? 0 : kGemmLaunch;
+  return launch_status();
 }
 
 }  // namespace
@@ -1156,7 +1488,7 @@ int gemm_tf32_sum(int M, int N, const GemmSegment* segs, int nseg, float* C, lon
     const int rc = launch_pair_majors<256>(live[0].a.mn_major, live[0].b.mn_major, ops, C, ldc, R, ldr, M, N, d_err,
                                            stream);
     if (rc) return rc;
-    return cudaGetLastError() == cudaSuccess ? 0 : kGemmLaunch;
+    return launch_status();
   }
   // one launch per segment, each after the first accumulating into C
   for (int g = 0; g < nseg; ++g) {
@@ -1169,6 +1501,38 @@ int gemm_tf32_sum(int M, int N, const GemmSegment* segs, int nseg, float* C, lon
     if (rc) return rc;
   }
   return 0;
+}
+
+bool gemm_3xtf32_pair_suits(int M, int N, int n_k) { return pair_suits(M, N, n_k); }
+
+int gemm_3xtf32_pair_sum(int M, int N, const GemmSegment* hi, const GemmSegment* lo, int nseg, float* C,
+                         long long ldc, const float* R, long long ldr, int* d_err, cudaStream_t stream) {
+  if (M <= 0 || N <= 0 || !C || !hi || !lo || nseg < 1 || nseg > kMaxSegments) return kGemmBadArgument;
+  if ((ldc & 3) || !aligned16(C) || (R && ((ldr & 3) || !aligned16(R)))) return kGemmMisaligned;
+  X3Operands ops{};
+  int end = 0;
+  for (int g = 0; g < nseg; ++g) {
+    const GemmSegment& h = hi[g];
+    const GemmSegment& l = lo[g];
+    if (h.K <= 0 || l.K != h.K || h.a.mn_major != hi[0].a.mn_major || h.b.mn_major != hi[0].b.mn_major ||
+        l.a.mn_major != h.a.mn_major || l.b.mn_major != h.b.mn_major || l.a.ld != h.a.ld || l.b.ld != h.b.ld)
+      return kGemmBadArgument;
+    int mn3d_lo = 0;
+    int rc = make_maps(M, N, h.K, h.a, h.b, 128, &ops.ah[g], &ops.bh[g], &ops.mn3d[g]);
+    if (!rc) rc = make_maps(M, N, l.K, l.a, l.b, 128, &ops.al[g], &ops.bl[g], &mn3d_lo);
+    if (rc) return rc;
+    end += (h.K + BK - 1) / BK;
+    ops.seg_end[g] = end;
+  }
+  ops.nseg = nseg;
+  const bool a_mn = hi[0].a.mn_major, b_mn = hi[0].b.mn_major;
+  int rc;
+  if (!a_mn && !b_mn) rc = launch_pair3x<false, false>(ops, C, ldc, R, ldr, M, N, d_err, stream);
+  else if (!a_mn) rc = launch_pair3x<false, true>(ops, C, ldc, R, ldr, M, N, d_err, stream);
+  else if (!b_mn) rc = launch_pair3x<true, false>(ops, C, ldc, R, ldr, M, N, d_err, stream);
+  else rc = launch_pair3x<true, true>(ops, C, ldc, R, ldr, M, N, d_err, stream);
+  if (rc) return rc;
+  return launch_status();
 }
 
 int gemm_tf32(int M, int N, int K, GemmOperand A, GemmOperand B, float* C, long long ldc, const float* R,
@@ -1213,7 +1577,7 @@ int gemm_tf32_batched(int batch, int M, int N, int K, const BatchedOperand& A, c
     launch_majors<128, true>(A.mn_major, B.mn_major, ta, tb, C, ldc, R, ldc, M, N, K, batch, bt, d_err, stream);
   else
     launch_majors<256, true>(A.mn_major, B.mn_major, ta, tb, C, ldc, R, ldc, M, N, K, batch, bt, d_err, stream);
-  return cudaGetLastError() == cudaSuccess ? 0 : kGemmLaunch;
+  return launch_status();
 }
 
 }  // namespace mm

@@ -100,4 +100,15 @@ void split_tf32(const float* x, float* hi, float* lo, long long n, cudaStream_t 
 // Uses the device scratch arena for the split operands.
 int gemm_3xtf32(int M, int N, int K, GemmOperand A, GemmOperand B, float* C, long long ldc,
                 const float* R, long long ldr, int* d_err, cudaStream_t stream);
+// Same contract as gemm_tf32_sum in 3xTF32: one launch for up to three segments
+// with the same majors when the shape runs on CTA pairs.
+int gemm_3xtf32_sum(int M, int N, const GemmSegment* segs, int nseg, float* C, long long ldc, const float* R,
+                    long long ldr, int* d_err, cudaStream_t stream);
+// The 3xTF32 CTA-pair kernel on split operands: hi[g] = (Ah, Bh, K), lo[g] =
+// (Al, Bl, K) with the leading dimensions and majors of hi[g]; 1 to 3 segments
+// with the same majors. C = sum_g (Al Bh + Ah Bl + Ah Bh) (+ R).
+int gemm_3xtf32_pair_sum(int M, int N, const GemmSegment* hi, const GemmSegment* lo, int nseg, float* C,
+                         long long ldc, const float* R, long long ldr, int* d_err, cudaStream_t stream);
+// Whether products of this shape (n_k K steps of 32 in all) run on CTA pairs.
+bool gemm_3xtf32_pair_suits(int M, int N, int n_k);
 }  // namespace mm

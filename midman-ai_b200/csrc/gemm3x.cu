@@ -59,8 +59,14 @@ constexpr int kChunkK = 256;
 
 }  // namespace
 
-int gemm_3xtf32(int M, int N, int K, GemmOperand A, GemmOperand B, float* C, long long ldc,
-                const float* R, long long ldr, int* d_err, cudaStream_t stream) {
+namespace {
+
+// One product as one launch per K chunk of kChunkK (the shapes the CTA-pair
+// kernel does not take): each launch accumulates one chunk from zero in tensor
+// memory and its epilogue adds the result to the sum so far (R = C) in f32 on
+// the CUDA cores, with round-to-nearest.
+int gemm_3xtf32_chunked(int M, int N, int K, GemmOperand A, GemmOperand B, float* C, long long ldc,
+                        const float* R, long long ldr, int* d_err, cudaStream_t stream) {
   if (M == 0 || N == 0 || K == 0) return gemm_tf32(M, N, K, A, B, C, ldc, R, ldr, d_err, stream);
   const long long na = A.mn_major ? footprint(K, M, A.ld) : footprint(M, K, A.ld);
   const long long nb = B.mn_major ? footprint(K, N, B.ld) : footprint(N, K, B.ld);
@@ -69,13 +75,6 @@ int gemm_3xtf32(int M, int N, int K, GemmOperand A, GemmOperand B, float* C, lon
   float *a_hi = ws, *a_lo = ws + pa, *b_hi = ws + 2 * pa, *b_lo = ws + 2 * pa + pb;
   split_tf32(A.ptr, a_hi, a_lo, na, stream);
   split_tf32(B.ptr, b_hi, b_lo, nb, stream);
-  // The tensor core's f32 accumulation loses a little on every step, in the
-  // same direction, so its error grows linearly with K (measured against
-  // float64: 4.8e-6 relative at K = 2048, 1.9e-5 at K = 8192, where f32 on the
-  // CUDA cores stays at 0.8-1.6e-6). K is therefore taken in chunks of
-  // kChunkK: each launch accumulates one chunk from zero in tensor memory and
-  // its epilogue adds the result to the sum so far (R = C) in f32 on the CUDA
-  // cores, with round-to-nearest.
   int rc = 0;
   for (int k0 = 0; k0 < K && rc == 0; k0 += kChunkK) {
     const int kc = K - k0 < kChunkK ? K - k0 : kChunkK;
@@ -91,6 +90,74 @@ int gemm_3xtf32(int M, int N, int K, GemmOperand A, GemmOperand B, float* C, lon
     rc = gemm_tf32_sum(M, N, terms, 3, C, ldc, k0 == 0 ? R : C, k0 == 0 ? ldr : ldc, d_err, stream);
   }
   return rc;
+}
+
+}  // namespace
+
+// The tensor core's f32 accumulation loses a little on every step, in the same
+// direction, so its error grows linearly with the number of products summed in
+// one accumulator (measured against float64: 4.8e-6 relative at K = 2048,
+// 1.9e-5 at K = 8192 in one accumulation, where f32 on the CUDA cores stays at
+// 0.8-1.6e-6). Both paths therefore sum short accumulations in f32 with
+// round-to-nearest: the CTA-pair kernel every 64 of K (24 UMMAs) in registers,
+// the chunked path every kChunkK of K through C.
+int gemm_3xtf32_sum(int M, int N, const GemmSegment* segs, int nseg, float* C, long long ldc, const float* R,
+                    long long ldr, int* d_err, cudaStream_t stream) {
+  if (nseg < 1 || !segs) return kGemmBadArgument;
+  GemmSegment live[3];
+  int n_live = 0, n_k = 0;
+  bool same = true;
+  for (int g = 0; g < nseg; ++g) {
+    if (segs[g].K < 0) return kGemmBadArgument;
+    if (segs[g].K == 0) continue;
+    if (n_live == 3) {
+      same = false;
+      break;
+    }
+    live[n_live] = segs[g];
+    same = same && segs[g].a.mn_major == live[0].a.mn_major && segs[g].b.mn_major == live[0].b.mn_major;
+    n_k += (segs[g].K + 31) / 32;
+    ++n_live;
+  }
+  if (n_live == 0 || M == 0 || N == 0) return gemm_tf32_sum(M, N, segs, nseg, C, ldc, R, ldr, d_err, stream);
+  if (same && gemm_3xtf32_pair_suits(M, N, n_k)) {
+    long long total = 0, na[3], nb[3];
+    for (int g = 0; g < n_live; ++g) {
+      const GemmSegment& s = live[g];
+      if (!s.a.ptr || !s.b.ptr) return kGemmBadArgument;
+      na[g] = round4(s.a.mn_major ? footprint(s.K, M, s.a.ld) : footprint(M, s.K, s.a.ld));
+      nb[g] = round4(s.b.mn_major ? footprint(s.K, N, s.b.ld) : footprint(N, s.K, s.b.ld));
+      total += 2 * (na[g] + nb[g]);
+    }
+    float* ws = static_cast<float*>(device_scratch(static_cast<size_t>(total) * sizeof(float), stream));
+    GemmSegment hi[3], lo[3];
+    for (int g = 0; g < n_live; ++g) {
+      const GemmSegment& s = live[g];
+      float *ah = ws, *al = ws + na[g], *bh = ws + 2 * na[g], *bl = ws + 2 * na[g] + nb[g];
+      ws += 2 * (na[g] + nb[g]);
+      split_tf32(s.a.ptr, ah, al, na[g], stream);
+      split_tf32(s.b.ptr, bh, bl, nb[g], stream);
+      hi[g] = {{ah, s.a.ld, s.a.mn_major}, {bh, s.b.ld, s.b.mn_major}, s.K};
+      lo[g] = {{al, s.a.ld, s.a.mn_major}, {bl, s.b.ld, s.b.mn_major}, s.K};
+    }
+    return gemm_3xtf32_pair_sum(M, N, hi, lo, n_live, C, ldc, R, ldr, d_err, stream);
+  }
+  int rc = 0;
+  bool first = true;
+  for (int g = 0; g < nseg && rc == 0; ++g) {
+    if (segs[g].K == 0) continue;
+    rc = gemm_3xtf32_chunked(M, N, segs[g].K, segs[g].a, segs[g].b, C, ldc, first ? R : C, first ? ldr : ldc,
+                             d_err, stream);
+    first = false;
+  }
+  return rc;
+}
+
+int gemm_3xtf32(int M, int N, int K, GemmOperand A, GemmOperand B, float* C, long long ldc,
+                const float* R, long long ldr, int* d_err, cudaStream_t stream) {
+  if (K < 0) return kGemmBadArgument;
+  const GemmSegment seg{A, B, K};
+  return gemm_3xtf32_sum(M, N, &seg, 1, C, ldc, R, ldr, d_err, stream);
 }
 
 }  // namespace mm

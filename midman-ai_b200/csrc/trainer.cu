@@ -463,8 +463,8 @@ void Trainer::gemm(int M, int N, int K, const float* A, long long lda, bool a_mn
   gemm_sum(M, N, &seg, 1, C, ldc, R, ldr, st);
 }
 
-// C = sum of the segments' products (+ R): one launch in TF32 when the shape runs
-// on CTA pairs (gemm_tf32_sum); in 3xTF32 one split product per segment.
+// C = sum of the segments' products (+ R): one launch when the shape runs on CTA
+// pairs (gemm_tf32_sum, or gemm_3xtf32_sum after the hi/lo splits).
 void Trainer::gemm_sum(int M, int N, const GemmSegment* segs, int nseg, float* C, long long ldc, const float* R,
                        long long ldr, cudaStream_t st) {
   if (!st) st = stream_;
@@ -475,9 +475,7 @@ void Trainer::gemm_sum(int M, int N, const GemmSegment* segs, int nseg, float* C
   if (precision_ == kPrecisionTF32) {
     rc = gemm_tf32_sum(M, N, segs, nseg, C, ldc, R, ldr, ctx.d_err, st);
   } else {
-    for (int g = 0; g < nseg && rc == 0; ++g)
-      rc = gemm_3xtf32(M, N, segs[g].K, segs[g].a, segs[g].b, C, ldc, g == 0 ? R : C, g == 0 ? ldr : ldc,
-                       ctx.d_err, st);
+    rc = gemm_3xtf32_sum(M, N, segs, nseg, C, ldc, R, ldr, ctx.d_err, st);
     launches_ += 2 * nseg;  // the hi/lo splits of A and B
   }
   if (rc) throw std::runtime_error(std::string("GEMM: ") + gemm_status_string(rc));
