@@ -102,45 +102,19 @@ int tile_for(int hd) { return hd <= 64 ? 64 : 128; }
 
 // ---------------------------------------------------------------- 3xTF32 products
 // A TF32 number pair (hi, lo) per operand element, and a product formed as
-// lo*hi + hi*lo + hi*hi, each term one launch of the batched GEMM accumulating
-// into C through its residual (the first launch writes C unless `accumulate`).
-// A contraction longer than kChunk is taken kChunk values at a time, each chunk
-// accumulated from zero in tensor memory and added to C by the epilogue in f32,
-// so the tensor core's accumulation error does not grow with the length.
-constexpr int kChunk = 256;
-
+// lo*hi + hi*lo + hi*hi in one launch of the batched 3xTF32 GEMM, which
+// restarts its tensor-memory accumulation every 64 of K and adds the partial
+// sums in f32, so the tensor core's accumulation error does not grow with the
+// contraction's length; with `accumulate` the product is added to C.
 struct Pair3 {
   BatchedOperand hi, lo;
 };
 
-// The view restricted to K values [k0, k0 + kc).
-BatchedOperand k_slice(BatchedOperand o, int k0, int kc) {
-  if (!o.mn_major) {  // K contiguous
-    o.ptr += k0;
-    o.inner = kc;
-  } else {  // K along the rows
-    o.ptr += static_cast<long long>(k0) * o.row_stride;
-    o.rows = kc;
-  }
-  return o;
-}
-
-void product3(int batch, int M, int N, int K, const Pair3& A, const Pair3& B, float* C, long long ldc, GemmBatch bt,
-              int bn, bool accumulate, int* d_err, cudaStream_t stream, const char* what) {
-  bool first = !accumulate;
-  const int k_base = bt.k_off;
-  for (int k0 = 0; k0 < K; k0 += kChunk) {
-    const int kc = K - k0 < kChunk ? K - k0 : kChunk;
-    bt.k_off = k_base + k0;
-    const BatchedOperand terms[3][2] = {{k_slice(A.lo, k0, kc), k_slice(B.hi, k0, kc)},
-                                        {k_slice(A.hi, k0, kc), k_slice(B.lo, k0, kc)},
-                                        {k_slice(A.hi, k0, kc), k_slice(B.hi, k0, kc)}};
-    for (const auto& t : terms) {
-      check_gemm(gemm_tf32_batched(batch, M, N, kc, t[0], t[1], C, ldc, bt, bn, d_err, stream, first ? nullptr : C),
-                 what);
-      first = false;
-    }
-  }
+void product3(int batch, int M, int N, int K, const Pair3& A, const Pair3& B, float* C, long long ldc,
+              const GemmBatch& bt, int bn, bool accumulate, int* d_err, cudaStream_t stream, const char* what) {
+  check_gemm(gemm_3xtf32_batched(batch, M, N, K, A.hi, A.lo, B.hi, B.lo, C, ldc, bt, bn, d_err, stream,
+                                 accumulate ? C : nullptr),
+             what);
 }
 
 // Head g of every key/value group of a token-major [B, T, H, hd] operand, as a
@@ -208,7 +182,7 @@ Ws3 carve(const AttnShape& s, float* ws, long long ld_dout) {
   return w;
 }
 
-// S = Q K^T (three terms; K = head_dim needs no chunks), tiles above the diagonal skipped.
+// S = Q K^T (three terms), tiles above the diagonal skipped.
 void scores3(const AttnShape& s, const Ws3& w, int* d_err, cudaStream_t st) {
   const int G = s.H / s.Hkv, BH = s.B * s.H;
   const long long ldS = attention_scores_ld(s.T);
@@ -218,7 +192,7 @@ void scores3(const AttnShape& s, const Ws3& w, int* d_err, cudaStream_t st) {
   bs.causal = kCausalSkipUpper;
   product3(BH, s.T, s.T, s.hd, {heads_view(w.qh, false, s, s.ldq, s.H, 1), heads_view(w.ql, false, s, s.ldq, s.H, 1)},
            {heads_view(w.kh, false, s, s.ldk, s.Hkv, G), heads_view(w.kl, false, s, s.ldk, s.Hkv, G)}, w.S, ldS, bs,
-           256, false, d_err, st, "attention (3xTF32) S = QK^T");
+           128, false, d_err, st, "attention (3xTF32) S = QK^T");
 }
 
 void softmax_into(const AttnShape& s, float* S, float* lse, cudaStream_t st) {
@@ -278,7 +252,7 @@ void attention_backward_3x(const AttnShape& s, const float* q, const float* k, c
     bd.causal = kCausalSkipUpper;
     product3(BH, s.T, s.T, s.hd, {heads_view(w.gh, false, s, lddo, s.H, 1), heads_view(w.gl, false, s, lddo, s.H, 1)},
              {heads_view(w.vh, false, s, s.ldv, s.Hkv, G), heads_view(w.vl, false, s, s.ldv, s.Hkv, G)}, w.D, ldS, bd,
-             256, false, d_err, st, "attention (3xTF32) dP = dO V^T");
+             128, false, d_err, st, "attention (3xTF32) dP = dO V^T");
   }
   attention_delta(s, o, dout, lddo, w.delta, st);
   // dV = P^T dO, summed over each key/value head's group; K = queries in chunks,

@@ -832,15 +832,17 @@ struct X3Operands {
   int nseg;
 };
 
-// A warp's running sum (its 32 rows, lane = row, and 128 columns from n0)
+// A warp's running sum (its 32 rows, lane = row, and NC columns from n0)
 // through the warp's staging tile to C (+ R): 8 lanes per 32-column row
 // segment, so every R load and C store instruction covers whole 128-byte
 // segments (the layout of store_tile).
-__device__ __forceinline__ void store_sum(const float (&sum)[128], float4* stage_tile, int wrow0, int n0, float* Ct,
+template <int NC>
+__device__ __forceinline__ void store_sum(const float (&sum)[NC], float4* stage_tile, int wrow0, int n0, float* Ct,
                                           long long ldc, const float* R, long long ldr, int M, int N) {
+  static_assert(NC % 32 == 0, "whole 32-column slices");
   const int lane = threadIdx.x % 32, sub = lane & 7, rsub = lane >> 3;
 #pragma unroll
-  for (int c = 0; c < 4; ++c) {
+  for (int c = 0; c < NC / 32; ++c) {
 #pragma unroll
     for (int g = 0; g < 8; ++g)
       stage_tile[lane * 8 + (g ^ (lane & 7))] =
@@ -1082,6 +1084,224 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(X3_THREADS, 1)
     tc_fence_after();
     tmem_dealloc_pair(tmem_base, 2 * PN);
   }
+}
+
+// The batched form of the 3xTF32 product (attention's exact mode): one CTA per
+// 128 x BN output tile of the batched GEMM (4-D operand views, causal tile
+// modes as in gemm_tf32_kernel), each stage holding Ah, Al, Bh, Bl for one K
+// step, the three terms issued by one thread, and the same per-chunk
+// accumulations summed in the epilogue warps' registers (warp w: TMEM lanes
+// 32 (w % 4).., columns (BN / 2) ((w - 2) / 4)..).
+template <int BN>
+struct X3BatchTile {
+  static constexpr int A_BYTES = BM * BK * 4;  // 16 KB
+  static constexpr int B_BYTES = BN * BK * 4;
+  static constexpr int STAGE = 2 * A_BYTES + 2 * B_BYTES;
+  static constexpr int STAGES = 196608 / STAGE > 4 ? 4 : 196608 / STAGE;
+  static constexpr int SMEM = STAGES * STAGE + 1024 + 256 + 8 * 32 * 32 * 4;
+};
+
+struct X3BatchMaps {
+  CUtensorMap ah, al, bh, bl;
+};
+
+template <bool A_MN, bool B_MN, int BN>
+__global__ void __launch_bounds__(X3_THREADS, 1)
+    gemm3x_batched_kernel(const __grid_constant__ X3BatchMaps maps, float* C, long long ldc, const float* R,
+                          long long ldr, int M, int N, int K, int* err, GemmBatch bt, int total_tiles) {
+  using TL = X3BatchTile<BN>;
+  constexpr int STAGES = TL::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (base - raw_addr);
+  const uint32_t bar_base = base + STAGES * TL::STAGE;
+  auto full_bar = [&](int s) { return bar_base + 8u * s; };
+  auto empty_bar = [&](int s) { return bar_base + 8u * (STAGES + s); };
+  auto acc_full = [&](int b) { return bar_base + 8u * (2 * STAGES + b); };
+  auto acc_empty = [&](int b) { return bar_base + 8u * (2 * STAGES + 2 + b); };
+  constexpr int kBars = 2 * STAGES + 4;
+  const uint32_t tmem_slot = bar_base + 8u * kBars;
+  uint8_t* tail = smem + STAGES * TL::STAGE + 8 * kBars;
+  uint32_t* tmem_slot_ptr = reinterpret_cast<uint32_t*>(tail);
+  int* loads_issued = reinterpret_cast<int*>(tail + 8);
+  int* loads_consumed = loads_issued + 1;
+  static_assert(8 * kBars + 16 <= 256, "barriers and counters fit their 256 bytes");
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&maps.ah);
+    tma_prefetch_desc(&maps.al);
+    tma_prefetch_desc(&maps.bh);
+    tma_prefetch_desc(&maps.bl);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(acc_full(b), 1);
+      mbar_init(acc_empty(b), 8);  // one arrival per epilogue warp
+    }
+    *loads_issued = 0;
+    *loads_consumed = 0;
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 2 * BN);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot_ptr;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer
+      int it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+        const TileInfo ti = tile_info<BN, true>(t, M, N, K, bt);
+        if (ti.skip) continue;
+        const int a_zb = ti.z / bt.a_zdiv, a_zh = (ti.z % bt.a_zdiv) / bt.a_zgroup;
+        const int b_zb = ti.z / bt.b_zdiv, b_zh = (ti.z % bt.b_zdiv) / bt.b_zgroup;
+        for (int i = 0; i < ti.n_k; ++i, ++it) {
+          const int s = it % STAGES, round = it / STAGES;
+          if (round > 0 && !mbar_wait(empty_bar(s), (round - 1) & 1, err, kErrWaitEmpty)) {
+            ok = false;
+            break;
+          }
+          const uint32_t sa = base + s * TL::STAGE, sb = sa + 2 * TL::A_BYTES;
+          mbar_arrive_expect_tx(full_bar(s), TL::STAGE);
+          const int k0 = (ti.kt_begin + i) * BK;
+          auto load_a = [&](uint32_t dst, const CUtensorMap* map) {
+            if (!A_MN) {
+              load_box<true>(dst, map, full_bar(s), k0, ti.m0, a_zh, a_zb);
+            } else {
+#pragma unroll
+              for (int j = 0; j < BM / 32; ++j)
+                load_box<true>(dst + j * MN_BLOCK_BYTES, map, full_bar(s), ti.m0 + 32 * j, k0, a_zh, a_zb);
+            }
+          };
+          auto load_b = [&](uint32_t dst, const CUtensorMap* map) {
+            if (!B_MN) {
+              load_box<true>(dst, map, full_bar(s), k0, ti.n0, b_zh, b_zb);
+            } else {
+#pragma unroll
+              for (int j = 0; j < BN / 32; ++j)
+                load_box<true>(dst + j * MN_BLOCK_BYTES, map, full_bar(s), ti.n0 + 32 * j, k0, b_zh, b_zb);
+            }
+          };
+          load_a(sa, &maps.ah);
+          load_a(sa + TL::A_BYTES, &maps.al);
+          load_b(sb, &maps.bh);
+          load_b(sb + TL::B_BYTES, &maps.bl);
+          *loads_issued = it + 1;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- UMMA issuer
+      constexpr uint32_t idesc = idesc_tf32(BM, BN, A_MN, B_MN);
+      int it = 0, j = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+        const TileInfo ti = tile_info<BN, true>(t, M, N, K, bt);
+        if (ti.skip) continue;
+        for (int cb = 0; cb < ti.n_k && ok; cb += X3_CHUNK) {
+          const int ce = min(ti.n_k, cb + X3_CHUNK);
+          const int buf = j & 1;
+          if (j >= 2 && !mbar_wait(acc_empty(buf), ((j >> 1) - 1) & 1, err, kErrWaitAccum)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t acc = tmem_base + buf * BN;
+          for (int i = cb; i < ce; ++i, ++it) {
+            const int s = it % STAGES, round = it / STAGES;
+            if (!mbar_wait(full_bar(s), round & 1, err, kErrWaitFull)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            *loads_consumed = it + 1;
+            const uint32_t sa = base + s * TL::STAGE, sb = sa + 2 * TL::A_BYTES;
+            // the (A, B) copies of the three terms, small ones first: Al Bh, Ah Bl, Ah Bh
+#pragma unroll
+            for (int term = 0; term < 3; ++term) {
+#pragma unroll
+              for (int k = 0; k < BK / 8; ++k) {
+                const uint32_t at = sa + (term == 0 ? TL::A_BYTES : 0);
+                const uint32_t bt_ = sb + (term == 1 ? TL::B_BYTES : 0);
+                const uint64_t adesc = A_MN ? smem_desc(at + k * 1024, MN_BLOCK_BYTES, 512, kLayoutSw128Base32)
+                                            : smem_desc(at + k * 32, 16, 1024, kLayoutSw128);
+                const uint64_t bdesc = B_MN ? smem_desc(bt_ + k * 1024, MN_BLOCK_BYTES, 512, kLayoutSw128Base32)
+                                            : smem_desc(bt_ + k * 32, 16, 1024, kLayoutSw128);
+                umma_tf32(acc, adesc, bdesc, idesc, (i != cb || term != 0 || k != 0) ? 1u : 0u);
+              }
+            }
+            umma_commit(empty_bar(s));
+          }
+          if (!ok) break;
+          umma_commit(acc_full(buf));
+          ++j;
+        }
+      }
+    }
+  } else {
+    // ---------------- epilogue: 32 rows x BN / 2 columns of the tile per warp
+    constexpr int NC = BN / 2;
+    const int quarter = warp & 3, half = (warp - 2) >> 2;
+    float4* stage_tile = reinterpret_cast<float4*>(smem + STAGES * TL::STAGE + 256) + (warp - 2) * 256;
+    int j = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+      const TileInfo ti = tile_info<BN, true>(t, M, N, K, bt);
+      if (ti.skip) continue;
+      float sum[NC];
+#pragma unroll
+      for (int e = 0; e < NC; ++e) sum[e] = 0.0f;
+      for (int cb = 0; cb < ti.n_k; cb += X3_CHUNK) {
+        const int buf = j & 1;
+        if (!mbar_wait(acc_full(buf), (j >> 1) & 1, err, kErrWaitAccum)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t acc = tmem_base + buf * BN + (static_cast<uint32_t>(quarter * 32) << 16) + half * NC;
+#pragma unroll
+        for (int c = 0; c < NC / 16; ++c) {
+          uint32_t r[16];
+          tmem_ld_32x32b_x16(acc + c * 16, r);
+#pragma unroll
+          for (int e = 0; e < 16; ++e) sum[c * 16 + e] += __uint_as_float(r[e]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(acc_empty(buf));
+        ++j;
+      }
+      if (!ok) break;
+      const long long zoff = (ti.z / bt.c_zdiv) * bt.c_sb + ((ti.z % bt.c_zdiv) / bt.c_zgroup) * bt.c_sh;
+      store_sum<NC>(sum, stage_tile, ti.m0 + quarter * 32, ti.n0 + half * NC, C + zoff, ldc, R ? R + zoff : nullptr,
+                    ldr, M, N);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int i = *loads_consumed; i < *loads_issued; ++i)
+      if (!mbar_wait(full_bar(i % STAGES), (i / STAGES) & 1, err, kErrWaitDrain, 1000000000ull)) break;
+  }
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 2 * BN);
+  }
+  __syncthreads();
 }
 
 }  // namespace
@@ -1373,6 +1593,34 @@ int launch_pair3x(const X3Operands& ops, float* C, long long ldc, const float* R
   return cudaEventRecord(w->last_use, stream) == cudaSuccess ? 0 : kGemmLaunch;
 }
 
+template <bool A_MN, bool B_MN, int BN>
+void launch_batched3x(const X3BatchMaps& maps, float* C, long long ldc, const float* R, long long ldr, int M, int N,
+                      int K, int batch, const GemmBatch& bt, int* err, cudaStream_t stream) {
+  using TL = X3BatchTile<BN>;
+  auto kern = gemm3x_batched_kernel<A_MN, B_MN, BN>;
+  static thread_local int configured_device = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_device != dev) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TL::SMEM);
+    configured_device = dev;
+  }
+  const long long tiles = static_cast<long long>(batch) * ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  const int sms = device_sms();
+  const int grid = static_cast<int>(tiles < sms ? tiles : sms);
+  kern<<<grid, X3_THREADS, TL::SMEM, stream>>>(maps, C, ldc, R, ldr, M, N, K, err, bt, static_cast<int>(tiles));
+  ++t_launches;
+}
+
+template <int BN>
+void launch_batched3x_majors(bool a_mn, bool b_mn, const X3BatchMaps& maps, float* C, long long ldc, const float* R,
+                             int M, int N, int K, int batch, const GemmBatch& bt, int* err, cudaStream_t s) {
+  if (!a_mn && !b_mn) launch_batched3x<false, false, BN>(maps, C, ldc, R, ldc, M, N, K, batch, bt, err, s);
+  else if (!a_mn) launch_batched3x<false, true, BN>(maps, C, ldc, R, ldc, M, N, K, batch, bt, err, s);
+  else if (!b_mn) launch_batched3x<true, false, BN>(maps, C, ldc, R, ldc, M, N, K, batch, bt, err, s);
+  else launch_batched3x<true, true, BN>(maps, C, ldc, R, ldc, M, N, K, batch, bt, err, s);
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace
@@ -1577,6 +1825,48 @@ int gemm_tf32_batched(int batch, int M, int N, int K, const BatchedOperand& A, c
     launch_majors<128, true>(A.mn_major, B.mn_major, ta, tb, C, ldc, R, ldc, M, N, K, batch, bt, d_err, stream);
   else
     launch_majors<256, true>(A.mn_major, B.mn_major, ta, tb, C, ldc, R, ldc, M, N, K, batch, bt, d_err, stream);
+  return launch_status();
+}
+
+int gemm_3xtf32_batched(int batch, int M, int N, int K, const BatchedOperand& Ah, const BatchedOperand& Al,
+                        const BatchedOperand& Bh, const BatchedOperand& Bl, float* C, long long ldc,
+                        const GemmBatch& bt_in, int bn, int* d_err, cudaStream_t stream, const float* R) {
+  GemmBatch bt = bt_in;
+  bt.a_zdiv = Ah.zdiv;
+  bt.a_zgroup = Ah.zgroup;
+  bt.b_zdiv = Bh.zdiv;
+  bt.b_zgroup = Bh.zgroup;
+  if (batch < 0 || M < 0 || N < 0 || K <= 0 || !C || !Ah.ptr || !Al.ptr || !Bh.ptr || !Bl.ptr) return kGemmBadArgument;
+  if (batch == 0 || M == 0 || N == 0) return 0;
+  if (bn != 64 && bn != 128 && bn != 256) return kGemmBadArgument;
+  auto same_view = [](const BatchedOperand& a, const BatchedOperand& b) {
+    return a.mn_major == b.mn_major && a.inner == b.inner && a.heads == b.heads && a.rows == b.rows &&
+           a.batches == b.batches && a.head_stride == b.head_stride && a.row_stride == b.row_stride &&
+           a.batch_stride == b.batch_stride && a.zdiv == b.zdiv && a.zgroup == b.zgroup;
+  };
+  if (!same_view(Ah, Al) || !same_view(Bh, Bl)) return kGemmBadArgument;
+  if ((ldc & 3) || !aligned16(C) || !aligned16(Ah.ptr) || !aligned16(Al.ptr) || !aligned16(Bh.ptr) ||
+      !aligned16(Bl.ptr))
+    return kGemmMisaligned;
+  if ((bt.c_sb & 3) || (bt.c_sh & 3) || bt.a_zdiv <= 0 || bt.b_zdiv <= 0 || bt.c_zdiv <= 0 || bt.a_zgroup <= 0 ||
+      bt.b_zgroup <= 0 || bt.c_zgroup <= 0 || bt.k_off < 0 || (bt.k_off % BK))
+    return kGemmBadArgument;
+  if (R && !aligned16(R)) return kGemmMisaligned;
+  bt.skip_empty = R == C ? 1 : 0;
+  X3BatchMaps maps{};
+  auto map_a = [&](CUtensorMap* m, const BatchedOperand& o) {
+    return o.mn_major ? make_map4d(m, o, 32, BK) : make_map4d(m, o, BK, BM);
+  };
+  auto map_b = [&](CUtensorMap* m, const BatchedOperand& o) {
+    return o.mn_major ? make_map4d(m, o, 32, BK) : make_map4d(m, o, BK, bn);
+  };
+  if (map_a(&maps.ah, Ah) || map_a(&maps.al, Al) || map_b(&maps.bh, Bh) || map_b(&maps.bl, Bl)) return kGemmTensorMap;
+  if (bn == 64)
+    launch_batched3x_majors<64>(Ah.mn_major, Bh.mn_major, maps, C, ldc, R, M, N, K, batch, bt, d_err, stream);
+  else if (bn == 128)
+    launch_batched3x_majors<128>(Ah.mn_major, Bh.mn_major, maps, C, ldc, R, M, N, K, batch, bt, d_err, stream);
+  else
+    launch_batched3x_majors<256>(Ah.mn_major, Bh.mn_major, maps, C, ldc, R, M, N, K, batch, bt, d_err, stream);
   return launch_status();
 }
 

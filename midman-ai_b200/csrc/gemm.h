@@ -91,6 +91,13 @@ int gemm_tf32_batched(int batch, int M, int N, int K, const BatchedOperand& A, c
                       long long ldc, const GemmBatch& bt, int bn, int* d_err, cudaStream_t stream,
                       const float* R = nullptr);
 
+// The batched form in 3xTF32 on split operands (hi/lo views of the same shape):
+// C = Al Bh + Ah Bl + Ah Bh (+ R) in one launch, the tensor-memory accumulation
+// restarted every 64 of K and the partial sums added in f32 in registers.
+int gemm_3xtf32_batched(int batch, int M, int N, int K, const BatchedOperand& Ah, const BatchedOperand& Al,
+                        const BatchedOperand& Bh, const BatchedOperand& Bl, float* C, long long ldc,
+                        const GemmBatch& bt, int bn, int* d_err, cudaStream_t stream, const float* R = nullptr);
+
 }  // namespace mm
 
 namespace mm {
