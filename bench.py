@@ -373,7 +373,7 @@ def run_kernels(args):
         line = {"metric": res["metric"], "value": res["value"], "unit": "TFLOP/s",
                 "config": {"workload": "linear", "shapes": res["shapes"]}}
     elif args.config == "gemm-step":
-        res = gemm_step_config(torch, mm, args.steps, args.warmup, tf32)
+        res = gemm_step_config(torch, mm, args.steps, args.warmup, tf32, precision)
         line = {"metric": res["metric"], "value": res["value"], "unit": "TFLOP/s",
                 "config": {"workload": "gemm-step", **{k: v for k, v in res.items() if k not in ("metric", "value")}}}
     else:
@@ -408,9 +408,11 @@ LARGE_STEP_GEMMS = [
 ]
 
 
-def gemm_step_config(torch, mm, steps, warmup, tf32):
-    """Each distinct TF32 product of the large step once, standalone (operands < 2 GB on the device): TFLOP/s per
-    shape and the step's mix. Small enough for an ncu capture of the products' DRAM traffic."""
+def gemm_step_config(torch, mm, steps, warmup, tf32, precision=0):
+    """Each distinct product of the large step once, standalone (operands < 2 GB on the device): TFLOP/s per
+    shape and the step's mix. Small enough for an ncu capture of the products' DRAM traffic. In 3xTF32
+    (precision 1) a summed product runs as one launch per term, each after the first adding into C (the
+    kernel-level ABI's sum is TF32 only; the trainer sums the terms in one launch)."""
     g = torch.Generator(device="cuda").manual_seed(0)
     out, total_ms, total_flops = [], 0.0, 0.0
     for M, N, ks, a_mn, b_mn, per_step in LARGE_STEP_GEMMS:
@@ -420,11 +422,11 @@ def gemm_step_config(torch, mm, steps, warmup, tf32):
             b = torch.randn(*((K, N) if b_mn else (N, K)), device="cuda", generator=g)
             terms.append((a, a.shape[1], b, b.shape[1], K))
         c = torch.empty(M, N, device="cuda")
-        if len(terms) == 1:
-            a, lda, b, ldb, K = terms[0]
-
+        if len(terms) == 1 or precision:
             def fn():
-                mm.gemm(a, b, c, m=M, n=N, k=K, lda=lda, ldb=ldb, ldc=N, a_mn_major=a_mn, b_mn_major=b_mn)
+                for g, (a, lda, b, ldb, K) in enumerate(terms):
+                    mm.gemm(a, b, c, m=M, n=N, k=K, lda=lda, ldb=ldb, ldc=N, a_mn_major=a_mn, b_mn_major=b_mn,
+                            r=c if g else None, ldr=N if g else 0, precision=precision)
         else:
             def fn():
                 mm.gemm_sum(terms, c, m=M, n=N, ldc=N, a_mn_major=a_mn, b_mn_major=b_mn)
@@ -436,7 +438,8 @@ def gemm_step_config(torch, mm, steps, warmup, tf32):
         total_ms += per_step * ms
         total_flops += per_step * flops
         del terms, c
-    return {"metric": "TF32 GEMM TFLOP/s over the large step's products", "value": total_flops / (total_ms * 1e-3) / 1e12,
+    return {"metric": f"{'3xTF32' if precision else 'TF32'} GEMM TFLOP/s over the large step's products",
+            "value": total_flops / (total_ms * 1e-3) / 1e12,
             "unit": "TFLOP/s", "frac_of_cublas_tf32": total_flops / (total_ms * 1e-3) / 1e12 / tf32, "shapes": out,
             "step_gemm_ms_serialized": total_ms}
 
