@@ -64,20 +64,65 @@ __global__ void softmax_rows_kernel(float* __restrict__ S, long long ldS, int T,
   if (lane == 0) lse[r] = m + logf(s);
 }
 
-// One warp per score row of dP: dS = P * (dP - delta) * scale for j <= i, zeros
-// for i < j < row_end (the softmax backward, ops_reduce.rs:131-142, then the
-// score scale; P is the softmax's output in the same layout).
-__global__ void softmax_grad_rows_kernel(const float* __restrict__ P, float* __restrict__ D, long long ldS, int T,
-                                         long long rows, const float* __restrict__ delta, float scale) {
+// Round to the nearest TF32 value (ties away from zero), as split_tf32 does.
+__device__ __forceinline__ float rn_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
+// The exact mode's softmax rows: as softmax_rows_kernel, but P goes out as its
+// TF32 pair (hi = rn_tf32(p), lo = rn_tf32(p - hi)) for the three-term
+// products, only up to the row's block end (the products read no further).
+__global__ void softmax_split_rows_kernel(const float* __restrict__ S, float* __restrict__ Ph, float* __restrict__ Pl,
+                                          long long ldS, int T, long long rows, float scale, float* __restrict__ lse) {
   const long long r = (blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x) / 32;
   const int lane = threadIdx.x & 31;
   if (r >= rows) return;
   const int i = static_cast<int>(r % T);
-  const float* prow = P + r * ldS;
-  float* drow = D + r * ldS;
+  const float* row = S + r * ldS;
+  float* hrow = Ph + r * ldS;
+  float* lrow = Pl + r * ldS;
+  const int n = i + 1, end = row_end(i, T);
+  float m = -INFINITY;
+  for (int j = lane; j < n; j += 32) m = fmaxf(m, row[j] * scale);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  float s = 0.0f;
+  for (int j = lane; j < n; j += 32) s += expf(row[j] * scale - m);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  const float inv = 1.0f / s;
+  for (int j = lane; j < end; j += 32) {
+    const float p = j < n ? expf(row[j] * scale - m) * inv : 0.0f;
+    const float h = rn_tf32(p);
+    hrow[j] = h;
+    lrow[j] = rn_tf32(p - h);
+  }
+  if (lse && lane == 0) lse[r] = m + logf(s);
+}
+
+// The exact mode's softmax gradient: P = Ph + Pl (within 2^-22 of the f32
+// probability), dS = P * (dP - delta) * scale for j <= i, written over (Ph, Pl)
+// as its TF32 pair, zeros for i < j < row_end.
+__global__ void softmax_grad_split_rows_kernel(float* __restrict__ Ph, float* __restrict__ Pl,
+                                               const float* __restrict__ D, long long ldS, int T, long long rows,
+                                               const float* __restrict__ delta, float scale) {
+  const long long r = (blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x) / 32;
+  const int lane = threadIdx.x & 31;
+  if (r >= rows) return;
+  const int i = static_cast<int>(r % T);
+  float* hrow = Ph + r * ldS;
+  float* lrow = Pl + r * ldS;
+  const float* drow = D + r * ldS;
   const int n = i + 1, end = row_end(i, T);
   const float dl = delta[r];
-  for (int j = lane; j < end; j += 32) drow[j] = j < n ? (prow[j] * (drow[j] - dl)) * scale : 0.0f;
+  for (int j = lane; j < end; j += 32) {
+    const float ds = j < n ? ((hrow[j] + lrow[j]) * (drow[j] - dl)) * scale : 0.0f;
+    const float h = rn_tf32(ds);
+    hrow[j] = h;
+    lrow[j] = rn_tf32(ds - h);
+  }
 }
 
 int blocks_for(long long threads) {
@@ -135,7 +180,7 @@ BatchedOperand group_scores_view(const float* p, const AttnShape& s, long long l
 }
 
 struct Ws3 {
-  float *S, *D, *Xh, *Xl, *qh, *ql, *kh, *kl, *vh, *vl, *gh, *gl, *lse, *delta;
+  float *S, *D, *Xh, *Xl, *qh, *ql, *kh, *kl, *vh, *vl, *gh, *gl, *delta;
 };
 
 long long rows_footprint(const AttnShape& s, long long ld, int heads) {
@@ -147,7 +192,7 @@ long long r4(long long n) { return (n + 63) & ~63ll; }
 // Sizes (floats) of the pieces of the workspace, in carve's order.
 struct Ws3Sizes {
   long long mat, nq, nk, nv, ng, nr;
-  long long total() const { return 4 * mat + 2 * (nq + nk + nv + ng) + 2 * nr; }
+  long long total() const { return 4 * mat + 2 * (nq + nk + nv + ng) + nr; }
 };
 
 Ws3Sizes ws3_sizes(const AttnShape& s, long long ld_dout) {
@@ -177,7 +222,6 @@ Ws3 carve(const AttnShape& s, float* ws, long long ld_dout) {
   w.vl = take(nv);
   w.gh = take(ng);
   w.gl = take(ng);
-  w.lse = take(nr);
   w.delta = take(nr);
   return w;
 }
@@ -195,14 +239,12 @@ void scores3(const AttnShape& s, const Ws3& w, int* d_err, cudaStream_t st) {
            128, false, d_err, st, "attention (3xTF32) S = QK^T");
 }
 
-void softmax_into(const AttnShape& s, float* S, float* lse, cudaStream_t st) {
+// P = softmax(S) of every score row into (Xh, Xl) as its TF32 pair (and lse).
+void softmax_split(const AttnShape& s, const Ws3& w, float* lse, cudaStream_t st) {
   const long long rows = static_cast<long long>(s.B) * s.H * s.T;
-  softmax_rows_kernel<<<blocks_for(rows * 32), 256, 0, st>>>(S, attention_scores_ld(s.T), s.T, rows, s.scale, lse);
+  softmax_split_rows_kernel<<<blocks_for(rows * 32), 256, 0, st>>>(w.S, w.Xh, w.Xl, attention_scores_ld(s.T), s.T,
+                                                                  rows, s.scale, lse);
   check("attention softmax");
-}
-
-void split_scores(const AttnShape& s, const float* X, const Ws3& w, cudaStream_t st) {
-  split_tf32(X, w.Xh, w.Xl, static_cast<long long>(s.B) * s.H * s.T * attention_scores_ld(s.T), st);
 }
 
 }  // namespace
@@ -218,9 +260,8 @@ void attention_forward_3x(const AttnShape& s, const float* q, const float* k, co
   split_tf32(k, w.kh, w.kl, rows_footprint(s, s.ldk, s.Hkv), st);
   split_tf32(v, w.vh, w.vl, rows_footprint(s, s.ldv, s.Hkv), st);
   scores3(s, w, d_err, st);
-  softmax_into(s, w.S, lse, st);
-  split_scores(s, w.S, w, st);
-  // O = P V, K = keys in chunks, each row block's K loop ending at its diagonal
+  softmax_split(s, w, lse, st);
+  // O = P V, each row block's K loop ending at its diagonal
   GemmBatch bo;
   bo.c_zdiv = s.H;
   bo.c_sb = static_cast<long long>(s.T) * s.ldo;
@@ -241,9 +282,9 @@ void attention_backward_3x(const AttnShape& s, const float* q, const float* k, c
   split_tf32(k, w.kh, w.kl, rows_footprint(s, s.ldk, s.Hkv), st);
   split_tf32(v, w.vh, w.vl, rows_footprint(s, s.ldv, s.Hkv), st);
   split_tf32(dout, w.gh, w.gl, rows_footprint(s, lddo, s.H), st);
-  // P again (the same arithmetic as the forward, so the same values)
+  // P again (the same arithmetic as the forward, so the same values), as its TF32 pair
   scores3(s, w, d_err, st);
-  softmax_into(s, w.S, w.lse, st);
+  softmax_split(s, w, nullptr, st);
   // dP = dO V^T into D
   {
     GemmBatch bd;
@@ -255,9 +296,8 @@ void attention_backward_3x(const AttnShape& s, const float* q, const float* k, c
              128, false, d_err, st, "attention (3xTF32) dP = dO V^T");
   }
   attention_delta(s, o, dout, lddo, w.delta, st);
-  // dV = P^T dO, summed over each key/value head's group; K = queries in chunks,
-  // each key row block's K loop starting at its first key
-  split_scores(s, w.S, w, st);
+  // dV = P^T dO, summed over each key/value head's group; each key row block's
+  // K loop starting at its first key
   GemmBatch bk;
   bk.c_zdiv = s.Hkv;
   bk.c_sb = static_cast<long long>(s.T) * s.ldv;
@@ -267,18 +307,18 @@ void attention_backward_3x(const AttnShape& s, const float* q, const float* k, c
     product3(BHkv, s.T, s.hd, s.T, {group_scores_view(w.Xh, s, ldS, g), group_scores_view(w.Xl, s, ldS, g)},
              {group_head_view(w.gh, true, s, lddo, g), group_head_view(w.gl, true, s, lddo, g)}, dv, s.ldv, bk,
              tile_for(s.hd), g > 0, d_err, st, "attention (3xTF32) dV = P^T dO");
-  // dS = P (dP - delta) * scale, in D
+  // dS = P (dP - delta) * scale, as its TF32 pair over P's
   const long long rows = static_cast<long long>(BH) * s.T;
-  softmax_grad_rows_kernel<<<blocks_for(rows * 32), 256, 0, st>>>(w.S, w.D, ldS, s.T, rows, w.delta, s.scale);
+  softmax_grad_split_rows_kernel<<<blocks_for(rows * 32), 256, 0, st>>>(w.Xh, w.Xl, w.D, ldS, s.T, rows, w.delta,
+                                                                       s.scale);
   check("attention softmax backward");
-  split_scores(s, w.D, w, st);
   // dK = dS^T Q, summed over the group
   bk.c_sb = static_cast<long long>(s.T) * s.ldk;
   for (int g = 0; g < G; ++g)
     product3(BHkv, s.T, s.hd, s.T, {group_scores_view(w.Xh, s, ldS, g), group_scores_view(w.Xl, s, ldS, g)},
              {group_head_view(w.qh, true, s, s.ldq, g), group_head_view(w.ql, true, s, s.ldq, g)}, dk, s.ldk, bk,
              tile_for(s.hd), g > 0, d_err, st, "attention (3xTF32) dK = dS^T Q");
-  // dQ = dS K, K = keys in chunks ending at each row block's diagonal
+  // dQ = dS K, K = keys ending at each row block's diagonal
   GemmBatch bq;
   bq.c_zdiv = s.H;
   bq.c_sb = static_cast<long long>(s.T) * s.ldq;
