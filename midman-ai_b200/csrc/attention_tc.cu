@@ -179,8 +179,11 @@ BatchedOperand group_scores_view(const float* p, const AttnShape& s, long long l
                         s.Hkv, 1};
 }
 
+// The exact mode's workspace. The hi part of q, k, v and dO is the tensor
+// itself (the tensor core reads its TF32 bits); only the lo parts are copies.
 struct Ws3 {
-  float *S, *D, *Xh, *Xl, *qh, *ql, *kh, *kl, *vh, *vl, *gh, *gl, *delta;
+  float *S, *D, *Xh, *Xl, *ql, *kl, *vl, *gl, *delta;
+  const float *qh, *kh, *vh, *gh;
 };
 
 long long rows_footprint(const AttnShape& s, long long ld, int heads) {
@@ -192,7 +195,7 @@ long long r4(long long n) { return (n + 63) & ~63ll; }
 // Sizes (floats) of the pieces of the workspace, in carve's order.
 struct Ws3Sizes {
   long long mat, nq, nk, nv, ng, nr;
-  long long total() const { return 4 * mat + 2 * (nq + nk + nv + ng) + nr; }
+  long long total() const { return 4 * mat + nq + nk + nv + ng + nr; }
 };
 
 Ws3Sizes ws3_sizes(const AttnShape& s, long long ld_dout) {
@@ -204,7 +207,8 @@ Ws3Sizes ws3_sizes(const AttnShape& s, long long ld_dout) {
                   r4(static_cast<long long>(s.B) * s.H * s.T)};
 }
 
-Ws3 carve(const AttnShape& s, float* ws, long long ld_dout) {
+Ws3 carve(const AttnShape& s, float* ws, long long ld_dout, const float* q, const float* k, const float* v,
+          const float* dout) {
   const Ws3Sizes z = ws3_sizes(s, ld_dout);
   const long long mat = z.mat, nq = z.nq, nk = z.nk, nv = z.nv, ng = z.ng, nr = z.nr;
   Ws3 w;
@@ -214,14 +218,14 @@ Ws3 carve(const AttnShape& s, float* ws, long long ld_dout) {
   w.D = take(mat);
   w.Xh = take(mat);
   w.Xl = take(mat);
-  w.qh = take(nq);
   w.ql = take(nq);
-  w.kh = take(nk);
   w.kl = take(nk);
-  w.vh = take(nv);
   w.vl = take(nv);
-  w.gh = take(ng);
   w.gl = take(ng);
+  w.qh = q;
+  w.kh = k;
+  w.vh = v;
+  w.gh = dout;
   w.delta = take(nr);
   return w;
 }
@@ -253,12 +257,12 @@ long long attention_3x_ws_floats(const AttnShape& s, long long ld_dout) { return
 
 void attention_forward_3x(const AttnShape& s, const float* q, const float* k, const float* v, float* o, float* lse,
                           float* ws, int* d_err, cudaStream_t st) {
-  const Ws3 w = carve(s, ws, s.ldo);
+  const Ws3 w = carve(s, ws, s.ldo, q, k, v, nullptr);
   const int G = s.H / s.Hkv, BH = s.B * s.H;
   const long long ldS = attention_scores_ld(s.T);
-  split_tf32(q, w.qh, w.ql, rows_footprint(s, s.ldq, s.H), st);
-  split_tf32(k, w.kh, w.kl, rows_footprint(s, s.ldk, s.Hkv), st);
-  split_tf32(v, w.vh, w.vl, rows_footprint(s, s.ldv, s.Hkv), st);
+  split_lo_tf32(q, w.ql, rows_footprint(s, s.ldq, s.H), st);
+  split_lo_tf32(k, w.kl, rows_footprint(s, s.ldk, s.Hkv), st);
+  split_lo_tf32(v, w.vl, rows_footprint(s, s.ldv, s.Hkv), st);
   scores3(s, w, d_err, st);
   softmax_split(s, w, lse, st);
   // O = P V, each row block's K loop ending at its diagonal
@@ -275,13 +279,13 @@ void attention_forward_3x(const AttnShape& s, const float* q, const float* k, co
 void attention_backward_3x(const AttnShape& s, const float* q, const float* k, const float* v, const float* o,
                            const float* dout, long long lddo, float* dq, float* dk, float* dv, float* ws, int* d_err,
                            cudaStream_t st) {
-  const Ws3 w = carve(s, ws, lddo);
+  const Ws3 w = carve(s, ws, lddo, q, k, v, dout);
   const int G = s.H / s.Hkv, BH = s.B * s.H, BHkv = s.B * s.Hkv;
   const long long ldS = attention_scores_ld(s.T);
-  split_tf32(q, w.qh, w.ql, rows_footprint(s, s.ldq, s.H), st);
-  split_tf32(k, w.kh, w.kl, rows_footprint(s, s.ldk, s.Hkv), st);
-  split_tf32(v, w.vh, w.vl, rows_footprint(s, s.ldv, s.Hkv), st);
-  split_tf32(dout, w.gh, w.gl, rows_footprint(s, lddo, s.H), st);
+  split_lo_tf32(q, w.ql, rows_footprint(s, s.ldq, s.H), st);
+  split_lo_tf32(k, w.kl, rows_footprint(s, s.ldk, s.Hkv), st);
+  split_lo_tf32(v, w.vl, rows_footprint(s, s.ldv, s.Hkv), st);
+  split_lo_tf32(dout, w.gl, rows_footprint(s, lddo, s.H), st);
   // P again (the same arithmetic as the forward, so the same values), as its TF32 pair
   scores3(s, w, d_err, st);
   softmax_split(s, w, nullptr, st);

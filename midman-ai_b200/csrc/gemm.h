@@ -103,6 +103,9 @@ int gemm_3xtf32_batched(int batch, int M, int N, int K, const BatchedOperand& Ah
 namespace mm {
 // hi = x rounded to TF32 (nearest), lo = (x - hi) rounded to TF32, for n values.
 void split_tf32(const float* x, float* hi, float* lo, long long n, cudaStream_t stream);
+// lo = (x - x with its low 13 mantissa bits cleared) rounded to TF32, for n
+// values: the tensor core reads x itself as the hi part.
+void split_lo_tf32(const float* x, float* lo, long long n, cudaStream_t stream);
 // Same contract as gemm_tf32, computed as hi*hi + hi*lo + lo*hi (3xTF32).
 // Uses the device scratch arena for the split operands.
 int gemm_3xtf32(int M, int N, int K, GemmOperand A, GemmOperand B, float* C, long long ldc,

@@ -7,6 +7,8 @@
 // |x - hi - lo| <= 2^-22 |x|, close to f32's own 2^-24, at 3x the MMA work.
 #include <cuda_runtime.h>
 
+#include <cstdint>
+
 #include "device.h"
 #include "gemm.h"
 
@@ -34,6 +36,24 @@ __global__ void split_tf32_kernel(const float* __restrict__ x, float* __restrict
   }
 }
 
+// The part of x below its TF32 value as the tensor core reads x (the 19 high
+// bits, the low 13 mantissa bits ignored), rounded to TF32 (nearest): a
+// kind::tf32 product of x itself and of this lo together see x to within
+// 2^-11 |x - trunc(x)| <= 2^-21 |x|, with no hi copy.
+__global__ void split_lo_kernel(const float* __restrict__ x, float* __restrict__ lo, long long n) {
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  const long long n4 = (reinterpret_cast<uintptr_t>(x) & 15u) == 0 && (reinterpret_cast<uintptr_t>(lo) & 15u) == 0
+                           ? n / 4
+                           : 0;
+  auto one = [](float v) { return to_tf32(v - __uint_as_float(__float_as_uint(v) & 0xffffe000u)); };
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n4; i += stride) {
+    const float4 v = reinterpret_cast<const float4*>(x)[i];
+    reinterpret_cast<float4*>(lo)[i] = make_float4(one(v.x), one(v.y), one(v.z), one(v.w));
+  }
+  for (long long i = 4 * n4 + blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n; i += stride)
+    lo[i] = one(x[i]);
+}
+
 // Elements an operand of `rows` x `cols` with leading dimension `ld` spans.
 long long footprint(long long rows, long long cols, long long ld) {
   return rows == 0 || cols == 0 ? 0 : (rows - 1) * ld + cols;
@@ -47,6 +67,15 @@ void split_tf32(const float* x, float* hi, float* lo, long long n, cudaStream_t 
   long long blocks = (n + threads - 1) / threads;
   if (blocks > 148 * 32) blocks = 148 * 32;
   split_tf32_kernel<<<static_cast<int>(blocks), threads, 0, s>>>(x, hi, lo, n);
+}
+
+void split_lo_tf32(const float* x, float* lo, long long n, cudaStream_t s) {
+  if (n <= 0) return;
+  const int threads = 256;
+  long long blocks = (n / 4 + threads - 1) / threads;
+  if (blocks < 1) blocks = 1;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  split_lo_kernel<<<static_cast<int>(blocks), threads, 0, s>>>(x, lo, n);
 }
 
 namespace {
@@ -94,7 +123,9 @@ int gemm_3xtf32_chunked(int M, int N, int K, GemmOperand A, GemmOperand B, float
 
 }  // namespace
 
-// The tensor core's f32 accumulation loses a little on every step, in the same
+// The CTA-pair path splits only lo: hi is the operand itself, whose low 13
+// mantissa bits the tensor core does not read (split_lo_kernel). The tensor
+// core's f32 accumulation loses a little on every step, in the same
 // direction, so its error grows linearly with the number of products summed in
 // one accumulator (measured against float64: 4.8e-6 relative at K = 2048,
 // 1.9e-5 at K = 8192 in one accumulation, where f32 on the CUDA cores stays at
@@ -121,23 +152,25 @@ int gemm_3xtf32_sum(int M, int N, const GemmSegment* segs, int nseg, float* C, l
   }
   if (n_live == 0 || M == 0 || N == 0) return gemm_tf32_sum(M, N, segs, nseg, C, ldc, R, ldr, d_err, stream);
   if (same && gemm_3xtf32_pair_suits(M, N, n_k)) {
+    // hi: the operands themselves (the tensor core reads their TF32 bits);
+    // lo: what those bits leave out, rounded to TF32 (split_lo_tf32)
     long long total = 0, na[3], nb[3];
     for (int g = 0; g < n_live; ++g) {
       const GemmSegment& s = live[g];
       if (!s.a.ptr || !s.b.ptr) return kGemmBadArgument;
-      na[g] = round4(s.a.mn_major ? footprint(s.K, M, s.a.ld) : footprint(M, s.K, s.a.ld));
-      nb[g] = round4(s.b.mn_major ? footprint(s.K, N, s.b.ld) : footprint(N, s.K, s.b.ld));
-      total += 2 * (na[g] + nb[g]);
+      na[g] = s.a.mn_major ? footprint(s.K, M, s.a.ld) : footprint(M, s.K, s.a.ld);
+      nb[g] = s.b.mn_major ? footprint(s.K, N, s.b.ld) : footprint(N, s.K, s.b.ld);
+      total += round4(na[g]) + round4(nb[g]);
     }
     float* ws = static_cast<float*>(device_scratch(static_cast<size_t>(total) * sizeof(float), stream));
     GemmSegment hi[3], lo[3];
     for (int g = 0; g < n_live; ++g) {
       const GemmSegment& s = live[g];
-      float *ah = ws, *al = ws + na[g], *bh = ws + 2 * na[g], *bl = ws + 2 * na[g] + nb[g];
-      ws += 2 * (na[g] + nb[g]);
-      split_tf32(s.a.ptr, ah, al, na[g], stream);
-      split_tf32(s.b.ptr, bh, bl, nb[g], stream);
-      hi[g] = {{ah, s.a.ld, s.a.mn_major}, {bh, s.b.ld, s.b.mn_major}, s.K};
+      float *al = ws, *bl = ws + round4(na[g]);
+      ws += round4(na[g]) + round4(nb[g]);
+      split_lo_tf32(s.a.ptr, al, na[g], stream);
+      split_lo_tf32(s.b.ptr, bl, nb[g], stream);
+      hi[g] = s;
       lo[g] = {{al, s.a.ld, s.a.mn_major}, {bl, s.b.ld, s.b.mn_major}, s.K};
     }
     return gemm_3xtf32_pair_sum(M, N, hi, lo, n_live, C, ldc, R, ldr, d_err, stream);
