@@ -110,10 +110,34 @@ void split_lo_tf32(const float* x, float* lo, long long n, cudaStream_t stream);
 // Uses the device scratch arena for the split operands.
 int gemm_3xtf32(int M, int N, int K, GemmOperand A, GemmOperand B, float* C, long long ldc,
                 const float* R, long long ldr, int* d_err, cudaStream_t stream);
+// Lo copies of 3xTF32 operands kept between products on one stream, so that an
+// operand used by consecutive products (a layer's input for its q, k and v
+// projections; dY for dX and dW) is copied once. Entries hold the operand's
+// address and extent, not its contents: a caller passes keep = true only when
+// no kernel has written any operand of the products since the last call
+// without it, which clears the cache. Operands above kMaxFloats are not kept.
+struct X3LoCache {
+  static constexpr int kSlots = 8;
+  static constexpr long long kMaxFloats = 128ll << 20;
+  struct Slot {
+    const float* src = nullptr;
+    long long n = 0, cap = 0;
+    float* lo = nullptr;
+    uint64_t stamp = 0;
+  };
+  Slot slot[kSlots];
+  uint64_t clock = 0;
+  X3LoCache() = default;
+  X3LoCache(const X3LoCache&) = delete;
+  X3LoCache& operator=(const X3LoCache&) = delete;
+  ~X3LoCache();
+};
+
 // Same contract as gemm_tf32_sum in 3xTF32: one launch for up to three segments
-// with the same majors when the shape runs on CTA pairs.
+// with the same majors when the shape runs on CTA pairs (the lo copies taken
+// from, and kept in, `cache` when one is given).
 int gemm_3xtf32_sum(int M, int N, const GemmSegment* segs, int nseg, float* C, long long ldc, const float* R,
-                    long long ldr, int* d_err, cudaStream_t stream);
+                    long long ldr, int* d_err, cudaStream_t stream, X3LoCache* cache = nullptr, bool keep = false);
 // The 3xTF32 CTA-pair kernel on split operands: hi[g] = (Ah, Bh, K), lo[g] =
 // (Al, Bl, K) with the leading dimensions and majors of hi[g]; 1 to 3 segments
 // with the same majors. C = sum_g (Al Bh + Ah Bl + Ah Bh) (+ R).

@@ -132,8 +132,49 @@ int gemm_3xtf32_chunked(int M, int N, int K, GemmOperand A, GemmOperand B, float
 // 0.8-1.6e-6). Both paths therefore sum short accumulations in f32 with
 // round-to-nearest: the CTA-pair kernel every 64 of K (24 UMMAs) in registers,
 // the chunked path every kChunkK of K through C.
+X3LoCache::~X3LoCache() {
+  for (Slot& s : slot)
+    if (s.lo) cudaFree(s.lo);
+}
+
+namespace {
+
+// The lo copy of `src` (n floats) from the cache, made when the cache does not
+// hold it. Slots of this call (stamp) are never taken for another operand of
+// it; otherwise the least recently used slot is, its buffer regrown in stream
+// order when too small. Null when an allocation fails.
+float* cached_lo(X3LoCache& c, const float* src, long long n, uint64_t stamp, cudaStream_t stream) {
+  for (X3LoCache::Slot& s : c.slot)
+    if (s.src == src && s.n == n) {
+      s.stamp = stamp;
+      return s.lo;
+    }
+  X3LoCache::Slot* v = nullptr;
+  for (X3LoCache::Slot& s : c.slot)
+    if (s.stamp != stamp && (!v || s.stamp < v->stamp)) v = &s;
+  if (!v) return nullptr;
+  if (v->cap < n) {
+    if (v->lo && cudaFreeAsync(v->lo, stream) != cudaSuccess) return nullptr;
+    v->lo = nullptr;
+    v->cap = 0;
+    void* p = nullptr;
+    if (cudaMallocAsync(&p, static_cast<size_t>(round4(n)) * sizeof(float), stream) != cudaSuccess) return nullptr;
+    v->lo = static_cast<float*>(p);
+    v->cap = round4(n);
+  }
+  v->src = src;
+  v->n = n;
+  v->stamp = stamp;
+  split_lo_tf32(src, v->lo, n, stream);
+  return v->lo;
+}
+
+}  // namespace
+
 int gemm_3xtf32_sum(int M, int N, const GemmSegment* segs, int nseg, float* C, long long ldc, const float* R,
-                    long long ldr, int* d_err, cudaStream_t stream) {
+                    long long ldr, int* d_err, cudaStream_t stream, X3LoCache* cache, bool keep) {
+  if (cache && !keep)
+    for (X3LoCache::Slot& s : cache->slot) s.src = nullptr;
   if (nseg < 1 || !segs) return kGemmBadArgument;
   GemmSegment live[3];
   int n_live = 0, n_k = 0;
@@ -153,25 +194,42 @@ int gemm_3xtf32_sum(int M, int N, const GemmSegment* segs, int nseg, float* C, l
   if (n_live == 0 || M == 0 || N == 0) return gemm_tf32_sum(M, N, segs, nseg, C, ldc, R, ldr, d_err, stream);
   if (same && gemm_3xtf32_pair_suits(M, N, n_k)) {
     // hi: the operands themselves (the tensor core reads their TF32 bits);
-    // lo: what those bits leave out, rounded to TF32 (split_lo_tf32)
-    long long total = 0, na[3], nb[3];
+    // lo: what those bits leave out, rounded to TF32 (split_lo_tf32), from the
+    // cache when one is given, else in the scratch arena
+    const float* src[6];
+    long long n[6], total = 0;
+    bool kept[6];
     for (int g = 0; g < n_live; ++g) {
       const GemmSegment& s = live[g];
       if (!s.a.ptr || !s.b.ptr) return kGemmBadArgument;
-      na[g] = s.a.mn_major ? footprint(s.K, M, s.a.ld) : footprint(M, s.K, s.a.ld);
-      nb[g] = s.b.mn_major ? footprint(s.K, N, s.b.ld) : footprint(N, s.K, s.b.ld);
-      total += round4(na[g]) + round4(nb[g]);
+      src[2 * g] = s.a.ptr;
+      src[2 * g + 1] = s.b.ptr;
+      n[2 * g] = s.a.mn_major ? footprint(s.K, M, s.a.ld) : footprint(M, s.K, s.a.ld);
+      n[2 * g + 1] = s.b.mn_major ? footprint(s.K, N, s.b.ld) : footprint(N, s.K, s.b.ld);
     }
-    float* ws = static_cast<float*>(device_scratch(static_cast<size_t>(total) * sizeof(float), stream));
+    for (int o = 0; o < 2 * n_live; ++o) {
+      kept[o] = cache && n[o] <= X3LoCache::kMaxFloats;
+      if (!kept[o]) total += round4(n[o]);
+    }
+    float* ws = total ? static_cast<float*>(device_scratch(static_cast<size_t>(total) * sizeof(float), stream))
+                      : nullptr;
+    const uint64_t stamp = cache ? ++cache->clock : 0;
+    float* lo_of[6];
+    for (int o = 0; o < 2 * n_live; ++o) {
+      if (kept[o]) {
+        lo_of[o] = cached_lo(*cache, src[o], n[o], stamp, stream);
+        if (!lo_of[o]) return kGemmLaunch;
+      } else {
+        lo_of[o] = ws;
+        ws += round4(n[o]);
+        split_lo_tf32(src[o], lo_of[o], n[o], stream);
+      }
+    }
     GemmSegment hi[3], lo[3];
     for (int g = 0; g < n_live; ++g) {
       const GemmSegment& s = live[g];
-      float *al = ws, *bl = ws + round4(na[g]);
-      ws += round4(na[g]) + round4(nb[g]);
-      split_lo_tf32(s.a.ptr, al, na[g], stream);
-      split_lo_tf32(s.b.ptr, bl, nb[g], stream);
       hi[g] = s;
-      lo[g] = {{al, s.a.ld, s.a.mn_major}, {bl, s.b.ld, s.b.mn_major}, s.K};
+      lo[g] = {{lo_of[2 * g], s.a.ld, s.a.mn_major}, {lo_of[2 * g + 1], s.b.ld, s.b.mn_major}, s.K};
     }
     return gemm_3xtf32_pair_sum(M, N, hi, lo, n_live, C, ldc, R, ldr, d_err, stream);
   }

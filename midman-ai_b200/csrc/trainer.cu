@@ -458,15 +458,15 @@ void Trainer::prof_collect() {
 }
 
 void Trainer::gemm(int M, int N, int K, const float* A, long long lda, bool a_mn, const float* B, long long ldb,
-                   bool b_mn, float* C, long long ldc, const float* R, long long ldr, cudaStream_t st) {
+                   bool b_mn, float* C, long long ldc, const float* R, long long ldr, cudaStream_t st, bool keep) {
   const GemmSegment seg{{A, lda, a_mn}, {B, ldb, b_mn}, K};
-  gemm_sum(M, N, &seg, 1, C, ldc, R, ldr, st);
+  gemm_sum(M, N, &seg, 1, C, ldc, R, ldr, st, keep);
 }
 
 // C = sum of the segments' products (+ R): one launch when the shape runs on CTA
 // pairs (gemm_tf32_sum, or gemm_3xtf32_sum after the hi/lo splits).
 void Trainer::gemm_sum(int M, int N, const GemmSegment* segs, int nseg, float* C, long long ldc, const float* R,
-                       long long ldr, cudaStream_t st) {
+                       long long ldr, cudaStream_t st, bool keep) {
   if (!st) st = stream_;
   const int slot = st == stream_ ? prof_begin() : -1;
   DeviceContext& ctx = device_context();
@@ -475,7 +475,7 @@ void Trainer::gemm_sum(int M, int N, const GemmSegment* segs, int nseg, float* C
   if (precision_ == kPrecisionTF32) {
     rc = gemm_tf32_sum(M, N, segs, nseg, C, ldc, R, ldr, ctx.d_err, st);
   } else {
-    rc = gemm_3xtf32_sum(M, N, segs, nseg, C, ldc, R, ldr, ctx.d_err, st);
+    rc = gemm_3xtf32_sum(M, N, segs, nseg, C, ldc, R, ldr, ctx.d_err, st, &lo_cache_, keep);
     launches_ += 2 * nseg;  // the hi/lo splits of A and B
   }
   if (rc) throw std::runtime_error(std::string("GEMM: ") + gemm_status_string(rc));

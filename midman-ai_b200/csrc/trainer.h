@@ -115,11 +115,12 @@ class Trainer {
   StepOut finish_collect(bool update);
   void finish_launch(float lr, const AdamHyper& h, bool update);
   void build_embedding_csr(const int32_t* inputs, int N, int slot);
-  // GEMMs on `st` (the trainer's stream when null)
+  // GEMMs on `st` (the trainer's stream when null). keep (3xTF32): no kernel has
+  // written any operand since the previous product, whose lo copies may be reused.
   void gemm(int M, int N, int K, const float* A, long long lda, bool a_mn, const float* B, long long ldb, bool b_mn,
-            float* C, long long ldc, const float* R, long long ldr, cudaStream_t st = nullptr);
+            float* C, long long ldc, const float* R, long long ldr, cudaStream_t st = nullptr, bool keep = false);
   void gemm_sum(int M, int N, const GemmSegment* segs, int nseg, float* C, long long ldc, const float* R,
-                long long ldr, cudaStream_t st = nullptr);
+                long long ldr, cudaStream_t st = nullptr, bool keep = false);
   StepOut finish_step(float lr, const AdamHyper& h, bool update);
 
  public:
@@ -202,6 +203,7 @@ class Trainer {
   bool attn_tc_ = false;
   bool attn_3x_ = false;       // 3xTF32 attention on the tensor cores (score buffers in attn3_ws_)
   float* attn3_ws_ = nullptr;
+  X3LoCache lo_cache_;  // 3xTF32 lo copies shared by consecutive products
   // The backward's side stream (weight-gradient products, the attention
   // backward's dQ kernel) and its events.
   cudaStream_t side_stream_ = nullptr;

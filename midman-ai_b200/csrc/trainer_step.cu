@@ -65,9 +65,9 @@ void Trainer::forward(int B, int T, bool train) {
     rmsnorm_forward(a.x, P_ + bo.attn_norm, N, D, eps, a.xn1, a.rstd1, stream_);
     to_side();
     gemm(N, KV, D, a.xn1, D, false, P_ + bo.k, KV, true, a.k, KV, nullptr, 0, ws);
-    gemm(N, KV, D, a.xn1, D, false, P_ + bo.v, KV, true, a.v, KV, nullptr, 0, ws);
+    gemm(N, KV, D, a.xn1, D, false, P_ + bo.v, KV, true, a.v, KV, nullptr, 0, ws, true);  // xn1 again
     rope(a.k, N, T, Hkv, hd, KV, d_cos_, d_sin_, false, ws);
-    gemm(N, D, D, a.xn1, D, false, P_ + bo.q, D, true, a.q, D, nullptr, 0);
+    gemm(N, D, D, a.xn1, D, false, P_ + bo.q, D, true, a.q, D, nullptr, 0, nullptr, true);
     rope(a.q, N, T, H, hd, D, d_cos_, d_sin_, false, stream_);
     from_side();
     const double attn_flops = 2.0 * B * H * static_cast<double>(T) * (T + 1) * hd;  // QK^T and PV, causal half
@@ -84,7 +84,7 @@ void Trainer::forward(int B, int T, bool train) {
     rmsnorm_forward(a.h, P_ + bo.mlp_norm, N, D, eps, a.xn2, a.rstd2, stream_);
     to_side();
     gemm(N, F, D, a.xn2, D, false, P_ + bo.up, F, true, a.u, F, nullptr, 0, ws);
-    gemm(N, F, D, a.xn2, D, false, P_ + bo.gate, F, true, a.g, F, nullptr, 0);
+    gemm(N, F, D, a.xn2, D, false, P_ + bo.gate, F, true, a.g, F, nullptr, 0, nullptr, true);  // xn2 again
     from_side();
     swiglu_forward(a.g, a.u, a.act, static_cast<long long>(N) * F, stream_);
     gemm(N, D, F, a.act, F, false, P_ + bo.down, D, true, next_x, D, a.h, D);
@@ -151,22 +151,22 @@ void Trainer::backward(int B, int T) {
     to_side();  // dx of this layer is ready
     gemm(F, D, N, a.act, F, true, dx, D, true, G_ + bo.down, D, nullptr, 0, ws);
     side_mark(1);  // dx read
-    gemm(N, F, D, dx, D, false, P_ + bo.down, D, false, dact_, F, nullptr, 0);
+    gemm(N, F, D, dx, D, false, P_ + bo.down, D, false, dact_, F, nullptr, 0, nullptr, true);  // dx again
     swiglu_backward(a.g, a.u, dact_, static_cast<long long>(N) * F, stream_);  // g <- dg, u <- du
     to_side();
     gemm(D, F, N, a.xn2, D, true, a.g, F, true, G_ + bo.gate, F, nullptr, 0, ws);
-    gemm(D, F, N, a.xn2, D, true, a.u, F, true, G_ + bo.up, F, nullptr, 0, ws);
+    gemm(D, F, N, a.xn2, D, true, a.u, F, true, G_ + bo.up, F, nullptr, 0, ws, true);
     {  // dxn = dg Wg^T + du Wu^T, one accumulator
       const GemmSegment segs[2] = {{{a.g, F, false}, {P_ + bo.gate, F, false}, F},
                                    {{a.u, F, false}, {P_ + bo.up, F, false}, F}};
-      gemm_sum(N, D, segs, 2, dxn_, D, nullptr, 0);
+      gemm_sum(N, D, segs, 2, dxn_, D, nullptr, 0, nullptr, true);  // dg, du again
     }
     if (l + 1 < L) main_waits(2);  // the layer above's products have read dh, dq, dk, dv
     rmsnorm_backward(a.h, P_ + bo.mlp_norm, a.rstd2, dxn_, N, D, dh, dx, G_ + bo.mlp_norm, norm_ws_, stream_);
     // h = x + o Wo
     to_side();
     gemm(D, D, N, a.o, D, true, dh, D, true, G_ + bo.o, D, nullptr, 0, ws);
-    gemm(N, D, D, dh, D, false, P_ + bo.o, D, false, do_, D, nullptr, 0);
+    gemm(N, D, D, dh, D, false, P_ + bo.o, D, false, do_, D, nullptr, 0, nullptr, true);  // dh again
     int slot = prof_begin();
     if (attn_tc_) {
       const BwdSide side{side_stream_, attn_side_ready_, attn_side_done_};
@@ -184,14 +184,14 @@ void Trainer::backward(int B, int T) {
     rope(dk_, N, T, Hkv, hd, KV, d_cos_, d_sin_, true, stream_);
     to_side();
     gemm(D, D, N, a.xn1, D, true, dq_, D, true, G_ + bo.q, D, nullptr, 0, ws);
-    gemm(D, KV, N, a.xn1, D, true, dk_, KV, true, G_ + bo.k, KV, nullptr, 0, ws);
-    gemm(D, KV, N, a.xn1, D, true, dv_, KV, true, G_ + bo.v, KV, nullptr, 0, ws);
+    gemm(D, KV, N, a.xn1, D, true, dk_, KV, true, G_ + bo.k, KV, nullptr, 0, ws, true);
+    gemm(D, KV, N, a.xn1, D, true, dv_, KV, true, G_ + bo.v, KV, nullptr, 0, ws, true);
     side_mark(2);  // this layer's weight gradients are done
     {  // dxn = dq Wq^T + dk Wk^T + dv Wv^T, one accumulator
       const GemmSegment segs[3] = {{{dq_, D, false}, {P_ + bo.q, D, false}, D},
                                    {{dk_, KV, false}, {P_ + bo.k, KV, false}, KV},
                                    {{dv_, KV, false}, {P_ + bo.v, KV, false}, KV}};
-      gemm_sum(N, D, segs, 3, dxn_, D, nullptr, 0);
+      gemm_sum(N, D, segs, 3, dxn_, D, nullptr, 0, nullptr, true);  // dq, dk, dv again
     }
     main_waits(1);  // the down projection's product has read dx
     rmsnorm_backward(a.x, P_ + bo.attn_norm, a.rstd1, dxn_, N, D, dx, dh, G_ + bo.attn_norm, norm_ws_, stream_);
