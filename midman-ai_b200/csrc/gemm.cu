@@ -232,8 +232,10 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int lane = threadIdx.x % 32;
 
   if (threadIdx.x == 0) {
-    tma_prefetch_desc(&tmA);
-    tma_prefetch_desc(&tmB);
+    if (K > 0) {  // with K = 0 the maps are not built (the tiles are R or zeros)
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmB);
+    }
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(full_bar(s), 1);
       mbar_init(empty_bar(s), 1);

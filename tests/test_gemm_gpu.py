@@ -90,6 +90,28 @@ def test_gemm_adds_the_residual_in_place(mm, precision, shape):
     assert rel_l2(c, want) < (TF32_TOL if precision == 0 else X3_TOL * max(1.0, (k / 1000) ** 0.5))
 
 
+@pytest.mark.parametrize("precision", [0, 1])
+def test_gemm_empty_sizes(mm, precision):
+    """M or N = 0 writes nothing; K = 0 makes C = R, or zeros without R (an empty sum)."""
+    a = torch.randn(64, 32, device="cuda")
+    b = torch.randn(48, 32, device="cuda")
+    c = torch.full((64, 48), float("nan"), device="cuda")
+    for m, n in ((0, 48), (64, 0)):
+        mm.gemm(a, b, c, m=m, n=n, k=32, lda=32, ldb=32, ldc=48, a_mn_major=False, b_mn_major=False,
+                precision=precision)
+    mm.device_status()
+    assert torch.isnan(c).all()
+    r = torch.randn(64, 48, device="cuda")
+    mm.gemm(a, b, c, m=64, n=48, k=0, lda=32, ldb=32, ldc=48, a_mn_major=False, b_mn_major=False, r=r, ldr=48,
+            precision=precision)
+    mm.device_status()
+    assert torch.equal(c, r)
+    mm.gemm(a, b, c, m=64, n=48, k=0, lda=32, ldb=32, ldc=48, a_mn_major=False, b_mn_major=False,
+            precision=precision)
+    mm.device_status()
+    assert not c.any()
+
+
 def test_gemm_rejects_misaligned_leading_dimensions(mm):
     a = torch.randn(16, 10, device="cuda")
     b = torch.randn(16, 12, device="cuda")
