@@ -39,16 +39,18 @@ long long attention_scores_ld(int T);
 void attention_forward_tc(const AttnShape& s, const float* q, const float* k, const float* v, float* o, float* lse,
                           float* S, int* d_err, cudaStream_t stream);
 // The exact mode on the tensor cores (attention_tc.cu): every product as three
-// TF32 terms of hi/lo operand pairs, contractions over T in chunks of 256 summed
-// in f32, the score matrices in `ws` (attention_3x_ws_floats floats: four
-// B*H*T*round4(T) matrices, hi/lo copies of q, k, v and dout, and two B*H*T
-// vectors). head_dim 32, 64 or 128 (attention_tc_supported).
+// TF32 terms of hi/lo operand pairs (the operand itself as hi), the
+// tensor-memory accumulations restarted every 64 of K and summed in f32, the
+// score matrices in `ws` (attention_3x_ws_floats floats: four B*H*T*round4(T)
+// matrices, lo copies of q, k, v and dout, and one B*H*T vector). head_dim 32,
+// 64 or 128 (attention_tc_supported).
 long long attention_3x_ws_floats(const AttnShape& s, long long ld_dout);
 void attention_forward_3x(const AttnShape& s, const float* q, const float* k, const float* v, float* o, float* lse,
                           float* ws, int* d_err, cudaStream_t stream);
+// The backward takes the forward's lse (P = exp(S * scale - lse)).
 void attention_backward_3x(const AttnShape& s, const float* q, const float* k, const float* v, const float* o,
-                           const float* dout, long long lddo, float* dq, float* dk, float* dv, float* ws, int* d_err,
-                           cudaStream_t stream);
+                           const float* lse, const float* dout, long long lddo, float* dq, float* dk, float* dv,
+                           float* ws, int* d_err, cudaStream_t stream);
 // Fused tensor-core forward (flash_tc.cu): scores stay on chip, no scratch.
 // head_dim 32, 64 or 128; row strides multiples of 4; 16-byte aligned pointers.
 bool attention_flash_supported(const AttnShape& s);

@@ -102,29 +102,6 @@ __global__ void softmax_split_rows_kernel(const float* __restrict__ S, float* __
   if (lse && lane == 0) lse[r] = m + logf(s);
 }
 
-// The exact mode's softmax gradient: P = Ph + Pl (within 2^-22 of the f32
-// probability), dS = P * (dP - delta) * scale for j <= i, written over (Ph, Pl)
-// as its TF32 pair, zeros for i < j < row_end.
-__global__ void softmax_grad_split_rows_kernel(float* __restrict__ Ph, float* __restrict__ Pl,
-                                               const float* __restrict__ D, long long ldS, int T, long long rows,
-                                               const float* __restrict__ delta, float scale) {
-  const long long r = (blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x) / 32;
-  const int lane = threadIdx.x & 31;
-  if (r >= rows) return;
-  const int i = static_cast<int>(r % T);
-  float* hrow = Ph + r * ldS;
-  float* lrow = Pl + r * ldS;
-  const float* drow = D + r * ldS;
-  const int n = i + 1, end = row_end(i, T);
-  const float dl = delta[r];
-  for (int j = lane; j < end; j += 32) {
-    const float ds = j < n ? ((hrow[j] + lrow[j]) * (drow[j] - dl)) * scale : 0.0f;
-    const float h = rn_tf32(ds);
-    hrow[j] = h;
-    lrow[j] = rn_tf32(ds - h);
-  }
-}
-
 int blocks_for(long long threads) {
   long long b = (threads + 255) / 256;
   return static_cast<int>(b < 1 ? 1 : b);
@@ -277,8 +254,8 @@ void attention_forward_3x(const AttnShape& s, const float* q, const float* k, co
 }
 
 void attention_backward_3x(const AttnShape& s, const float* q, const float* k, const float* v, const float* o,
-                           const float* dout, long long lddo, float* dq, float* dk, float* dv, float* ws, int* d_err,
-                           cudaStream_t st) {
+                           const float* lse, const float* dout, long long lddo, float* dq, float* dk, float* dv,
+                           float* ws, int* d_err, cudaStream_t st) {
   const Ws3 w = carve(s, ws, lddo, q, k, v, dout);
   const int G = s.H / s.Hkv, BH = s.B * s.H, BHkv = s.B * s.Hkv;
   const long long ldS = attention_scores_ld(s.T);
@@ -286,20 +263,22 @@ void attention_backward_3x(const AttnShape& s, const float* q, const float* k, c
   split_lo_tf32(k, w.kl, rows_footprint(s, s.ldk, s.Hkv), st);
   split_lo_tf32(v, w.vl, rows_footprint(s, s.ldv, s.Hkv), st);
   split_lo_tf32(dout, w.gl, rows_footprint(s, lddo, s.H), st);
-  // P again (the same arithmetic as the forward, so the same values), as its TF32 pair
-  scores3(s, w, d_err, st);
-  softmax_split(s, w, nullptr, st);
-  // dP = dO V^T into D
-  {
-    GemmBatch bd;
-    bd.c_zdiv = BH;
-    bd.c_sh = static_cast<long long>(s.T) * ldS;
-    bd.causal = kCausalSkipUpper;
-    product3(BH, s.T, s.T, s.hd, {heads_view(w.gh, false, s, lddo, s.H, 1), heads_view(w.gl, false, s, lddo, s.H, 1)},
-             {heads_view(w.vh, false, s, s.ldv, s.Hkv, G), heads_view(w.vl, false, s, s.ldv, s.Hkv, G)}, w.D, ldS, bd,
-             128, false, d_err, st, "attention (3xTF32) dP = dO V^T");
-  }
   attention_delta(s, o, dout, lddo, w.delta, st);
+  // One launch for the score tiles: S = QK^T and dP = dO V^T, then
+  // P = exp(S * scale - lse) (the forward's lse) and dS = P (dP - delta) * scale,
+  // as TF32 pairs: P into (Xh, Xl), dS into (S, D)
+  {
+    GemmBatch bs;
+    bs.c_zdiv = BH;
+    bs.c_sh = static_cast<long long>(s.T) * ldS;
+    check_gemm(attention_scores_grad_3x(
+                   BH, s.T, s.hd, heads_view(w.qh, false, s, s.ldq, s.H, 1), heads_view(w.ql, false, s, s.ldq, s.H, 1),
+                   heads_view(w.kh, false, s, s.ldk, s.Hkv, G), heads_view(w.kl, false, s, s.ldk, s.Hkv, G),
+                   heads_view(w.gh, false, s, lddo, s.H, 1), heads_view(w.gl, false, s, lddo, s.H, 1),
+                   heads_view(w.vh, false, s, s.ldv, s.Hkv, G), heads_view(w.vl, false, s, s.ldv, s.Hkv, G), w.Xh,
+                   w.Xl, w.S, w.D, ldS, bs, lse, w.delta, s.scale, d_err, st),
+               "attention (3xTF32) P, dS");
+  }
   // dV = P^T dO, summed over each key/value head's group; each key row block's
   // K loop starting at its first key
   GemmBatch bk;
@@ -311,15 +290,10 @@ void attention_backward_3x(const AttnShape& s, const float* q, const float* k, c
     product3(BHkv, s.T, s.hd, s.T, {group_scores_view(w.Xh, s, ldS, g), group_scores_view(w.Xl, s, ldS, g)},
              {group_head_view(w.gh, true, s, lddo, g), group_head_view(w.gl, true, s, lddo, g)}, dv, s.ldv, bk,
              tile_for(s.hd), g > 0, d_err, st, "attention (3xTF32) dV = P^T dO");
-  // dS = P (dP - delta) * scale, as its TF32 pair over P's
-  const long long rows = static_cast<long long>(BH) * s.T;
-  softmax_grad_split_rows_kernel<<<blocks_for(rows * 32), 256, 0, st>>>(w.Xh, w.Xl, w.D, ldS, s.T, rows, w.delta,
-                                                                       s.scale);
-  check("attention softmax backward");
   // dK = dS^T Q, summed over the group
   bk.c_sb = static_cast<long long>(s.T) * s.ldk;
   for (int g = 0; g < G; ++g)
-    product3(BHkv, s.T, s.hd, s.T, {group_scores_view(w.Xh, s, ldS, g), group_scores_view(w.Xl, s, ldS, g)},
+    product3(BHkv, s.T, s.hd, s.T, {group_scores_view(w.S, s, ldS, g), group_scores_view(w.D, s, ldS, g)},
              {group_head_view(w.qh, true, s, s.ldq, g), group_head_view(w.ql, true, s, s.ldq, g)}, dk, s.ldk, bk,
              tile_for(s.hd), g > 0, d_err, st, "attention (3xTF32) dK = dS^T Q");
   // dQ = dS K, K = keys ending at each row block's diagonal
@@ -328,7 +302,7 @@ void attention_backward_3x(const AttnShape& s, const float* q, const float* k, c
   bq.c_sb = static_cast<long long>(s.T) * s.ldq;
   bq.c_sh = s.hd;
   bq.causal = kCausalKBelow;
-  product3(BH, s.T, s.hd, s.T, {scores_view(w.Xh, false, s, ldS), scores_view(w.Xl, false, s, ldS)},
+  product3(BH, s.T, s.hd, s.T, {scores_view(w.S, false, s, ldS), scores_view(w.D, false, s, ldS)},
            {heads_view(w.kh, true, s, s.ldk, s.Hkv, G), heads_view(w.kl, true, s, s.ldk, s.Hkv, G)}, dq, s.ldq, bq,
            tile_for(s.hd), false, d_err, st, "attention (3xTF32) dQ = dS K");
 }

@@ -182,7 +182,7 @@ int32_t mm_gpu_attention_backward(int32_t batch, int32_t seq, int32_t n_heads, i
     } else if (precision == MM_GPU_3XTF32 && mm::attention_tc_supported(s)) {
       float* ws = static_cast<float*>(mm::device_scratch(
           static_cast<size_t>(mm::attention_3x_ws_floats(s, ldq)) * sizeof(float), st));
-      mm::attention_backward_3x(s, q, k, v, o, dout, ldq, dq, dk, dv, ws, mm::device_context().d_err, st);
+      mm::attention_backward_3x(s, q, k, v, o, lse, dout, ldq, dq, dk, dv, ws, mm::device_context().d_err, st);
     } else {
       float* delta = static_cast<float*>(mm::device_scratch(rows * sizeof(float), st));
       mm::attention_backward(s, q, k, v, o, lse, dout, ldq, dq, dk, dv, delta, st);

@@ -1306,6 +1306,271 @@ __global__ void __launch_bounds__(X3_THREADS, 1)
   __syncthreads();
 }
 
+__device__ __forceinline__ float rn_tf32_dev(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
+// Writes a warp's 32 rows (lane = row) x NC values through its staging tile as
+// TF32 pairs, hi = rn(v) to H and lo = rn(v - hi) to L (8 lanes per 32-column
+// row segment, as store_sum).
+template <int NC>
+__device__ __forceinline__ void store_pair(const float (&val)[NC], float4* stage_tile, int wrow0, int n0, float* H,
+                                           float* L, long long ld, int M, int N) {
+  const int lane = threadIdx.x % 32, sub = lane & 7, rsub = lane >> 3;
+#pragma unroll
+  for (int c = 0; c < NC / 32; ++c) {
+#pragma unroll
+    for (int g = 0; g < 8; ++g)
+      stage_tile[lane * 8 + (g ^ (lane & 7))] =
+          make_float4(val[c * 32 + 4 * g], val[c * 32 + 4 * g + 1], val[c * 32 + 4 * g + 2], val[c * 32 + 4 * g + 3]);
+    __syncwarp();
+    const int col = n0 + c * 32 + 4 * sub;
+#pragma unroll 2
+    for (int it = 0; it < 8; ++it) {
+      const int rr = it * 4 + rsub, row = wrow0 + rr;
+      const float4 v = stage_tile[rr * 8 + (sub ^ (rr & 7))];
+      if (row >= M || col >= N) continue;
+      const float4 h = make_float4(rn_tf32_dev(v.x), rn_tf32_dev(v.y), rn_tf32_dev(v.z), rn_tf32_dev(v.w));
+      const float4 l = make_float4(rn_tf32_dev(v.x - h.x), rn_tf32_dev(v.y - h.y), rn_tf32_dev(v.z - h.z),
+                                   rn_tf32_dev(v.w - h.w));
+      const long long off = static_cast<long long>(row) * ld + col;
+      if (col + 3 < N) {
+        *reinterpret_cast<float4*>(H + off) = h;
+        *reinterpret_cast<float4*>(L + off) = l;
+      } else {
+        const float hh[4] = {h.x, h.y, h.z, h.w}, ll[4] = {l.x, l.y, l.z, l.w};
+        for (int e = 0; e < 4 && col + e < N; ++e) {
+          H[off + e] = hh[e];
+          L[off + e] = ll[e];
+        }
+      }
+    }
+    __syncwarp();
+  }
+}
+
+// The exact-mode attention backward's score tiles in one launch. For every
+// causal 128 x BN tile (queries x keys) of every (batch, head): S = Q K^T and
+// dP = dO V^T as 3xTF32 products (the two products' K steps one after the
+// other through the stage ring, each product's accumulations summed in its own
+// registers), then P = exp(S * scale - lse) and dS = P (dP - delta) * scale per
+// element (zero above the diagonal), written as TF32 pairs (hi = rn(v),
+// lo = rn(v - hi)): P to Ph, Pl and dS to Dh, Dl, the score buffers' layout.
+struct X3ScoreMaps {
+  CUtensorMap qh, ql, kh, kl, gh, gl, vh, vl;  // g: dO
+};
+
+struct X3ScoreOut {
+  float *ph, *pl, *dh, *dl;
+  long long ldS;
+  const float* lse;    // [batch * T], the forward's log-sum-exp per query row
+  const float* delta;  // [batch * T], rowsum(dO * O)
+  float scale;
+};
+
+template <int BN>
+__global__ void __launch_bounds__(X3_THREADS, 1)
+    attn3x_scores_grad_kernel(const __grid_constant__ X3ScoreMaps maps, X3ScoreOut out, int T, int K, int* err,
+                              GemmBatch bt, int total_tiles) {
+  using TL = X3BatchTile<BN>;
+  constexpr int STAGES = TL::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (base - raw_addr);
+  const uint32_t bar_base = base + STAGES * TL::STAGE;
+  auto full_bar = [&](int s) { return bar_base + 8u * s; };
+  auto empty_bar = [&](int s) { return bar_base + 8u * (STAGES + s); };
+  auto acc_full = [&](int b) { return bar_base + 8u * (2 * STAGES + b); };
+  auto acc_empty = [&](int b) { return bar_base + 8u * (2 * STAGES + 2 + b); };
+  constexpr int kBars = 2 * STAGES + 4;
+  const uint32_t tmem_slot = bar_base + 8u * kBars;
+  uint8_t* tail = smem + STAGES * TL::STAGE + 8 * kBars;
+  uint32_t* tmem_slot_ptr = reinterpret_cast<uint32_t*>(tail);
+  int* loads_issued = reinterpret_cast<int*>(tail + 8);
+  int* loads_consumed = loads_issued + 1;
+  static_assert(8 * kBars + 16 <= 256, "barriers and counters fit their 256 bytes");
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&maps.qh);
+    tma_prefetch_desc(&maps.ql);
+    tma_prefetch_desc(&maps.kh);
+    tma_prefetch_desc(&maps.kl);
+    tma_prefetch_desc(&maps.gh);
+    tma_prefetch_desc(&maps.gl);
+    tma_prefetch_desc(&maps.vh);
+    tma_prefetch_desc(&maps.vl);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(acc_full(b), 1);
+      mbar_init(acc_empty(b), 8);
+    }
+    *loads_issued = 0;
+    *loads_consumed = 0;
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 2 * BN);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot_ptr;
+  const int n_k = (K + BK - 1) / BK;  // K steps of each product
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer: S's K steps, then dP's
+      int it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+        const TileInfo ti = tile_info<BN, true>(t, T, T, K, bt);
+        if (ti.skip) continue;
+        const int a_zb = ti.z / bt.a_zdiv, a_zh = (ti.z % bt.a_zdiv) / bt.a_zgroup;
+        const int b_zb = ti.z / bt.b_zdiv, b_zh = (ti.z % bt.b_zdiv) / bt.b_zgroup;
+        for (int i = 0; i < 2 * n_k; ++i, ++it) {
+          const int s = it % STAGES, round = it / STAGES;
+          if (round > 0 && !mbar_wait(empty_bar(s), (round - 1) & 1, err, kErrWaitEmpty)) {
+            ok = false;
+            break;
+          }
+          const uint32_t sa = base + s * TL::STAGE, sb = sa + 2 * TL::A_BYTES;
+          mbar_arrive_expect_tx(full_bar(s), TL::STAGE);
+          const bool dp = i >= n_k;
+          const int k0 = (dp ? i - n_k : i) * BK;
+          load_box<true>(sa, dp ? &maps.gh : &maps.qh, full_bar(s), k0, ti.m0, a_zh, a_zb);
+          load_box<true>(sa + TL::A_BYTES, dp ? &maps.gl : &maps.ql, full_bar(s), k0, ti.m0, a_zh, a_zb);
+          load_box<true>(sb, dp ? &maps.vh : &maps.kh, full_bar(s), k0, ti.n0, b_zh, b_zb);
+          load_box<true>(sb + TL::B_BYTES, dp ? &maps.vl : &maps.kl, full_bar(s), k0, ti.n0, b_zh, b_zb);
+          *loads_issued = it + 1;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- UMMA issuer: X3_CHUNK-step accumulations, none spanning the two products
+      constexpr uint32_t idesc = idesc_tf32(BM, BN, false, false);
+      int it = 0, j = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+        const TileInfo ti = tile_info<BN, true>(t, T, T, K, bt);
+        if (ti.skip) continue;
+        for (int pr = 0; pr < 2 && ok; ++pr) {
+          for (int cb = 0; cb < n_k && ok; cb += X3_CHUNK) {
+            const int ce = min(n_k, cb + X3_CHUNK);
+            const int buf = j & 1;
+            if (j >= 2 && !mbar_wait(acc_empty(buf), ((j >> 1) - 1) & 1, err, kErrWaitAccum)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t acc = tmem_base + buf * BN;
+            for (int i = cb; i < ce; ++i, ++it) {
+              const int s = it % STAGES, round = it / STAGES;
+              if (!mbar_wait(full_bar(s), round & 1, err, kErrWaitFull)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              *loads_consumed = it + 1;
+              const uint32_t sa = base + s * TL::STAGE, sb = sa + 2 * TL::A_BYTES;
+#pragma unroll
+              for (int term = 0; term < 3; ++term) {
+#pragma unroll
+                for (int k = 0; k < BK / 8; ++k) {
+                  const uint32_t at = sa + (term == 0 ? TL::A_BYTES : 0);
+                  const uint32_t bt_ = sb + (term == 1 ? TL::B_BYTES : 0);
+                  umma_tf32(acc, smem_desc(at + k * 32, 16, 1024, kLayoutSw128),
+                            smem_desc(bt_ + k * 32, 16, 1024, kLayoutSw128), idesc,
+                            (i != cb || term != 0 || k != 0) ? 1u : 0u);
+                }
+              }
+              umma_commit(empty_bar(s));
+            }
+            if (!ok) break;
+            umma_commit(acc_full(buf));
+            ++j;
+          }
+        }
+      }
+    }
+  } else {
+    // ---------------- epilogue: 32 query rows x BN / 2 keys of the tile per warp
+    constexpr int NC = BN / 2;
+    const int quarter = warp & 3, half = (warp - 2) >> 2;
+    float4* stage_tile = reinterpret_cast<float4*>(smem + STAGES * TL::STAGE + 256) + (warp - 2) * 256;
+    int j = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+      const TileInfo ti = tile_info<BN, true>(t, T, T, K, bt);
+      if (ti.skip) continue;
+      const int q = ti.m0 + quarter * 32 + lane, k0 = ti.n0 + half * NC;  // this thread's query row, first key
+      const long long li = static_cast<long long>(ti.z) * T + q;
+      const long long zoff = (ti.z / bt.c_zdiv) * bt.c_sb + ((ti.z % bt.c_zdiv) / bt.c_zgroup) * bt.c_sh;
+      const int wrow0 = ti.m0 + quarter * 32;
+      float pv[NC], sum[NC];
+#pragma unroll
+      for (int pr = 0; pr < 2; ++pr) {  // S, then dP
+#pragma unroll
+        for (int e = 0; e < NC; ++e) sum[e] = 0.0f;
+        for (int cb = 0; ok && cb < n_k; cb += X3_CHUNK) {
+          const int buf = j & 1;
+          if (!mbar_wait(acc_full(buf), (j >> 1) & 1, err, kErrWaitAccum)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t acc = tmem_base + buf * BN + (static_cast<uint32_t>(quarter * 32) << 16) + half * NC;
+#pragma unroll
+          for (int c = 0; c < NC / 16; ++c) {
+            uint32_t r[16];
+            tmem_ld_32x32b_x16(acc + c * 16, r);
+#pragma unroll
+            for (int e = 0; e < 16; ++e) sum[c * 16 + e] += __uint_as_float(r[e]);
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(acc_empty(buf));
+          ++j;
+        }
+        if (!ok) break;
+        if (pr == 0) {  // P = exp(S * scale - lse), written while the UMMAs form dP
+          const float lse = q < T ? out.lse[li] : 0.0f;
+#pragma unroll
+          for (int e = 0; e < NC; ++e) pv[e] = (q < T && k0 + e <= q) ? expf(sum[e] * out.scale - lse) : 0.0f;
+          store_pair<NC>(pv, stage_tile, wrow0, k0, out.ph + zoff, out.pl + zoff, out.ldS, T, T);
+        } else {  // dS = P (dP - delta) * scale
+          const float dl = q < T ? out.delta[li] : 0.0f;
+#pragma unroll
+          for (int e = 0; e < NC; ++e) sum[e] = (pv[e] * (sum[e] - dl)) * out.scale;
+          store_pair<NC>(sum, stage_tile, wrow0, k0, out.dh + zoff, out.dl + zoff, out.ldS, T, T);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int i = *loads_consumed; i < *loads_issued; ++i)
+      if (!mbar_wait(full_bar(i % STAGES), (i / STAGES) & 1, err, kErrWaitDrain, 1000000000ull)) break;
+  }
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 2 * BN);
+  }
+  __syncthreads();
+}
+
 }  // namespace
 
 namespace {
@@ -1827,6 +2092,53 @@ int gemm_tf32_batched(int batch, int M, int N, int K, const BatchedOperand& A, c
     launch_majors<128, true>(A.mn_major, B.mn_major, ta, tb, C, ldc, R, ldc, M, N, K, batch, bt, d_err, stream);
   else
     launch_majors<256, true>(A.mn_major, B.mn_major, ta, tb, C, ldc, R, ldc, M, N, K, batch, bt, d_err, stream);
+  return launch_status();
+}
+
+int attention_scores_grad_3x(int batch, int T, int hd, const BatchedOperand& Qh, const BatchedOperand& Ql,
+                             const BatchedOperand& Kh, const BatchedOperand& Kl, const BatchedOperand& Gh,
+                             const BatchedOperand& Gl, const BatchedOperand& Vh, const BatchedOperand& Vl, float* Ph,
+                             float* Pl, float* Dh, float* Dl, long long ldS, const GemmBatch& bt_in, const float* lse,
+                             const float* delta, float scale, int* d_err, cudaStream_t stream) {
+  GemmBatch bt = bt_in;
+  bt.a_zdiv = Qh.zdiv;
+  bt.a_zgroup = Qh.zgroup;
+  bt.b_zdiv = Kh.zdiv;
+  bt.b_zgroup = Kh.zgroup;
+  if (batch < 0 || T < 0 || hd <= 0 || !Ph || !Pl || !Dh || !Dl || !lse || !delta) return kGemmBadArgument;
+  if (batch == 0 || T == 0) return 0;
+  const BatchedOperand* ops[8] = {&Qh, &Ql, &Kh, &Kl, &Gh, &Gl, &Vh, &Vl};
+  for (const BatchedOperand* o : ops)
+    if (!o->ptr || o->mn_major || !aligned16(o->ptr)) return o->ptr && !o->mn_major ? kGemmMisaligned : kGemmBadArgument;
+  if (Gh.zdiv != Qh.zdiv || Gh.zgroup != Qh.zgroup || Vh.zdiv != Kh.zdiv || Vh.zgroup != Kh.zgroup)
+    return kGemmBadArgument;  // dO is addressed like Q, V like K
+  if ((ldS & 3) || !aligned16(Ph) || !aligned16(Pl) || !aligned16(Dh) || !aligned16(Dl) || (bt.c_sb & 3) ||
+      (bt.c_sh & 3))
+    return kGemmMisaligned;
+  bt.causal = kCausalSkipUpper;
+  bt.k_off = 0;
+  bt.skip_empty = 0;
+  constexpr int BN = 128;
+  X3ScoreMaps maps{};
+  auto map = [&](CUtensorMap* m, const BatchedOperand& o, int rows) { return make_map4d(m, o, BK, rows); };
+  if (map(&maps.qh, Qh, BM) || map(&maps.ql, Ql, BM) || map(&maps.gh, Gh, BM) || map(&maps.gl, Gl, BM) ||
+      map(&maps.kh, Kh, BN) || map(&maps.kl, Kl, BN) || map(&maps.vh, Vh, BN) || map(&maps.vl, Vl, BN))
+    return kGemmTensorMap;
+  using TL = X3BatchTile<BN>;
+  auto kern = attn3x_scores_grad_kernel<BN>;
+  static thread_local int configured_device = -1;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (configured_device != dev) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TL::SMEM);
+    configured_device = dev;
+  }
+  const long long tiles = static_cast<long long>(batch) * ((T + BM - 1) / BM) * ((T + BN - 1) / BN);
+  const int sms = device_sms();
+  const X3ScoreOut out{Ph, Pl, Dh, Dl, ldS, lse, delta, scale};
+  kern<<<static_cast<int>(tiles < sms ? tiles : sms), X3_THREADS, TL::SMEM, stream>>>(maps, out, T, hd, d_err, bt,
+                                                                                      static_cast<int>(tiles));
+  ++t_launches;
   return launch_status();
 }
 

@@ -143,6 +143,18 @@ int gemm_3xtf32_sum(int M, int N, const GemmSegment* segs, int nseg, float* C, l
 // with the same majors. C = sum_g (Al Bh + Ah Bl + Ah Bh) (+ R).
 int gemm_3xtf32_pair_sum(int M, int N, const GemmSegment* hi, const GemmSegment* lo, int nseg, float* C,
                          long long ldc, const float* R, long long ldr, int* d_err, cudaStream_t stream);
+// The exact-mode attention backward's score tiles in one launch: for every
+// causal 128 x 128 tile (queries x keys) of every one of `batch` matrices,
+// S = Q K^T and dP = dO V^T (3xTF32, K = hd; hi/lo views as gemm_3xtf32_batched,
+// all K-major, dO addressed like Q and V like K), then P = exp(S * scale - lse)
+// and dS = P (dP - delta) * scale (zero above the diagonal) as TF32 pairs: P to
+// (Ph, Pl), dS to (Dh, Dl), [batch, T, ldS] through bt's output offsets; lse and
+// delta are [batch * T]. Tiles wholly above the diagonal are not written.
+int attention_scores_grad_3x(int batch, int T, int hd, const BatchedOperand& Qh, const BatchedOperand& Ql,
+                             const BatchedOperand& Kh, const BatchedOperand& Kl, const BatchedOperand& Gh,
+                             const BatchedOperand& Gl, const BatchedOperand& Vh, const BatchedOperand& Vl, float* Ph,
+                             float* Pl, float* Dh, float* Dl, long long ldS, const GemmBatch& bt, const float* lse,
+                             const float* delta, float scale, int* d_err, cudaStream_t stream);
 // Whether products of this shape (n_k K steps of 32 in all) run on CTA pairs.
 bool gemm_3xtf32_pair_suits(int M, int N, int n_k);
 }  // namespace mm

@@ -592,7 +592,7 @@ uint64_t mm_op_causal_attention(uint32_t tape, uint64_t q_h, uint64_t k_h, uint6
                                  dk->ptr, dv->ptr, delta->ptr, device_context().d_err, tpp->stream);
       } else if (tc3) {
         Buf ws = tpp->alloc(static_cast<size_t>(attention_3x_ws_floats(s, s.ldo)));
-        attention_backward_3x(s, q->data->ptr, k->data->ptr, v->data->ptr, o->ptr, dout, s.ldo, dq->ptr, dk->ptr,
+        attention_backward_3x(s, q->data->ptr, k->data->ptr, v->data->ptr, o->ptr, lse->ptr, dout, s.ldo, dq->ptr, dk->ptr,
                               dv->ptr, ws->ptr, device_context().d_err, tpp->stream);
       } else {
         attention_backward(s, q->data->ptr, k->data->ptr, v->data->ptr, o->ptr, lse->ptr, dout, s.ldo, dq->ptr,

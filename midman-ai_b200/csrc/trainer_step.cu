@@ -173,7 +173,7 @@ void Trainer::backward(int B, int T) {
       attention_backward_flash(shape, a.q, a.k, a.v, a.o, a.lse, do_, D, dq_, dk_, dv_, delta_, device_context().d_err,
                                stream_, &side);
     } else if (attn_3x_) {
-      attention_backward_3x(shape, a.q, a.k, a.v, a.o, do_, D, dq_, dk_, dv_, attn3_ws_, device_context().d_err,
+      attention_backward_3x(shape, a.q, a.k, a.v, a.o, a.lse, do_, D, dq_, dk_, dv_, attn3_ws_, device_context().d_err,
                             stream_);
     } else {
       attention_backward(shape, a.q, a.k, a.v, a.o, a.lse, do_, D, dq_, dk_, dv_, delta_, stream_);
