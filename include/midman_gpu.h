@@ -97,9 +97,10 @@ MM_GPU_EXPORT int32_t mm_gpu_gemm_sum(int32_t m, int32_t n, int32_t nseg, const 
  * lse and delta are [batch, n_heads, seq]. precision MM_GPU_TF32 runs the score
  * and value products on the tensor cores in the fused flash kernels;
  * MM_GPU_3XTF32 runs them on the tensor cores as three TF32 terms of hi/lo
- * operand pairs through score buffers, with the contractions over seq summed
- * in f32 every 256 values (about 4 * batch * n_heads * seq * seq floats of
- * library scratch). Both need head_dim 32, 64 or 128, row strides multiples of
+ * operand pairs through score buffers, the tensor-memory accumulations summed
+ * in f32 every 64 values of the contraction (about 4 * batch * n_heads * seq *
+ * seq floats of library scratch). The backward forms P from the lse the
+ * forward returned. Both need head_dim 32, 64 or 128, row strides multiples of
  * 4 and 16-byte aligned operands; other shapes run the FP32 flash kernels. */
 MM_GPU_EXPORT int32_t mm_gpu_attention_forward(int32_t batch, int32_t seq, int32_t n_heads, int32_t n_kv_heads,
                                                int32_t head_dim, const float *q, const float *k, const float *v,
