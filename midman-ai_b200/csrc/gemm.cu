@@ -1543,10 +1543,12 @@ __global__ void __launch_bounds__(X3_THREADS, 1)
           ++j;
         }
         if (!ok) break;
-        if (pr == 0) {  // P = exp(S * scale - lse), written while the UMMAs form dP
-          const float lse = q < T ? out.lse[li] : 0.0f;
+        if (pr == 0) {  // P = exp(S * scale - lse) = 2^(S * scale log2 e - lse log2 e), written while the UMMAs form dP
+          constexpr float kLog2e = 1.4426950408889634f;
+          const float lse2 = q < T ? out.lse[li] * kLog2e : 0.0f, scale2 = out.scale * kLog2e;
 #pragma unroll
-          for (int e = 0; e < NC; ++e) pv[e] = (q < T && k0 + e <= q) ? expf(sum[e] * out.scale - lse) : 0.0f;
+          for (int e = 0; e < NC; ++e)
+            pv[e] = (q < T && k0 + e <= q) ? ex2_approx(fmaf(sum[e], scale2, -lse2)) : 0.0f;
           store_pair<NC>(pv, stage_tile, wrow0, k0, out.ph + zoff, out.pl + zoff, out.ldS, T, T);
         } else {  // dS = P (dP - delta) * scale
           const float dl = q < T ? out.delta[li] : 0.0f;
@@ -2118,7 +2120,7 @@ int attention_scores_grad_3x(int batch, int T, int hd, const BatchedOperand& Qh,
   bt.causal = kCausalSkipUpper;
   bt.k_off = 0;
   bt.skip_empty = 0;
-  constexpr int BN = 128;
+  constexpr int BN = 128;  // 128 x 64 tiles measured 5% slower (each UMMA then reads A for half the work)
   X3ScoreMaps maps{};
   auto map = [&](CUtensorMap* m, const BatchedOperand& o, int rows) { return make_map4d(m, o, BK, rows); };
   if (map(&maps.qh, Qh, BM) || map(&maps.ql, Ql, BM) || map(&maps.gh, Gh, BM) || map(&maps.gl, Gl, BM) ||
