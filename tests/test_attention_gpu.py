@@ -3,7 +3,9 @@
 The reference computes softmax(q k^T / sqrt(hd) + mask(-1e9)) v with grouped heads
 expanded by copying (crates/midman-nn/src/attention.rs:79-102); its backward is the
 autograd of that chain. MM_GPU_TF32 runs the score/value products on the tensor cores
-(relative L2 within 5e-3), MM_GPU_3XTF32 the FP32 flash kernels (within 1e-5).
+in the fused flash kernels (relative L2 within 5e-3), MM_GPU_3XTF32 as three-term TF32
+products on the tensor cores through score buffers (within 1e-5); head_dim 16 runs the
+FP32 flash kernels in both.
 """
 import math
 
