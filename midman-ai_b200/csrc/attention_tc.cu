@@ -22,6 +22,7 @@
 #include "attention.h"
 #include "device.h"
 #include "gemm.h"
+#include "ptx.cuh"
 
 namespace mm {
 
@@ -84,22 +85,26 @@ __global__ void softmax_split_rows_kernel(const float* __restrict__ S, float* __
   float* hrow = Ph + r * ldS;
   float* lrow = Pl + r * ldS;
   const int n = i + 1, end = row_end(i, T);
+  // exp(x) as 2^(x log2 e) on the special-function unit (relative error ~2^-22,
+  // the TF32 pair's own level), with the scale folded into one multiply-add
+  constexpr float kLog2e = 1.4426950408889634f;
+  const float scale2 = scale * kLog2e;
   float m = -INFINITY;
-  for (int j = lane; j < n; j += 32) m = fmaxf(m, row[j] * scale);
+  for (int j = lane; j < n; j += 32) m = fmaxf(m, row[j] * scale2);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
   float s = 0.0f;
-  for (int j = lane; j < n; j += 32) s += expf(row[j] * scale - m);
+  for (int j = lane; j < n; j += 32) s += ex2_approx(fmaf(row[j], scale2, -m));
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
   const float inv = 1.0f / s;
   for (int j = lane; j < end; j += 32) {
-    const float p = j < n ? expf(row[j] * scale - m) * inv : 0.0f;
+    const float p = j < n ? ex2_approx(fmaf(row[j], scale2, -m)) * inv : 0.0f;
     const float h = rn_tf32(p);
     hrow[j] = h;
     lrow[j] = rn_tf32(p - h);
   }
-  if (lse && lane == 0) lse[r] = m + logf(s);
+  if (lse && lane == 0) lse[r] = (m + log2f(s)) / kLog2e;  // ln(sum exp): back from base 2
 }
 
 int blocks_for(long long threads) {
